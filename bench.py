@@ -1,0 +1,430 @@
+#!/usr/bin/env python
+"""SANTA++ sparse decode attention throughput on B200.
+
+One step = one decode step of SANTA++ attention for every (sequence, query
+head) of the batch: cluster selection (q . centroid scoring, top-k) plus the
+gather attention over the selected clusters, the uniformly sampled remainder
+and the exact recent window.  Default workload: Qwen2.5-7B attention shape
+(28 query heads, 4 KV heads, head_dim 128), bf16 K/V, batch 8 at 32K context,
+256 centroids per KV head, top-16 clusters + 256 samples per head, 128 steps
+with fresh queries.  Data: seeded synthetic Gaussian-mixture keys.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).  ``--impl reference`` times the CPU
+restatement of the reference algorithm on the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "opus-lab-notebooks_b200"))
+sys.path.insert(0, REPO)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+from santapp_b200.synthetic import QWEN3_8B_128K, QWEN7B_32K, make_decode_workload  # noqa: E402
+
+WORKLOADS = {"qwen7b-32k": QWEN7B_32K, "qwen3-8b-128k": QWEN3_8B_128K}
+METRIC = "SANTA++ decode attn tokens/s @32K-128K ctx; achieved HBM GB/s vs 8 TB/s peak"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="qwen7b-32k")
+    ap.add_argument("--mode", default="hybrid")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0,
+                    help="bound on the CPU-baseline sample")
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait()
+        self.file.flush()
+        rows = [r.split(",") for r in open(self.file.name).read().strip().splitlines() if r]
+        os.unlink(self.file.name)
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            if len(r) < 9:
+                continue
+            for name, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def algorithmic_bytes(step_runner, q, step, shape, summ):
+    """Distinct K/V rows the attend kernel must read for this step (union of
+    the group's selected clusters, the recent window, distinct sampled rows
+    outside that union), plus what the select kernel must read."""
+    from santapp_b200.attention import santapp as S
+    sel, rows, _ = S.santa_decode_select(
+        q, step_runner.key_cache, step_runner.value_cache, summ, mode=step_runner.mode,
+        n_total=shape.context, topk_clusters=shape.topk_clusters, samples=shape.samples,
+        seed=step_runner.p.seed, step=step)
+    B, Hq, G = sel.shape
+    g = shape.group
+    Hkv = Hq // g
+    N = shape.sample_end
+    covered = torch.zeros(B, Hkv, N, dtype=torch.bool, device=q.device)
+    union = sel.view(B, Hkv, g, G).amax(dim=2).bool()              # [B, Hkv, G]
+    starts = summ.starts.long()
+    lens = summ.lengths_long.long()
+    pos = torch.arange(N, device=q.device)
+    # row -> cluster row via the cluster starts (rows are cluster-contiguous)
+    for b in range(B):
+        for kv in range(Hkv):
+            ng = int(summ.n_groups[b, kv])
+            st = starts[b, kv, :ng]
+            cid = torch.searchsorted(st, pos, right=True) - 1
+            covered[b, kv] = union[b, kv, cid]
+    union_rows = int(covered.sum())
+    srows = rows.view(B, Hkv, g * shape.samples).long()
+    extra = 0
+    for b in range(B):
+        for kv in range(Hkv):
+            r = srows[b, kv]
+            r = r[r >= 0]
+            r = torch.unique(r)
+            extra += int((~covered[b, kv, r]).sum())
+    recent = B * Hkv * (shape.context - shape.sample_end)
+    esize = 2 if shape.kv_dtype == torch.bfloat16 else 4
+    row_bytes = 2 * shape.head_dim * esize  # K and V
+    attend = (union_rows + extra + recent) * row_bytes
+    select = B * Hkv * shape.n_clusters * (shape.head_dim * 4 + 12)  # centroids + starts/len/log_n
+    del lens
+    return attend, select, union_rows + extra + recent
+
+
+def run_ours(args, rank, world):
+    from santapp_b200.attention import santapp as S
+    shape = WORKLOADS[args.workload]
+    if world > 1:
+        raise SystemExit("multi-GPU decode is run by bench_multi (sequence shards)")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n_q = max(shape.steps, args.steps + args.warmup)
+    from santapp_b200.synthetic import scaled_shape
+    w = make_decode_workload(scaled_shape(shape, steps=n_q), seed=args.seed, device=dev)
+    labels = w.labels[:, :, :shape.sample_end].contiguous()
+    summ = S.build_summary(w.keys, w.values, labels, shape.n_clusters,
+                           sample_end=shape.sample_end, n_total=shape.context)
+    del labels
+    runner = S.DecodeStep(w.keys, w.values, summ, num_query_heads=shape.num_query_heads,
+                          mode=args.mode, n_total=shape.context,
+                          topk_clusters=shape.topk_clusters, samples=shape.samples,
+                          seed=args.seed)
+    queries = w.queries
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize()
+
+    # algorithmic bytes of every timed step (selection read back, outside timing)
+    attend_bytes, select_bytes, rows_touched = [], [], []
+    for i in range(args.steps):
+        step = args.warmup + i
+        a_b, s_b, r_t = algorithmic_bytes(runner, queries[step], step, shape, summ)
+        attend_bytes.append(a_b)
+        select_bytes.append(s_b)
+        rows_touched.append(r_t)
+    torch.cuda.synchronize()
+
+    for i in range(args.warmup):
+        flush.zero_()
+        runner(queries[i], step=i)
+    torch.cuda.synchronize()
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step = args.warmup + i
+        flush.zero_()                       # L2 flush outside the timed events
+        ev[i][0].record()
+        runner.plan(queries[step], step=step)
+        ev[i][1].record()
+        runner.execute()
+        ev[i][2].record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    clk = clocks.stop()
+    plan_ms = np.array([e[0].elapsed_time(e[1]) for e in ev])
+    att_ms = np.array([e[1].elapsed_time(e[2]) for e in ev])
+    step_ms = plan_ms + att_ms
+    total_s = step_ms.sum() / 1e3
+    value = shape.batch * args.steps / total_s
+    peak, peak_kind = peaks()
+    achieved = float(np.sum(attend_bytes) / (att_ms.sum() / 1e3) / 1e9)
+    traffic = load_traffic(shape)
+
+    e2e = None if args.no_e2e else run_e2e(args, shape, w, summ, runner)
+    cpu = None if args.no_cpu_baseline else cpu_baseline_sample(args, shape, w, summ)
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": float(step_ms.mean()),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16" if shape.kv_dtype == torch.bfloat16 else "f32",
+        "data": "synthetic (seeded Gaussian-mixture keys, N(0,1) values and queries)",
+        "config": {
+            "workload": shape.name,
+            "query_heads": shape.num_query_heads, "kv_heads": shape.num_kv_heads,
+            "head_dim": shape.head_dim, "batch": shape.batch, "context": shape.context,
+            "clusters": shape.n_clusters, "topk_clusters": shape.topk_clusters,
+            "samples": shape.samples, "recent_window": shape.recent_window, "mode": args.mode,
+            "parallelism": "single GPU",
+            "l2": f"flushed before every step ({L2_FLUSH_BYTES >> 20} MiB write, outside events)",
+        },
+        "phase_ms": {"select": float(plan_ms.mean()), "attend": float(att_ms.mean())},
+        "roofline": {
+            "kernel": "decode_attend_mma_kernel",
+            "bound": "hbm",
+            "achieved": achieved,
+            "peak": peak,
+            "peak_kind": peak_kind,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "traffic": traffic,
+            "algorithmic_bytes_per_launch": float(np.mean(attend_bytes)),
+            "rows_touched_per_step": float(np.mean(rows_touched)),
+            "dense_kv_bytes_per_step": float(shape.batch * shape.num_kv_heads * shape.context
+                                             * shape.head_dim * 2 * 2),
+        },
+        "select_roofline": {
+            "achieved": float(np.sum(select_bytes) / (plan_ms.sum() / 1e3) / 1e9),
+            "unit": "GB/s",
+        },
+        "wall_s": wall,
+        "clocks": clk,
+        "gpu_launches": runner.kernels_per_call * args.steps,
+        "e2e": e2e,
+        "cpu_baseline": cpu,
+    }
+    return line
+
+
+def load_traffic(shape):
+    """Per-launch DRAM bytes of the attend kernel from the committed ncu summary."""
+    path = os.path.join(REPO, "profiles", f"decode_attend_{shape.name}.json")
+    if not os.path.exists(path):
+        return None
+    try:
+        return float(json.load(open(path))["dram_bytes_per_launch"])
+    except (KeyError, ValueError):
+        return None
+
+
+def run_e2e(args, shape, w, summ, runner):
+    """Through the public santa_decode API with host buffers: per step copy
+    the queries host->device from pinned memory, decode, read the output back."""
+    from santapp_b200.attention import santapp as S
+    steps = args.steps
+    q_host = w.queries[:steps].cpu().pin_memory()
+    out_host = torch.empty(shape.batch, shape.num_query_heads, shape.head_dim).pin_memory()
+    q_dev = torch.empty_like(w.queries[0])
+    ws = S.DecodeWorkspace()
+    kw = dict(mode=args.mode, n_total=shape.context, topk_clusters=shape.topk_clusters,
+              samples=shape.samples, seed=args.seed, workspace=ws)
+    for i in range(2):
+        q_dev.copy_(q_host[i], non_blocking=True)
+        r = S.santa_decode(q_dev, w.keys, w.values, summ, step=i, **kw)
+        out_host.copy_(r.out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(steps):
+        q_dev.copy_(q_host[i], non_blocking=True)
+        r = S.santa_decode(q_dev, w.keys, w.values, summ, step=i, **kw)
+        out_host.copy_(r.out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    dt = time.perf_counter() - t0
+    return {"value": shape.batch * steps / dt, "unit": "tokens/s",
+            "h2d_bytes_per_step": int(q_host[0].numel() * 4),
+            "d2h_bytes_per_step": int(out_host.numel() * 4),
+            "api": "santapp_b200.attention.santa_decode (ctypes -> santa_decode C ABI)"}
+
+
+def _oracle_inputs(shape, w, summ, pairs):
+    from oracle import santa_oracle as O
+    data = {}
+    for b, kv in pairs:
+        K = w.keys[b, kv].float().cpu().numpy()
+        V = w.values[b, kv].float().cpu().numpy()
+        lab = w.labels[b, kv, :shape.sample_end].cpu().numpy()
+        data[(b, kv)] = (K, V, O.build_summary(K[:shape.sample_end], lab, shape.n_clusters))
+    return data
+
+
+def _cpu_head_call(shape, data, q, b, h, step, seed):
+    from oracle import santa_oracle as O
+    kv = h // shape.group
+    K, V, o = data[(b, kv)]
+    g = O.centroid_guess(o, q, shape.scale)
+    chosen = O.select_topk(g, shape.topk_clusters)
+    n_rest = shape.sample_end - int(o.lengths[chosen].sum())
+    ranks = O.philox_ranks(seed, step, b, h, shape.samples, n_rest)
+    return O.decode_hybrid(q, K, V, o, shape.sample_end, shape.topk_clusters, ranks, shape.scale)
+
+
+def cpu_baseline_sample(args, shape, w, summ):
+    """The CPU restatement timed on one host core over a bounded sample of
+    head calls of one step; reported as tokens/s (Hq head calls = 1 token)."""
+    pairs = [(0, kv) for kv in range(shape.num_kv_heads)]
+    data = _oracle_inputs(shape, w, summ, pairs)
+    q = w.queries[args.warmup].cpu().numpy()
+    calls = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < args.cpu_seconds and calls < 4 * shape.num_query_heads:
+        h = calls % shape.num_query_heads
+        _cpu_head_call(shape, data, q[0, h], 0, h, args.warmup, args.seed)
+        calls += 1
+    dt = time.perf_counter() - t0
+    return {"value": calls / shape.num_query_heads / dt, "unit": "tokens/s", "cores": 1,
+            "kind": "port",
+            "sample": f"{calls} query-head calls of sequence 0 at step {args.warmup} "
+                      f"({calls / shape.num_query_heads:.1f} tokens), numpy/C oracle, 1 thread"}
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the CPU restatement on all host cores
+# ---------------------------------------------------------------------------
+
+_REF = {}
+
+
+def _ref_worker(task):
+    b, h, step = task
+    shape, data, queries, seed = _REF["shape"], _REF["data"], _REF["queries"], _REF["seed"]
+    _cpu_head_call(shape, data, queries[step][b, h], b, h, step, seed)
+    return 1
+
+
+def run_reference(args, rank, world):
+    import multiprocessing as mp
+    if rank != 0:
+        return None
+    shape = WORKLOADS[args.workload]
+    from santapp_b200.synthetic import scaled_shape
+    # one sequence's cache (its 4 KV heads) is enough to time per-token cost;
+    # each step decodes that sequence's Hq heads across all host cores
+    sh1 = scaled_shape(shape, batch=1, steps=args.steps + args.warmup)
+    w = make_decode_workload(sh1, seed=args.seed, device="cpu")
+    pairs = [(0, kv) for kv in range(shape.num_kv_heads)]
+    data = _oracle_inputs(sh1, w, None, pairs)
+    _REF.update(shape=sh1, data=data, queries=w.queries.numpy(), seed=args.seed)
+    cores = os.cpu_count() or 1
+    ctx = mp.get_context("fork")  # no CUDA in this process: fork shares the cache arrays
+    with ctx.Pool(cores) as pool:
+        for i in range(args.warmup):
+            pool.map(_ref_worker, [(0, h, i) for h in range(shape.num_query_heads)])
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            step = args.warmup + i
+            pool.map(_ref_worker, [(0, h, step) for h in range(shape.num_query_heads)])
+        dt = time.perf_counter() - t0
+    value = args.steps / dt
+    sample = (f"sequence 0 of the batch ({shape.num_query_heads} query-head calls per step, "
+              f"{shape.num_kv_heads} KV heads x {shape.context} tokens), numpy/C oracle")
+    return {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded Gaussian-mixture keys, N(0,1) values and queries)",
+        "config": {"workload": shape.name, "mode": args.mode, "batch": shape.batch,
+                   "context": shape.context, "timed_batch": 1},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "the reference is pure Python/PyTorch and is not present at run time; its "
+                "CPU algorithm is timed through the oracle restatement",
+    }
+
+
+def main():
+    args = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    if world > 1 or args.gpus > 1:
+        from santapp_b200.parallel_bench import run_sharded
+        line = run_sharded(args, WORKLOADS, METRIC)
+    else:
+        line = run_ours(args, rank, world)
+    if line is not None and rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,184 @@
+/*
+ * santa_b200.h -- C ABI of the B200 (sm_100a) SANTA++ attention library.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t,
+ * is stream-ordered (no host synchronisation unless stated), allocates no
+ * device memory and returns SANTA_OK (0) or a negative status code.  Callers
+ * own all buffers; scratch space is passed in as a workspace whose size the
+ * matching *_workspace_bytes query reports.
+ *
+ * Reference interfaces replaced (paths inside santapp-ruler-bench/src):
+ *   santa_build_summary        santapp_ruler/attention/santapp.py:508-540
+ *                              (SantaPlusEngine._build_summary)
+ *   santa_decode               santapp_ruler/attention/santapp.py:365-506
+ *                              (SantaPlusEngine._approximate_attention), batched
+ *                              over (batch, query head) as the decode branch of
+ *                              _attention_forward does per head at :347-358
+ */
+#ifndef SANTA_B200_H
+#define SANTA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------- */
+#define SANTA_OK 0
+#define SANTA_ERR_INVALID_ARGUMENT -1 /* bad shape, stride, index or budget */
+#define SANTA_ERR_UNSUPPORTED -2      /* valid but not built (dtype, head_dim) */
+#define SANTA_ERR_CUDA -3             /* a CUDA runtime call failed */
+#define SANTA_ERR_WORKSPACE -4        /* workspace missing or too small */
+
+/* ---- enums ----------------------------------------------------------- */
+#define SANTA_DTYPE_F32 0
+#define SANTA_DTYPE_BF16 1
+
+/* decode modes: the four reference modes (santapp.py:395-468) plus the
+ * exact-top-k-plus-uniform-samples estimator. */
+#define SANTA_MODE_TOPK 0    /* budget walk over ranked clusters, plain softmax */
+#define SANTA_MODE_GUIDED 1  /* cluster-guided importance sampling */
+#define SANTA_MODE_UNIFORM 2 /* uniform importance sampling over the prefix */
+#define SANTA_MODE_SANTA 3   /* exact-softmax proposal (reads every old key) */
+#define SANTA_MODE_HYBRID 4  /* exact top-k clusters + uniform samples of the rest */
+
+#define SANTA_SAMPLES_DEVICE 0   /* draw samples on the device (Philox4x32-10) */
+#define SANTA_SAMPLES_INJECTED 1 /* caller passes the draws (parity runs) */
+
+/* ---- shapes ---------------------------------------------------------- */
+
+/* Geometry of one attention layer's KV cache.
+ * key/value caches are [batch, num_kv_heads, capacity, head_dim], row-major;
+ * tokens [0, n_total) are valid; [0, sample_end) is the clustered old prefix
+ * (santapp.py:374-379), [sample_end, n_total) is attended exactly. */
+typedef struct SantaGeometry {
+    int32_t batch;
+    int32_t num_kv_heads;
+    int32_t group;        /* query heads per KV head (GQA), <= 8 */
+    int32_t head_dim;     /* 64 or 128 */
+    int32_t capacity;     /* row stride of the cache in tokens */
+    int32_t n_total;      /* valid tokens */
+    int32_t sample_end;   /* end of the clustered prefix, 0 < sample_end <= n_total */
+    int32_t kv_dtype;     /* SANTA_DTYPE_F32 or SANTA_DTYPE_BF16 */
+} SantaGeometry;
+
+/* Cluster summary of every (batch, KV head): the ClusterSummary fields of
+ * santapp.py:53-63 in fixed-stride arrays, plus a copy of the old prefix of
+ * K and V physically reordered so that each cluster is a contiguous run.
+ * Per (b, kv): rows [0, n_groups) of starts/lengths/log_n/centroids are the
+ * non-empty clusters in ascending cluster id (santapp.py:513-524). */
+typedef struct SantaSummary {
+    int32_t *members;      /* [B, Hkv, sample_end] token ids, sorted by (cluster, token) */
+    int32_t *positions;    /* [B, Hkv, sample_end] inverse permutation of members */
+    int32_t *starts;       /* [B, Hkv, max_groups] start of each cluster in members */
+    int32_t *lengths;      /* [B, Hkv, max_groups] */
+    float *log_n;          /* [B, Hkv, max_groups] fl32(log(fl64(length))) */
+    float *centroids;      /* [B, Hkv, max_groups, head_dim] mean key, fp32 */
+    int32_t *n_groups;     /* [B, Hkv] number of non-empty clusters */
+    void *sorted_key;      /* [B, Hkv, sample_end, head_dim] cache dtype */
+    void *sorted_value;    /* [B, Hkv, sample_end, head_dim] cache dtype */
+    int32_t max_groups;    /* cluster id bound (n_clusters), <= 1024 */
+} SantaSummary;
+
+typedef struct SantaDecodeParams {
+    int32_t mode;          /* SANTA_MODE_* */
+    int32_t topk_clusters; /* HYBRID: exact clusters per query head */
+    int32_t token_budget;  /* TOPK: samples_per_head of the reference (santapp.py:391, 409) */
+    int32_t samples;       /* GUIDED/UNIFORM/SANTA/HYBRID: draws per query head, <= 1024 */
+    float scale;           /* softmax scale, 1/sqrt(head_dim) in the reference */
+    int32_t sample_source; /* SANTA_SAMPLES_DEVICE or SANTA_SAMPLES_INJECTED */
+    uint64_t seed;         /* Philox key for device sampling */
+    uint64_t step;         /* Philox counter word (decode step) */
+    int32_t num_splits;    /* CTAs per (batch, KV head); 0 = pick automatically */
+} SantaDecodeParams;
+
+/* ---- library --------------------------------------------------------- */
+const char *santa_status_string(int status);
+/* Last CUDA error recorded by an entry point that returned SANTA_ERR_CUDA. */
+int santa_last_cuda_error(void);
+const char *santa_version(void);
+
+/* ---- cluster summary -------------------------------------------------- */
+
+/* Workspace for santa_build_summary. */
+int santa_build_summary_workspace_bytes(const SantaGeometry *geo, int32_t n_clusters,
+                                        size_t *bytes);
+
+/* Build the cluster summary from per-token cluster labels.
+ * key_cache/value_cache: the layer's cache (geometry above).
+ * labels: [B, Hkv, sample_end] int32 in [0, n_clusters).
+ * Replaces SantaPlusEngine._build_summary (santapp.py:508-540): counts by
+ * bincount, members by a stable sort on the label, starts by exclusive
+ * cumsum, centroids as sequential fp32 sums in ascending token order (the
+ * order CPU index_add_ uses) divided by the count.  Also writes the
+ * cluster-sorted K/V copy that santa_decode streams from. */
+int santa_build_summary(const SantaGeometry *geo, const void *key_cache,
+                        const void *value_cache, const int32_t *labels,
+                        int32_t n_clusters, const SantaSummary *out,
+                        void *workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* ---- sparse decode ---------------------------------------------------- */
+
+int santa_decode_workspace_bytes(const SantaGeometry *geo, const SantaDecodeParams *p,
+                                 int32_t max_groups, size_t *bytes);
+
+/* One decode step for every (batch, query head).
+ * q:        [B, Hkv*group, head_dim] fp32 query (RoPE already applied).
+ * sample_a / sample_b: [B, Hq, samples] int32 draws when
+ *           sample_source == SANTA_SAMPLES_INJECTED, else NULL:
+ *             HYBRID  a = rank in [0, n_rest) among non-selected prefix tokens
+ *             GUIDED  a = cluster row in [0, n_groups), b = offset inside it
+ *             UNIFORM a = token id in [0, sample_end)
+ *             SANTA   a = token id in [0, sample_end)
+ * out:      [B, Hq, head_dim] fp32 attention output.
+ * lse:      [B, Hq] fp32 log of the estimator's softmax denominator (natural
+ *           log), for merging partial results across sequence shards.
+ * n_exact:  [B, Hq] int32 exact old-prefix tokens (TOPK/HYBRID), or NULL.
+ * ess:      [B, Hq] fp32 effective sample size / samples (santapp.py:481-485)
+ *           for sampling modes, or NULL. */
+int santa_decode(const SantaGeometry *geo, const SantaDecodeParams *p, const float *q,
+                 const void *key_cache, const void *value_cache,
+                 const SantaSummary *summary, const int32_t *sample_a,
+                 const int32_t *sample_b, float *out, float *lse, int32_t *n_exact,
+                 float *ess, void *workspace, size_t workspace_bytes,
+                 cudaStream_t stream);
+
+/* santa_decode in two stream-ordered halves sharing one workspace:
+ *   santa_decode_plan     centroid scoring, ranking, selection and draws
+ *                         (santapp.py:395-468); writes the per-(b, kv) work
+ *                         list into the workspace and n_exact if non-NULL;
+ *   santa_decode_execute  the gather attention and the LSE merge over that
+ *                         work list (santapp.py:472-506).
+ * Both must be called with the same geometry, params, q and summary. */
+int santa_decode_plan(const SantaGeometry *geo, const SantaDecodeParams *p, const float *q,
+                      const void *key_cache, const void *value_cache,
+                      const SantaSummary *summary, const int32_t *sample_a,
+                      const int32_t *sample_b, int32_t *n_exact, void *workspace,
+                      size_t workspace_bytes, cudaStream_t stream);
+int santa_decode_execute(const SantaGeometry *geo, const SantaDecodeParams *p, const float *q,
+                         const void *key_cache, const void *value_cache,
+                         const SantaSummary *summary, float *out, float *lse, float *ess,
+                         void *workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* Selection step of santa_decode alone, read out per query head: which
+ * clusters are attended exactly and which sorted rows were sampled.  Same
+ * arguments and workspace as santa_decode.  Replaces the ranking and draw
+ * part of _approximate_attention (santapp.py:397-411, 429-468) for tests and
+ * for the distinct-row traffic accounting.
+ * selected:    [B, Hq, max_groups] uint8, 1 = cluster row attended exactly, or NULL.
+ * sample_rows: [B, Hq, samples] int32 row in the cluster-sorted copy, -1 = none, or NULL.
+ * n_exact:     [B, Hq] int32, or NULL. */
+int santa_decode_select(const SantaGeometry *geo, const SantaDecodeParams *p, const float *q,
+                        const void *key_cache, const void *value_cache,
+                        const SantaSummary *summary, const int32_t *sample_a,
+                        const int32_t *sample_b, uint8_t *selected, int32_t *sample_rows,
+                        int32_t *n_exact, void *workspace, size_t workspace_bytes,
+                        cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SANTA_B200_H */

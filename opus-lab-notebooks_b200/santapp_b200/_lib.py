@@ -1,0 +1,138 @@
+"""ctypes binding of the C ABI declared in include/santa_b200.h.
+
+Only plain pointers, sizes and the raw ``cudaStream_t`` cross the boundary;
+torch is used on this side for device memory and streams only.  Loading fails
+loudly when the shared library is missing: there is no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+from . import _build
+
+SANTA_OK = 0
+SANTA_ERR_INVALID_ARGUMENT = -1
+SANTA_ERR_UNSUPPORTED = -2
+SANTA_ERR_CUDA = -3
+SANTA_ERR_WORKSPACE = -4
+
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
+
+MODE_TOPK = 0
+MODE_GUIDED = 1
+MODE_UNIFORM = 2
+MODE_SANTA = 3
+MODE_HYBRID = 4
+MODES = {"topk": MODE_TOPK, "guided": MODE_GUIDED, "uniform": MODE_UNIFORM,
+         "santa": MODE_SANTA, "hybrid": MODE_HYBRID}
+
+SAMPLES_DEVICE = 0
+SAMPLES_INJECTED = 1
+
+_vp = ctypes.c_void_p
+_i32 = ctypes.c_int32
+
+
+class SantaGeometry(ctypes.Structure):
+    _fields_ = [("batch", _i32), ("num_kv_heads", _i32), ("group", _i32), ("head_dim", _i32),
+                ("capacity", _i32), ("n_total", _i32), ("sample_end", _i32), ("kv_dtype", _i32)]
+
+
+class SantaSummary(ctypes.Structure):
+    _fields_ = [("members", _vp), ("positions", _vp), ("starts", _vp), ("lengths", _vp),
+                ("log_n", _vp), ("centroids", _vp), ("n_groups", _vp), ("sorted_key", _vp),
+                ("sorted_value", _vp), ("max_groups", _i32)]
+
+
+class SantaDecodeParams(ctypes.Structure):
+    _fields_ = [("mode", _i32), ("topk_clusters", _i32), ("token_budget", _i32),
+                ("samples", _i32), ("scale", ctypes.c_float), ("sample_source", _i32),
+                ("seed", ctypes.c_uint64), ("step", ctypes.c_uint64), ("num_splits", _i32)]
+
+
+# Every symbol include/santa_b200.h declares, with its ctypes signature.
+_P = ctypes.POINTER
+SIGNATURES = {
+    "santa_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "santa_last_cuda_error": (ctypes.c_int, []),
+    "santa_version": (ctypes.c_char_p, []),
+    "santa_build_summary_workspace_bytes": (ctypes.c_int, [_P(SantaGeometry), _i32,
+                                                           _P(ctypes.c_size_t)]),
+    "santa_build_summary": (ctypes.c_int, [_P(SantaGeometry), _vp, _vp, _vp, _i32,
+                                           _P(SantaSummary), _vp, ctypes.c_size_t, _vp]),
+    "santa_decode_workspace_bytes": (ctypes.c_int, [_P(SantaGeometry), _P(SantaDecodeParams),
+                                                    _i32, _P(ctypes.c_size_t)]),
+    "santa_decode": (ctypes.c_int, [_P(SantaGeometry), _P(SantaDecodeParams), _vp, _vp, _vp,
+                                    _P(SantaSummary), _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                    ctypes.c_size_t, _vp]),
+    "santa_decode_plan": (ctypes.c_int, [_P(SantaGeometry), _P(SantaDecodeParams), _vp, _vp,
+                                         _vp, _P(SantaSummary), _vp, _vp, _vp, _vp,
+                                         ctypes.c_size_t, _vp]),
+    "santa_decode_execute": (ctypes.c_int, [_P(SantaGeometry), _P(SantaDecodeParams), _vp, _vp,
+                                            _vp, _P(SantaSummary), _vp, _vp, _vp, _vp,
+                                            ctypes.c_size_t, _vp]),
+    "santa_decode_select": (ctypes.c_int, [_P(SantaGeometry), _P(SantaDecodeParams), _vp, _vp,
+                                           _vp, _P(SantaSummary), _vp, _vp, _vp, _vp, _vp, _vp,
+                                           ctypes.c_size_t, _vp]),
+}
+
+_lock = threading.Lock()
+_handle = None
+
+
+class SantaError(RuntimeError):
+    """Raised when a C ABI entry point returns a non-zero status."""
+
+    def __init__(self, fn: str, status: int):
+        lib = _handle
+        msg = lib.santa_status_string(status).decode() if lib is not None else str(status)
+        if status == SANTA_ERR_CUDA and lib is not None:
+            msg += f" (cudaError {lib.santa_last_cuda_error()})"
+        super().__init__(f"{fn} failed: {msg}")
+        self.status = status
+
+
+def library_path() -> str:
+    return _build.LIB_PATH
+
+
+def load(build_if_missing: bool = True):
+    """Load libsanta_b200.so (building it with nvcc first if it is absent)."""
+    global _handle
+    with _lock:
+        if _handle is not None:
+            return _handle
+        path = _build.LIB_PATH
+        if not os.path.exists(path):
+            if not build_if_missing:
+                raise RuntimeError(f"SANTA++ CUDA library not built: {path}")
+            _build.build()
+        lib = ctypes.CDLL(path)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _handle = lib
+        return lib
+
+
+def check(fn: str, status: int) -> None:
+    if status != SANTA_OK:
+        raise SantaError(fn, status)
+
+
+def ptr(t) -> int | None:
+    """Raw device pointer of a tensor (None for a missing optional tensor)."""
+    if t is None:
+        return None
+    return t.data_ptr()
+
+
+def stream_handle(stream=None) -> int:
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream

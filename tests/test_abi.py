@@ -1,0 +1,87 @@
+"""The C ABI library loads and exports every symbol include/*.h declares (CPU only)."""
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+from santapp_b200 import _build, _lib
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = []
+    for h in glob.glob(os.path.join(REPO, "include", "*.h")):
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        for m in re.finditer(r"^\s*(?:const\s+)?[A-Za-z_][A-Za-z0-9_]*\s*\*?\s*(santa_[a-z0-9_]+)\s*\(",
+                             src, flags=re.M):
+            names.append(m.group(1))
+    return sorted(set(names))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    for want in ("santa_build_summary", "santa_decode", "santa_decode_select",
+                 "santa_decode_workspace_bytes", "santa_status_string"):
+        assert want in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_status_strings_and_version():
+    lib = _lib.load()
+    assert lib.santa_status_string(0) == b"ok"
+    assert b"workspace" in lib.santa_status_string(-4)
+    assert b"sm_100a" in lib.santa_version()
+
+
+def test_struct_layout_matches_c():
+    # SantaDecodeParams: 4 x int32, float, int32, 2 x uint64, int32 (+pad)
+    assert ctypes.sizeof(_lib.SantaDecodeParams) == 48
+    assert _lib.SantaDecodeParams.seed.offset == 24
+    assert ctypes.sizeof(_lib.SantaGeometry) == 32
+    assert _lib.SantaSummary.max_groups.offset == 72
+
+
+def test_workspace_queries_validate_arguments():
+    lib = _lib.load()
+    geo = _lib.SantaGeometry(8, 4, 7, 128, 32768, 32768, 32704, _lib.DTYPE_BF16)
+    n = ctypes.c_size_t()
+    assert lib.santa_build_summary_workspace_bytes(ctypes.byref(geo), 256, ctypes.byref(n)) == 0
+    assert n.value > 0
+    p = _lib.SantaDecodeParams(_lib.MODE_HYBRID, 16, 0, 256, 0.088, 0, 0, 0, 0)
+    assert lib.santa_decode_workspace_bytes(ctypes.byref(geo), ctypes.byref(p), 256,
+                                            ctypes.byref(n)) == 0
+    bad = _lib.SantaGeometry(8, 4, 7, 96, 32768, 32768, 32704, _lib.DTYPE_BF16)
+    assert lib.santa_decode_workspace_bytes(ctypes.byref(bad), ctypes.byref(p), 256,
+                                            ctypes.byref(n)) == _lib.SANTA_ERR_UNSUPPORTED
+    bad = _lib.SantaGeometry(8, 4, 7, 128, 32768, 32768, 40000, _lib.DTYPE_BF16)
+    assert lib.santa_decode_workspace_bytes(ctypes.byref(bad), ctypes.byref(p), 256,
+                                            ctypes.byref(n)) == _lib.SANTA_ERR_INVALID_ARGUMENT
+    p_bad = _lib.SantaDecodeParams(_lib.MODE_HYBRID, 16, 0, 5000, 0.088, 0, 0, 0, 0)
+    assert lib.santa_decode_workspace_bytes(ctypes.byref(geo), ctypes.byref(p_bad), 256,
+                                            ctypes.byref(n)) == _lib.SANTA_ERR_INVALID_ARGUMENT
+    # a compute call without a workspace is refused before touching the device
+    s = _lib.SantaSummary(*([1] * 9), 256)
+    assert lib.santa_decode(ctypes.byref(geo), ctypes.byref(p), 1, 1, 1, ctypes.byref(s), None,
+                            None, 1, 1, None, None, None, 0, None) == _lib.SANTA_ERR_WORKSPACE
+
+
+def test_python_entry_points_refuse_cpu_tensors():
+    import torch
+    from santapp_b200.attention import santapp as S
+    k = torch.zeros(1, 1, 16, 64)
+    with pytest.raises(ValueError, match="CUDA"):
+        S.build_summary(k, k, torch.zeros(1, 1, 8, dtype=torch.int64), 2, sample_end=8)
+
+
+def test_build_is_sm100a():
+    assert "arch=compute_100a,code=sm_100a" in " ".join(_build.ARCH_FLAGS)
