@@ -19,11 +19,8 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
-import subprocess
 import sys
-import tempfile
 import time
 
 REPO = os.path.dirname(os.path.abspath(__file__))
@@ -51,6 +48,8 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="skip the host-side extras (byte accounting, e2e, CPU baseline)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="bound on the CPU-baseline sample")
     return ap.parse_args()
@@ -65,94 +64,99 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle samples during the timed region."""
+    """SM clock and throttle reasons sampled through NVML every millisecond
+    while the timed region runs (nvidia-smi's 200 ms polling is too coarse
+    for a sub-second region)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, index: int):
-        self.index = index
-        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-        self.proc = None
+    def __init__(self, index: int, period_s: float = 0.001):
+        import threading
+        self.index, self.period = index, period_s
+        self.samples, self.reasons = [], 0
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self.max_mhz = None
+        self.ok = False
+
+    def _run(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = int(visible.split(",")[self.index]) if visible else self.index
+            h = nv.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.ok = True
+            while not self._stop.is_set():
+                self.samples.append(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                self.reasons |= int(get_reasons(h))
+                time.sleep(self.period)
+            nv.nvmlShutdown()
+        except Exception as e:  # NVML missing: report it rather than guess
+            self.error = repr(e)
 
     def start(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=self.file, stderr=subprocess.DEVNULL)
-        except OSError:
-            self.proc = None
+        self._thread.start()
+        t0 = time.time()
+        while not self.ok and self._thread.is_alive() and time.time() - t0 < 5:
+            time.sleep(0.001)
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        self.proc.wait()
-        self.file.flush()
-        rows = [r.split(",") for r in open(self.file.name).read().strip().splitlines() if r]
-        os.unlink(self.file.name)
-        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            if len(r) < 9:
-                continue
-            for name, v in zip(names, r[5:9]):
-                if v.strip().lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": float(np.median(sm)) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(rows)}
+        self._stop.set()
+        self._thread.join(timeout=5)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz,
+                    "reasons": [getattr(self, "error", "no samples")], "samples": 0}
+        return {"sm_mhz": float(np.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(n for b, n in self.REASONS.items() if self.reasons & b),
+                "samples": len(self.samples)}
 
 
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
 
-def algorithmic_bytes(step_runner, q, step, shape, summ):
-    """Distinct K/V rows the attend kernel must read for this step (union of
-    the group's selected clusters, the recent window, distinct sampled rows
-    outside that union), plus what the select kernel must read."""
+def algorithmic_bytes(runner, q, step, shape, summ, cid):
+    """Bytes the two decode kernels must move for this step.
+
+    attend: distinct K and V rows touched = the union of the GQA group's
+    selected clusters + the exact recent window + distinct sampled rows outside
+    that union, per (sequence, KV head).  select: centroids and cluster
+    metadata of every (sequence, KV head)."""
     from santapp_b200.attention import santapp as S
     sel, rows, _ = S.santa_decode_select(
-        q, step_runner.key_cache, step_runner.value_cache, summ, mode=step_runner.mode,
+        q, runner.key_cache, runner.value_cache, summ, mode=runner.mode,
         n_total=shape.context, topk_clusters=shape.topk_clusters, samples=shape.samples,
-        seed=step_runner.p.seed, step=step)
+        seed=runner.p.seed, step=step)
     B, Hq, G = sel.shape
-    g = shape.group
-    Hkv = Hq // g
-    N = shape.sample_end
-    covered = torch.zeros(B, Hkv, N, dtype=torch.bool, device=q.device)
-    union = sel.view(B, Hkv, g, G).amax(dim=2).bool()              # [B, Hkv, G]
-    starts = summ.starts.long()
-    lens = summ.lengths_long.long()
-    pos = torch.arange(N, device=q.device)
-    # row -> cluster row via the cluster starts (rows are cluster-contiguous)
-    for b in range(B):
-        for kv in range(Hkv):
-            ng = int(summ.n_groups[b, kv])
-            st = starts[b, kv, :ng]
-            cid = torch.searchsorted(st, pos, right=True) - 1
-            covered[b, kv] = union[b, kv, cid]
-    union_rows = int(covered.sum())
-    srows = rows.view(B, Hkv, g * shape.samples).long()
-    extra = 0
-    for b in range(B):
-        for kv in range(Hkv):
-            r = srows[b, kv]
-            r = r[r >= 0]
-            r = torch.unique(r)
-            extra += int((~covered[b, kv, r]).sum())
-    recent = B * Hkv * (shape.context - shape.sample_end)
+    g, N = shape.group, shape.sample_end
+    BH = B * (Hq // g)
+    union = sel.view(BH, g, G).amax(dim=1).bool()                      # [BH, G]
+    covered = torch.gather(union, 1, cid)                               # [BH, N]
+    srows = rows.reshape(BH, -1).long()
+    sampled = torch.zeros(BH, N + 1, dtype=torch.bool, device=q.device)
+    sampled.scatter_(1, torch.where(srows >= 0, srows, N), True)
+    extra = int((sampled[:, :N] & ~covered).sum())
+    rows_touched = int(covered.sum()) + extra + BH * (shape.context - shape.sample_end)
     esize = 2 if shape.kv_dtype == torch.bfloat16 else 4
-    row_bytes = 2 * shape.head_dim * esize  # K and V
-    attend = (union_rows + extra + recent) * row_bytes
-    select = B * Hkv * shape.n_clusters * (shape.head_dim * 4 + 12)  # centroids + starts/len/log_n
-    del lens
-    return attend, select, union_rows + extra + recent
+    attend = rows_touched * 2 * shape.head_dim * esize
+    select = BH * shape.n_clusters * (shape.head_dim * 4 + 12) + q.numel() * 4
+    return attend, select, rows_touched
+
+
+def cluster_of_row(summ, shape):
+    """[BH, N] cluster row of every position of the cluster-sorted prefix."""
+    BH = summ.n_groups.numel()
+    N, G = shape.sample_end, summ.max_groups
+    starts = summ.starts.view(BH, G).long()
+    active = torch.arange(G, device=starts.device)[None, :] < summ.n_groups.view(BH, 1)
+    marks = torch.zeros(BH, N + 1, dtype=torch.long, device=starts.device)
+    marks.scatter_add_(1, torch.where(active, starts, N), active.long())
+    return (torch.cumsum(marks[:, :N], dim=1) - 1).clamp_min_(0)
 
 
 def run_ours(args, rank, world):
@@ -179,17 +183,35 @@ def run_ours(args, rank, world):
 
     # algorithmic bytes of every timed step (selection read back, outside timing)
     attend_bytes, select_bytes, rows_touched = [], [], []
-    for i in range(args.steps):
-        step = args.warmup + i
-        a_b, s_b, r_t = algorithmic_bytes(runner, queries[step], step, shape, summ)
-        attend_bytes.append(a_b)
-        select_bytes.append(s_b)
-        rows_touched.append(r_t)
+    if not args.profile:
+        cid = cluster_of_row(summ, shape)
+        for i in range(args.steps):
+            step = args.warmup + i
+            a_b, s_b, r_t = algorithmic_bytes(runner, queries[step], step, shape, summ, cid)
+            attend_bytes.append(a_b)
+            select_bytes.append(s_b)
+            rows_touched.append(r_t)
+        del cid
     torch.cuda.synchronize()
 
     for i in range(args.warmup):
         flush.zero_()
         runner(queries[i], step=i)
+    torch.cuda.synchronize()
+
+    # one CUDA graph per phase per step: no host launch gaps inside the events
+    plans, execs = [], []
+    cap = torch.cuda.Stream()
+    with torch.cuda.stream(cap):
+        for i in range(args.steps):
+            step = args.warmup + i
+            gp, ge = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gp, stream=cap):
+                runner.plan(queries[step], step=step)
+            with torch.cuda.graph(ge, stream=cap):
+                runner.execute()
+            plans.append(gp)
+            execs.append(ge)
     torch.cuda.synchronize()
 
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
@@ -198,12 +220,11 @@ def run_ours(args, rank, world):
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for i in range(args.steps):
-        step = args.warmup + i
         flush.zero_()                       # L2 flush outside the timed events
         ev[i][0].record()
-        runner.plan(queries[step], step=step)
+        plans[i].replay()
         ev[i][1].record()
-        runner.execute()
+        execs[i].replay()
         ev[i][2].record()
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
@@ -214,11 +235,16 @@ def run_ours(args, rank, world):
     total_s = step_ms.sum() / 1e3
     value = shape.batch * args.steps / total_s
     peak, peak_kind = peaks()
-    achieved = float(np.sum(attend_bytes) / (att_ms.sum() / 1e3) / 1e9)
+    if attend_bytes:
+        achieved = float(np.sum(attend_bytes) / (att_ms.sum() / 1e3) / 1e9)
+    else:
+        achieved = float("nan")
     traffic = load_traffic(shape)
+    del plans, execs
 
-    e2e = None if args.no_e2e else run_e2e(args, shape, w, summ, runner)
-    cpu = None if args.no_cpu_baseline else cpu_baseline_sample(args, shape, w, summ)
+    e2e = None if (args.no_e2e or args.profile) else run_e2e(args, shape, w, summ, runner)
+    cpu = (None if (args.no_cpu_baseline or args.profile)
+           else cpu_baseline_sample(args, shape, w, summ))
     line = {
         "metric": METRIC,
         "value": value,
@@ -251,15 +277,17 @@ def run_ours(args, rank, world):
             "unit": "GB/s",
             "frac": achieved / peak,
             "traffic": traffic,
-            "algorithmic_bytes_per_launch": float(np.mean(attend_bytes)),
-            "rows_touched_per_step": float(np.mean(rows_touched)),
+            "algorithmic_bytes_per_launch": float(np.mean(attend_bytes)) if attend_bytes else None,
+            "rows_touched_per_step": float(np.mean(rows_touched)) if rows_touched else None,
             "dense_kv_bytes_per_step": float(shape.batch * shape.num_kv_heads * shape.context
                                              * shape.head_dim * 2 * 2),
         },
         "select_roofline": {
-            "achieved": float(np.sum(select_bytes) / (plan_ms.sum() / 1e3) / 1e9),
+            "achieved": (float(np.sum(select_bytes) / (plan_ms.sum() / 1e3) / 1e9)
+                         if select_bytes else None),
             "unit": "GB/s",
         },
+        "timing": "CUDA events around one CUDA graph per phase per step",
         "wall_s": wall,
         "clocks": clk,
         "gpu_launches": runner.kernels_per_call * args.steps,
