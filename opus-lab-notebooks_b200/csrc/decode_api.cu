@@ -1,0 +1,161 @@
+// C ABI of the SANTA++ sparse decode (include/santa_b200.h).
+//
+// santa_decode replaces SantaPlusEngine._approximate_attention
+// (santapp_ruler/attention/santapp.py:365-506) for every (batch, query head)
+// of a decode step; santa_decode_plan / santa_decode_execute are its two
+// stream-ordered halves, santa_decode_select reads the selection out.
+#include "decode_common.cuh"
+
+using namespace santa;
+
+extern "C" int santa_check_geometry(const SantaGeometry *geo);
+
+static int pick_splits(const SantaGeometry *geo, const SantaDecodeParams *p) {
+    if (p->num_splits > 0) return p->num_splits;
+    const int BH = geo->batch * geo->num_kv_heads;
+    int s = (2 * num_sms()) / BH;
+    if (s < 1) s = 1;
+    if (s > 64) s = 64;
+    return s;
+}
+
+static int check_decode(const SantaGeometry *geo, const SantaDecodeParams *p, int max_groups) {
+    int st = santa_check_geometry(geo);
+    if (st) return st;
+    if (!p) return SANTA_ERR_INVALID_ARGUMENT;
+    if (p->mode < SANTA_MODE_TOPK || p->mode > SANTA_MODE_HYBRID) return SANTA_ERR_INVALID_ARGUMENT;
+    if (max_groups <= 0 || max_groups > SANTA_MAX_CLUSTERS) return SANTA_ERR_INVALID_ARGUMENT;
+    if (p->samples < 0 || p->samples > SANTA_MAX_SAMPLES) return SANTA_ERR_INVALID_ARGUMENT;
+    if (p->mode != SANTA_MODE_TOPK && p->samples <= 0) return SANTA_ERR_INVALID_ARGUMENT;
+    if (p->mode == SANTA_MODE_TOPK && p->token_budget <= 0) return SANTA_ERR_INVALID_ARGUMENT;
+    if (p->mode == SANTA_MODE_HYBRID && (p->topk_clusters < 0 || p->topk_clusters > max_groups))
+        return SANTA_ERR_INVALID_ARGUMENT;
+    if (geo->sample_end >= (1 << 24)) return SANTA_ERR_UNSUPPORTED;
+    if (!(p->scale > 0.f)) return SANTA_ERR_INVALID_ARGUMENT;
+    if (p->num_splits < 0 || p->num_splits > 256) return SANTA_ERR_INVALID_ARGUMENT;
+    return SANTA_OK;
+}
+
+static size_t workspace_bytes(const SantaGeometry *geo, const SantaDecodeParams *p,
+                              int max_groups, int nsplit) {
+    const int BH = geo->batch * geo->num_kv_heads;
+    return decode_ws_layout(BH, max_groups, geo->group, p->samples,
+                            attend_partial_slots(geo, nsplit), geo->head_dim, nullptr, nullptr);
+}
+
+extern "C" int santa_decode_workspace_bytes(const SantaGeometry *geo, const SantaDecodeParams *p,
+                                            int32_t max_groups, size_t *bytes) {
+    int st = check_decode(geo, p, max_groups);
+    if (st) return st;
+    if (!bytes) return SANTA_ERR_INVALID_ARGUMENT;
+    *bytes = workspace_bytes(geo, p, max_groups, pick_splits(geo, p));
+    return SANTA_OK;
+}
+
+static int prepare_decode(const SantaGeometry *geo, const SantaDecodeParams *p, const float *q,
+                          const void *key_cache, const void *value_cache,
+                          const SantaSummary *summary, const int32_t *sample_a,
+                          const int32_t *sample_b, bool need_draws, void *workspace,
+                          size_t ws_bytes, DecodeArgs *a) {
+    if (!summary) return SANTA_ERR_INVALID_ARGUMENT;
+    int st = check_decode(geo, p, summary->max_groups);
+    if (st) return st;
+    if (!q || !key_cache || !value_cache) return SANTA_ERR_INVALID_ARGUMENT;
+    const bool needs_summary = p->mode == SANTA_MODE_TOPK || p->mode == SANTA_MODE_GUIDED ||
+                               p->mode == SANTA_MODE_HYBRID;
+    if (needs_summary && (!summary->starts || !summary->lengths || !summary->log_n ||
+                          !summary->centroids || !summary->n_groups))
+        return SANTA_ERR_INVALID_ARGUMENT;
+    if (!summary->sorted_key || !summary->sorted_value) return SANTA_ERR_INVALID_ARGUMENT;
+    if ((p->mode == SANTA_MODE_UNIFORM || p->mode == SANTA_MODE_SANTA) && !summary->positions)
+        return SANTA_ERR_INVALID_ARGUMENT;
+    if (need_draws && p->sample_source == SANTA_SAMPLES_INJECTED && p->mode != SANTA_MODE_TOPK) {
+        if (!sample_a) return SANTA_ERR_INVALID_ARGUMENT;
+        if (p->mode == SANTA_MODE_GUIDED && !sample_b) return SANTA_ERR_INVALID_ARGUMENT;
+    }
+    const int BH = geo->batch * geo->num_kv_heads;
+    const int nsplit = pick_splits(geo, p);
+    if (!workspace || ws_bytes < workspace_bytes(geo, p, summary->max_groups, nsplit))
+        return SANTA_ERR_WORKSPACE;
+    a->geo = *geo;
+    a->p = *p;
+    a->sum = *summary;
+    a->q = q;
+    a->key_cache = (const char *)key_cache;
+    a->value_cache = (const char *)value_cache;
+    a->sample_a = sample_a;
+    a->sample_b = sample_b;
+    a->out = nullptr;
+    a->lse = nullptr;
+    a->n_exact = nullptr;
+    a->ess = nullptr;
+    a->nsplit = nsplit;
+    decode_ws_layout(BH, summary->max_groups, geo->group, p->samples,
+                     attend_partial_slots(geo, nsplit), geo->head_dim, (char *)workspace, &a->ws);
+    return SANTA_OK;
+}
+
+extern "C" int santa_decode_plan(const SantaGeometry *geo, const SantaDecodeParams *p,
+                                 const float *q, const void *key_cache, const void *value_cache,
+                                 const SantaSummary *summary, const int32_t *sample_a,
+                                 const int32_t *sample_b, int32_t *n_exact, void *workspace,
+                                 size_t workspace_bytes, cudaStream_t stream) {
+    DecodeArgs a;
+    int st = prepare_decode(geo, p, q, key_cache, value_cache, summary, sample_a, sample_b, true,
+                            workspace, workspace_bytes, &a);
+    if (st) return st;
+    a.n_exact = n_exact;
+    return launch_plan(a, stream);
+}
+
+extern "C" int santa_decode_execute(const SantaGeometry *geo, const SantaDecodeParams *p,
+                                    const float *q, const void *key_cache,
+                                    const void *value_cache, const SantaSummary *summary,
+                                    float *out, float *lse, float *ess, void *workspace,
+                                    size_t workspace_bytes, cudaStream_t stream) {
+    if (!out) return SANTA_ERR_INVALID_ARGUMENT;
+    DecodeArgs a;
+    int st = prepare_decode(geo, p, q, key_cache, value_cache, summary, nullptr, nullptr, false,
+                            workspace, workspace_bytes, &a);
+    if (st) return st;
+    a.out = out;
+    a.lse = lse;
+    a.ess = ess;
+    return launch_execute(a, stream);
+}
+
+extern "C" int santa_decode(const SantaGeometry *geo, const SantaDecodeParams *p, const float *q,
+                            const void *key_cache, const void *value_cache,
+                            const SantaSummary *summary, const int32_t *sample_a,
+                            const int32_t *sample_b, float *out, float *lse, int32_t *n_exact,
+                            float *ess, void *workspace, size_t workspace_bytes,
+                            cudaStream_t stream) {
+    if (!out) return SANTA_ERR_INVALID_ARGUMENT;
+    DecodeArgs a;
+    int st = prepare_decode(geo, p, q, key_cache, value_cache, summary, sample_a, sample_b, true,
+                            workspace, workspace_bytes, &a);
+    if (st) return st;
+    a.out = out;
+    a.lse = lse;
+    a.n_exact = n_exact;
+    a.ess = ess;
+    st = launch_plan(a, stream);
+    if (st) return st;
+    return launch_execute(a, stream);
+}
+
+extern "C" int santa_decode_select(const SantaGeometry *geo, const SantaDecodeParams *p,
+                                   const float *q, const void *key_cache, const void *value_cache,
+                                   const SantaSummary *summary, const int32_t *sample_a,
+                                   const int32_t *sample_b, uint8_t *selected,
+                                   int32_t *sample_rows, int32_t *n_exact, void *workspace,
+                                   size_t workspace_bytes, cudaStream_t stream) {
+    DecodeArgs a;
+    int st = prepare_decode(geo, p, q, key_cache, value_cache, summary, sample_a, sample_b, true,
+                            workspace, workspace_bytes, &a);
+    if (st) return st;
+    a.n_exact = n_exact;
+    st = launch_plan(a, stream);
+    if (st) return st;
+    return launch_expand(a, selected, sample_rows, stream);
+}

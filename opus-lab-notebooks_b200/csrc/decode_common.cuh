@@ -1,0 +1,355 @@
+// Shared definitions of the SANTA++ decode kernels (selection + attention).
+//
+// A decode step is two launches:
+//   select  one CTA per (batch, KV head) = segment bh: centroid guesses for
+//           the GQA group, ranking, top-k / budget walk, the union of the
+//           group's selections and the importance samples.  It writes a work
+//           list for the segment into the workspace.
+//   attend  streams the rows of every segment's work list (selected clusters
+//           of the cluster-sorted copy, the exact recent window of the cache,
+//           sampled rows) with an online softmax per query head, and merges
+//           partial results with an LSE merge.
+//
+// Every segment's work list is a virtual row space [0, U + R + NS):
+//   [0, U)          rows of the union of selected clusters (ascending cluster)
+//   [U, U + R)      the exact recent window [sample_end, n_total) of the cache
+//   [U + R, ...)    the sampled rows, head-major
+#pragma once
+
+#include "common.cuh"
+
+namespace santa {
+
+constexpr int kSelThreads = 512;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// packed sample word: bits 0-23 sorted row, 24-26 local head, 27 = absolute
+// log weight (santa mode: lw does not depend on the row's score)
+constexpr uint32_t kPosMask = 0xFFFFFFu;
+constexpr int kHeadShift = 24;
+constexpr uint32_t kAbsBit = 1u << 27;
+
+// row mask bits: 0-7 local heads the row contributes to, 8 = sampled row,
+// 9 = absolute log weight
+constexpr int kMaskSample = 256;
+constexpr int kMaskAbs = 512;
+
+// error flags in DecodeWs::flag
+constexpr int kFlagBadDraw = 0;     // an injected draw was out of range (clamped)
+constexpr int kFlagWaitTimeout = 1; // an mbarrier wait hit its time limit
+
+struct DecodeWs {
+    int32_t *counters;   // [BH] CTAs finished per segment (last one merges)
+    int32_t *flag;       // [4] error flags, see kFlag*
+    int32_t *meta;       // [BH][8]: 0 n_union, 1 U, 2 R, 3 n_samples, 4 total rows
+    int32_t *head_meta;  // [BH][8][2]: n_exact, n_samples
+    int32_t *u_start;    // [BH][G] sorted-row start of each union entry
+    int32_t *u_mask;     // [BH][G] heads that selected it
+    int32_t *u_cid;      // [BH][G] cluster row of each union entry
+    int32_t *u_off;      // [BH][G+1] prefix of union rows
+    int32_t *s_pos;      // [BH][g*S] packed sample words
+    float *s_off;        // [BH][g*S] log2-units offset (or absolute log2 weight)
+    float *lse_old;      // [BH][8] santa mode: log2-sum-exp2 of old scores
+    float *partial;      // [n_slots][g][D + 8] split partials
+};
+
+__host__ __device__ inline int partial_stride(int D) { return D + 8; }
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+inline size_t decode_ws_layout(int BH, int G, int g, int S, int n_slots, int D, char *base,
+                               DecodeWs *ws) {
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off = align_up(off + bytes, 256);
+        return o;
+    };
+    const int gs = g * (S > 0 ? S : 1);
+    size_t o_cnt = take((size_t)BH * 4);
+    size_t o_flag = take(16);
+    size_t o_meta = take((size_t)BH * 8 * 4);
+    size_t o_hm = take((size_t)BH * 16 * 4);
+    size_t o_us = take((size_t)BH * G * 4);
+    size_t o_um = take((size_t)BH * G * 4);
+    size_t o_uc = take((size_t)BH * G * 4);
+    size_t o_uo = take((size_t)BH * (G + 1) * 4);
+    size_t o_sp = take((size_t)BH * gs * 4);
+    size_t o_so = take((size_t)BH * gs * 4);
+    size_t o_lo = take((size_t)BH * 8 * 4);
+    size_t o_pa = take((size_t)n_slots * g * partial_stride(D) * 4);
+    if (base && ws) {
+        ws->counters = (int32_t *)(base + o_cnt);
+        ws->flag = (int32_t *)(base + o_flag);
+        ws->meta = (int32_t *)(base + o_meta);
+        ws->head_meta = (int32_t *)(base + o_hm);
+        ws->u_start = (int32_t *)(base + o_us);
+        ws->u_mask = (int32_t *)(base + o_um);
+        ws->u_cid = (int32_t *)(base + o_uc);
+        ws->u_off = (int32_t *)(base + o_uo);
+        ws->s_pos = (int32_t *)(base + o_sp);
+        ws->s_off = (float *)(base + o_so);
+        ws->lse_old = (float *)(base + o_lo);
+        ws->partial = (float *)(base + o_pa);
+    }
+    return off;
+}
+
+struct DecodeArgs {
+    SantaGeometry geo;
+    SantaDecodeParams p;
+    SantaSummary sum;
+    const float *q;
+    const char *key_cache;
+    const char *value_cache;
+    const int32_t *sample_a;
+    const int32_t *sample_b;
+    float *out;
+    float *lse;
+    int32_t *n_exact;
+    float *ess;
+    int nsplit;   // SIMT attend: CTAs per segment
+    DecodeWs ws;
+};
+
+// ---------------------------------------------------------------------------
+// row resolution: virtual row v of segment bh -> K/V row addresses + weights
+// ---------------------------------------------------------------------------
+struct RowInfo {
+    const char *k;
+    const char *v;
+    float off;  // log2-units additive offset (or absolute weight when kMaskAbs)
+    int mask;   // see kMask*
+};
+
+__device__ __forceinline__ RowInfo resolve_row(const DecodeArgs &a, int bh, int v, int U, int R,
+                                               int total, int n_union, const int *u_off,
+                                               const int *u_start, const int *u_mask,
+                                               int row_bytes) {
+    RowInfo ri;
+    const int g = a.geo.group;
+    const int sample_end = a.geo.sample_end;
+    const char *sk = (const char *)a.sum.sorted_key + (int64_t)bh * sample_end * row_bytes;
+    const char *sv = (const char *)a.sum.sorted_value + (int64_t)bh * sample_end * row_bytes;
+    if (v >= total) {
+        ri.k = sk;
+        ri.v = sv;
+        ri.off = 0.f;
+        ri.mask = 0;
+    } else if (v < U) {
+        int lo = 0, hi = n_union - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (u_off[mid] <= v) lo = mid;
+            else hi = mid - 1;
+        }
+        const int row = u_start[lo] + (v - u_off[lo]);
+        ri.k = sk + (int64_t)row * row_bytes;
+        ri.v = sv + (int64_t)row * row_bytes;
+        ri.off = 0.f;
+        ri.mask = u_mask[lo];
+    } else if (v < U + R) {
+        const int64_t row = (int64_t)bh * a.geo.capacity + sample_end + (v - U);
+        ri.k = a.key_cache + row * row_bytes;
+        ri.v = a.value_cache + row * row_bytes;
+        ri.off = 0.f;
+        ri.mask = (1 << g) - 1;
+    } else {
+        const int j = v - U - R;
+        const uint32_t pk = (uint32_t)a.ws.s_pos[(int64_t)bh * g * a.p.samples + j];
+        const int row = (int)(pk & kPosMask);
+        const int h = (int)((pk >> kHeadShift) & 7u);
+        ri.k = sk + (int64_t)row * row_bytes;
+        ri.v = sv + (int64_t)row * row_bytes;
+        ri.off = a.ws.s_off[(int64_t)bh * g * a.p.samples + j];
+        ri.mask = (1 << h) | kMaskSample | ((pk & kAbsBit) ? kMaskAbs : 0);
+    }
+    return ri;
+}
+
+// Per-warp online-softmax state for a warp merge in shared memory.
+template <int D>
+struct WarpState {
+    float m[SANTA_MAX_GROUP], l[SANTA_MAX_GROUP];
+    float ms[SANTA_MAX_GROUP], e1[SANTA_MAX_GROUP], e2[SANTA_MAX_GROUP];
+    float o[SANTA_MAX_GROUP][D];
+};
+
+// Merge NW warp states into one partial (m, l, ms, e1, e2, pad, o[D]) per
+// head at dst (stride PSTR); threads [0, nthreads) participate.
+template <int D>
+__device__ void merge_warp_states(const WarpState<D> *ws, int NW, int g, float *dst, int tid,
+                                  int nthreads) {
+    const int PSTR = partial_stride(D);
+    if (tid < g) {
+        const int h = tid;
+        float M = -INFINITY, MS = -INFINITY;
+        for (int w = 0; w < NW; ++w) {
+            M = fmaxf(M, ws[w].m[h]);
+            MS = fmaxf(MS, ws[w].ms[h]);
+        }
+        float L = 0.f, E1 = 0.f, E2 = 0.f;
+        for (int w = 0; w < NW; ++w) {
+            if (ws[w].l[h] > 0.f) L += ws[w].l[h] * exp2f(ws[w].m[h] - M);
+            if (ws[w].e1[h] > 0.f) {
+                E1 += ws[w].e1[h] * exp2f(ws[w].ms[h] - MS);
+                E2 += ws[w].e2[h] * exp2f(2.f * (ws[w].ms[h] - MS));
+            }
+        }
+        dst[h * PSTR + 0] = M;
+        dst[h * PSTR + 1] = L;
+        dst[h * PSTR + 2] = MS;
+        dst[h * PSTR + 3] = E1;
+        dst[h * PSTR + 4] = E2;
+    }
+    for (int i = tid; i < g * D; i += nthreads) {
+        const int h = i / D, d = i - h * D;
+        float M = -INFINITY;
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, ws[w].m[h]);
+        float acc = 0.f;
+        for (int w = 0; w < NW; ++w)
+            if (ws[w].l[h] > 0.f) acc += ws[w].o[h][d] * exp2f(ws[w].m[h] - M);
+        dst[h * PSTR + 8 + d] = acc;
+    }
+}
+
+// Merge partial slots first..first+count-1 (stride slot_step slots) of
+// segment bh into out / lse / ess.
+template <int D>
+__device__ void merge_partials_to_output(const DecodeArgs &a, int bh, const float *pall,
+                                         int count, int tid, int nthreads) {
+    const int g = a.geo.group;
+    const int PSTR = partial_stride(D);
+    const int b = bh / a.geo.num_kv_heads, kv = bh - b * a.geo.num_kv_heads;
+    for (int i = tid; i < g * D; i += nthreads) {
+        const int h = i / D, d = i - h * D;
+        float M = -INFINITY;
+        for (int s = 0; s < count; ++s) M = fmaxf(M, pall[(s * g + h) * PSTR + 0]);
+        float L = 0.f, acc = 0.f;
+        for (int s = 0; s < count; ++s) {
+            const float *ps = pall + (s * g + h) * PSTR;
+            if (ps[1] > 0.f) {
+                const float f = exp2f(ps[0] - M);
+                L += ps[1] * f;
+                acc += ps[8 + d] * f;
+            }
+        }
+        const int64_t oh = (int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g + h;
+        a.out[oh * D + d] = L > 0.f ? acc / L : 0.f;
+        if (d == 0) {
+            if (a.lse) a.lse[oh] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
+            if (a.ess) {
+                float MS = -INFINITY;
+                for (int s = 0; s < count; ++s) MS = fmaxf(MS, pall[(s * g + h) * PSTR + 2]);
+                float E1 = 0.f, E2 = 0.f;
+                for (int s = 0; s < count; ++s) {
+                    const float *ps = pall + (s * g + h) * PSTR;
+                    if (ps[3] > 0.f) {
+                        E1 += ps[3] * exp2f(ps[2] - MS);
+                        E2 += ps[4] * exp2f(2.f * (ps[2] - MS));
+                    }
+                }
+                const int ns = a.ws.head_meta[((int64_t)bh * 8 + h) * 2 + 1];
+                a.ess[oh] = (ns > 0 && E2 > 0.f) ? (E1 * E1 / E2) / (float)ns : 0.f;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// PTX helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2,
+                                            uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t &r0, uint32_t &r1,
+                                                  uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *(const uint32_t *)&v;
+}
+
+// mbarrier + bulk-copy (TMA engine, non-tensor form) helpers
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+    return t;
+}
+// Bounded wait: gives up after ~2 s of wall time and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 0u && global_timer_ns() - t0 > 2000000000ull) return false;
+    }
+}
+__device__ __forceinline__ void bulk_g2s(void *dst_smem, const void *src, uint32_t bytes,
+                                         uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+            smem_u32(dst_smem)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// launchers (host, defined in decode_select.cu / decode_attend.cu)
+// ---------------------------------------------------------------------------
+int launch_plan(DecodeArgs &a, cudaStream_t stream);
+int launch_execute(DecodeArgs &a, cudaStream_t stream);
+int launch_expand(DecodeArgs &a, uint8_t *selected, int32_t *sample_rows, cudaStream_t stream);
+int num_sms();
+int attend_partial_slots(const SantaGeometry *geo, int nsplit);
+
+}  // namespace santa
