@@ -123,10 +123,13 @@ struct RowInfo {
     int mask;   // see kMask*
 };
 
+// sp / so: optional copy of the segment's first scap sample words and
+// offsets in shared memory (rows beyond it are read from the workspace).
 __device__ __forceinline__ RowInfo resolve_row(const DecodeArgs &a, int bh, int v, int U, int R,
                                                int total, int n_union, const int *u_off,
                                                const int *u_start, const int *u_mask,
-                                               int row_bytes) {
+                                               int row_bytes, const int32_t *sp = nullptr,
+                                               const float *so = nullptr, int scap = 0) {
     RowInfo ri;
     const int g = a.geo.group;
     const int sample_end = a.geo.sample_end;
@@ -157,12 +160,13 @@ __device__ __forceinline__ RowInfo resolve_row(const DecodeArgs &a, int bh, int 
         ri.mask = (1 << g) - 1;
     } else {
         const int j = v - U - R;
-        const uint32_t pk = (uint32_t)a.ws.s_pos[(int64_t)bh * g * a.p.samples + j];
+        const uint32_t pk = j < scap ? (uint32_t)sp[j]
+                                     : (uint32_t)a.ws.s_pos[(int64_t)bh * g * a.p.samples + j];
         const int row = (int)(pk & kPosMask);
         const int h = (int)((pk >> kHeadShift) & 7u);
         ri.k = sk + (int64_t)row * row_bytes;
         ri.v = sv + (int64_t)row * row_bytes;
-        ri.off = a.ws.s_off[(int64_t)bh * g * a.p.samples + j];
+        ri.off = j < scap ? so[j] : a.ws.s_off[(int64_t)bh * g * a.p.samples + j];
         ri.mask = (1 << h) | kMaskSample | ((pk & kAbsBit) ? kMaskAbs : 0);
     }
     return ri;
@@ -341,6 +345,17 @@ __device__ __forceinline__ void bulk_g2s(void *dst_smem, const void *src, uint32
 }
 __device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
+}
+// 16-byte asynchronous global->shared copy (L1 bypass)
+__device__ __forceinline__ void cp_async16(void *dst_smem, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst_smem)), "l"(src)
+                 : "memory");
+}
+// The mbarrier receives one arrival once every cp.async this thread issued
+// so far has landed (the barrier's expected count includes these arrivals).
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(smem_u32(bar))
+                 : "memory");
 }
 
 // ---------------------------------------------------------------------------

@@ -67,8 +67,8 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
     int *len_s = starts_s + Gmax;                               // [Gmax]
     int *mask_s = len_s + Gmax;                                 // [Gmax]
     float *guess_s = (float *)(mask_s + Gmax);                  // [8][Gmax]
-    int *selasc = (int *)(guess_s + SANTA_MAX_GROUP * Gmax);    // [8][Gmax]
-    int *sw = selasc + SANTA_MAX_GROUP * Gmax;                  // [40]
+    int *selasc = (int *)(guess_s + SANTA_MAX_GROUP * Gmax);    // [8][2*Gmax+1] gap / cum
+    int *sw = selasc + SANTA_MAX_GROUP * (2 * Gmax + 1);        // [40]
     int *head_sel = sw + 40;                                    // [8] selected clusters per head
     int *head_exact = head_sel + 8;                             // [8]
     int *head_ns = head_exact + 8;                              // [8] samples per head
@@ -159,12 +159,13 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
                                                          : n_groups;
             int nsel = 0, exact = 0;
             while (nsel < kmax) {
-                uint64_t m = best;
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const uint64_t y = __shfl_xor_sync(0xffffffffu, m, o);
-                    m = y > m ? y : m;
-                }
+                // 64-bit warp max in two redux.sync steps: the largest high
+                // word, then the largest low word among the lanes holding it
+                const uint32_t bhi = (uint32_t)(best >> 32);
+                const uint32_t mhi = __reduce_max_sync(0xffffffffu, bhi);
+                const uint32_t mlo =
+                    __reduce_max_sync(0xffffffffu, bhi == mhi ? (uint32_t)best : 0u);
+                const uint64_t m = ((uint64_t)mhi << 32) | mlo;
                 if (m == 0) break;  // no cluster left
                 const int c = (int)(0xFFFFFFFFu - (uint32_t)(m & 0xFFFFFFFFu));
                 const int l = len_s[c];
@@ -285,16 +286,34 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
         const uint2 key = make_uint2((uint32_t)a.p.seed, (uint32_t)(a.p.seed >> 32));
         const float logS = logf((float)ns);
         if (mode == SANTA_MODE_HYBRID) {
-            // selected clusters of this head in ascending cluster (= start) order
-            int *sel = selasc + h * Gmax;
-            int cnt = 0;
+            // Selected clusters of this head in ascending cluster (= start)
+            // order, as gap[j] = non-selected positions before cluster j and
+            // cum[j] = selected positions before cluster j.  Rank r maps to
+            // position r + cum[J] with J = #{j : gap[j] <= r}.
+            int *gap = selasc + h * (2 * Gmax + 1);
+            int *cum = gap + Gmax;
+            int cnt = 0, carry = 0;
             for (int c0 = 0; c0 < n_groups; c0 += 32) {
                 const int c = c0 + lane;
                 const bool on = c < n_groups && ((mask_s[c] >> h) & 1);
                 const unsigned bal = __ballot_sync(0xffffffffu, on);
-                if (on) sel[cnt + __popc(bal & ((1u << lane) - 1u))] = c;
+                int l = on ? len_s[c] : 0;
+                int x = l;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(0xffffffffu, x, o);
+                    if (lane >= o) x += y;
+                }
+                if (on) {
+                    const int j = cnt + __popc(bal & ((1u << lane) - 1u));
+                    const int before = carry + x - l;
+                    gap[j] = starts_s[c] - before;
+                    cum[j] = before;
+                }
                 cnt += __popc(bal);
+                carry += __shfl_sync(0xffffffffu, x, 31);
             }
+            if (lane == 0) cum[cnt] = carry;
             __syncwarp();
             const int n_rest = sample_end - head_exact[h];
             const float off = (logf((float)n_rest) - logS) * kLog2e;
@@ -313,12 +332,13 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
                         key);
                     r = (uint32_t)(((uint64_t)uint4_word(w, i & 3) * (uint64_t)n_rest) >> 32);
                 }
-                int p = (int)r;
-                for (int j = 0; j < cnt; ++j) {
-                    const int c = sel[j];
-                    if (p >= starts_s[c]) p += len_s[c];
-                    else break;
+                int lo = 0, hi = cnt;  // J = first j with gap[j] > r
+                while (lo < hi) {
+                    const int mid = (lo + hi) >> 1;
+                    if (gap[mid] <= (int)r) lo = mid + 1;
+                    else hi = mid;
                 }
+                const int p = (int)r + cum[lo];
                 spos[i] = (int32_t)((uint32_t)p | ((uint32_t)h << kHeadShift));
                 soff[i] = off;
             }
@@ -507,7 +527,7 @@ static size_t select_smem_bytes(int D, int Gmax) {
     b += 64 * (D + 1) * 4;
     b += 3 * (size_t)Gmax * 4;
     b += SANTA_MAX_GROUP * (size_t)Gmax * 4;  // guess
-    b += SANTA_MAX_GROUP * (size_t)Gmax * 4;  // selasc
+    b += SANTA_MAX_GROUP * (2 * (size_t)Gmax + 1) * 4;  // gap / cum per head
     b += 40 * 4 + 32 * 4 + 32 * 4 + 32;
     b += SANTA_MAX_GROUP * (size_t)Gp * 8;    // keys
     return b;
