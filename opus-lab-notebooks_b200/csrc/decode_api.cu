@@ -40,7 +40,8 @@ static size_t workspace_bytes(const SantaGeometry *geo, const SantaDecodeParams 
                               int max_groups, int nsplit) {
     const int BH = geo->batch * geo->num_kv_heads;
     return decode_ws_layout(BH, max_groups, geo->group, p->samples,
-                            attend_partial_slots(geo, nsplit), geo->head_dim, nullptr, nullptr);
+                            attend_partial_slots(geo, nsplit), geo->head_dim, geo->sample_end,
+                            nullptr, nullptr);
 }
 
 extern "C" int santa_decode_workspace_bytes(const SantaGeometry *geo, const SantaDecodeParams *p,
@@ -91,7 +92,8 @@ static int prepare_decode(const SantaGeometry *geo, const SantaDecodeParams *p, 
     a->ess = nullptr;
     a->nsplit = nsplit;
     decode_ws_layout(BH, summary->max_groups, geo->group, p->samples,
-                     attend_partial_slots(geo, nsplit), geo->head_dim, (char *)workspace, &a->ws);
+                     attend_partial_slots(geo, nsplit), geo->head_dim, geo->sample_end,
+                     (char *)workspace, &a->ws);
     return SANTA_OK;
 }
 

@@ -8,18 +8,20 @@
 //            factor folded into the sampled rows' log weights)
 //
 // Two kernels:
-//   decode_attend_pipe_kernel   bf16 caches.  One CTA per SM, the virtual row
-//       spaces of all (batch, KV head) segments concatenated and split evenly
-//       over the CTAs.  Warp 4 is a producer that resolves 64-row tiles from
-//       tables in shared memory and streams the rows with row-cooperative,
-//       coalesced 16-byte cp.async copies into a 4-stage ring of padded
-//       shared-memory tiles, completing on mbarriers (cp.async.mbarrier.arrive);
-//       per-row bulk copies through the TMA engine were measured 4x slower on
-//       these 256-byte gathers: the engine is request-bound at that size;
-//       warps 0-3 consume 16 rows each with mma.sync m16n8k16 (GQA heads on
-//       the M dimension, q and p split into bf16 hi + lo for fp32-level
-//       accuracy) and an online softmax.  At every segment end the CTA writes
-//       one partial; the last CTA of a segment merges them (LSE merge).
+//   decode_attend_gather_kernel  bf16 caches.  One CTA of 8 warps per SM; the
+//       virtual row spaces of all (batch, KV head) segments are concatenated
+//       and split evenly over the CTAs.  Inside a CTA every warp works alone
+//       on every 8th 16-row tile: it loads the tile's row entries (expanded
+//       union rows, the recent window, sampled rows) one tile ahead, gathers
+//       the K/V rows with row-cooperative coalesced 16-byte cp.async copies
+//       into its own 3-stage ring of padded shared-memory tiles, and runs
+//       mma.sync m16n8k16 (GQA heads on M; q and p split into bf16 hi + lo for
+//       fp32-level accuracy) with an online softmax.  No barrier crosses
+//       warps.  At a segment end each warp writes a partial; the last warp of
+//       the segment merges them (LSE merge).
+//       (Two earlier designs were measured slower on B200: one bulk copy per
+//       256-byte row through the TMA engine is request-bound, and a single
+//       producer warp cannot keep enough 16-byte copies in flight.)
 //   decode_attend_simt_kernel  fp32 caches, a warp per row.
 #include "decode_common.cuh"
 
@@ -155,69 +157,73 @@ __global__ void __launch_bounds__(kSimtThreads) decode_attend_simt_kernel(Decode
 }
 
 // ---------------------------------------------------------------------------
-// producer / consumer pipeline kernel (bf16 caches)
+// warp-independent gather kernel (bf16 caches)
 // ---------------------------------------------------------------------------
-constexpr int kRows = 64;     // rows per tile
-constexpr int kNS = 4;        // pipeline stages
-constexpr int kCons = 4;      // consumer warps, 16 rows each
-constexpr int kPipeThreads = 32 * (kCons + 1);
-constexpr int kSampCap = 4096; // sample words of a segment kept in shared memory
+constexpr int kGW = 8;        // warps per CTA
+constexpr int kGRows = 16;    // rows per warp tile (the mma N/K granule)
+constexpr int kGStages = 3;   // cp.async ring depth per warp
+constexpr int kGThreads = 32 * kGW;
 
 template <int D>
-struct PipeGeom {
-    static constexpr int ROWB = D * 2;           // bytes of one bf16 row
-    static constexpr int PITCH = ROWB + 16;      // padded smem pitch: 8 rows hit 8 bank groups
-    static constexpr int TILE = kRows * PITCH;   // bytes of one K (or V) stage
+struct GatherGeom {
+    static constexpr int ROWB = D * 2;                // bytes of one bf16 row
+    static constexpr int PITCH = ROWB + 16;           // padded pitch: 8 rows hit 8 bank groups
+    static constexpr int TILE = kGRows * PITCH;       // one K (or V) warp tile
+    static constexpr int STAGE = 2 * TILE;            // K + V
+    static constexpr int META = 2 * kGRows * 4;       // row masks + offsets of a stage
+    static constexpr int WARP = kGStages * (STAGE + META);
+    static constexpr int CPR = ROWB / 16;             // 16-byte chunks per row
+    static constexpr int RPI = 32 / CPR;              // rows per copy instruction
 };
 
 template <int D>
-__host__ __device__ inline size_t pipe_smem_bytes(int BH, int Gmax) {
-    size_t b = 128;                                    // alignment slack
-    b += 2 * (size_t)kNS * PipeGeom<D>::TILE;           // K and V stages
-    b += 2 * (size_t)kNS * kRows * 4;                  // row mask + offset
-    b += 2 * kNS * 8;                                  // full / empty mbarriers
-    b += ((size_t)BH + 1) * 4;                         // segment prefix
-    b += (3 * (size_t)Gmax + 1) * 4;                   // producer's union table
-    b += 2 * (size_t)kSampCap * 4;                     // producer's sample table
-    return b;
+inline size_t gather_smem_bytes(int BH) {
+    return 128 + (size_t)kGW * GatherGeom<D>::WARP + ((size_t)BH + 1) * 4;
+}
+
+// A row entry prefetched one tile ahead of its copy.
+struct RowEntry {
+    int kind;   // 0 none, 1 union row, 2 recent row, 3 sampled row
+    int32_t e;  // union: row | mask << 24; recent: row offset; sampled: packed sample word
+    float off;
+};
+
+__device__ __forceinline__ RowEntry load_entry(const DecodeArgs &a, int bh, int v, int s1, int U,
+                                               int R) {
+    RowEntry r;
+    r.kind = 0;
+    r.e = 0;
+    r.off = 0.f;
+    if (v >= s1) return r;
+    if (v < U) {
+        r.kind = 1;
+        r.e = a.ws.w_row[(int64_t)bh * a.geo.sample_end + v];
+    } else if (v < U + R) {
+        r.kind = 2;
+        r.e = v - U;
+    } else {
+        const int64_t j = (int64_t)bh * a.geo.group * a.p.samples + (v - U - R);
+        r.kind = 3;
+        r.e = a.ws.s_pos[j];
+        r.off = a.ws.s_off[j];
+    }
+    return r;
 }
 
 template <int D>
-__global__ void __launch_bounds__(kPipeThreads, 1) decode_attend_pipe_kernel(DecodeArgs a) {
-    using TG = PipeGeom<D>;
+__global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(DecodeArgs a) {
+    using GG = GatherGeom<D>;
     constexpr int NT_O = D / 8;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int BH = a.geo.batch * a.geo.num_kv_heads;
-    const int Gmax = a.sum.max_groups, g = a.geo.group;
+    const int g = a.geo.group;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int gid = lane >> 2, tig = lane & 3;
 
-    unsigned char *p = (unsigned char *)(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
-    char *kbuf = (char *)p;                  p += kNS * TG::TILE;
-    char *vbuf = (char *)p;                  p += kNS * TG::TILE;
-    int *rmask = (int *)p;                   p += kNS * kRows * 4;
-    float *roff = (float *)p;                p += kNS * kRows * 4;
-    uint64_t *full = (uint64_t *)p;          p += kNS * 8;
-    uint64_t *empty = (uint64_t *)p;         p += kNS * 8;
-    int *pre = (int *)p;                     p += (BH + 1) * 4;
-    int *u_off = (int *)p;                   p += (Gmax + 1) * 4;
-    int *u_start = (int *)p;                 p += Gmax * 4;
-    int *u_mask = (int *)p;                  p += Gmax * 4;
-    int32_t *s_tab = (int32_t *)p;           p += kSampCap * 4;
-    float *s_offt = (float *)p;              p += kSampCap * 4;
-    constexpr int CPR = TG::ROWB / 16;           // 16-byte chunks per row
-    constexpr int kRowsPerIter = 32 / CPR;
+    unsigned char *base = (unsigned char *)(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
+    unsigned char *wbase = base + warp * GG::WARP;     // this warp's ring
+    int *pre = (int *)(base + kGW * GG::WARP);         // segment prefix [BH + 1]
 
-    // ---- set-up: zero the stages (rows past a tile's end are multiplied by
-    // p = 0 and must hold finite values), barriers, segment prefix ----
-    for (int i = tid; i < 2 * kNS * TG::TILE / 16; i += kPipeThreads)
-        ((int4 *)kbuf)[i] = make_int4(0, 0, 0, 0);
-    if (tid == 0) {
-        for (int s = 0; s < kNS; ++s) {
-            mbar_init(&full[s], 32);  // one cp.async arrival per producer lane
-            mbar_init(&empty[s], kCons);
-        }
-        mbar_fence_init();
-    }
     if (warp == 0) {
         int carry = 0;
         for (int i0 = 0; i0 < BH; i0 += 32) {
@@ -233,8 +239,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) decode_attend_pipe_kernel(Dec
         }
         if (lane == 0) pre[0] = 0;
     }
-    fence_proxy_async_smem();  // order the generic zero-fill before async-proxy copies
-    __syncthreads();
+    __syncthreads();  // the only block-wide barrier
 
     const int T_all = pre[BH];
     const int P = max(1, ceil_div(T_all, (int)gridDim.x));
@@ -243,96 +248,28 @@ __global__ void __launch_bounds__(kPipeThreads, 1) decode_attend_pipe_kernel(Dec
     int bh0 = 0;
     while (bh0 < BH && pre[bh0 + 1] <= r0) ++bh0;
 
-    if (warp == kCons) {
-        // ===================== producer warp =====================
-        int it = 0;
-        bool err = false;
-        for (int bh = bh0; bh < BH && pre[bh] < r1 && !err; ++bh) {
-            const int seg0 = pre[bh], total = pre[bh + 1] - seg0;
-            const int s0 = max(r0, seg0) - seg0, s1 = min(r1, seg0 + total) - seg0;
-            if (s0 >= s1) continue;
-            const int32_t *meta = a.ws.meta + (int64_t)bh * 8;
-            const int n_union = meta[0], U = meta[1], R = meta[2];
-            for (int i = lane; i <= n_union; i += 32)
-                u_off[i] = a.ws.u_off[(int64_t)bh * (Gmax + 1) + i];
-            for (int i = lane; i < n_union; i += 32) {
-                u_start[i] = a.ws.u_start[(int64_t)bh * Gmax + i];
-                u_mask[i] = a.ws.u_mask[(int64_t)bh * Gmax + i];
-            }
-            // the segment's sample table, so row resolution never waits on HBM
-            const int nsamp = min(meta[3], kSampCap);
-            const int64_t sbase = (int64_t)bh * g * a.p.samples;
-            for (int i = lane; i < nsamp; i += 32) {
-                s_tab[i] = a.ws.s_pos[sbase + i];
-                s_offt[i] = a.ws.s_off[sbase + i];
-            }
-            __syncwarp();
-            for (int t0 = s0; t0 < s1; t0 += kRows, ++it) {
-                const int st = it % kNS;
-                const uint32_t ph = (uint32_t)(it / kNS) & 1u;
-                if (it >= kNS && !mbar_wait(&empty[st], ph ^ 1u)) {
-                    err = true;
-                    break;
-                }
-                const int nrows = min(kRows, s1 - t0);
-                const char *kp[2], *vp[2];
-#pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const int row = lane + 32 * j;
-                    RowInfo ri;
-                    ri.k = ri.v = nullptr;
-                    ri.mask = 0;
-                    ri.off = 0.f;
-                    if (row < nrows)
-                        ri = resolve_row(a, bh, t0 + row, U, R, total, n_union, u_off, u_start,
-                                         u_mask, TG::ROWB, s_tab, s_offt, nsamp);
-                    kp[j] = ri.k;
-                    vp[j] = ri.v;
-                    rmask[st * kRows + row] = ri.mask;
-                    roff[st * kRows + row] = ri.off;
-                }
-                // row-cooperative 16-byte copies: CPR lanes cover one row, so a
-                // warp instruction moves 32 / CPR whole rows, fully coalesced
-                char *kd = kbuf + st * TG::TILE;
-                char *vd = vbuf + st * TG::TILE;
-#pragma unroll
-                for (int i = 0; i < kRows / kRowsPerIter; ++i) {
-                    const int r = i * kRowsPerIter + lane / CPR;   // tile row
-                    const int c = lane % CPR;                      // 16-byte chunk
-                    const int slot = (i * kRowsPerIter) / 32;      // uniform per iteration
-                    const char *ks = (const char *)__shfl_sync(
-                        0xffffffffu, (unsigned long long)(slot ? kp[1] : kp[0]), r & 31);
-                    const char *vs = (const char *)__shfl_sync(
-                        0xffffffffu, (unsigned long long)(slot ? vp[1] : vp[0]), r & 31);
-                    if (r < nrows) {
-                        cp_async16(kd + r * TG::PITCH + c * 16, ks + c * 16);
-                        cp_async16(vd + r * TG::PITCH + c * 16, vs + c * 16);
-                    }
-                }
-                __syncwarp();
-                cp_async_mbar_arrive(&full[st]);
-            }
-        }
-        if (err && lane == 0) atomicExch(a.ws.flag + kFlagWaitTimeout, 1);
-        // no copy may still be landing in shared memory when the CTA exits
-        for (int k = max(0, it - kNS); k < it; ++k)
-            mbar_wait(&full[k % kNS], (uint32_t)(k / kNS) & 1u);
-        return;
-    }
-
-    // ===================== consumer warps =====================
     const float qscale = a.p.scale * kLog2e;
-    const int gid = lane >> 2, tig = lane & 3;
-    const int rbase = warp * 16;  // this warp's rows inside a tile
     const int PSTR = partial_stride(D);
-    int it = 0;
-    bool err = false;
+    const char *sk_all = (const char *)a.sum.sorted_key;
+    const char *sv_all = (const char *)a.sum.sorted_value;
+    int k_base = 0;  // CTA tiles before the current segment
     for (int bh = bh0; bh < BH && pre[bh] < r1; ++bh) {
         const int seg0 = pre[bh], total = pre[bh + 1] - seg0;
         const int s0 = max(r0, seg0) - seg0, s1 = min(r1, seg0 + total) - seg0;
         if (s0 >= s1) continue;
-        // q fragments of this (batch, KV head): rows = heads, split bf16 hi + lo
+        const int nt = ceil_div(s1 - s0, kGRows);
+        const int j0 = ((warp - k_base) % kGW + kGW) % kGW;  // my first tile in the segment
+        const int n_my = nt > j0 ? ceil_div(nt - j0, kGW) : 0;
+        k_base += nt;
+        const int32_t *meta = a.ws.meta + (int64_t)bh * 8;
+        const int U = meta[1], R = meta[2];
         const int b = bh / a.geo.num_kv_heads, kv = bh - b * a.geo.num_kv_heads;
+        const char *sk = sk_all + (int64_t)bh * a.geo.sample_end * GG::ROWB;
+        const char *sv = sv_all + (int64_t)bh * a.geo.sample_end * GG::ROWB;
+        const char *ck = a.key_cache + ((int64_t)bh * a.geo.capacity + a.geo.sample_end) * GG::ROWB;
+        const char *cv = a.value_cache + ((int64_t)bh * a.geo.capacity + a.geo.sample_end) * GG::ROWB;
+
+        // q fragments of this (batch, KV head): rows = heads, split bf16 hi + lo
         const float *qb = a.q + ((int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g) * D;
         uint32_t qh[D / 16][2], ql[D / 16][2];
 #pragma unroll
@@ -356,107 +293,175 @@ __global__ void __launch_bounds__(kPipeThreads, 1) decode_attend_pipe_kernel(Dec
 #pragma unroll
         for (int i = 0; i < NT_O; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
 
-        for (int t0 = s0; t0 < s1; t0 += kRows, ++it) {
-            const int st = it % kNS;
-            const uint32_t ph = (uint32_t)(it / kNS) & 1u;
-            if (!mbar_wait(&full[st], ph)) {
-                err = true;
-                break;
+        // first virtual row of my i-th tile
+        auto tile_row0 = [&](int i) { return s0 + (j0 + i * kGW) * kGRows; };
+        // issue the copies of my i-th tile into stage st from its prefetched entry
+        auto issue = [&](int i, int st, const RowEntry &en) {
+            unsigned char *stg = wbase + st * (GG::STAGE + GG::META);
+            int *mk = (int *)(stg + GG::STAGE);
+            float *of = (float *)(mk + kGRows);
+            const char *kp = sk, *vp = sv;
+            int mask = 0;
+            if (en.kind == 1) {
+                const int row = en.e & (int)kPosMask;
+                kp = sk + (int64_t)row * GG::ROWB;
+                vp = sv + (int64_t)row * GG::ROWB;
+                mask = (int)((uint32_t)en.e >> 24);
+            } else if (en.kind == 2) {
+                kp = ck + (int64_t)en.e * GG::ROWB;
+                vp = cv + (int64_t)en.e * GG::ROWB;
+                mask = (1 << g) - 1;
+            } else if (en.kind == 3) {
+                const uint32_t pk = (uint32_t)en.e;
+                const int row = (int)(pk & kPosMask);
+                kp = sk + (int64_t)row * GG::ROWB;
+                vp = sv + (int64_t)row * GG::ROWB;
+                mask = (1 << ((pk >> kHeadShift) & 7u)) | kMaskSample |
+                       ((pk & kAbsBit) ? kMaskAbs : 0);
             }
-            const int nrows = min(kRows, s1 - t0);
-            if (rbase < nrows) {
-                const char *ks_ = kbuf + st * TG::TILE;
-                const char *vs_ = vbuf + st * TG::TILE;
-                const int mat = lane >> 3, mrow = lane & 7;
-                float s0v[4] = {0.f, 0.f, 0.f, 0.f}, s1v[4] = {0.f, 0.f, 0.f, 0.f};
+            if (lane < kGRows) {
+                mk[lane] = mask;
+                of[lane] = en.off;
+            }
+            const int valid = en.kind != 0;
 #pragma unroll
-                for (int ks = 0; ks < D / 16; ++ks) {
-                    uint32_t b0, b1, b2, b3;
-                    const int r = rbase + ((mat >> 1) << 3) + mrow;
-                    const int c = 2 * ks + (mat & 1);
-                    ldmatrix_x4(smem_u32(ks_ + r * TG::PITCH + c * 16), b0, b1, b2, b3);
-                    mma_bf16(s0v, qh[ks][0], 0u, qh[ks][1], 0u, b0, b1);
-                    mma_bf16(s0v, ql[ks][0], 0u, ql[ks][1], 0u, b0, b1);
-                    mma_bf16(s1v, qh[ks][0], 0u, qh[ks][1], 0u, b2, b3);
-                    mma_bf16(s1v, ql[ks][0], 0u, ql[ks][1], 0u, b2, b3);
-                }
-                const int *mk = rmask + st * kRows;
-                const float *of = roff + st * kRows;
-                const int rr[4] = {rbase + 2 * tig, rbase + 2 * tig + 1, rbase + 8 + 2 * tig,
-                                   rbase + 9 + 2 * tig};
-                const float raw[4] = {s0v[0], s0v[1], s1v[0], s1v[1]};
-                float sv[4];
-                bool any_sample = false;
+            for (int it = 0; it < kGRows / GG::RPI; ++it) {
+                const int r = it * GG::RPI + lane / GG::CPR;
+                const int c = lane % GG::CPR;
+                const char *ks = (const char *)__shfl_sync(0xffffffffu, (unsigned long long)kp, r);
+                const char *vs = (const char *)__shfl_sync(0xffffffffu, (unsigned long long)vp, r);
+                const int ok = __shfl_sync(0xffffffffu, valid, r) ? 16 : 0;
+                const uint32_t kd = smem_u32(stg + r * GG::PITCH + c * 16);
+                const uint32_t vd = smem_u32(stg + GG::TILE + r * GG::PITCH + c * 16);
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(kd),
+                             "l"(ks + c * 16), "r"(ok)
+                             : "memory");
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(vd),
+                             "l"(vs + c * 16), "r"(ok)
+                             : "memory");
+            }
+            (void)i;
+        };
+        auto entry_of = [&](int i) {
+            RowEntry en;
+            en.kind = 0;
+            en.e = 0;
+            en.off = 0.f;
+            if (i < n_my && lane < kGRows) en = load_entry(a, bh, tile_row0(i) + lane, s1, U, R);
+            return en;
+        };
+
+        // prologue: tiles 0 .. kGStages-2 in flight, entry of the next one loaded
+        RowEntry en_next = entry_of(0);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int mm = mk[rr[i]];
-                    const bool on = gid < g && ((mm >> gid) & 1);
-                    sv[i] = on ? ((mm & kMaskAbs) ? of[rr[i]] : raw[i] + of[rr[i]]) : -INFINITY;
-                    any_sample |= on && (mm & kMaskSample);
-                }
-                float tmax = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
-                tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
-                tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
-                const float m_new = fmaxf(m_run, tmax);
-                float pr[4];
-                float alpha = 1.f;
-                if (m_new == -INFINITY) {
-                    pr[0] = pr[1] = pr[2] = pr[3] = 0.f;
-                } else {
-                    alpha = exp2f(m_run - m_new);
+        for (int i = 0; i < kGStages - 1; ++i) {
+            const RowEntry en = en_next;
+            en_next = entry_of(i + 1);
+            if (i < n_my) issue(i, i % kGStages, en);
+            asm volatile("cp.async.commit_group;\n" ::: "memory");
+        }
+        for (int i = 0; i < n_my; ++i) {
+            const int ni = i + kGStages - 1;
+            if (ni < n_my) {
+                const RowEntry en = en_next;
+                en_next = entry_of(ni + 1);
+                issue(ni, ni % kGStages, en);
+            }
+            asm volatile("cp.async.commit_group;\n" ::: "memory");
+            asm volatile("cp.async.wait_group %0;\n" ::"n"(kGStages - 1) : "memory");
+            __syncwarp();
+
+            const int st = i % kGStages;
+            const unsigned char *stg = wbase + st * (GG::STAGE + GG::META);
+            const char *ks_ = (const char *)stg;
+            const char *vs_ = (const char *)stg + GG::TILE;
+            const int *mk = (const int *)(stg + GG::STAGE);
+            const float *of = (const float *)(mk + kGRows);
+            const int mat = lane >> 3, mrow = lane & 7;
+            float s0v[4] = {0.f, 0.f, 0.f, 0.f}, s1v[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) pr[i] = exp2f(sv[i] - m_new);
-                    m_run = m_new;
-                }
-                l_run = l_run * alpha + (pr[0] + pr[1] + pr[2] + pr[3]);
+            for (int kk = 0; kk < D / 16; ++kk) {
+                uint32_t b0, b1, b2, b3;
+                const int r = ((mat >> 1) << 3) + mrow;
+                const int c = 2 * kk + (mat & 1);
+                ldmatrix_x4(smem_u32(ks_ + r * GG::PITCH + c * 16), b0, b1, b2, b3);
+                mma_bf16(s0v, qh[kk][0], 0u, qh[kk][1], 0u, b0, b1);
+                mma_bf16(s0v, ql[kk][0], 0u, ql[kk][1], 0u, b0, b1);
+                mma_bf16(s1v, qh[kk][0], 0u, qh[kk][1], 0u, b2, b3);
+                mma_bf16(s1v, ql[kk][0], 0u, ql[kk][1], 0u, b2, b3);
+            }
+            const int rr[4] = {2 * tig, 2 * tig + 1, 8 + 2 * tig, 9 + 2 * tig};
+            const float raw[4] = {s0v[0], s0v[1], s1v[0], s1v[1]};
+            float sv4[4];
+            bool any_sample = false;
 #pragma unroll
-                for (int i = 0; i < NT_O; ++i) {
-                    o[i][0] *= alpha;
-                    o[i][1] *= alpha;
-                }
-                if (__any_sync(0xffffffffu, any_sample)) {
+            for (int q = 0; q < 4; ++q) {
+                const int mm = mk[rr[q]];
+                const bool on = gid < g && ((mm >> gid) & 1);
+                sv4[q] = on ? ((mm & kMaskAbs) ? of[rr[q]] : raw[q] + of[rr[q]]) : -INFINITY;
+                any_sample |= on && (mm & kMaskSample);
+            }
+            float tmax = fmaxf(fmaxf(sv4[0], sv4[1]), fmaxf(sv4[2], sv4[3]));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
+            const float m_new = fmaxf(m_run, tmax);
+            float pr[4];
+            float alpha = 1.f;
+            if (m_new == -INFINITY) {
+                pr[0] = pr[1] = pr[2] = pr[3] = 0.f;
+            } else {
+                alpha = exp2f(m_run - m_new);
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int mm = mk[rr[i]];
-                        if (gid < g && ((mm >> gid) & 1) && (mm & kMaskSample)) {
-                            const float lw = sv[i];
-                            if (lw > ms_run) {
-                                const float f = exp2f(ms_run - lw);
-                                e1_run = e1_run * f + 1.f;
-                                e2_run = e2_run * f * f + 1.f;
-                                ms_run = lw;
-                            } else {
-                                const float f = exp2f(lw - ms_run);
-                                e1_run += f;
-                                e2_run += f * f;
-                            }
+                for (int q = 0; q < 4; ++q) pr[q] = exp2f(sv4[q] - m_new);
+                m_run = m_new;
+            }
+            l_run = l_run * alpha + (pr[0] + pr[1] + pr[2] + pr[3]);
+#pragma unroll
+            for (int q = 0; q < NT_O; ++q) {
+                o[q][0] *= alpha;
+                o[q][1] *= alpha;
+            }
+            if (__any_sync(0xffffffffu, any_sample)) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int mm = mk[rr[q]];
+                    if (gid < g && ((mm >> gid) & 1) && (mm & kMaskSample)) {
+                        const float lw = sv4[q];
+                        if (lw > ms_run) {
+                            const float f = exp2f(ms_run - lw);
+                            e1_run = e1_run * f + 1.f;
+                            e2_run = e2_run * f * f + 1.f;
+                            ms_run = lw;
+                        } else {
+                            const float f = exp2f(lw - ms_run);
+                            e1_run += f;
+                            e2_run += f * f;
                         }
                     }
                 }
-                const uint32_t ph0 = pack_bf16(pr[0], pr[1]);
-                const uint32_t ph2 = pack_bf16(pr[2], pr[3]);
-                const float2 f0 = __bfloat1622float2(*(const __nv_bfloat162 *)&ph0);
-                const float2 f2 = __bfloat1622float2(*(const __nv_bfloat162 *)&ph2);
-                const uint32_t pl0 = pack_bf16(pr[0] - f0.x, pr[1] - f0.y);
-                const uint32_t pl2 = pack_bf16(pr[2] - f2.x, pr[3] - f2.y);
-#pragma unroll
-                for (int j = 0; j < D / 16; ++j) {
-                    uint32_t b0, b1, b2, b3;
-                    const int r = rbase + ((mat & 1) << 3) + mrow;
-                    const int c = 2 * j + (mat >> 1);
-                    ldmatrix_x4_trans(smem_u32(vs_ + r * TG::PITCH + c * 16), b0, b1, b2, b3);
-                    mma_bf16(o[2 * j], ph0, 0u, ph2, 0u, b0, b1);
-                    mma_bf16(o[2 * j], pl0, 0u, pl2, 0u, b0, b1);
-                    mma_bf16(o[2 * j + 1], ph0, 0u, ph2, 0u, b2, b3);
-                    mma_bf16(o[2 * j + 1], pl0, 0u, pl2, 0u, b2, b3);
-                }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[st]);
+            const uint32_t ph0 = pack_bf16(pr[0], pr[1]);
+            const uint32_t ph2 = pack_bf16(pr[2], pr[3]);
+            const float2 f0 = __bfloat1622float2(*(const __nv_bfloat162 *)&ph0);
+            const float2 f2 = __bfloat1622float2(*(const __nv_bfloat162 *)&ph2);
+            const uint32_t pl0 = pack_bf16(pr[0] - f0.x, pr[1] - f0.y);
+            const uint32_t pl2 = pack_bf16(pr[2] - f2.x, pr[3] - f2.y);
+#pragma unroll
+            for (int j = 0; j < D / 16; ++j) {
+                uint32_t b0, b1, b2, b3;
+                const int r = ((mat & 1) << 3) + mrow;
+                const int c = 2 * j + (mat >> 1);
+                ldmatrix_x4_trans(smem_u32(vs_ + r * GG::PITCH + c * 16), b0, b1, b2, b3);
+                mma_bf16(o[2 * j], ph0, 0u, ph2, 0u, b0, b1);
+                mma_bf16(o[2 * j], pl0, 0u, pl2, 0u, b0, b1);
+                mma_bf16(o[2 * j + 1], ph0, 0u, ph2, 0u, b2, b3);
+                mma_bf16(o[2 * j + 1], pl0, 0u, pl2, 0u, b2, b3);
+            }
+            __syncwarp();  // stage st is refilled by the next iteration's issue
         }
-        if (err) break;
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
 
-        // ---- this CTA is done with segment bh: write its partial ----
+        // ---- this warp is done with segment bh: write its partial ----
         l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
         l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
         {
@@ -472,12 +477,9 @@ __global__ void __launch_bounds__(kPipeThreads, 1) decode_attend_pipe_kernel(Dec
             e1_run = E1;
             e2_run = E2;
         }
-        // Each consumer warp writes its own partial (no intra-CTA barrier, so
-        // a timed-out wait in one warp cannot stall the others).  Slot
-        // (c + bh) * kCons + warp is unique: the segments a CTA meets form an
-        // increasing range and the ranges of consecutive CTAs touch at most
-        // at one segment.
-        const int64_t slot = ((int64_t)blockIdx.x + bh) * kCons + warp;
+        // slot (c + bh) * kGW + warp is unique: the segments a CTA meets form an
+        // increasing range and consecutive CTAs' ranges share at most one segment
+        const int64_t slot = ((int64_t)blockIdx.x + bh) * kGW + warp;
         float *part = a.ws.partial + slot * g * PSTR;
         if (gid < g) {
             if (tig == 0) {
@@ -488,33 +490,32 @@ __global__ void __launch_bounds__(kPipeThreads, 1) decode_attend_pipe_kernel(Dec
                 part[gid * PSTR + 4] = e2_run;
             }
 #pragma unroll
-            for (int i = 0; i < NT_O; ++i) {
-                part[gid * PSTR + 8 + i * 8 + 2 * tig] = o[i][0];
-                part[gid * PSTR + 8 + i * 8 + 2 * tig + 1] = o[i][1];
+            for (int q = 0; q < NT_O; ++q) {
+                part[gid * PSTR + 8 + q * 8 + 2 * tig] = o[q][0];
+                part[gid * PSTR + 8 + q * 8 + 2 * tig + 1] = o[q][1];
             }
         }
         __threadfence();
         __syncwarp();
         const int first = seg0 / P, last = (seg0 + total - 1) / P;
-        const int contributors = (last - first + 1) * kCons;
+        const int contributors = (last - first + 1) * kGW;
         int is_last = 0;
         if (lane == 0) is_last = (atomicAdd(&a.ws.counters[bh], 1) == contributors - 1);
         is_last = __shfl_sync(0xffffffffu, is_last, 0);
         if (is_last) {
             __threadfence();
-            merge_partials_to_output<D>(
-                a, bh, a.ws.partial + ((int64_t)first + bh) * kCons * g * PSTR, contributors, lane,
-                32);
+            merge_partials_to_output<D>(a, bh,
+                                        a.ws.partial + ((int64_t)first + bh) * kGW * g * PSTR,
+                                        contributors, lane, 32);
             if (lane == 0) a.ws.counters[bh] = 0;
         }
     }
-    if (err && lane == 0) atomicExch(a.ws.flag + kFlagWaitTimeout, 1);
     // segments with no rows at all (every head empty) still get an output
-    if (blockIdx.x == 0 && !err) {
+    if (blockIdx.x == 0 && warp == 0) {
         for (int bh = 0; bh < BH; ++bh) {
             if (pre[bh + 1] != pre[bh]) continue;
             const int b = bh / a.geo.num_kv_heads, kv = bh - b * a.geo.num_kv_heads;
-            for (int i = tid; i < g * D; i += 32 * kCons) {
+            for (int i = lane; i < g * D; i += 32) {
                 const int h = i / D, d = i - h * D;
                 const int64_t oh = (int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g + h;
                 a.out[oh * D + d] = 0.f;
@@ -539,8 +540,8 @@ static size_t simt_smem_bytes(int Gmax) {
 int attend_partial_slots(const SantaGeometry *geo, int nsplit) {
     const int BH = geo->batch * geo->num_kv_heads;
     const int simt = BH * nsplit;
-    const int pipe = (num_sms() + BH) * kCons;
-    return simt > pipe ? simt : pipe;
+    const int gather = (num_sms() + BH) * kGW;
+    return simt > gather ? simt : gather;
 }
 
 template <int D>
@@ -550,15 +551,15 @@ static int launch_execute_d(DecodeArgs &a, cudaStream_t stream) {
     SANTA_CUDA_CHECK(cudaMemsetAsync(a.ws.counters, 0, (size_t)BH * 4, stream));
     if (a.geo.kv_dtype == SANTA_DTYPE_BF16) {
         static size_t done = 0;
-        const size_t sm = pipe_smem_bytes<D>(BH, Gmax);
+        const size_t sm = gather_smem_bytes<D>(BH);
         if (sm > 227 * 1024) return SANTA_ERR_UNSUPPORTED;
         if (done < sm) {
-            SANTA_CUDA_CHECK(cudaFuncSetAttribute(decode_attend_pipe_kernel<D>,
+            SANTA_CUDA_CHECK(cudaFuncSetAttribute(decode_attend_gather_kernel<D>,
                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                   (int)sm));
             done = sm;
         }
-        decode_attend_pipe_kernel<D><<<num_sms(), kPipeThreads, sm, stream>>>(a);
+        decode_attend_gather_kernel<D><<<num_sms(), kGThreads, sm, stream>>>(a);
     } else {
         static size_t done = 0;
         const size_t sm = simt_smem_bytes<D>(Gmax);

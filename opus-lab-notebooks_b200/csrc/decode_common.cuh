@@ -52,13 +52,14 @@ struct DecodeWs {
     float *s_off;        // [BH][g*S] log2-units offset (or absolute log2 weight)
     float *lse_old;      // [BH][8] santa mode: log2-sum-exp2 of old scores
     float *partial;      // [n_slots][g][D + 8] split partials
+    int32_t *w_row;      // [BH][sample_end] union rows expanded: row | (head mask << 24)
 };
 
 __host__ __device__ inline int partial_stride(int D) { return D + 8; }
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-inline size_t decode_ws_layout(int BH, int G, int g, int S, int n_slots, int D, char *base,
+inline size_t decode_ws_layout(int BH, int G, int g, int S, int n_slots, int D, int N, char *base,
                                DecodeWs *ws) {
     size_t off = 0;
     auto take = [&](size_t bytes) {
@@ -79,7 +80,9 @@ inline size_t decode_ws_layout(int BH, int G, int g, int S, int n_slots, int D, 
     size_t o_so = take((size_t)BH * gs * 4);
     size_t o_lo = take((size_t)BH * 8 * 4);
     size_t o_pa = take((size_t)n_slots * g * partial_stride(D) * 4);
+    size_t o_wr = take((size_t)BH * N * 4);
     if (base && ws) {
+        ws->w_row = (int32_t *)(base + o_wr);
         ws->counters = (int32_t *)(base + o_cnt);
         ws->flag = (int32_t *)(base + o_flag);
         ws->meta = (int32_t *)(base + o_meta);

@@ -193,6 +193,11 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
     // ---- union of the group's selections (ascending cluster order) ----
     int n_union = 0, U = 0;
     {
+        // union entries also kept in shared memory (the centroid tile area is
+        // free after scoring: 64 * (D + 1) floats >= 3 * 1024 ints)
+        int *ue_start = (int *)ct;
+        int *ue_off = ue_start + Gmax;
+        int *ue_mask = ue_off + Gmax;
         int base = 0, rows = 0;
         for (int c0 = 0; c0 < n_groups; c0 += kSelThreads) {
             const int c = c0 + tid;
@@ -206,6 +211,9 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
                 a.ws.u_mask[(int64_t)bh * Gmax + base + ui] = m;
                 a.ws.u_cid[(int64_t)bh * Gmax + base + ui] = c;
                 a.ws.u_off[(int64_t)bh * (Gmax + 1) + base + ui] = rows + ro;
+                ue_start[base + ui] = starts_s[c];
+                ue_off[base + ui] = rows + ro;
+                ue_mask[base + ui] = m;
             }
             base += cnt;
             rows += rtot;
@@ -213,6 +221,16 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
         n_union = base;
         U = rows;
         if (tid == 0) a.ws.u_off[(int64_t)bh * (Gmax + 1) + n_union] = U;
+        __syncthreads();
+        // expanded row list of the union: entry v = sorted row | (head mask << 24),
+        // so the attention kernel resolves a row with one coalesced load
+        int32_t *wr = a.ws.w_row + (int64_t)bh * sample_end;
+        for (int j = warp; j < n_union; j += kSelThreads / 32) {
+            const int off = ue_off[j];
+            const int len = (j + 1 < n_union ? ue_off[j + 1] : U) - off;
+            const int tag = ue_mask[j] << 24;
+            for (int r = lane; r < len; r += 32) wr[off + r] = (ue_start[j] + r) | tag;
+        }
     }
 
     // ---- per-head sample counts ----
