@@ -17,8 +17,9 @@
 //       into its own 3-stage ring of padded shared-memory tiles, and runs
 //       mma.sync m16n8k16 (GQA heads on M; q and p split into bf16 hi + lo for
 //       fp32-level accuracy) with an online softmax.  No barrier crosses
-//       warps.  At a segment end each warp writes a partial; the last warp of
-//       the segment merges them (LSE merge).
+//       warps.  At a segment end each warp writes a partial (m, l, o[D]);
+//       decode_merge_kernel then LSE-merges the partials of every (segment,
+//       query head) in parallel.
 //       (Two earlier designs were measured slower on B200: one bulk copy per
 //       256-byte row through the TMA engine is request-bound, and a single
 //       producer warp cannot keep enough 16-byte copies in flight.)
@@ -495,35 +496,85 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
                 part[gid * PSTR + 8 + q * 8 + 2 * tig + 1] = o[q][1];
             }
         }
-        __threadfence();
-        __syncwarp();
-        const int first = seg0 / P, last = (seg0 + total - 1) / P;
-        const int contributors = (last - first + 1) * kGW;
-        int is_last = 0;
-        if (lane == 0) is_last = (atomicAdd(&a.ws.counters[bh], 1) == contributors - 1);
-        is_last = __shfl_sync(0xffffffffu, is_last, 0);
-        if (is_last) {
-            __threadfence();
-            merge_partials_to_output<D>(a, bh,
-                                        a.ws.partial + ((int64_t)first + bh) * kGW * g * PSTR,
-                                        contributors, lane, 32);
-            if (lane == 0) a.ws.counters[bh] = 0;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// LSE merge of the gather kernel's per-warp partials: one CTA per (segment,
+// query head), one thread per output element.  Separate from the gather
+// kernel because a single merging warp serialises an L2 round trip per
+// partial and ends up on the critical path.
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(D) decode_merge_kernel(DecodeArgs a, int n_ctas) {
+    const int bh = blockIdx.x / a.geo.group, h = blockIdx.x - bh * a.geo.group;
+    const int g = a.geo.group, BH = a.geo.batch * a.geo.num_kv_heads;
+    const int d = threadIdx.x, lane = d & 31;
+    const int PSTR = partial_stride(D);
+    __shared__ int s_seg0, s_tall;
+    if (d < 32) {  // prefix of segment sizes: start of bh and the grand total
+        int before = 0, all = 0;
+        for (int i = lane; i < BH; i += 32) {
+            const int t = a.ws.meta[(int64_t)i * 8 + 4];
+            all += t;
+            if (i < bh) before += t;
+        }
+        before = warp_sum_int(before);
+        all = warp_sum_int(all);
+        if (lane == 0) {
+            s_seg0 = before;
+            s_tall = all;
         }
     }
-    // segments with no rows at all (every head empty) still get an output
-    if (blockIdx.x == 0 && warp == 0) {
-        for (int bh = 0; bh < BH; ++bh) {
-            if (pre[bh + 1] != pre[bh]) continue;
-            const int b = bh / a.geo.num_kv_heads, kv = bh - b * a.geo.num_kv_heads;
-            for (int i = lane; i < g * D; i += 32) {
-                const int h = i / D, d = i - h * D;
-                const int64_t oh = (int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g + h;
-                a.out[oh * D + d] = 0.f;
-                if (d == 0) {
-                    if (a.lse) a.lse[oh] = -INFINITY;
-                    if (a.ess) a.ess[oh] = 0.f;
+    __syncthreads();
+    const int seg0 = s_seg0, T_all = s_tall;
+    const int total = a.ws.meta[(int64_t)bh * 8 + 4];
+    const int b = bh / a.geo.num_kv_heads, kv = bh - b * a.geo.num_kv_heads;
+    const int64_t oh = (int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g + h;
+    if (total == 0) {  // no rows at all for this segment
+        a.out[oh * D + d] = 0.f;
+        if (d == 0) {
+            if (a.lse) a.lse[oh] = -INFINITY;
+            if (a.ess) a.ess[oh] = 0.f;
+        }
+        return;
+    }
+    const int P = max(1, ceil_div(T_all, n_ctas));
+    const int first = seg0 / P, last = (seg0 + total - 1) / P;
+    const int count = (last - first + 1) * kGW;
+    const float *pall = a.ws.partial + ((int64_t)first + bh) * kGW * g * PSTR + h * PSTR;
+    const int64_t step = (int64_t)g * PSTR;
+    float M = -INFINITY, L = 0.f, acc = 0.f;
+#pragma unroll 4
+    for (int s = 0; s < count; ++s) {
+        const float *ps = pall + s * step;
+        const float m = ps[0], l = ps[1], o = ps[8 + d];
+        if (l > 0.f) {
+            const float mn = fmaxf(M, m);
+            const float f0 = exp2f(M - mn), f1 = exp2f(m - mn);
+            L = L * f0 + l * f1;
+            acc = acc * f0 + o * f1;
+            M = mn;
+        }
+    }
+    a.out[oh * D + d] = L > 0.f ? acc / L : 0.f;
+    if (d == 0) {
+        if (a.lse) a.lse[oh] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
+        if (a.ess) {
+            float MS = -INFINITY, E1 = 0.f, E2 = 0.f;
+            for (int s = 0; s < count; ++s) {
+                const float *ps = pall + s * step;
+                const float ms = ps[2], e1 = ps[3], e2 = ps[4];
+                if (e1 > 0.f) {
+                    const float mn = fmaxf(MS, ms);
+                    const float f0 = exp2f(MS - mn), f1 = exp2f(ms - mn);
+                    E1 = E1 * f0 + e1 * f1;
+                    E2 = E2 * f0 * f0 + e2 * f1 * f1;
+                    MS = mn;
                 }
             }
+            const int ns = a.ws.head_meta[((int64_t)bh * 8 + h) * 2 + 1];
+            a.ess[oh] = (ns > 0 && E2 > 0.f) ? (E1 * E1 / E2) / (float)ns : 0.f;
         }
     }
 }
@@ -560,6 +611,8 @@ static int launch_execute_d(DecodeArgs &a, cudaStream_t stream) {
             done = sm;
         }
         decode_attend_gather_kernel<D><<<num_sms(), kGThreads, sm, stream>>>(a);
+        SANTA_LAUNCH_CHECK();
+        decode_merge_kernel<D><<<BH * a.geo.group, D, 0, stream>>>(a, num_sms());
     } else {
         static size_t done = 0;
         const size_t sm = simt_smem_bytes<D>(Gmax);
