@@ -544,35 +544,71 @@ __global__ void __launch_bounds__(D) decode_merge_kernel(DecodeArgs a, int n_cta
     const int count = (last - first + 1) * kGW;
     const float *pall = a.ws.partial + ((int64_t)first + bh) * kGW * g * PSTR + h * PSTR;
     const int64_t step = (int64_t)g * PSTR;
-    float M = -INFINITY, L = 0.f, acc = 0.f;
-#pragma unroll 4
-    for (int s = 0; s < count; ++s) {
+    extern __shared__ float fac[];  // [count] weight of each partial
+    __shared__ float red[5][D / 32];
+    constexpr int NWM = D / 32;
+    const int wid = d >> 5;
+    // pass 1: maxima of the partials' log-scales (independent loads, no branch chain)
+    float M = -INFINITY, MS = -INFINITY;
+    for (int s = d; s < count; s += D) {
         const float *ps = pall + s * step;
-        const float m = ps[0], l = ps[1], o = ps[8 + d];
-        if (l > 0.f) {
-            const float mn = fmaxf(M, m);
-            const float f0 = exp2f(M - mn), f1 = exp2f(m - mn);
-            L = L * f0 + l * f1;
-            acc = acc * f0 + o * f1;
-            M = mn;
-        }
+        const float m = ps[0], l = ps[1], ms = ps[2], e1 = ps[3];
+        M = fmaxf(M, l > 0.f ? m : -INFINITY);
+        MS = fmaxf(MS, e1 > 0.f ? ms : -INFINITY);
     }
+    M = warp_max(M);
+    MS = warp_max(MS);
+    if (lane == 0) {
+        red[0][wid] = M;
+        red[1][wid] = MS;
+    }
+    __syncthreads();
+    M = red[0][0];
+    MS = red[1][0];
+#pragma unroll
+    for (int w = 1; w < NWM; ++w) {
+        M = fmaxf(M, red[0][w]);
+        MS = fmaxf(MS, red[1][w]);
+    }
+    // pass 2: per-partial factors into shared memory, denominators
+    float L = 0.f, E1 = 0.f, E2 = 0.f;
+    for (int s = d; s < count; s += D) {
+        const float *ps = pall + s * step;
+        const float m = ps[0], l = ps[1], ms = ps[2], e1 = ps[3], e2 = ps[4];
+        const float f = l > 0.f ? exp2f(m - M) : 0.f;
+        fac[s] = f;
+        L += l * f;
+        const float fe = e1 > 0.f ? exp2f(ms - MS) : 0.f;
+        E1 += e1 * fe;
+        E2 += e2 * fe * fe;
+    }
+    L = warp_sum(L);
+    E1 = warp_sum(E1);
+    E2 = warp_sum(E2);
+    __syncthreads();  // red[0..1] reads above are done before reuse
+    if (lane == 0) {
+        red[2][wid] = L;
+        red[3][wid] = E1;
+        red[4][wid] = E2;
+    }
+    __syncthreads();
+    L = 0.f;
+    E1 = 0.f;
+    E2 = 0.f;
+#pragma unroll
+    for (int w = 0; w < NWM; ++w) {
+        L += red[2][w];
+        E1 += red[3][w];
+        E2 += red[4][w];
+    }
+    // pass 3: branch-free weighted sum of the partial outputs
+    float acc = 0.f;
+#pragma unroll 8
+    for (int s = 0; s < count; ++s) acc = fmaf(fac[s], pall[s * step + 8 + d], acc);
     a.out[oh * D + d] = L > 0.f ? acc / L : 0.f;
     if (d == 0) {
         if (a.lse) a.lse[oh] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
         if (a.ess) {
-            float MS = -INFINITY, E1 = 0.f, E2 = 0.f;
-            for (int s = 0; s < count; ++s) {
-                const float *ps = pall + s * step;
-                const float ms = ps[2], e1 = ps[3], e2 = ps[4];
-                if (e1 > 0.f) {
-                    const float mn = fmaxf(MS, ms);
-                    const float f0 = exp2f(MS - mn), f1 = exp2f(ms - mn);
-                    E1 = E1 * f0 + e1 * f1;
-                    E2 = E2 * f0 * f0 + e2 * f1 * f1;
-                    MS = mn;
-                }
-            }
             const int ns = a.ws.head_meta[((int64_t)bh * 8 + h) * 2 + 1];
             a.ess[oh] = (ns > 0 && E2 > 0.f) ? (E1 * E1 / E2) / (float)ns : 0.f;
         }
@@ -612,7 +648,8 @@ static int launch_execute_d(DecodeArgs &a, cudaStream_t stream) {
         }
         decode_attend_gather_kernel<D><<<num_sms(), kGThreads, sm, stream>>>(a);
         SANTA_LAUNCH_CHECK();
-        decode_merge_kernel<D><<<BH * a.geo.group, D, 0, stream>>>(a, num_sms());
+        const size_t msm = (size_t)(num_sms() + BH) * kGW * sizeof(float);  // >= partials per head
+        decode_merge_kernel<D><<<BH * a.geo.group, D, msm, stream>>>(a, num_sms());
     } else {
         static size_t done = 0;
         const size_t sm = simt_smem_bytes<D>(Gmax);
