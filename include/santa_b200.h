@@ -163,6 +163,34 @@ int santa_decode_execute(const SantaGeometry *geo, const SantaDecodeParams *p, c
                          const SantaSummary *summary, float *out, float *lse, float *ess,
                          void *workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* Size of the fixed scratch array behind santa_decode_static_scratch. */
+#define SANTA_DECODE_STATIC_SCRATCH_BYTES (16u << 20) /* 16 MiB */
+
+/* santa_decode for callers that cannot allocate device memory.  It has no
+ * counterpart in the reference.  Some callers may not call cudaMalloc: a
+ * serving stack whose memory manager has reserved all device memory for its
+ * own pools, a host application that loads this library as a plugin and bans
+ * device allocations after start-up, or a decode loop that cannot afford
+ * cudaMalloc's implicit device synchronisation.  This entry point takes the
+ * same inputs and outputs as santa_decode but no workspace: the scratch lives
+ * in a fixed SANTA_DECODE_STATIC_SCRATCH_BYTES array inside the library, held
+ * by every GPU that loads the library until the process exits.  It allocates
+ * nothing.
+ *   - Geometries whose santa_decode_workspace_bytes exceeds the array are
+ *     refused with SANTA_ERR_WORKSPACE.
+ *   - The first call on a device looks up the array's device address (once
+ *     per device, with that device current); make that first call before any
+ *     stream capture.
+ *   - All calls on a device share the one array and it keeps the previous
+ *     call's contents; each call clears what must start at zero, but calls
+ *     whose work overlaps on the GPU (other streams, other host threads) race
+ *     on it and must be serialised by the caller. */
+int santa_decode_static_scratch(const SantaGeometry *geo, const SantaDecodeParams *p,
+                                const float *q, const void *key_cache, const void *value_cache,
+                                const SantaSummary *summary, const int32_t *sample_a,
+                                const int32_t *sample_b, float *out, float *lse,
+                                int32_t *n_exact, float *ess, cudaStream_t stream);
+
 /* Selection step of santa_decode alone, read out per query head: which
  * clusters are attended exactly and which sorted rows were sampled.  Same
  * arguments and workspace as santa_decode.  Replaces the ranking and draw

@@ -75,6 +75,9 @@ SIGNATURES = {
     "santa_decode_execute": (ctypes.c_int, [_P(SantaGeometry), _P(SantaDecodeParams), _vp, _vp,
                                             _vp, _P(SantaSummary), _vp, _vp, _vp, _vp,
                                             ctypes.c_size_t, _vp]),
+    "santa_decode_static_scratch": (ctypes.c_int, [_P(SantaGeometry), _P(SantaDecodeParams), _vp,
+                                                   _vp, _vp, _P(SantaSummary), _vp, _vp, _vp,
+                                                   _vp, _vp, _vp, _vp]),
     "santa_decode_select": (ctypes.c_int, [_P(SantaGeometry), _P(SantaDecodeParams), _vp, _vp,
                                            _vp, _P(SantaSummary), _vp, _vp, _vp, _vp, _vp, _vp,
                                            ctypes.c_size_t, _vp]),
