@@ -11,11 +11,24 @@
 // The guess follows the oracle's defined arithmetic bit for bit: the dot
 // product is a sequential fmaf chain over head_dim, then fl32(dot * scale),
 // then fl32(log_n + that).
+//
+// Structure (512 threads = 16 warps):
+//   1. q, cluster starts/lengths and the first 128-centroid tile are loaded
+//      together; each later tile is prefetched into registers while the
+//      current one is scored.  A thread scores two centroids for one query
+//      head with two interleaved fmaf chains.
+//   2. Top-k: one warp per query head; every lane keeps its clusters' keys
+//      (orderable guess << 32 | ~index) sorted in registers, so extracting
+//      the next best cluster is two redux.sync steps and a register shift.
+//   3. Union of the group's selections and its expanded row list.
+//   4. Draws: two warps per query head.
 #include "decode_common.cuh"
 
 #include <math.h>
 
 namespace santa {
+
+constexpr int kTileC = 128;  // centroids per scoring tile
 
 __device__ int sel_block_exclusive_scan(int v, int *sw, int *total) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -47,6 +60,16 @@ __device__ int sel_block_exclusive_scan(int v, int *sw, int *total) {
 }
 
 template <int D>
+struct SelSmem {
+    static constexpr int CT_FLOATS = kTileC * (D + 1);
+    static_assert(CT_FLOATS >= SANTA_MAX_GROUP * SANTA_MAX_CLUSTERS,
+                  "the centroid tile area also holds the guided CDF");
+    static_assert(CT_FLOATS >= 3 * SANTA_MAX_CLUSTERS,
+                  "the centroid tile area also holds the union entries");
+};
+
+// KPL: keys per lane in the top-k extraction (clusters lane, lane+32, ...).
+template <int D, int KPL>
 __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int bh = blockIdx.x;
@@ -59,27 +82,40 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
     const int sample_end = a.geo.sample_end;
     const bool uses_clusters = (mode == SANTA_MODE_TOPK || mode == SANTA_MODE_GUIDED ||
                                 mode == SANTA_MODE_HYBRID);
+    const int kcap = (mode == SANTA_MODE_HYBRID) ? max(a.p.topk_clusters, 1) : 1;
 
     // shared memory carve-up
     float *qs = (float *)smem_raw;                              // [8][D]
-    float *ct = qs + SANTA_MAX_GROUP * D;                       // [64][D+1]
-    int *starts_s = (int *)(ct + 64 * (D + 1));                 // [Gmax]
+    float *ct = qs + SANTA_MAX_GROUP * D;                       // [kTileC][D+1]
+    int *starts_s = (int *)(ct + SelSmem<D>::CT_FLOATS);        // [Gmax]
     int *len_s = starts_s + Gmax;                               // [Gmax]
     int *mask_s = len_s + Gmax;                                 // [Gmax]
     float *guess_s = (float *)(mask_s + Gmax);                  // [8][Gmax]
-    int *selasc = (int *)(guess_s + SANTA_MAX_GROUP * Gmax);    // [8][2*Gmax+1] gap / cum
-    int *sw = selasc + SANTA_MAX_GROUP * (2 * Gmax + 1);        // [40]
-    int *head_sel = sw + 40;                                    // [8] selected clusters per head
+    int *gapcum = (int *)(guess_s + SANTA_MAX_GROUP * Gmax);    // [8][2*kcap+1]
+    int *sw = gapcum + SANTA_MAX_GROUP * (2 * kcap + 1);        // [40]
+    int *head_sel = sw + 40;                                    // [8]
     int *head_exact = head_sel + 8;                             // [8]
-    int *head_ns = head_exact + 8;                              // [8] samples per head
+    int *head_ns = head_exact + 8;                              // [8]
     int *head_sbase = head_ns + 8;                              // [8]
-    float *head_f = (float *)(head_sbase + 8);                  // [8][4] misc floats
-    uint64_t *keys = (uint64_t *)(((uintptr_t)(head_f + 32) + 15) & ~(uintptr_t)15);  // [8][Gp]
+    int *head_cnt = head_sbase + 8;                             // [8]
+    float *head_f = (float *)(head_cnt + 8);                    // [8][4]
 
+    // ---- 1. loads: q, cluster metadata and the first centroid tile together ----
+    const float *cent = a.sum.centroids + (int64_t)bh * Gmax * D;
+    constexpr int V4 = kTileC * D / 4 / kSelThreads;  // float4 per thread per tile
+    float4 pre[V4];
+    const int rows0 = min(kTileC, Gmax);  // in-bounds rows of the first tile
+    auto load_tile = [&](int c0, int nrow) {
+#pragma unroll
+        for (int j = 0; j < V4; ++j) {
+            const int i = tid + j * kSelThreads;  // float4 index in the tile
+            const int r = (i * 4) / D;
+            pre[j] = r < nrow ? *(const float4 *)(cent + (int64_t)(c0 + r) * D + (i * 4 - r * D))
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    if (uses_clusters) load_tile(0, rows0);
     const int n_groups = uses_clusters ? a.sum.n_groups[bh] : 0;
-    int Gp = 1;
-    while (Gp < n_groups) Gp <<= 1;
-
     const float *qb = a.q + ((int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g) * D;
     for (int i = tid; i < g * D; i += kSelThreads) qs[i] = qb[i];
     for (int i = tid; i < n_groups; i += kSelThreads) {
@@ -91,30 +127,13 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
         head_sel[tid] = 0;
         head_exact[tid] = 0;
         head_ns[tid] = 0;
+        head_cnt[tid] = 0;
     }
-    __syncthreads();
 
-    // ---- centroid guesses: fl32(log_n + fl32(dot * scale)), dot = fmaf chain ----
+    // ---- 2. centroid guesses: fl32(log_n + fl32(dot * scale)), dot = fmaf chain ----
     if (uses_clusters) {
-        const float *cent = a.sum.centroids + (int64_t)bh * Gmax * D;
         const float *logn = a.sum.log_n + (int64_t)bh * Gmax;
-        // 64-centroid tiles, loaded as float4 into registers one tile ahead so
-        // the HBM round trip of tile t+1 overlaps the dot products of tile t.
-        constexpr int V4 = 64 * D / 4 / kSelThreads;  // float4 per thread per tile
-        float4 pre[V4];
-        auto load_tile = [&](int c0) {
-            const int nc = min(64, n_groups - c0);
-#pragma unroll
-            for (int j = 0; j < V4; ++j) {
-                const int i = tid + j * kSelThreads;  // float4 index in the tile
-                const int r = (i * 4) / D;
-                pre[j] = r < nc ? *(const float4 *)(cent + (int64_t)(c0 + r) * D + (i * 4 - r * D))
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-        };
-        if (n_groups > 0) load_tile(0);
-        for (int c0 = 0; c0 < n_groups; c0 += 64) {
-            const int nc = min(64, n_groups - c0);
+        for (int c0 = 0; c0 < n_groups; c0 += kTileC) {
 #pragma unroll
             for (int j = 0; j < V4; ++j) {
                 const int i = tid + j * kSelThreads;
@@ -126,75 +145,91 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
                 dst[3] = pre[j].w;
             }
             __syncthreads();
-            if (c0 + 64 < n_groups) load_tile(c0 + 64);
-            const int c = tid & 63, h = tid >> 6;  // 512 threads = 64 centroids x 8 heads
-            if (c < nc && h < g) {
-                const float *crow = ct + c * (D + 1);
+            if (c0 + kTileC < n_groups) load_tile(c0 + kTileC, min(kTileC, n_groups - c0 - kTileC));
+            const int nc = min(kTileC, n_groups - c0);
+            const int c = tid & 63, h = tid >> 6;  // 64 centroid slots x 8 heads; 2 centroids each
+            if (h < g && c < nc) {
+                const float *r0p = ct + c * (D + 1);
+                const float *r1p = ct + (c + 64) * (D + 1);
                 const float *qh = qs + h * D;
-                float acc = 0.0f;
+                float acc0 = 0.0f, acc1 = 0.0f;
 #pragma unroll 8
-                for (int d = 0; d < D; ++d) acc = fmaf(crow[d], qh[d], acc);
-                const float gs = __fadd_rn(logn[c0 + c], __fmul_rn(acc, a.p.scale));
-                guess_s[h * Gmax + c0 + c] = gs;
+                for (int d = 0; d < D; ++d) {
+                    const float qd = qh[d];
+                    acc0 = fmaf(r0p[d], qd, acc0);
+                    acc1 = fmaf(r1p[d], qd, acc1);
+                }
+                guess_s[h * Gmax + c0 + c] = __fadd_rn(logn[c0 + c], __fmul_rn(acc0, a.p.scale));
+                if (c + 64 < nc)
+                    guess_s[h * Gmax + c0 + c + 64] =
+                        __fadd_rn(logn[c0 + c + 64], __fmul_rn(acc1, a.p.scale));
             }
             __syncthreads();
         }
     }
+    __syncthreads();
 
-    // ---- ranking (TOPK / HYBRID): one warp per query head extracts clusters
-    // in descending (guess, -index) order by repeated warp arg-max; this is
-    // the prefix of argsort(guess, descending, stable) that the selection uses.
-    if (mode == SANTA_MODE_TOPK || mode == SANTA_MODE_HYBRID) {
-        if (warp < g) {
-            const int h = warp;
-            uint64_t *arr = keys + h * Gp;
-            uint64_t best = 0;  // lane-local maximum key
-            for (int c = lane; c < n_groups; c += 32) {
-                const uint64_t k = ((uint64_t)float_order_key(guess_s[h * Gmax + c]) << 32) |
-                                   (uint64_t)(0xFFFFFFFFu - (uint32_t)c);
-                arr[c] = k;
-                best = k > best ? k : best;
-            }
-            const int kmax = (mode == SANTA_MODE_HYBRID) ? min(a.p.topk_clusters, n_groups)
-                                                         : n_groups;
-            int nsel = 0, exact = 0;
-            while (nsel < kmax) {
-                // 64-bit warp max in two redux.sync steps: the largest high
-                // word, then the largest low word among the lanes holding it
-                const uint32_t bhi = (uint32_t)(best >> 32);
-                const uint32_t mhi = __reduce_max_sync(0xffffffffu, bhi);
-                const uint32_t mlo =
-                    __reduce_max_sync(0xffffffffu, bhi == mhi ? (uint32_t)best : 0u);
-                const uint64_t m = ((uint64_t)mhi << 32) | mlo;
-                if (m == 0) break;  // no cluster left
-                const int c = (int)(0xFFFFFFFFu - (uint32_t)(m & 0xFFFFFFFFu));
-                const int l = len_s[c];
-                if (lane == (c & 31)) {
-                    atomicOr(&mask_s[c], 1 << h);
-                    arr[c] = 0;
-                    best = 0;
-                    for (int cc = lane; cc < n_groups; cc += 32)
-                        best = arr[cc] > best ? arr[cc] : best;
+    // ---- 3. ranking (TOPK / HYBRID): warp per query head, per-lane sorted keys ----
+    if ((mode == SANTA_MODE_TOPK || mode == SANTA_MODE_HYBRID) && warp < g) {
+        const int h = warp;
+        uint64_t key[KPL];
+#pragma unroll
+        for (int j = 0; j < KPL; ++j) {
+            const int c = lane + 32 * j;
+            key[j] = c < n_groups ? (((uint64_t)float_order_key(guess_s[h * Gmax + c]) << 32) |
+                                     (uint64_t)(0xFFFFFFFFu - (uint32_t)c))
+                                  : 0ull;
+        }
+        // bitonic sort, descending, entirely in registers
+#pragma unroll
+        for (int k = 2; k <= KPL; k <<= 1) {
+#pragma unroll
+            for (int j = k >> 1; j > 0; j >>= 1) {
+#pragma unroll
+                for (int i = 0; i < KPL; ++i) {
+                    const int l = i ^ j;
+                    if (l > i) {
+                        const bool desc = (i & k) == 0;
+                        const uint64_t x = key[i], y = key[l];
+                        if (desc ? (x < y) : (x > y)) {
+                            key[i] = y;
+                            key[l] = x;
+                        }
+                    }
                 }
-                exact += l;
-                ++nsel;
-                // budget walk (santapp.py:404-410): stop once the chosen
-                // clusters hold at least token_budget tokens
-                if (mode == SANTA_MODE_TOPK && exact >= a.p.token_budget) break;
-            }
-            if (lane == 0) {
-                head_sel[h] = nsel;
-                head_exact[h] = exact;
             }
         }
-        __syncthreads();
+        const int kmax = (mode == SANTA_MODE_HYBRID) ? min(a.p.topk_clusters, n_groups) : n_groups;
+        int nsel = 0, exact = 0;
+        while (nsel < kmax) {
+            const uint32_t bhi = (uint32_t)(key[0] >> 32);
+            const uint32_t mhi = __reduce_max_sync(0xffffffffu, bhi);
+            const uint32_t mlo = __reduce_max_sync(0xffffffffu, bhi == mhi ? (uint32_t)key[0] : 0u);
+            if (mhi == 0u && mlo == 0u) break;  // no cluster left
+            const int c = (int)(0xFFFFFFFFu - mlo);
+            if (lane == (c & 31)) {
+                atomicOr(&mask_s[c], 1 << h);
+#pragma unroll
+                for (int j = 0; j + 1 < KPL; ++j) key[j] = key[j + 1];
+                key[KPL - 1] = 0ull;
+            }
+            exact += len_s[c];
+            ++nsel;
+            // budget walk (santapp.py:404-410): stop once the chosen clusters
+            // hold at least token_budget tokens
+            if (mode == SANTA_MODE_TOPK && exact >= a.p.token_budget) break;
+        }
+        if (lane == 0) {
+            head_sel[h] = nsel;
+            head_exact[h] = exact;
+        }
     }
+    __syncthreads();
 
-    // ---- union of the group's selections (ascending cluster order) ----
+    // ---- 4. union of the group's selections (ascending cluster order) ----
     int n_union = 0, U = 0;
     {
-        // union entries also kept in shared memory (the centroid tile area is
-        // free after scoring: 64 * (D + 1) floats >= 3 * 1024 ints)
+        // union entries kept in the (now free) centroid tile area
         int *ue_start = (int *)ct;
         int *ue_off = ue_start + Gmax;
         int *ue_mask = ue_off + Gmax;
@@ -242,7 +277,7 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
         else if (mode == SANTA_MODE_UNIFORM || mode == SANTA_MODE_SANTA) ns = S;
         head_ns[tid] = ns;
     }
-    __syncthreads();
+    __syncthreads();  // also: the union expansion is done with the tile area
     if (tid == 0) {
         int acc = 0;
         for (int h = 0; h < g; ++h) {
@@ -262,60 +297,23 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
         if (a.n_exact) a.n_exact[(int64_t)bh * g + tid] = head_exact[tid];
     }
 
-    // ---- guided: per-head softmax over guesses for the proposal ----
-    if (mode == SANTA_MODE_GUIDED && warp < g) {
-        const int h = warp;
-        float mx = -INFINITY;
-        for (int c = lane; c < n_groups; c += 32) mx = fmaxf(mx, guess_s[h * Gmax + c]);
-        mx = warp_max(mx);
-        float z = 0.0f;
-        for (int c = lane; c < n_groups; c += 32) z += expf(guess_s[h * Gmax + c] - mx);
-        z = warp_sum(z);
-        if (lane == 0) {
-            head_f[h * 4 + 0] = mx;
-            head_f[h * 4 + 1] = logf(z);
-        }
-        // inclusive cdf of the unnormalised probabilities (keys[] reused as floats)
-        float *cdf = (float *)keys + h * Gmax;
-        float carry = 0.0f;
-        for (int c0 = 0; c0 < n_groups; c0 += 32) {
-            const int c = c0 + lane;
-            float v = c < n_groups ? expf(guess_s[h * Gmax + c] - mx) : 0.0f;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                float y = __shfl_up_sync(0xffffffffu, v, o);
-                if (lane >= o) v += y;
-            }
-            if (c < n_groups) cdf[c] = carry + v;
-            carry += __shfl_sync(0xffffffffu, v, 31);
-        }
-    }
-    __syncthreads();
-
-    // ---- samples ----
+    // ---- 5a. per-head tables for the draws (one warp per head) ----
+    float *cdf_all = ct;  // guided CDF [8][Gmax], in the free tile area
     if (warp < g && head_ns[warp] > 0) {
         const int h = warp;
-        const int ns = head_ns[h];
-        const int sbase = head_sbase[h];
-        const int gh = kv * g + h;  // global query head
-        int32_t *spos = a.ws.s_pos + (int64_t)bh * g * S + sbase;
-        float *soff = a.ws.s_off + (int64_t)bh * g * S + sbase;
-        const int64_t inj = ((int64_t)b * a.geo.num_kv_heads * g + gh) * S;
-        const uint2 key = make_uint2((uint32_t)a.p.seed, (uint32_t)(a.p.seed >> 32));
-        const float logS = logf((float)ns);
         if (mode == SANTA_MODE_HYBRID) {
-            // Selected clusters of this head in ascending cluster (= start)
-            // order, as gap[j] = non-selected positions before cluster j and
-            // cum[j] = selected positions before cluster j.  Rank r maps to
-            // position r + cum[J] with J = #{j : gap[j] <= r}.
-            int *gap = selasc + h * (2 * Gmax + 1);
-            int *cum = gap + Gmax;
+            // selected clusters of this head in ascending start order, as
+            // gap[j] = non-selected positions before cluster j and cum[j] =
+            // selected positions before it: rank r maps to r + cum[J] with
+            // J = #{j : gap[j] <= r}
+            int *gap = gapcum + h * (2 * kcap + 1);
+            int *cum = gap + kcap;
             int cnt = 0, carry = 0;
             for (int c0 = 0; c0 < n_groups; c0 += 32) {
                 const int c = c0 + lane;
                 const bool on = c < n_groups && ((mask_s[c] >> h) & 1);
                 const unsigned bal = __ballot_sync(0xffffffffu, on);
-                int l = on ? len_s[c] : 0;
+                const int l = on ? len_s[c] : 0;
                 int x = l;
 #pragma unroll
                 for (int o = 1; o < 32; o <<= 1) {
@@ -331,11 +329,56 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
                 cnt += __popc(bal);
                 carry += __shfl_sync(0xffffffffu, x, 31);
             }
-            if (lane == 0) cum[cnt] = carry;
-            __syncwarp();
+            if (lane == 0) {
+                cum[cnt] = carry;
+                head_cnt[h] = cnt;
+            }
+        } else if (mode == SANTA_MODE_GUIDED) {
+            float mx = -INFINITY;
+            for (int c = lane; c < n_groups; c += 32) mx = fmaxf(mx, guess_s[h * Gmax + c]);
+            mx = warp_max(mx);
+            float z = 0.0f;
+            for (int c = lane; c < n_groups; c += 32) z += expf(guess_s[h * Gmax + c] - mx);
+            z = warp_sum(z);
+            if (lane == 0) {
+                head_f[h * 4 + 0] = mx;
+                head_f[h * 4 + 1] = logf(z);
+            }
+            float *cdf = cdf_all + h * Gmax;
+            float carry = 0.0f;
+            for (int c0 = 0; c0 < n_groups; c0 += 32) {
+                const int c = c0 + lane;
+                float v = c < n_groups ? expf(guess_s[h * Gmax + c] - mx) : 0.0f;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const float y = __shfl_up_sync(0xffffffffu, v, o);
+                    if (lane >= o) v += y;
+                }
+                if (c < n_groups) cdf[c] = carry + v;
+                carry += __shfl_sync(0xffffffffu, v, 31);
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- 5b. draws: two warps per query head, 32-draw chunks alternating ----
+    const int h = warp & 7, half = warp >> 3;
+    if (h < g && head_ns[h] > 0) {
+        const int ns = head_ns[h];
+        const int sbase = head_sbase[h];
+        const int gh = kv * g + h;  // global query head
+        int32_t *spos = a.ws.s_pos + (int64_t)bh * g * S + sbase;
+        float *soff = a.ws.s_off + (int64_t)bh * g * S + sbase;
+        const int64_t inj = ((int64_t)b * a.geo.num_kv_heads * g + gh) * S;
+        const uint2 key = make_uint2((uint32_t)a.p.seed, (uint32_t)(a.p.seed >> 32));
+        const float logS = logf((float)ns);
+        if (mode == SANTA_MODE_HYBRID) {
+            const int *gap = gapcum + h * (2 * kcap + 1);
+            const int *cum = gap + kcap;
+            const int cnt = head_cnt[h];
             const int n_rest = sample_end - head_exact[h];
             const float off = (logf((float)n_rest) - logS) * kLog2e;
-            for (int i = lane; i < ns; i += 32) {
+            for (int i = half * 32 + lane; i < ns; i += 64) {
                 uint32_t r;
                 if (a.p.sample_source == SANTA_SAMPLES_INJECTED) {
                     int v = a.sample_a[inj + i];
@@ -362,10 +405,10 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
             }
         } else if (mode == SANTA_MODE_GUIDED) {
             const float mx = head_f[h * 4 + 0], logz = head_f[h * 4 + 1];
-            const float *cdf = (const float *)keys + h * Gmax;
+            const float *cdf = cdf_all + h * Gmax;
             const float total = cdf[n_groups - 1];
             const float *logn = a.sum.log_n + (int64_t)bh * Gmax;
-            for (int i = lane; i < ns; i += 32) {
+            for (int i = half * 32 + lane; i < ns; i += 64) {
                 int grp, within;
                 if (a.p.sample_source == SANTA_SAMPLES_INJECTED) {
                     grp = a.sample_a[inj + i];
@@ -404,7 +447,7 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
             const int32_t *posmap = a.sum.positions + (int64_t)bh * sample_end;
             const float off_u = (logf((float)sample_end) - logS) * kLog2e;
             const float lse_o = (mode == SANTA_MODE_SANTA) ? a.ws.lse_old[(int64_t)bh * 8 + h] : 0.f;
-            for (int i = lane; i < ns; i += 32) {
+            for (int i = half * 32 + lane; i < ns; i += 64) {
                 int t;
                 if (a.p.sample_source == SANTA_SAMPLES_INJECTED) {
                     t = a.sample_a[inj + i];
@@ -537,24 +580,38 @@ __global__ void decode_expand_kernel(DecodeArgs a, uint8_t *selected, int32_t *s
 // ---------------------------------------------------------------------------
 // host launchers
 // ---------------------------------------------------------------------------
-static size_t select_smem_bytes(int D, int Gmax) {
-    int Gp = 1;
-    while (Gp < Gmax) Gp <<= 1;
+static size_t select_smem_bytes(int D, int Gmax, int kcap) {
     size_t b = 0;
-    b += SANTA_MAX_GROUP * D * 4;
-    b += 64 * (D + 1) * 4;
-    b += 3 * (size_t)Gmax * 4;
-    b += SANTA_MAX_GROUP * (size_t)Gmax * 4;  // guess
-    b += SANTA_MAX_GROUP * (2 * (size_t)Gmax + 1) * 4;  // gap / cum per head
-    b += 40 * 4 + 32 * 4 + 32 * 4 + 32;
-    b += SANTA_MAX_GROUP * (size_t)Gp * 8;    // keys
+    b += SANTA_MAX_GROUP * D * 4;                                 // q
+    b += (size_t)kTileC * (D + 1) * 4;                            // centroid tile
+    b += 3 * (size_t)Gmax * 4;                                    // starts, lengths, masks
+    b += SANTA_MAX_GROUP * (size_t)Gmax * 4;                      // guesses
+    b += SANTA_MAX_GROUP * (2 * (size_t)kcap + 1) * 4;            // gap / cum
+    b += 40 * 4 + 5 * 8 * 4 + 32 * 4;                             // scan + per-head
     return b;
+}
+
+template <int D, int KPL>
+static int launch_select(DecodeArgs &a, cudaStream_t stream) {
+    const int BH = a.geo.batch * a.geo.num_kv_heads;
+    const int kcap = (a.p.mode == SANTA_MODE_HYBRID) ? (a.p.topk_clusters > 0 ? a.p.topk_clusters : 1) : 1;
+    static size_t done = 0;
+    const size_t smem = select_smem_bytes(D, a.sum.max_groups, kcap);
+    if (smem > 227 * 1024) return SANTA_ERR_UNSUPPORTED;
+    if (done < smem) {
+        SANTA_CUDA_CHECK(cudaFuncSetAttribute(decode_select_kernel<D, KPL>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)smem));
+        done = smem;
+    }
+    decode_select_kernel<D, KPL><<<BH, kSelThreads, smem, stream>>>(a);
+    SANTA_LAUNCH_CHECK();
+    return SANTA_OK;
 }
 
 template <int D>
 static int launch_plan_d(DecodeArgs &a, cudaStream_t stream) {
     const int BH = a.geo.batch * a.geo.num_kv_heads;
-    const int Gmax = a.sum.max_groups;
     SANTA_CUDA_CHECK(cudaMemsetAsync(a.ws.flag, 0, 16, stream));
     if (a.p.mode == SANTA_MODE_SANTA) {
         if (a.geo.kv_dtype == SANTA_DTYPE_BF16)
@@ -563,17 +620,7 @@ static int launch_plan_d(DecodeArgs &a, cudaStream_t stream) {
             decode_old_lse_kernel<D, float><<<BH, 256, 0, stream>>>(a);
         SANTA_LAUNCH_CHECK();
     }
-    static size_t done = 0;
-    const size_t smem = select_smem_bytes(D, Gmax);
-    if (done < smem) {
-        SANTA_CUDA_CHECK(cudaFuncSetAttribute(decode_select_kernel<D>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              (int)smem));
-        done = smem;
-    }
-    decode_select_kernel<D><<<BH, kSelThreads, smem, stream>>>(a);
-    SANTA_LAUNCH_CHECK();
-    return SANTA_OK;
+    return a.sum.max_groups <= 256 ? launch_select<D, 8>(a, stream) : launch_select<D, 32>(a, stream);
 }
 
 int launch_plan(DecodeArgs &a, cudaStream_t stream) {

@@ -368,3 +368,46 @@ def test_full_size_hybrid_selection_bit_exact_and_output_close():
                     assert np.abs(out[b, h] - r.out).max() < 2e-2
                     checked += 1
     assert checked >= 8
+
+
+@pytest.mark.parametrize("mode", ["hybrid", "topk"])
+def test_many_clusters_selection_bit_exact(mode):
+    """More than 256 clusters per KV head takes the 32-keys-per-lane top-k path."""
+    sh = scaled_shape(QWEN7B_32K, name="qwen2.5-7b-attn-ctx8192-g600", batch=1, context=8192,
+                      true_clusters=600, n_clusters=600, topk_clusters=40, samples=96, steps=1)
+    w = make_decode_workload(sh, seed=3)
+    kc, vc = w.keys.cuda(), w.values.cuda()
+    labels = w.labels[:, :, :sh.sample_end]
+    summ = S.build_summary(kc, vc, labels.cuda(), sh.n_clusters, sample_end=sh.sample_end,
+                           n_total=sh.context)
+    q = w.queries[0].cuda()
+    budget = 40 * (sh.sample_end // sh.n_clusters)
+    kw = dict(mode=mode, n_total=sh.context, seed=4, step=1)
+    if mode == "hybrid":
+        kw.update(topk_clusters=sh.topk_clusters, samples=sh.samples)
+    else:
+        kw.update(token_budget=budget)
+    sel, rows, n_exact = S.santa_decode_select(q, kc, vc, summ, **kw)
+    res = S.santa_decode(q, kc, vc, summ, **kw)
+    sel, rows, out = sel.cpu().numpy(), rows.cpu().numpy(), res.out.cpu().numpy()
+    for kv in range(sh.num_kv_heads):
+        K = w.keys[0, kv].float().numpy()
+        V = w.values[0, kv].float().numpy()
+        o = O.build_summary(K[:sh.sample_end], labels[0, kv].numpy(), sh.n_clusters)
+        for hh in range(sh.group):
+            h = kv * sh.group + hh
+            qh = w.queries[0, 0, h].numpy()
+            if mode == "hybrid":
+                chosen = O.select_topk(O.centroid_guess(o, qh, sh.scale), sh.topk_clusters)
+                n_rest = sh.sample_end - int(o.lengths[chosen].sum())
+                ranks = O.philox_ranks(4, 1, 0, h, sh.samples, n_rest)
+                assert np.array_equal(rows[0, h], O.hybrid_positions(o, chosen, ranks))
+                r = O.decode_hybrid(qh, K, V, o, sh.sample_end, sh.topk_clusters, ranks, sh.scale)
+            else:
+                r = O.decode_topk(qh, K, V, o, sh.sample_end, budget, sh.scale)
+                chosen = r.selected
+            want = np.zeros(sh.n_clusters, np.uint8)
+            want[chosen] = 1
+            assert np.array_equal(sel[0, h], want), (kv, hh)
+            assert int(n_exact[0, h]) == int(o.lengths[chosen].sum())
+            assert np.abs(out[0, h] - r.out).max() < 2e-2
