@@ -352,20 +352,27 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
             return en;
         };
 
-        // prologue: tiles 0 .. kGStages-2 in flight, entry of the next one loaded
-        RowEntry en_next = entry_of(0);
+        // Row entries are loaded three tiles before their copies are issued
+        // (a register ring e0..e2), copies two tiles before their compute, so
+        // neither the entry loads nor the row copies stall the warp.
+        // prologue: entries of tiles 0..4 requested, copies of tiles 0..1 issued
+        RowEntry e0 = entry_of(0), e1 = entry_of(1), e2 = entry_of(2);
 #pragma unroll
         for (int i = 0; i < kGStages - 1; ++i) {
-            const RowEntry en = en_next;
-            en_next = entry_of(i + 1);
+            const RowEntry en = e0;
+            e0 = e1;
+            e1 = e2;
+            e2 = entry_of(i + 3);
             if (i < n_my) issue(i, i % kGStages, en);
             asm volatile("cp.async.commit_group;\n" ::: "memory");
         }
         for (int i = 0; i < n_my; ++i) {
             const int ni = i + kGStages - 1;
             if (ni < n_my) {
-                const RowEntry en = en_next;
-                en_next = entry_of(ni + 1);
+                const RowEntry en = e0;
+                e0 = e1;
+                e1 = e2;
+                e2 = entry_of(ni + 3);
                 issue(ni, ni % kGStages, en);
             }
             asm volatile("cp.async.commit_group;\n" ::: "memory");

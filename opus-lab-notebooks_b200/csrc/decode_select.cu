@@ -59,14 +59,22 @@ __device__ int sel_block_exclusive_scan(int v, int *sw, int *total) {
     return r;
 }
 
-template <int D>
+// KPL == 8 (at most 256 clusters): the whole centroid block is loaded at
+// once; otherwise 128-centroid tiles.
+template <int D, int KPL>
 struct SelSmem {
-    static constexpr int CT_FLOATS = kTileC * (D + 1);
-    static_assert(CT_FLOATS >= SANTA_MAX_GROUP * SANTA_MAX_CLUSTERS,
-                  "the centroid tile area also holds the guided CDF");
-    static_assert(CT_FLOATS >= 3 * SANTA_MAX_CLUSTERS,
-                  "the centroid tile area also holds the union entries");
+    static constexpr int ROWS = KPL == 8 ? 256 : kTileC;
+    static constexpr int CT_FLOATS = ROWS * (D + 1);
+    static constexpr int MAXG = KPL * 32;
+    static_assert(CT_FLOATS >= SANTA_MAX_GROUP * MAXG,
+                  "the centroid area also holds the guided CDF");
+    static_assert(CT_FLOATS >= 3 * MAXG, "the centroid area also holds the union entries");
 };
+
+__device__ __forceinline__ void cp_async4(void *dst_smem, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32(dst_smem)), "l"(src)
+                 : "memory");
+}
 
 // KPL: keys per lane in the top-k extraction (clusters lane, lane+32, ...).
 template <int D, int KPL>
@@ -86,8 +94,8 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
 
     // shared memory carve-up
     float *qs = (float *)smem_raw;                              // [8][D]
-    float *ct = qs + SANTA_MAX_GROUP * D;                       // [kTileC][D+1]
-    int *starts_s = (int *)(ct + SelSmem<D>::CT_FLOATS);        // [Gmax]
+    float *ct = qs + SANTA_MAX_GROUP * D;                       // [ROWS][D+1]
+    int *starts_s = (int *)(ct + SelSmem<D, KPL>::CT_FLOATS);   // [Gmax]
     int *len_s = starts_s + Gmax;                               // [Gmax]
     int *mask_s = len_s + Gmax;                                 // [Gmax]
     float *guess_s = (float *)(mask_s + Gmax);                  // [8][Gmax]
@@ -100,11 +108,10 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
     int *head_cnt = head_sbase + 8;                             // [8]
     float *head_f = (float *)(head_cnt + 8);                    // [8][4]
 
-    // ---- 1. loads: q, cluster metadata and the first centroid tile together ----
+    // ---- 1. loads: q, cluster metadata and centroids requested together ----
     const float *cent = a.sum.centroids + (int64_t)bh * Gmax * D;
     constexpr int V4 = kTileC * D / 4 / kSelThreads;  // float4 per thread per tile
-    float4 pre[V4];
-    const int rows0 = min(kTileC, Gmax);  // in-bounds rows of the first tile
+    float4 pre[KPL == 8 ? 1 : V4];
     auto load_tile = [&](int c0, int nrow) {
 #pragma unroll
         for (int j = 0; j < V4; ++j) {
@@ -114,15 +121,33 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
                               : make_float4(0.f, 0.f, 0.f, 0.f);
         }
     };
-    if (uses_clusters) load_tile(0, rows0);
+    if (uses_clusters) {
+        if constexpr (KPL == 8) {
+            // the whole block (<= 256 rows) straight into shared memory, pitch
+            // D + 1 so that the scoring reads are bank-conflict free
+            for (int i = tid; i < Gmax * D; i += kSelThreads) {
+                const int r = i / D;
+                cp_async4(ct + r * (D + 1) + (i - r * D), cent + i);
+            }
+            for (int i = tid; i < Gmax; i += kSelThreads) {
+                cp_async4(starts_s + i, a.sum.starts + (int64_t)bh * Gmax + i);
+                cp_async4(len_s + i, a.sum.lengths + (int64_t)bh * Gmax + i);
+            }
+            asm volatile("cp.async.commit_group;\n" ::: "memory");
+        } else {
+            load_tile(0, min(kTileC, Gmax));
+        }
+    }
     const int n_groups = uses_clusters ? a.sum.n_groups[bh] : 0;
     const float *qb = a.q + ((int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g) * D;
     for (int i = tid; i < g * D; i += kSelThreads) qs[i] = qb[i];
-    for (int i = tid; i < n_groups; i += kSelThreads) {
-        starts_s[i] = a.sum.starts[(int64_t)bh * Gmax + i];
-        len_s[i] = a.sum.lengths[(int64_t)bh * Gmax + i];
-        mask_s[i] = 0;
+    if constexpr (KPL != 8) {
+        for (int i = tid; i < n_groups; i += kSelThreads) {
+            starts_s[i] = a.sum.starts[(int64_t)bh * Gmax + i];
+            len_s[i] = a.sum.lengths[(int64_t)bh * Gmax + i];
+        }
     }
+    for (int i = tid; i < Gmax; i += kSelThreads) mask_s[i] = 0;
     if (tid < 8) {
         head_sel[tid] = 0;
         head_exact[tid] = 0;
@@ -131,7 +156,32 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
     }
 
     // ---- 2. centroid guesses: fl32(log_n + fl32(dot * scale)), dot = fmaf chain ----
-    if (uses_clusters) {
+    if constexpr (KPL == 8) {
+      if (uses_clusters) {
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+        __syncthreads();
+        const float *logn = a.sum.log_n + (int64_t)bh * Gmax;
+        const int c = tid & 63, h = tid >> 6;  // 64 slots x 8 heads, 4 centroids a thread
+        if (h < g) {
+            const float *qh = qs + h * D;
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+            for (int d = 0; d < D; ++d) {
+                const float qd = qh[d];
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    acc[k] = fmaf(ct[(c + 64 * k) * (D + 1) + d], qd, acc[k]);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int cc = c + 64 * k;
+                if (cc < n_groups)
+                    guess_s[h * Gmax + cc] = __fadd_rn(logn[cc], __fmul_rn(acc[k], a.p.scale));
+            }
+        }
+      }
+    } else {
+      if (uses_clusters) {
         const float *logn = a.sum.log_n + (int64_t)bh * Gmax;
         for (int c0 = 0; c0 < n_groups; c0 += kTileC) {
 #pragma unroll
@@ -166,6 +216,7 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
             }
             __syncthreads();
         }
+      }
     }
     __syncthreads();
 
@@ -208,16 +259,32 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
             if (mhi == 0u && mlo == 0u) break;  // no cluster left
             const int c = (int)(0xFFFFFFFFu - mlo);
             if (lane == (c & 31)) {
-                atomicOr(&mask_s[c], 1 << h);
 #pragma unroll
                 for (int j = 0; j + 1 < KPL; ++j) key[j] = key[j + 1];
                 key[KPL - 1] = 0ull;
             }
-            exact += len_s[c];
+            if (mode == SANTA_MODE_HYBRID) {
+                // chosen list in the (still unused) gap table; mask bits and
+                // lengths are applied after the loop, off its critical path
+                if (lane == 0) gapcum[h * (2 * kcap + 1) + nsel] = c;
+            } else {
+                if (lane == (c & 31)) atomicOr(&mask_s[c], 1 << h);
+                exact += len_s[c];
+            }
             ++nsel;
             // budget walk (santapp.py:404-410): stop once the chosen clusters
             // hold at least token_budget tokens
             if (mode == SANTA_MODE_TOPK && exact >= a.p.token_budget) break;
+        }
+        if (mode == SANTA_MODE_HYBRID) {
+            __syncwarp();
+            int ex = 0;
+            for (int j = lane; j < nsel; j += 32) {
+                const int c = gapcum[h * (2 * kcap + 1) + j];
+                atomicOr(&mask_s[c], 1 << h);
+                ex += len_s[c];
+            }
+            exact = warp_sum_int(ex);
         }
         if (lane == 0) {
             head_sel[h] = nsel;
@@ -580,10 +647,11 @@ __global__ void decode_expand_kernel(DecodeArgs a, uint8_t *selected, int32_t *s
 // ---------------------------------------------------------------------------
 // host launchers
 // ---------------------------------------------------------------------------
-static size_t select_smem_bytes(int D, int Gmax, int kcap) {
+template <int D, int KPL>
+static size_t select_smem_bytes(int Gmax, int kcap) {
     size_t b = 0;
     b += SANTA_MAX_GROUP * D * 4;                                 // q
-    b += (size_t)kTileC * (D + 1) * 4;                            // centroid tile
+    b += (size_t)SelSmem<D, KPL>::CT_FLOATS * 4;                  // centroid area
     b += 3 * (size_t)Gmax * 4;                                    // starts, lengths, masks
     b += SANTA_MAX_GROUP * (size_t)Gmax * 4;                      // guesses
     b += SANTA_MAX_GROUP * (2 * (size_t)kcap + 1) * 4;            // gap / cum
@@ -596,7 +664,7 @@ static int launch_select(DecodeArgs &a, cudaStream_t stream) {
     const int BH = a.geo.batch * a.geo.num_kv_heads;
     const int kcap = (a.p.mode == SANTA_MODE_HYBRID) ? (a.p.topk_clusters > 0 ? a.p.topk_clusters : 1) : 1;
     static size_t done = 0;
-    const size_t smem = select_smem_bytes(D, a.sum.max_groups, kcap);
+    const size_t smem = select_smem_bytes<D, KPL>(a.sum.max_groups, kcap);
     if (smem > 227 * 1024) return SANTA_ERR_UNSUPPORTED;
     if (done < smem) {
         SANTA_CUDA_CHECK(cudaFuncSetAttribute(decode_select_kernel<D, KPL>,
