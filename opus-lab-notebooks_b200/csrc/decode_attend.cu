@@ -301,22 +301,18 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
             unsigned char *stg = wbase + st * (GG::STAGE + GG::META);
             int *mk = (int *)(stg + GG::STAGE);
             float *of = (float *)(mk + kGRows);
-            const char *kp = sk, *vp = sv;
-            int mask = 0;
+            // row code: >= 0 row of the cluster-sorted copy, -1 - x row x of
+            // the recent window in the cache, INT_MIN no row
+            int code = INT_MIN, mask = 0;
             if (en.kind == 1) {
-                const int row = en.e & (int)kPosMask;
-                kp = sk + (int64_t)row * GG::ROWB;
-                vp = sv + (int64_t)row * GG::ROWB;
+                code = en.e & (int)kPosMask;
                 mask = (int)((uint32_t)en.e >> 24);
             } else if (en.kind == 2) {
-                kp = ck + (int64_t)en.e * GG::ROWB;
-                vp = cv + (int64_t)en.e * GG::ROWB;
+                code = -1 - en.e;
                 mask = (1 << g) - 1;
             } else if (en.kind == 3) {
                 const uint32_t pk = (uint32_t)en.e;
-                const int row = (int)(pk & kPosMask);
-                kp = sk + (int64_t)row * GG::ROWB;
-                vp = sv + (int64_t)row * GG::ROWB;
+                code = (int)(pk & kPosMask);
                 mask = (1 << ((pk >> kHeadShift) & 7u)) | kMaskSample |
                        ((pk & kAbsBit) ? kMaskAbs : 0);
             }
@@ -324,21 +320,24 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
                 mk[lane] = mask;
                 of[lane] = en.off;
             }
-            const int valid = en.kind != 0;
+            const int c = lane % GG::CPR;
+            const uint32_t kd0 = smem_u32(stg + (lane / GG::CPR) * GG::PITCH + c * 16);
 #pragma unroll
             for (int it = 0; it < kGRows / GG::RPI; ++it) {
                 const int r = it * GG::RPI + lane / GG::CPR;
-                const int c = lane % GG::CPR;
-                const char *ks = (const char *)__shfl_sync(0xffffffffu, (unsigned long long)kp, r);
-                const char *vs = (const char *)__shfl_sync(0xffffffffu, (unsigned long long)vp, r);
-                const int ok = __shfl_sync(0xffffffffu, valid, r) ? 16 : 0;
-                const uint32_t kd = smem_u32(stg + r * GG::PITCH + c * 16);
-                const uint32_t vd = smem_u32(stg + GG::TILE + r * GG::PITCH + c * 16);
+                const int rc = __shfl_sync(0xffffffffu, code, r);
+                const char *ks = rc >= 0 ? sk + (int64_t)rc * GG::ROWB
+                                         : ck + (int64_t)(rc == INT_MIN ? 0 : -1 - rc) * GG::ROWB;
+                // byte distance from the K row to the V row of the same source
+                const int64_t dv = rc >= 0 ? (int64_t)((uintptr_t)sv - (uintptr_t)sk)
+                                           : (int64_t)((uintptr_t)cv - (uintptr_t)ck);
+                const int ok = rc == INT_MIN ? 0 : 16;
+                const uint32_t kd = kd0 + it * GG::RPI * GG::PITCH;
                 asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(kd),
                              "l"(ks + c * 16), "r"(ok)
                              : "memory");
-                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(vd),
-                             "l"(vs + c * 16), "r"(ok)
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(kd + GG::TILE),
+                             "l"(ks + dv + c * 16), "r"(ok)
                              : "memory");
             }
             (void)i;
@@ -393,13 +392,14 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
                 const int r = ((mat >> 1) << 3) + mrow;
                 const int c = 2 * kk + (mat & 1);
                 ldmatrix_x4(smem_u32(ks_ + r * GG::PITCH + c * 16), b0, b1, b2, b3);
-                mma_bf16(s0v, qh[kk][0], 0u, qh[kk][1], 0u, b0, b1);
-                mma_bf16(s0v, ql[kk][0], 0u, ql[kk][1], 0u, b0, b1);
-                mma_bf16(s1v, qh[kk][0], 0u, qh[kk][1], 0u, b2, b3);
-                mma_bf16(s1v, ql[kk][0], 0u, ql[kk][1], 0u, b2, b3);
+                // A rows 0-7 = q hi parts, rows 8-15 = q lo parts (GQA heads
+                // fill at most 8 rows): one mma yields both halves
+                mma_bf16(s0v, qh[kk][0], ql[kk][0], qh[kk][1], ql[kk][1], b0, b1);
+                mma_bf16(s1v, qh[kk][0], ql[kk][0], qh[kk][1], ql[kk][1], b2, b3);
             }
             const int rr[4] = {2 * tig, 2 * tig + 1, 8 + 2 * tig, 9 + 2 * tig};
-            const float raw[4] = {s0v[0], s0v[1], s1v[0], s1v[1]};
+            const float raw[4] = {s0v[0] + s0v[2], s0v[1] + s0v[3], s1v[0] + s1v[2],
+                                  s1v[1] + s1v[3]};
             float sv4[4];
             bool any_sample = false;
 #pragma unroll
@@ -428,6 +428,8 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
             for (int q = 0; q < NT_O; ++q) {
                 o[q][0] *= alpha;
                 o[q][1] *= alpha;
+                o[q][2] *= alpha;
+                o[q][3] *= alpha;
             }
             if (__any_sync(0xffffffffu, any_sample)) {
 #pragma unroll
@@ -460,10 +462,10 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
                 const int r = ((mat & 1) << 3) + mrow;
                 const int c = 2 * j + (mat >> 1);
                 ldmatrix_x4_trans(smem_u32(vs_ + r * GG::PITCH + c * 16), b0, b1, b2, b3);
-                mma_bf16(o[2 * j], ph0, 0u, ph2, 0u, b0, b1);
-                mma_bf16(o[2 * j], pl0, 0u, pl2, 0u, b0, b1);
-                mma_bf16(o[2 * j + 1], ph0, 0u, ph2, 0u, b2, b3);
-                mma_bf16(o[2 * j + 1], pl0, 0u, pl2, 0u, b2, b3);
+                // A rows 0-7 = p hi, rows 8-15 = p lo: accumulator rows gid
+                // and gid + 8 hold the two halves of head gid's output
+                mma_bf16(o[2 * j], ph0, pl0, ph2, pl2, b0, b1);
+                mma_bf16(o[2 * j + 1], ph0, pl0, ph2, pl2, b2, b3);
             }
             __syncwarp();  // stage st is refilled by the next iteration's issue
         }
@@ -499,8 +501,8 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
             }
 #pragma unroll
             for (int q = 0; q < NT_O; ++q) {
-                part[gid * PSTR + 8 + q * 8 + 2 * tig] = o[q][0];
-                part[gid * PSTR + 8 + q * 8 + 2 * tig + 1] = o[q][1];
+                part[gid * PSTR + 8 + q * 8 + 2 * tig] = o[q][0] + o[q][2];
+                part[gid * PSTR + 8 + q * 8 + 2 * tig + 1] = o[q][1] + o[q][3];
             }
         }
     }
