@@ -164,6 +164,7 @@ constexpr int kGW = 8;        // warps per CTA
 constexpr int kGRows = 16;    // rows per warp tile (the mma N/K granule)
 constexpr int kGStages = 3;   // cp.async ring depth per warp
 constexpr int kGThreads = 32 * kGW;
+constexpr int kMergeChunk = 64;  // partials staged per round in the merge kernel
 
 template <int D>
 struct GatherGeom {
@@ -320,24 +321,27 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
                 mk[lane] = mask;
                 of[lane] = en.off;
             }
-            const int c = lane % GG::CPR;
-            const uint32_t kd0 = smem_u32(stg + (lane / GG::CPR) * GG::PITCH + c * 16);
+            // a lane pair per row: lane l copies chunks (l & 1) + 2k of row
+            // l >> 1, so every instruction reads whole 32-byte sectors and a
+            // lane computes its row address once
+            const int r = lane >> 1;
+            const int rc = __shfl_sync(0xffffffffu, code, r);
+            const char *ks = rc >= 0 ? sk + (int64_t)rc * GG::ROWB
+                                     : ck + (int64_t)(rc == INT_MIN ? 0 : -1 - rc) * GG::ROWB;
+            // byte distance from the K row to the V row of the same source
+            const int64_t dv = rc >= 0 ? (int64_t)((uintptr_t)sv - (uintptr_t)sk)
+                                       : (int64_t)((uintptr_t)cv - (uintptr_t)ck);
+            const int ok = rc == INT_MIN ? 0 : 16;
+            const char *src = ks + (lane & 1) * 16;
+            const uint32_t kd = smem_u32(stg + r * GG::PITCH + (lane & 1) * 16);
 #pragma unroll
-            for (int it = 0; it < kGRows / GG::RPI; ++it) {
-                const int r = it * GG::RPI + lane / GG::CPR;
-                const int rc = __shfl_sync(0xffffffffu, code, r);
-                const char *ks = rc >= 0 ? sk + (int64_t)rc * GG::ROWB
-                                         : ck + (int64_t)(rc == INT_MIN ? 0 : -1 - rc) * GG::ROWB;
-                // byte distance from the K row to the V row of the same source
-                const int64_t dv = rc >= 0 ? (int64_t)((uintptr_t)sv - (uintptr_t)sk)
-                                           : (int64_t)((uintptr_t)cv - (uintptr_t)ck);
-                const int ok = rc == INT_MIN ? 0 : 16;
-                const uint32_t kd = kd0 + it * GG::RPI * GG::PITCH;
-                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(kd),
-                             "l"(ks + c * 16), "r"(ok)
+            for (int k = 0; k < GG::CPR / 2; ++k) {
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(kd + k * 32),
+                             "l"(src + k * 32), "r"(ok)
                              : "memory");
-                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(kd + GG::TILE),
-                             "l"(ks + dv + c * 16), "r"(ok)
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(
+                                 kd + GG::TILE + k * 32),
+                             "l"(src + dv + k * 32), "r"(ok)
                              : "memory");
             }
             (void)i;
@@ -424,12 +428,16 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
                 m_run = m_new;
             }
             l_run = l_run * alpha + (pr[0] + pr[1] + pr[2] + pr[3]);
+            // once the running maxima settle most tiles leave them unchanged:
+            // skip the accumulator rescale then (warp-uniform branch)
+            if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-            for (int q = 0; q < NT_O; ++q) {
-                o[q][0] *= alpha;
-                o[q][1] *= alpha;
-                o[q][2] *= alpha;
-                o[q][3] *= alpha;
+                for (int q = 0; q < NT_O; ++q) {
+                    o[q][0] *= alpha;
+                    o[q][1] *= alpha;
+                    o[q][2] *= alpha;
+                    o[q][3] *= alpha;
+                }
             }
             if (__any_sync(0xffffffffu, any_sample)) {
 #pragma unroll
@@ -553,67 +561,52 @@ __global__ void __launch_bounds__(D) decode_merge_kernel(DecodeArgs a, int n_cta
     const int count = (last - first + 1) * kGW;
     const float *pall = a.ws.partial + ((int64_t)first + bh) * kGW * g * PSTR + h * PSTR;
     const int64_t step = (int64_t)g * PSTR;
-    extern __shared__ float fac[];  // [count] weight of each partial
-    __shared__ float red[5][D / 32];
-    constexpr int NWM = D / 32;
-    const int wid = d >> 5;
-    // pass 1: maxima of the partials' log-scales (independent loads, no branch chain)
-    float M = -INFINITY, MS = -INFINITY;
-    for (int s = d; s < count; s += D) {
-        const float *ps = pall + s * step;
-        const float m = ps[0], l = ps[1], ms = ps[2], e1 = ps[3];
-        M = fmaxf(M, l > 0.f ? m : -INFINITY);
-        MS = fmaxf(MS, e1 > 0.f ? ms : -INFINITY);
-    }
-    M = warp_max(M);
-    MS = warp_max(MS);
-    if (lane == 0) {
-        red[0][wid] = M;
-        red[1][wid] = MS;
-    }
-    __syncthreads();
-    M = red[0][0];
-    MS = red[1][0];
-#pragma unroll
-    for (int w = 1; w < NWM; ++w) {
-        M = fmaxf(M, red[0][w]);
-        MS = fmaxf(MS, red[1][w]);
-    }
-    // pass 2: per-partial factors into shared memory, denominators
-    float L = 0.f, E1 = 0.f, E2 = 0.f;
-    for (int s = d; s < count; s += D) {
-        const float *ps = pall + s * step;
-        const float m = ps[0], l = ps[1], ms = ps[2], e1 = ps[3], e2 = ps[4];
-        const float f = l > 0.f ? exp2f(m - M) : 0.f;
-        fac[s] = f;
-        L += l * f;
-        const float fe = e1 > 0.f ? exp2f(ms - MS) : 0.f;
-        E1 += e1 * fe;
-        E2 += e2 * fe * fe;
-    }
-    L = warp_sum(L);
-    E1 = warp_sum(E1);
-    E2 = warp_sum(E2);
-    __syncthreads();  // red[0..1] reads above are done before reuse
-    if (lane == 0) {
-        red[2][wid] = L;
-        red[3][wid] = E1;
-        red[4][wid] = E2;
-    }
-    __syncthreads();
-    L = 0.f;
-    E1 = 0.f;
-    E2 = 0.f;
-#pragma unroll
-    for (int w = 0; w < NWM; ++w) {
-        L += red[2][w];
-        E1 += red[3][w];
-        E2 += red[4][w];
-    }
-    // pass 3: branch-free weighted sum of the partial outputs
-    float acc = 0.f;
+    // Partials are staged kMergeChunk at a time into shared memory with one
+    // batch of 16-byte cp.async (one memory round trip per chunk); every
+    // thread then reads the chunk's scalars by broadcast and merges online.
+    extern __shared__ __align__(16) float stage[];  // [kMergeChunk][PSTR]
+    constexpr int Q4 = (D + 8) / 4;                  // 16-byte pieces of a partial
+    float M = -INFINITY, L = 0.f, acc = 0.f, MS = -INFINITY, E1 = 0.f, E2 = 0.f;
+    for (int s0 = 0; s0 < count; s0 += kMergeChunk) {
+        const int n = min(kMergeChunk, count - s0);
+        for (int idx = d; idx < n * Q4; idx += D) {
+            const int s = idx / Q4, q = idx - s * Q4;
+            cp_async16(stage + s * PSTR + q * 4, pall + (int64_t)(s0 + s) * step + q * 4);
+        }
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+        __syncthreads();
+        float cm = -INFINITY, cms = -INFINITY;
+        for (int s = 0; s < n; ++s) {
+            const float *ps = stage + s * PSTR;
+            cm = fmaxf(cm, ps[1] > 0.f ? ps[0] : -INFINITY);
+            cms = fmaxf(cms, ps[3] > 0.f ? ps[2] : -INFINITY);
+        }
+        const float nm = fmaxf(M, cm), nms = fmaxf(MS, cms);
+        if (nm != -INFINITY) {
+            const float f0 = M == -INFINITY ? 0.f : exp2f(M - nm);
+            L *= f0;
+            acc *= f0;
+            M = nm;
+        }
+        if (nms != -INFINITY) {
+            const float f0 = MS == -INFINITY ? 0.f : exp2f(MS - nms);
+            E1 *= f0;
+            E2 *= f0 * f0;
+            MS = nms;
+        }
 #pragma unroll 8
-    for (int s = 0; s < count; ++s) acc = fmaf(fac[s], pall[s * step + 8 + d], acc);
+        for (int s = 0; s < n; ++s) {
+            const float *ps = stage + s * PSTR;
+            const float f = ps[1] > 0.f ? exp2f(ps[0] - M) : 0.f;
+            L = fmaf(ps[1], f, L);
+            acc = fmaf(f, ps[8 + d], acc);
+            const float fe = ps[3] > 0.f ? exp2f(ps[2] - MS) : 0.f;
+            E1 = fmaf(ps[3], fe, E1);
+            E2 = fmaf(ps[4], fe * fe, E2);
+        }
+        __syncthreads();  // the next chunk overwrites the stage
+    }
     a.out[oh * D + d] = L > 0.f ? acc / L : 0.f;
     if (d == 0) {
         if (a.lse) a.lse[oh] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
@@ -657,7 +650,7 @@ static int launch_execute_d(DecodeArgs &a, cudaStream_t stream) {
         }
         decode_attend_gather_kernel<D><<<num_sms(), kGThreads, sm, stream>>>(a);
         SANTA_LAUNCH_CHECK();
-        const size_t msm = (size_t)(num_sms() + BH) * kGW * sizeof(float);  // >= partials per head
+        const size_t msm = (size_t)kMergeChunk * partial_stride(D) * sizeof(float);
         decode_merge_kernel<D><<<BH * a.geo.group, D, msm, stream>>>(a, num_sms());
     } else {
         static size_t done = 0;
