@@ -269,7 +269,7 @@ def run_ours(args, rank, world):
         },
         "phase_ms": {"select": float(plan_ms.mean()), "attend": float(att_ms.mean())},
         "roofline": {
-            "kernel": "decode_attend_gather_kernel (+ decode_merge_kernel, timed together)",
+            "kernel": "decode_attend_gather_kernel",
             "bound": "hbm",
             "achieved": achieved,
             "peak": peak,

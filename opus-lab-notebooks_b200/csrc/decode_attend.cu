@@ -12,14 +12,16 @@
 //       virtual row spaces of all (batch, KV head) segments are concatenated
 //       and split evenly over the CTAs.  Inside a CTA every warp works alone
 //       on every 8th 16-row tile: it loads the tile's row entries (expanded
-//       union rows, the recent window, sampled rows) one tile ahead, gathers
-//       the K/V rows with row-cooperative coalesced 16-byte cp.async copies
-//       into its own 3-stage ring of padded shared-memory tiles, and runs
-//       mma.sync m16n8k16 (GQA heads on M; q and p split into bf16 hi + lo for
-//       fp32-level accuracy) with an online softmax.  No barrier crosses
-//       warps.  At a segment end each warp writes a partial (m, l, o[D]);
-//       decode_merge_kernel then LSE-merges the partials of every (segment,
-//       query head) in parallel.
+//       union rows, the recent window, sampled rows) three tiles ahead,
+//       gathers the K/V rows with row-cooperative coalesced 16-byte cp.async
+//       copies into its own 3-stage ring of padded shared-memory tiles, and
+//       runs mma.sync m16n8k16 with an online softmax.  GQA heads fill M rows
+//       0-7 with the bf16 hi part of q (or p) and rows 8-15 with the lo part,
+//       so one MMA gives fp32-level accuracy.  No barrier crosses warps in
+//       the main loop.  At a segment end each warp writes a partial
+//       (m, l, o[D]); after one block barrier at the end the CTA folds its
+//       warps' partials, and the last CTA of a segment (atomic counter)
+//       LSE-merges the CTAs' partials into the output.
 //       (Two earlier designs were measured slower on B200: one bulk copy per
 //       256-byte row through the TMA engine is request-bound, and a single
 //       producer warp cannot keep enough 16-byte copies in flight.)
@@ -164,7 +166,6 @@ constexpr int kGW = 8;        // warps per CTA
 constexpr int kGRows = 16;    // rows per warp tile (the mma N/K granule)
 constexpr int kGStages = 3;   // cp.async ring depth per warp
 constexpr int kGThreads = 32 * kGW;
-constexpr int kMergeChunk = 64;  // partials staged per round in the merge kernel
 
 template <int D>
 struct GatherGeom {
@@ -183,7 +184,55 @@ inline size_t gather_smem_bytes(int BH) {
     return 128 + (size_t)kGW * GatherGeom<D>::WARP + ((size_t)BH + 1) * 4;
 }
 
-// A row entry prefetched one tile ahead of its copy.
+// LSE merge of `count` partials of segment bh laid out `stride` floats apart
+// (per head at + h * PSTR) into out / lse / ess.
+template <int D>
+__device__ void merge_strided_to_output(const DecodeArgs &a, int bh, const float *base, int count,
+                                        int64_t stride, int tid, int nthreads) {
+    const int g = a.geo.group, PSTR = partial_stride(D);
+    const int b = bh / a.geo.num_kv_heads, kv = bh - b * a.geo.num_kv_heads;
+    for (int i = tid; i < g * D; i += nthreads) {
+        const int h = i / D, d = i - h * D;
+        float M = -INFINITY;
+        for (int s = 0; s < count; ++s) {
+            const float *ps = base + s * stride + h * PSTR;
+            if (ps[1] > 0.f) M = fmaxf(M, ps[0]);
+        }
+        float L = 0.f, acc = 0.f;
+        for (int s = 0; s < count; ++s) {
+            const float *ps = base + s * stride + h * PSTR;
+            if (ps[1] > 0.f) {
+                const float f = exp2f(ps[0] - M);
+                L = fmaf(ps[1], f, L);
+                acc = fmaf(ps[8 + d], f, acc);
+            }
+        }
+        const int64_t oh = (int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g + h;
+        a.out[oh * D + d] = L > 0.f ? acc / L : 0.f;
+        if (d == 0) {
+            if (a.lse) a.lse[oh] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
+            if (a.ess) {
+                float MS = -INFINITY, E1 = 0.f, E2 = 0.f;
+                for (int s = 0; s < count; ++s) {
+                    const float *ps = base + s * stride + h * PSTR;
+                    if (ps[3] > 0.f) MS = fmaxf(MS, ps[2]);
+                }
+                for (int s = 0; s < count; ++s) {
+                    const float *ps = base + s * stride + h * PSTR;
+                    if (ps[3] > 0.f) {
+                        const float f = exp2f(ps[2] - MS);
+                        E1 += ps[3] * f;
+                        E2 += ps[4] * f * f;
+                    }
+                }
+                const int ns = a.ws.head_meta[((int64_t)bh * 8 + h) * 2 + 1];
+                a.ess[oh] = (ns > 0 && E2 > 0.f) ? (E1 * E1 / E2) / (float)ns : 0.f;
+            }
+        }
+    }
+}
+
+// A row entry prefetched ahead of its copy.
 struct RowEntry {
     int kind;   // 0 none, 1 union row, 2 recent row, 3 sampled row
     int32_t e;  // union: row | mask << 24; recent: row offset; sampled: packed sample word
@@ -321,27 +370,27 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
                 mk[lane] = mask;
                 of[lane] = en.off;
             }
-            // a lane pair per row: lane l copies chunks (l & 1) + 2k of row
-            // l >> 1, so every instruction reads whole 32-byte sectors and a
-            // lane computes its row address once
-            const int r = lane >> 1;
-            const int rc = __shfl_sync(0xffffffffu, code, r);
-            const char *ks = rc >= 0 ? sk + (int64_t)rc * GG::ROWB
-                                     : ck + (int64_t)(rc == INT_MIN ? 0 : -1 - rc) * GG::ROWB;
-            // byte distance from the K row to the V row of the same source
-            const int64_t dv = rc >= 0 ? (int64_t)((uintptr_t)sv - (uintptr_t)sk)
-                                       : (int64_t)((uintptr_t)cv - (uintptr_t)ck);
-            const int ok = rc == INT_MIN ? 0 : 16;
-            const char *src = ks + (lane & 1) * 16;
-            const uint32_t kd = smem_u32(stg + r * GG::PITCH + (lane & 1) * 16);
+            // row-cooperative copies: CPR lanes cover one row, so every
+            // instruction moves RPI whole rows (few cache lines per request;
+            // mapping a lane pair to each row instead measured 40% slower)
+            const int c = lane % GG::CPR;
+            const uint32_t kd0 = smem_u32(stg + (lane / GG::CPR) * GG::PITCH + c * 16);
 #pragma unroll
-            for (int k = 0; k < GG::CPR / 2; ++k) {
-                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(kd + k * 32),
-                             "l"(src + k * 32), "r"(ok)
+            for (int it = 0; it < kGRows / GG::RPI; ++it) {
+                const int r = it * GG::RPI + lane / GG::CPR;
+                const int rc = __shfl_sync(0xffffffffu, code, r);
+                const char *ks = rc >= 0 ? sk + (int64_t)rc * GG::ROWB
+                                         : ck + (int64_t)(rc == INT_MIN ? 0 : -1 - rc) * GG::ROWB;
+                // byte distance from the K row to the V row of the same source
+                const int64_t dv = rc >= 0 ? (int64_t)((uintptr_t)sv - (uintptr_t)sk)
+                                           : (int64_t)((uintptr_t)cv - (uintptr_t)ck);
+                const int ok = rc == INT_MIN ? 0 : 16;
+                const uint32_t kd = kd0 + it * GG::RPI * GG::PITCH;
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(kd),
+                             "l"(ks + c * 16), "r"(ok)
                              : "memory");
-                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(
-                                 kd + GG::TILE + k * 32),
-                             "l"(src + dv + k * 32), "r"(ok)
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(kd + GG::TILE),
+                             "l"(ks + dv + c * 16), "r"(ok)
                              : "memory");
             }
             (void)i;
@@ -514,105 +563,97 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
             }
         }
     }
-}
 
-// ---------------------------------------------------------------------------
-// LSE merge of the gather kernel's per-warp partials: one CTA per (segment,
-// query head), one thread per output element.  Separate from the gather
-// kernel because a single merging warp serialises an L2 round trip per
-// partial and ends up on the critical path.
-// ---------------------------------------------------------------------------
-template <int D>
-__global__ void __launch_bounds__(D) decode_merge_kernel(DecodeArgs a, int n_ctas) {
-    const int bh = blockIdx.x / a.geo.group, h = blockIdx.x - bh * a.geo.group;
-    const int g = a.geo.group, BH = a.geo.batch * a.geo.num_kv_heads;
-    const int d = threadIdx.x, lane = d & 31;
-    const int PSTR = partial_stride(D);
-    __shared__ int s_seg0, s_tall;
-    if (d < 32) {  // prefix of segment sizes: start of bh and the grand total
-        int before = 0, all = 0;
-        for (int i = lane; i < BH; i += 32) {
-            const int t = a.ws.meta[(int64_t)i * 8 + 4];
-            all += t;
-            if (i < bh) before += t;
-        }
-        before = warp_sum_int(before);
-        all = warp_sum_int(all);
-        if (lane == 0) {
-            s_seg0 = before;
-            s_tall = all;
-        }
-    }
+    // ---- two-level LSE merge.  Every warp reaches this barrier (the loops
+    // above have no early exit and no waits that can time out) ----
     __syncthreads();
-    const int seg0 = s_seg0, T_all = s_tall;
-    const int total = a.ws.meta[(int64_t)bh * 8 + 4];
-    const int b = bh / a.geo.num_kv_heads, kv = bh - b * a.geo.num_kv_heads;
-    const int64_t oh = (int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g + h;
-    if (total == 0) {  // no rows at all for this segment
-        a.out[oh * D + d] = 0.f;
-        if (d == 0) {
-            if (a.lse) a.lse[oh] = -INFINITY;
-            if (a.ess) a.ess[oh] = 0.f;
+    __shared__ int s_last;
+    const int64_t wstride = (int64_t)g * PSTR;  // floats between warp slots
+    constexpr int OPT = (SANTA_MAX_GROUP * D + kGThreads - 1) / kGThreads;
+    for (int bh = bh0; bh < BH && pre[bh] < r1; ++bh) {
+        const int seg0 = pre[bh], total = pre[bh + 1] - seg0;
+        if (max(r0, seg0) >= min(r1, seg0 + total)) continue;
+        // (a) this CTA's kGW warp partials of the segment -> warp 0's slot
+        float *wp = a.ws.partial + ((int64_t)blockIdx.x + bh) * kGW * wstride;
+        float res[OPT];
+#pragma unroll
+        for (int k = 0; k < OPT; ++k) {
+            const int i = tid + k * kGThreads;
+            res[k] = 0.f;
+            if (i < g * D) {
+                const int hh = i / D, dd = i - hh * D;
+                float mx = -INFINITY;
+#pragma unroll
+                for (int w = 0; w < kGW; ++w) {
+                    const float *pw = wp + w * wstride + hh * PSTR;
+                    if (pw[1] > 0.f) mx = fmaxf(mx, pw[0]);
+                }
+                float acc = 0.f;
+#pragma unroll
+                for (int w = 0; w < kGW; ++w) {
+                    const float *pw = wp + w * wstride + hh * PSTR;
+                    if (pw[1] > 0.f) acc = fmaf(pw[8 + dd], exp2f(pw[0] - mx), acc);
+                }
+                res[k] = acc;
+            }
         }
-        return;
-    }
-    const int P = max(1, ceil_div(T_all, n_ctas));
-    const int first = seg0 / P, last = (seg0 + total - 1) / P;
-    const int count = (last - first + 1) * kGW;
-    const float *pall = a.ws.partial + ((int64_t)first + bh) * kGW * g * PSTR + h * PSTR;
-    const int64_t step = (int64_t)g * PSTR;
-    // Partials are staged kMergeChunk at a time into shared memory with one
-    // batch of 16-byte cp.async (one memory round trip per chunk); every
-    // thread then reads the chunk's scalars by broadcast and merges online.
-    extern __shared__ __align__(16) float stage[];  // [kMergeChunk][PSTR]
-    constexpr int Q4 = (D + 8) / 4;                  // 16-byte pieces of a partial
-    float M = -INFINITY, L = 0.f, acc = 0.f, MS = -INFINITY, E1 = 0.f, E2 = 0.f;
-    for (int s0 = 0; s0 < count; s0 += kMergeChunk) {
-        const int n = min(kMergeChunk, count - s0);
-        for (int idx = d; idx < n * Q4; idx += D) {
-            const int s = idx / Q4, q = idx - s * Q4;
-            cp_async16(stage + s * PSTR + q * 4, pall + (int64_t)(s0 + s) * step + q * 4);
+        float sc[5] = {-INFINITY, 0.f, -INFINITY, 0.f, 0.f};
+        if (tid < g) {
+            for (int w = 0; w < kGW; ++w) {
+                const float *pw = wp + w * wstride + tid * PSTR;
+                if (pw[1] > 0.f) sc[0] = fmaxf(sc[0], pw[0]);
+                if (pw[3] > 0.f) sc[2] = fmaxf(sc[2], pw[2]);
+            }
+            for (int w = 0; w < kGW; ++w) {
+                const float *pw = wp + w * wstride + tid * PSTR;
+                if (pw[1] > 0.f) sc[1] += pw[1] * exp2f(pw[0] - sc[0]);
+                if (pw[3] > 0.f) {
+                    const float f = exp2f(pw[2] - sc[2]);
+                    sc[3] += pw[3] * f;
+                    sc[4] += pw[4] * f * f;
+                }
+            }
         }
-        asm volatile("cp.async.commit_group;\n" ::: "memory");
-        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+        __syncthreads();  // all reads of the warp slots are done
+#pragma unroll
+        for (int k = 0; k < OPT; ++k) {
+            const int i = tid + k * kGThreads;
+            if (i < g * D) {
+                const int hh = i / D, dd = i - hh * D;
+                wp[hh * PSTR + 8 + dd] = res[k];
+            }
+        }
+        if (tid < g)
+#pragma unroll
+            for (int j = 0; j < 5; ++j) wp[tid * PSTR + j] = sc[j];
+        __threadfence();
         __syncthreads();
-        float cm = -INFINITY, cms = -INFINITY;
-        for (int s = 0; s < n; ++s) {
-            const float *ps = stage + s * PSTR;
-            cm = fmaxf(cm, ps[1] > 0.f ? ps[0] : -INFINITY);
-            cms = fmaxf(cms, ps[3] > 0.f ? ps[2] : -INFINITY);
+        // (b) the last CTA of the segment merges the CTA partials
+        const int first = seg0 / P, last = (seg0 + total - 1) / P;
+        if (tid == 0) s_last = (atomicAdd(&a.ws.counters[bh], 1) == last - first);
+        __syncthreads();
+        if (s_last) {
+            __threadfence();
+            merge_strided_to_output<D>(a, bh,
+                                       a.ws.partial + ((int64_t)first + bh) * kGW * wstride,
+                                       last - first + 1, (int64_t)kGW * wstride, tid, kGThreads);
         }
-        const float nm = fmaxf(M, cm), nms = fmaxf(MS, cms);
-        if (nm != -INFINITY) {
-            const float f0 = M == -INFINITY ? 0.f : exp2f(M - nm);
-            L *= f0;
-            acc *= f0;
-            M = nm;
-        }
-        if (nms != -INFINITY) {
-            const float f0 = MS == -INFINITY ? 0.f : exp2f(MS - nms);
-            E1 *= f0;
-            E2 *= f0 * f0;
-            MS = nms;
-        }
-#pragma unroll 8
-        for (int s = 0; s < n; ++s) {
-            const float *ps = stage + s * PSTR;
-            const float f = ps[1] > 0.f ? exp2f(ps[0] - M) : 0.f;
-            L = fmaf(ps[1], f, L);
-            acc = fmaf(f, ps[8 + d], acc);
-            const float fe = ps[3] > 0.f ? exp2f(ps[2] - MS) : 0.f;
-            E1 = fmaf(ps[3], fe, E1);
-            E2 = fmaf(ps[4], fe * fe, E2);
-        }
-        __syncthreads();  // the next chunk overwrites the stage
+        __syncthreads();
     }
-    a.out[oh * D + d] = L > 0.f ? acc / L : 0.f;
-    if (d == 0) {
-        if (a.lse) a.lse[oh] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
-        if (a.ess) {
-            const int ns = a.ws.head_meta[((int64_t)bh * 8 + h) * 2 + 1];
-            a.ess[oh] = (ns > 0 && E2 > 0.f) ? (E1 * E1 / E2) / (float)ns : 0.f;
+    // segments with no rows at all (every head empty) still get an output
+    if (blockIdx.x == 0) {
+        for (int bh = 0; bh < BH; ++bh) {
+            if (pre[bh + 1] != pre[bh]) continue;
+            const int b = bh / a.geo.num_kv_heads, kv = bh - b * a.geo.num_kv_heads;
+            for (int i = tid; i < g * D; i += kGThreads) {
+                const int h = i / D, d = i - h * D;
+                const int64_t oh = (int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g + h;
+                a.out[oh * D + d] = 0.f;
+                if (d == 0) {
+                    if (a.lse) a.lse[oh] = -INFINITY;
+                    if (a.ess) a.ess[oh] = 0.f;
+                }
+            }
         }
     }
 }
@@ -649,9 +690,6 @@ static int launch_execute_d(DecodeArgs &a, cudaStream_t stream) {
             done = sm;
         }
         decode_attend_gather_kernel<D><<<num_sms(), kGThreads, sm, stream>>>(a);
-        SANTA_LAUNCH_CHECK();
-        const size_t msm = (size_t)kMergeChunk * partial_stride(D) * sizeof(float);
-        decode_merge_kernel<D><<<BH * a.geo.group, D, msm, stream>>>(a, num_sms());
     } else {
         static size_t done = 0;
         const size_t sm = simt_smem_bytes<D>(Gmax);

@@ -337,10 +337,9 @@ class DecodeStep:
 
     @property
     def kernels_per_call(self) -> int:
-        """Kernels of this library launched per step: select, attend and (bf16
-        caches) the partial merge, plus the old-prefix LSE pass in santa mode."""
-        n = 2 + (1 if self.key_cache.dtype == torch.bfloat16 else 0)
-        return n + (1 if self.mode == "santa" else 0)
+        """Kernels of this library launched per step: select and attend, plus
+        the old-prefix LSE pass in santa mode."""
+        return 2 + (1 if self.mode == "santa" else 0)
 
 
 def santa_decode_select(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
