@@ -31,6 +31,13 @@ static int check_decode(const SantaGeometry *geo, const SantaDecodeParams *p, in
     if (p->mode == SANTA_MODE_HYBRID && (p->topk_clusters < 0 || p->topk_clusters > max_groups))
         return SANTA_ERR_INVALID_ARGUMENT;
     if (geo->sample_end >= (1 << 24)) return SANTA_ERR_UNSUPPORTED;
+    {
+        // the attention kernel balances rows on a 32-bit cost scale
+        // (at most 3 per row: union + recent + sampled rows of every segment)
+        const int64_t rows = (int64_t)geo->n_total + (int64_t)geo->group * p->samples;
+        if ((int64_t)geo->batch * geo->num_kv_heads * rows * 3 >= ((int64_t)1 << 31))
+            return SANTA_ERR_UNSUPPORTED;
+    }
     if (!(p->scale > 0.f)) return SANTA_ERR_INVALID_ARGUMENT;
     if (p->num_splits < 0 || p->num_splits > 256) return SANTA_ERR_INVALID_ARGUMENT;
     return SANTA_OK;

@@ -10,18 +10,21 @@
 // Two kernels:
 //   decode_attend_gather_kernel  bf16 caches.  One CTA of 8 warps per SM; the
 //       virtual row spaces of all (batch, KV head) segments are concatenated
-//       and split evenly over the CTAs.  Inside a CTA every warp works alone
-//       on every 8th 16-row tile: it loads the tile's row entries (expanded
-//       union rows, the recent window, sampled rows) three tiles ahead,
-//       gathers the K/V rows with row-cooperative coalesced 16-byte cp.async
-//       copies into its own 3-stage ring of padded shared-memory tiles, and
-//       runs mma.sync m16n8k16 with an online softmax.  GQA heads fill M rows
-//       0-7 with the bf16 hi part of q (or p) and rows 8-15 with the lo part,
-//       so one MMA gives fp32-level accuracy.  No barrier crosses warps in
-//       the main loop.  At a segment end each warp writes a partial
-//       (m, l, o[D]); after one block barrier at the end the CTA folds its
-//       warps' partials, and the last CTA of a segment (atomic counter)
-//       LSE-merges the CTAs' partials into the output.
+//       and split over the CTAs in equal shares of a row cost (sampled rows,
+//       scattered over the cache, cost 1.5x a contiguous cluster row).
+//       Inside a CTA every warp works alone on every 8th 16-row tile: it
+//       loads the tile's row entries (expanded union rows, the recent window,
+//       sampled rows) three tiles ahead, gathers the K/V rows with
+//       row-cooperative coalesced 16-byte cp.async copies into its own
+//       3-stage ring of padded shared-memory tiles, and runs mma.sync
+//       m16n8k16 with an online softmax.  GQA heads fill M rows 0-7 with the
+//       bf16 hi part of q (or p) and rows 8-15 with the lo part, so one MMA
+//       gives fp32-level accuracy.  No barrier crosses warps inside a
+//       segment.  At a segment end each warp leaves its partial
+//       (m, l, o[D]) in its drained ring, the CTA folds the 8 partials into
+//       one CTA partial in global memory, and after the last segment the
+//       last CTA of each segment (atomic counter) stages the segment's CTA
+//       partials into shared memory and LSE-merges them into the output.
 //       (Two earlier designs were measured slower on B200: one bulk copy per
 //       256-byte row through the TMA engine is request-bound, and a single
 //       producer warp cannot keep enough 16-byte copies in flight.)
@@ -166,6 +169,8 @@ constexpr int kGW = 8;        // warps per CTA
 constexpr int kGRows = 16;    // rows per warp tile (the mma N/K granule)
 constexpr int kGStages = 3;   // cp.async ring depth per warp
 constexpr int kGThreads = 32 * kGW;
+constexpr int kCostRow = 2;     // balancing cost of a union or recent-window row
+constexpr int kCostSample = 3;  // balancing cost of a sampled (scattered) row
 
 template <int D>
 struct GatherGeom {
@@ -274,12 +279,18 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
     unsigned char *base = (unsigned char *)(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
     unsigned char *wbase = base + warp * GG::WARP;     // this warp's ring
     int *pre = (int *)(base + kGW * GG::WARP);         // segment prefix [BH + 1]
+    __shared__ float s_wfac[SANTA_MAX_GROUP][kGW];     // CTA fold: factor per head and warp
 
     if (warp == 0) {
         int carry = 0;
         for (int i0 = 0; i0 < BH; i0 += 32) {
             const int i = i0 + lane;
-            int x = i < BH ? a.ws.meta[(int64_t)i * 8 + 4] : 0;
+            // segment cost: kCostRow per union / recent row, kCostSample per
+            // sampled row (scattered rows stream ~1.5x slower than contiguous
+            // cluster rows)
+            int x = i < BH ? kCostRow * a.ws.meta[(int64_t)i * 8 + 4] +
+                                 (kCostSample - kCostRow) * a.ws.meta[(int64_t)i * 8 + 3]
+                           : 0;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const int y = __shfl_up_sync(0xffffffffu, x, o);
@@ -292,10 +303,18 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
     }
     __syncthreads();  // the only block-wide barrier
 
+    // every CTA takes an equal share [r0, r1) of the total cost; within a
+    // segment, row v starts at cost kCostRow * v (union and recent rows) or
+    // kCostRow * (U + R) + kCostSample * (v - U - R) (sampled rows), and
+    // belongs to the CTA whose share holds that start
     const int T_all = pre[BH];
     const int P = max(1, ceil_div(T_all, (int)gridDim.x));
     const int r0 = min(T_all, (int)blockIdx.x * P);
     const int r1 = min(T_all, r0 + P);
+    auto row_at_cost = [](int c, int ur) {  // first row whose cost start is >= c
+        return c <= kCostRow * ur ? ceil_div(c, kCostRow)
+                                  : ur + ceil_div(c - kCostRow * ur, kCostSample);
+    };
     int bh0 = 0;
     while (bh0 < BH && pre[bh0 + 1] <= r0) ++bh0;
 
@@ -306,14 +325,17 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
     int k_base = 0;  // CTA tiles before the current segment
     for (int bh = bh0; bh < BH && pre[bh] < r1; ++bh) {
         const int seg0 = pre[bh], total = pre[bh + 1] - seg0;
-        const int s0 = max(r0, seg0) - seg0, s1 = min(r1, seg0 + total) - seg0;
-        if (s0 >= s1) continue;
+        const int c0 = max(r0, seg0) - seg0, c1 = min(r1, seg0 + total) - seg0;
+        // a CTA whose share meets the segment takes part in its merge even
+        // when the share holds no row start (its warps write empty partials)
+        if (c0 >= c1) continue;
+        const int32_t *meta = a.ws.meta + (int64_t)bh * 8;
+        const int U = meta[1], R = meta[2];
+        const int s0 = row_at_cost(c0, U + R), s1 = row_at_cost(c1, U + R);
         const int nt = ceil_div(s1 - s0, kGRows);
         const int j0 = ((warp - k_base) % kGW + kGW) % kGW;  // my first tile in the segment
         const int n_my = nt > j0 ? ceil_div(nt - j0, kGW) : 0;
         k_base += nt;
-        const int32_t *meta = a.ws.meta + (int64_t)bh * 8;
-        const int U = meta[1], R = meta[2];
         const int b = bh / a.geo.num_kv_heads, kv = bh - b * a.geo.num_kv_heads;
         const char *sk = sk_all + (int64_t)bh * a.geo.sample_end * GG::ROWB;
         const char *sv = sv_all + (int64_t)bh * a.geo.sample_end * GG::ROWB;
@@ -544,99 +566,196 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
             e1_run = E1;
             e2_run = E2;
         }
-        // slot (c + bh) * kGW + warp is unique: the segments a CTA meets form an
-        // increasing range and consecutive CTAs' ranges share at most one segment
-        const int64_t slot = ((int64_t)blockIdx.x + bh) * kGW + warp;
-        float *part = a.ws.partial + slot * g * PSTR;
+        // the ring is drained (wait_group 0 above): the warp's partial goes
+        // into its first bytes
+        float *wpart = (float *)wbase;
         if (gid < g) {
             if (tig == 0) {
-                part[gid * PSTR + 0] = m_run;
-                part[gid * PSTR + 1] = l_run;
-                part[gid * PSTR + 2] = ms_run;
-                part[gid * PSTR + 3] = e1_run;
-                part[gid * PSTR + 4] = e2_run;
+                wpart[gid * PSTR + 0] = m_run;
+                wpart[gid * PSTR + 1] = l_run;
+                wpart[gid * PSTR + 2] = ms_run;
+                wpart[gid * PSTR + 3] = e1_run;
+                wpart[gid * PSTR + 4] = e2_run;
             }
 #pragma unroll
             for (int q = 0; q < NT_O; ++q) {
-                part[gid * PSTR + 8 + q * 8 + 2 * tig] = o[q][0] + o[q][2];
-                part[gid * PSTR + 8 + q * 8 + 2 * tig + 1] = o[q][1] + o[q][3];
+                wpart[gid * PSTR + 8 + q * 8 + 2 * tig] = o[q][0] + o[q][2];
+                wpart[gid * PSTR + 8 + q * 8 + 2 * tig + 1] = o[q][1] + o[q][3];
             }
         }
+        // ---- CTA fold: the kGW warp partials of this segment -> one CTA
+        // partial in slot c + bh, unique because the segments a CTA meets form
+        // an increasing range and consecutive CTAs' shares overlap in at most
+        // one segment.  Every warp of the CTA walks the same segments (the
+        // loop bounds are CTA-uniform), so the block barriers line up ----
+        __syncthreads();
+        float *cpart = a.ws.partial + ((int64_t)blockIdx.x + bh) * g * PSTR;
+        if (tid < g) {  // per head: maxima, denominators, the warps' factors
+            const int h = tid;
+            float M = -INFINITY, MS = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < kGW; ++w) {
+                const float *pw = (const float *)(base + w * GG::WARP) + h * PSTR;
+                if (pw[1] > 0.f) M = fmaxf(M, pw[0]);
+                if (pw[3] > 0.f) MS = fmaxf(MS, pw[2]);
+            }
+            float L = 0.f, E1 = 0.f, E2 = 0.f;
+#pragma unroll
+            for (int w = 0; w < kGW; ++w) {
+                const float *pw = (const float *)(base + w * GG::WARP) + h * PSTR;
+                const float f = pw[1] > 0.f ? exp2f(pw[0] - M) : 0.f;
+                s_wfac[h][w] = f;
+                L = fmaf(pw[1], f, L);
+                if (pw[3] > 0.f) {
+                    const float fe = exp2f(pw[2] - MS);
+                    E1 = fmaf(pw[3], fe, E1);
+                    E2 = fmaf(pw[4], fe * fe, E2);
+                }
+            }
+            cpart[h * PSTR + 0] = M;
+            cpart[h * PSTR + 1] = L;
+            cpart[h * PSTR + 2] = MS;
+            cpart[h * PSTR + 3] = E1;
+            cpart[h * PSTR + 4] = E2;
+        }
+        __syncthreads();
+        for (int i = tid; i < g * D; i += kGThreads) {
+            const int hh = i / D, dd = i - hh * D;
+            float acc = 0.f;
+#pragma unroll
+            for (int w = 0; w < kGW; ++w)
+                acc = fmaf(s_wfac[hh][w],
+                           ((const float *)(base + w * GG::WARP))[hh * PSTR + 8 + dd], acc);
+            cpart[hh * PSTR + 8 + dd] = acc;
+        }
+        __syncthreads();  // the rings are refilled by the next segment
     }
 
-    // ---- two-level LSE merge.  Every warp reaches this barrier (the loops
-    // above have no early exit and no waits that can time out) ----
+    // ---- LSE merge.  Every warp reaches this barrier (the loops above have
+    // no early exit and no waits that can time out), so the stage rings are
+    // free and every partial of this CTA is written ----
+    __threadfence();
     __syncthreads();
     __shared__ int s_last;
-    const int64_t wstride = (int64_t)g * PSTR;  // floats between warp slots
+    const int64_t wstride = (int64_t)g * PSTR;  // floats between partial slots
     constexpr int OPT = (SANTA_MAX_GROUP * D + kGThreads - 1) / kGThreads;
+    constexpr int kFacCap = 64;                 // partials merged per staged chunk
+    float *stage_f = (float *)base;             // staged partials
+    const int region = kGW * GG::WARP / 4;      // floats of the stage area
+    float *fac = stage_f + region - SANTA_MAX_GROUP * kFacCap - SANTA_MAX_GROUP * 8;
+    float *hsc = fac + SANTA_MAX_GROUP * kFacCap;  // per head: M, L, MS, E1, E2, f0
+    const int cap = min(kFacCap, (int)((region - SANTA_MAX_GROUP * (kFacCap + 8)) / wstride));
     for (int bh = bh0; bh < BH && pre[bh] < r1; ++bh) {
         const int seg0 = pre[bh], total = pre[bh + 1] - seg0;
         if (max(r0, seg0) >= min(r1, seg0 + total)) continue;
-        // (a) this CTA's kGW warp partials of the segment -> warp 0's slot
-        float *wp = a.ws.partial + ((int64_t)blockIdx.x + bh) * kGW * wstride;
-        float res[OPT];
-#pragma unroll
-        for (int k = 0; k < OPT; ++k) {
-            const int i = tid + k * kGThreads;
-            res[k] = 0.f;
-            if (i < g * D) {
-                const int hh = i / D, dd = i - hh * D;
-                float mx = -INFINITY;
-#pragma unroll
-                for (int w = 0; w < kGW; ++w) {
-                    const float *pw = wp + w * wstride + hh * PSTR;
-                    if (pw[1] > 0.f) mx = fmaxf(mx, pw[0]);
-                }
-                float acc = 0.f;
-#pragma unroll
-                for (int w = 0; w < kGW; ++w) {
-                    const float *pw = wp + w * wstride + hh * PSTR;
-                    if (pw[1] > 0.f) acc = fmaf(pw[8 + dd], exp2f(pw[0] - mx), acc);
-                }
-                res[k] = acc;
-            }
-        }
-        float sc[5] = {-INFINITY, 0.f, -INFINITY, 0.f, 0.f};
-        if (tid < g) {
-            for (int w = 0; w < kGW; ++w) {
-                const float *pw = wp + w * wstride + tid * PSTR;
-                if (pw[1] > 0.f) sc[0] = fmaxf(sc[0], pw[0]);
-                if (pw[3] > 0.f) sc[2] = fmaxf(sc[2], pw[2]);
-            }
-            for (int w = 0; w < kGW; ++w) {
-                const float *pw = wp + w * wstride + tid * PSTR;
-                if (pw[1] > 0.f) sc[1] += pw[1] * exp2f(pw[0] - sc[0]);
-                if (pw[3] > 0.f) {
-                    const float f = exp2f(pw[2] - sc[2]);
-                    sc[3] += pw[3] * f;
-                    sc[4] += pw[4] * f * f;
-                }
-            }
-        }
-        __syncthreads();  // all reads of the warp slots are done
-#pragma unroll
-        for (int k = 0; k < OPT; ++k) {
-            const int i = tid + k * kGThreads;
-            if (i < g * D) {
-                const int hh = i / D, dd = i - hh * D;
-                wp[hh * PSTR + 8 + dd] = res[k];
-            }
-        }
-        if (tid < g)
-#pragma unroll
-            for (int j = 0; j < 5; ++j) wp[tid * PSTR + j] = sc[j];
-        __threadfence();
-        __syncthreads();
-        // (b) the last CTA of the segment merges the CTA partials
         const int first = seg0 / P, last = (seg0 + total - 1) / P;
         if (tid == 0) s_last = (atomicAdd(&a.ws.counters[bh], 1) == last - first);
         __syncthreads();
         if (s_last) {
+            // the last CTA of the segment: the (last - first + 1) CTA
+            // partials are consecutive slots; stage up to cap of them with one
+            // batch of cp.async, compute each partial's factor once per head,
+            // then one FMA pass per output element from shared memory
             __threadfence();
-            merge_strided_to_output<D>(a, bh,
-                                       a.ws.partial + ((int64_t)first + bh) * kGW * wstride,
-                                       last - first + 1, (int64_t)kGW * wstride, tid, kGThreads);
+            if (tid == 0) a.ws.counters[bh] = 0;  // every CTA of the segment has arrived
+            const int count = last - first + 1;
+            const float *src = a.ws.partial + ((int64_t)first + bh) * wstride;
+            float acc[OPT];
+#pragma unroll
+            for (int k = 0; k < OPT; ++k) acc[k] = 0.f;
+            if (tid < SANTA_MAX_GROUP) {
+                hsc[tid * 8 + 0] = -INFINITY;
+                hsc[tid * 8 + 1] = 0.f;
+                hsc[tid * 8 + 2] = -INFINITY;
+                hsc[tid * 8 + 3] = 0.f;
+                hsc[tid * 8 + 4] = 0.f;
+            }
+            for (int s0 = 0; s0 < count; s0 += cap) {
+                const int n = min(cap, count - s0);
+                const int n16 = n * (int)wstride / 4;
+                for (int i = tid; i < n16; i += kGThreads)
+                    cp_async16(stage_f + 4 * i, src + (int64_t)s0 * wstride + 4 * i);
+                asm volatile("cp.async.commit_group;\n" ::: "memory");
+                asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+                __syncthreads();
+                if (warp < g) {  // per-head factors of this chunk
+                    const int h = warp;
+                    float cm = -INFINITY, cms = -INFINITY;
+                    for (int s = lane; s < n; s += 32) {
+                        const float *ps = stage_f + s * wstride + h * PSTR;
+                        if (ps[1] > 0.f) cm = fmaxf(cm, ps[0]);
+                        if (ps[3] > 0.f) cms = fmaxf(cms, ps[2]);
+                    }
+                    cm = warp_max(cm);
+                    cms = warp_max(cms);
+                    const float Mo = hsc[h * 8 + 0], MSo = hsc[h * 8 + 2];
+                    const float Mn = fmaxf(Mo, cm), MSn = fmaxf(MSo, cms);
+                    float lc = 0.f, e1c = 0.f, e2c = 0.f;
+                    for (int s = lane; s < n; s += 32) {
+                        const float *ps = stage_f + s * wstride + h * PSTR;
+                        const float f = (ps[1] > 0.f) ? exp2f(ps[0] - Mn) : 0.f;
+                        fac[h * kFacCap + s] = f;
+                        lc = fmaf(ps[1], f, lc);
+                        if (ps[3] > 0.f) {
+                            const float fe = exp2f(ps[2] - MSn);
+                            e1c = fmaf(ps[3], fe, e1c);
+                            e2c = fmaf(ps[4], fe * fe, e2c);
+                        }
+                    }
+                    lc = warp_sum(lc);
+                    e1c = warp_sum(e1c);
+                    e2c = warp_sum(e2c);
+                    if (lane == 0) {
+                        const float f0 = (Mo == -INFINITY || Mn == -INFINITY) ? 0.f : exp2f(Mo - Mn);
+                        const float fe0 =
+                            (MSo == -INFINITY || MSn == -INFINITY) ? 0.f : exp2f(MSo - MSn);
+                        hsc[h * 8 + 0] = Mn;
+                        hsc[h * 8 + 1] = hsc[h * 8 + 1] * f0 + lc;
+                        hsc[h * 8 + 2] = MSn;
+                        hsc[h * 8 + 3] = hsc[h * 8 + 3] * fe0 + e1c;
+                        hsc[h * 8 + 4] = hsc[h * 8 + 4] * fe0 * fe0 + e2c;
+                        hsc[h * 8 + 5] = f0;
+                    }
+                }
+                __syncthreads();
+                // the OPT accumulators of a thread advance together, so their
+                // FMA chains and shared-memory loads interleave
+                int fo[OPT], co[OPT];
+#pragma unroll
+                for (int k = 0; k < OPT; ++k) {
+                    const int i = min(tid + k * kGThreads, g * D - 1);
+                    const int hh = i / D, dd = i - hh * D;
+                    fo[k] = hh * kFacCap;
+                    co[k] = hh * PSTR + 8 + dd;
+                    acc[k] *= hsc[hh * 8 + 5];
+                }
+#pragma unroll 4
+                for (int s = 0; s < n; ++s) {
+                    const float *ps = stage_f + s * wstride;
+#pragma unroll
+                    for (int k = 0; k < OPT; ++k) acc[k] = fmaf(fac[fo[k] + s], ps[co[k]], acc[k]);
+                }
+                __syncthreads();  // the next chunk overwrites the stage
+            }
+            const int b = bh / a.geo.num_kv_heads, kv = bh - b * a.geo.num_kv_heads;
+#pragma unroll
+            for (int k = 0; k < OPT; ++k) {
+                const int i = tid + k * kGThreads;
+                if (i < g * D) {
+                    const int hh = i / D, dd = i - hh * D;
+                    const int64_t oh = (int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g + hh;
+                    const float L = hsc[hh * 8 + 1];
+                    a.out[oh * D + dd] = L > 0.f ? acc[k] / L : 0.f;
+                    if (dd == 0) {
+                        if (a.lse) a.lse[oh] = L > 0.f ? (hsc[hh * 8 + 0] + log2f(L)) * kLn2 : -INFINITY;
+                        if (a.ess) {
+                            const int ns = a.ws.head_meta[((int64_t)bh * 8 + hh) * 2 + 1];
+                            const float E1 = hsc[hh * 8 + 3], E2 = hsc[hh * 8 + 4];
+                            a.ess[oh] = (ns > 0 && E2 > 0.f) ? (E1 * E1 / E2) / (float)ns : 0.f;
+                        }
+                    }
+                }
+            }
         }
         __syncthreads();
     }
@@ -670,7 +789,7 @@ static size_t simt_smem_bytes(int Gmax) {
 int attend_partial_slots(const SantaGeometry *geo, int nsplit) {
     const int BH = geo->batch * geo->num_kv_heads;
     const int simt = BH * nsplit;
-    const int gather = (num_sms() + BH) * kGW;
+    const int gather = num_sms() + BH;  // one CTA partial per (CTA, segment met)
     return simt > gather ? simt : gather;
 }
 
@@ -678,7 +797,8 @@ template <int D>
 static int launch_execute_d(DecodeArgs &a, cudaStream_t stream) {
     const int BH = a.geo.batch * a.geo.num_kv_heads;
     const int Gmax = a.sum.max_groups;
-    SANTA_CUDA_CHECK(cudaMemsetAsync(a.ws.counters, 0, (size_t)BH * 4, stream));
+    // the segment counters are zeroed by the selection kernel and put back
+    // to zero by each segment's merging CTA
     if (a.geo.kv_dtype == SANTA_DTYPE_BF16) {
         static size_t done = 0;
         const size_t sm = gather_smem_bytes<D>(BH);

@@ -148,6 +148,7 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
         }
     }
     for (int i = tid; i < Gmax; i += kSelThreads) mask_s[i] = 0;
+    if (tid == 0) a.ws.counters[bh] = 0;  // arrival counter of the attention merge
     if (tid < 8) {
         head_sel[tid] = 0;
         head_exact[tid] = 0;
