@@ -189,49 +189,85 @@ inline size_t gather_smem_bytes(int BH) {
     return 128 + (size_t)kGW * GatherGeom<D>::WARP + ((size_t)BH + 1) * 4;
 }
 
-// LSE merge of `count` partials of segment bh laid out `stride` floats apart
-// (per head at + h * PSTR) into out / lse / ess.
+// LSE merge of `count` partials (header m, l, ms, e1, e2 at [0, 5), values
+// at [8, 8 + D) per head, heads PSTR floats apart) that lie `wstride` floats
+// apart from `src`, into out / lse / ess of segment bh.  The whole CTA
+// (kGThreads threads) calls it.  Up to 32 partials at a time are staged into
+// `stage` with one batch of 16-byte cp.async; lane s of every warp computes
+// partial s's factor for the warp's head and the FMA pass broadcasts it by
+// shuffle (a warp's 32 output elements belong to one head), so no block
+// barrier separates the factors from the sums.
 template <int D>
-__device__ void merge_strided_to_output(const DecodeArgs &a, int bh, const float *base, int count,
-                                        int64_t stride, int tid, int nthreads) {
+__device__ void merge_staged_to_output(const DecodeArgs &a, int bh, const float *src, int count,
+                                       int wstride, float *stage, int stage_floats) {
+    constexpr int NT = kGThreads;
+    constexpr int OPT = (SANTA_MAX_GROUP * D + NT - 1) / NT;
+    static_assert(D % 32 == 0, "a warp's output elements must share one head");
     const int g = a.geo.group, PSTR = partial_stride(D);
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int cap = min(32, stage_floats / wstride);
+    float M[OPT], L[OPT], acc[OPT], MS[OPT], E1[OPT], E2[OPT];
+#pragma unroll
+    for (int k = 0; k < OPT; ++k) {
+        M[k] = -INFINITY;
+        MS[k] = -INFINITY;
+        L[k] = acc[k] = E1[k] = E2[k] = 0.f;
+    }
+    for (int s0 = 0; s0 < count; s0 += cap) {
+        const int n = min(cap, count - s0);
+        const int n16 = n * wstride / 4;
+        for (int i = tid; i < n16; i += NT)
+            cp_async16(stage + 4 * i, src + (int64_t)s0 * wstride + 4 * i);
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+        __syncthreads();
+        float f[OPT];
+        int col[OPT];
+#pragma unroll
+        for (int k = 0; k < OPT; ++k) {
+            const int i = min(tid + k * NT, g * D - 1);
+            const int hh = i / D;  // warp-uniform
+            col[k] = hh * PSTR + 8 + (i - hh * D);
+            const float *hs = stage + min(lane, n - 1) * wstride + hh * PSTR;
+            const bool have = lane < n;
+            const float m = have ? hs[0] : -INFINITY, l = have ? hs[1] : 0.f;
+            const float ms = have ? hs[2] : -INFINITY, e1 = have ? hs[3] : 0.f;
+            const float e2 = have ? hs[4] : 0.f;
+            const float Mn = fmaxf(M[k], warp_max(l > 0.f ? m : -INFINITY));
+            f[k] = l > 0.f ? exp2f(m - Mn) : 0.f;
+            const float r = M[k] == -INFINITY ? 0.f : exp2f(M[k] - Mn);
+            acc[k] *= r;
+            L[k] = L[k] * r + warp_sum(l * f[k]);
+            M[k] = Mn;
+            const float MSn = fmaxf(MS[k], warp_max(e1 > 0.f ? ms : -INFINITY));
+            const float fe = e1 > 0.f ? exp2f(ms - MSn) : 0.f;
+            const float re = MS[k] == -INFINITY ? 0.f : exp2f(MS[k] - MSn);
+            E1[k] = E1[k] * re + warp_sum(e1 * fe);
+            E2[k] = E2[k] * re * re + warp_sum(e2 * fe * fe);
+            MS[k] = MSn;
+        }
+        for (int s = 0; s < n; ++s) {
+            const float *ps = stage + s * wstride;
+#pragma unroll
+            for (int k = 0; k < OPT; ++k)
+                acc[k] = fmaf(__shfl_sync(0xffffffffu, f[k], s), ps[col[k]], acc[k]);
+        }
+        __syncthreads();  // the next chunk overwrites the stage
+    }
     const int b = bh / a.geo.num_kv_heads, kv = bh - b * a.geo.num_kv_heads;
-    for (int i = tid; i < g * D; i += nthreads) {
-        const int h = i / D, d = i - h * D;
-        float M = -INFINITY;
-        for (int s = 0; s < count; ++s) {
-            const float *ps = base + s * stride + h * PSTR;
-            if (ps[1] > 0.f) M = fmaxf(M, ps[0]);
-        }
-        float L = 0.f, acc = 0.f;
-        for (int s = 0; s < count; ++s) {
-            const float *ps = base + s * stride + h * PSTR;
-            if (ps[1] > 0.f) {
-                const float f = exp2f(ps[0] - M);
-                L = fmaf(ps[1], f, L);
-                acc = fmaf(ps[8 + d], f, acc);
-            }
-        }
-        const int64_t oh = (int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g + h;
-        a.out[oh * D + d] = L > 0.f ? acc / L : 0.f;
-        if (d == 0) {
-            if (a.lse) a.lse[oh] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
-            if (a.ess) {
-                float MS = -INFINITY, E1 = 0.f, E2 = 0.f;
-                for (int s = 0; s < count; ++s) {
-                    const float *ps = base + s * stride + h * PSTR;
-                    if (ps[3] > 0.f) MS = fmaxf(MS, ps[2]);
+#pragma unroll
+    for (int k = 0; k < OPT; ++k) {
+        const int i = tid + k * NT;
+        if (i < g * D) {
+            const int hh = i / D, dd = i - hh * D;
+            const int64_t oh = (int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g + hh;
+            a.out[oh * D + dd] = L[k] > 0.f ? acc[k] / L[k] : 0.f;
+            if (dd == 0) {
+                if (a.lse) a.lse[oh] = L[k] > 0.f ? (M[k] + log2f(L[k])) * kLn2 : -INFINITY;
+                if (a.ess) {
+                    const int ns = a.ws.head_meta[((int64_t)bh * 8 + hh) * 2 + 1];
+                    a.ess[oh] = (ns > 0 && E2[k] > 0.f) ? (E1[k] * E1[k] / E2[k]) / (float)ns : 0.f;
                 }
-                for (int s = 0; s < count; ++s) {
-                    const float *ps = base + s * stride + h * PSTR;
-                    if (ps[3] > 0.f) {
-                        const float f = exp2f(ps[2] - MS);
-                        E1 += ps[3] * f;
-                        E2 += ps[4] * f * f;
-                    }
-                }
-                const int ns = a.ws.head_meta[((int64_t)bh * 8 + h) * 2 + 1];
-                a.ess[oh] = (ns > 0 && E2 > 0.f) ? (E1 * E1 / E2) / (float)ns : 0.f;
             }
         }
     }
@@ -633,131 +669,39 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
 
     // ---- LSE merge.  Every warp reaches this barrier (the loops above have
     // no early exit and no waits that can time out), so the stage rings are
-    // free and every partial of this CTA is written ----
+    // free and every CTA partial of this CTA is written ----
     __threadfence();
     __syncthreads();
-    __shared__ int s_last;
-    const int64_t wstride = (int64_t)g * PSTR;  // floats between partial slots
-    constexpr int OPT = (SANTA_MAX_GROUP * D + kGThreads - 1) / kGThreads;
-    constexpr int kFacCap = 64;                 // partials merged per staged chunk
-    float *stage_f = (float *)base;             // staged partials
-    const int region = kGW * GG::WARP / 4;      // floats of the stage area
-    float *fac = stage_f + region - SANTA_MAX_GROUP * kFacCap - SANTA_MAX_GROUP * 8;
-    float *hsc = fac + SANTA_MAX_GROUP * kFacCap;  // per head: M, L, MS, E1, E2, f0
-    const int cap = min(kFacCap, (int)((region - SANTA_MAX_GROUP * (kFacCap + 8)) / wstride));
-    for (int bh = bh0; bh < BH && pre[bh] < r1; ++bh) {
-        const int seg0 = pre[bh], total = pre[bh + 1] - seg0;
-        if (max(r0, seg0) >= min(r1, seg0 + total)) continue;
-        const int first = seg0 / P, last = (seg0 + total - 1) / P;
-        if (tid == 0) s_last = (atomicAdd(&a.ws.counters[bh], 1) == last - first);
-        __syncthreads();
-        if (s_last) {
-            // the last CTA of the segment: the (last - first + 1) CTA
-            // partials are consecutive slots; stage up to cap of them with one
-            // batch of cp.async, compute each partial's factor once per head,
-            // then one FMA pass per output element from shared memory
-            __threadfence();
-            if (tid == 0) a.ws.counters[bh] = 0;  // every CTA of the segment has arrived
-            const int count = last - first + 1;
-            const float *src = a.ws.partial + ((int64_t)first + bh) * wstride;
-            float acc[OPT];
-#pragma unroll
-            for (int k = 0; k < OPT; ++k) acc[k] = 0.f;
-            if (tid < SANTA_MAX_GROUP) {
-                hsc[tid * 8 + 0] = -INFINITY;
-                hsc[tid * 8 + 1] = 0.f;
-                hsc[tid * 8 + 2] = -INFINITY;
-                hsc[tid * 8 + 3] = 0.f;
-                hsc[tid * 8 + 4] = 0.f;
-            }
-            for (int s0 = 0; s0 < count; s0 += cap) {
-                const int n = min(cap, count - s0);
-                const int n16 = n * (int)wstride / 4;
-                for (int i = tid; i < n16; i += kGThreads)
-                    cp_async16(stage_f + 4 * i, src + (int64_t)s0 * wstride + 4 * i);
-                asm volatile("cp.async.commit_group;\n" ::: "memory");
-                asm volatile("cp.async.wait_group 0;\n" ::: "memory");
-                __syncthreads();
-                if (warp < g) {  // per-head factors of this chunk
-                    const int h = warp;
-                    float cm = -INFINITY, cms = -INFINITY;
-                    for (int s = lane; s < n; s += 32) {
-                        const float *ps = stage_f + s * wstride + h * PSTR;
-                        if (ps[1] > 0.f) cm = fmaxf(cm, ps[0]);
-                        if (ps[3] > 0.f) cms = fmaxf(cms, ps[2]);
-                    }
-                    cm = warp_max(cm);
-                    cms = warp_max(cms);
-                    const float Mo = hsc[h * 8 + 0], MSo = hsc[h * 8 + 2];
-                    const float Mn = fmaxf(Mo, cm), MSn = fmaxf(MSo, cms);
-                    float lc = 0.f, e1c = 0.f, e2c = 0.f;
-                    for (int s = lane; s < n; s += 32) {
-                        const float *ps = stage_f + s * wstride + h * PSTR;
-                        const float f = (ps[1] > 0.f) ? exp2f(ps[0] - Mn) : 0.f;
-                        fac[h * kFacCap + s] = f;
-                        lc = fmaf(ps[1], f, lc);
-                        if (ps[3] > 0.f) {
-                            const float fe = exp2f(ps[2] - MSn);
-                            e1c = fmaf(ps[3], fe, e1c);
-                            e2c = fmaf(ps[4], fe * fe, e2c);
-                        }
-                    }
-                    lc = warp_sum(lc);
-                    e1c = warp_sum(e1c);
-                    e2c = warp_sum(e2c);
-                    if (lane == 0) {
-                        const float f0 = (Mo == -INFINITY || Mn == -INFINITY) ? 0.f : exp2f(Mo - Mn);
-                        const float fe0 =
-                            (MSo == -INFINITY || MSn == -INFINITY) ? 0.f : exp2f(MSo - MSn);
-                        hsc[h * 8 + 0] = Mn;
-                        hsc[h * 8 + 1] = hsc[h * 8 + 1] * f0 + lc;
-                        hsc[h * 8 + 2] = MSn;
-                        hsc[h * 8 + 3] = hsc[h * 8 + 3] * fe0 + e1c;
-                        hsc[h * 8 + 4] = hsc[h * 8 + 4] * fe0 * fe0 + e2c;
-                        hsc[h * 8 + 5] = f0;
-                    }
-                }
-                __syncthreads();
-                // the OPT accumulators of a thread advance together, so their
-                // FMA chains and shared-memory loads interleave
-                int fo[OPT], co[OPT];
-#pragma unroll
-                for (int k = 0; k < OPT; ++k) {
-                    const int i = min(tid + k * kGThreads, g * D - 1);
-                    const int hh = i / D, dd = i - hh * D;
-                    fo[k] = hh * kFacCap;
-                    co[k] = hh * PSTR + 8 + dd;
-                    acc[k] *= hsc[hh * 8 + 5];
-                }
-#pragma unroll 4
-                for (int s = 0; s < n; ++s) {
-                    const float *ps = stage_f + s * wstride;
-#pragma unroll
-                    for (int k = 0; k < OPT; ++k) acc[k] = fmaf(fac[fo[k] + s], ps[co[k]], acc[k]);
-                }
-                __syncthreads();  // the next chunk overwrites the stage
-            }
-            const int b = bh / a.geo.num_kv_heads, kv = bh - b * a.geo.num_kv_heads;
-#pragma unroll
-            for (int k = 0; k < OPT; ++k) {
-                const int i = tid + k * kGThreads;
-                if (i < g * D) {
-                    const int hh = i / D, dd = i - hh * D;
-                    const int64_t oh = (int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g + hh;
-                    const float L = hsc[hh * 8 + 1];
-                    a.out[oh * D + dd] = L > 0.f ? acc[k] / L : 0.f;
-                    if (dd == 0) {
-                        if (a.lse) a.lse[oh] = L > 0.f ? (hsc[hh * 8 + 0] + log2f(L)) * kLn2 : -INFINITY;
-                        if (a.ess) {
-                            const int ns = a.ws.head_meta[((int64_t)bh * 8 + hh) * 2 + 1];
-                            const float E1 = hsc[hh * 8 + 3], E2 = hsc[hh * 8 + 4];
-                            a.ess[oh] = (ns > 0 && E2 > 0.f) ? (E1 * E1 / E2) / (float)ns : 0.f;
-                        }
-                    }
+    __shared__ unsigned s_lastmask;
+    const int wstride = g * PSTR;  // floats between partial slots
+    // arrivals at up to 32 segments at once (one atomic round trip), then
+    // the merges of the segments this CTA completed
+    for (int b0 = bh0; b0 < BH && pre[b0] < r1; b0 += 32) {
+        if (warp == 0) {
+            const int bh = b0 + lane;
+            bool done = false;
+            if (bh < BH && pre[bh] < r1) {
+                const int seg0 = pre[bh], total = pre[bh + 1] - seg0;
+                if (max(r0, seg0) < min(r1, seg0 + total)) {
+                    const int first = seg0 / P, last = (seg0 + total - 1) / P;
+                    done = atomicAdd(&a.ws.counters[bh], 1) == last - first;
                 }
             }
+            const unsigned m = __ballot_sync(0xffffffffu, done);
+            if (lane == 0) s_lastmask = m;
         }
         __syncthreads();
+        for (unsigned m = s_lastmask; m; m &= m - 1) {
+            const int bh = b0 + __ffs(m) - 1;
+            const int seg0 = pre[bh], total = pre[bh + 1] - seg0;
+            const int first = seg0 / P, last = (seg0 + total - 1) / P;
+            __threadfence();
+            if (tid == 0) a.ws.counters[bh] = 0;  // every CTA of the segment has arrived
+            merge_staged_to_output<D>(a, bh, a.ws.partial + ((int64_t)first + bh) * wstride,
+                                      last - first + 1, wstride, (float *)base,
+                                      kGW * GG::WARP / 4);
+        }
+        __syncthreads();  // s_lastmask is rewritten by the next batch
     }
     // segments with no rows at all (every head empty) still get an output
     if (blockIdx.x == 0) {
