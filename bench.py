@@ -402,6 +402,152 @@ def cpu_baseline_sample(args, shape, w, summ):
 
 
 # ---------------------------------------------------------------------------
+# our arm on N GPUs: sequence shards
+# ---------------------------------------------------------------------------
+
+def run_sharded(args, rank, world):
+    """Weak scaling over sequence shards: the job decodes ``batch * N``
+    sequences of the workload's context; every sequence's clustered prefix
+    is split into N contiguous shards, one per rank, so each GPU holds as
+    many cache tokens as the single-GPU run.  One step = candidates ->
+    NCCL all-gather of the top-k keys -> select -> attend -> NCCL all-gather
+    of the partials -> merge.  Time = max over ranks of the device time."""
+    import datetime
+    import torch.distributed as dist
+    from santapp_b200.attention import santapp as S
+    from santapp_b200.attention.sharded import ShardedDecodeStep
+    from santapp_b200.synthetic import make_shard_workload, scaled_shape
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    try:
+        base = WORKLOADS[args.workload]
+        shape = scaled_shape(base, batch=base.batch * world,
+                             steps=max(base.steps, args.steps + args.warmup))
+        p = make_shard_workload(shape, rank, world, seed=args.seed, device=dev)
+        summ = S.build_summary(p.keys, p.values, p.labels, p.n_clusters,
+                               sample_end=p.sample_end, n_total=p.n_total)
+        runner = ShardedDecodeStep(p.keys, p.values, summ, num_query_heads=shape.num_query_heads,
+                                   n_total=p.n_total, topk_clusters=shape.topk_clusters,
+                                   samples=p.samples, shard_index=rank, num_shards=world,
+                                   cluster_base=p.cluster_base, seed=args.seed)
+        queries = p.queries
+        flush = L2Flush(dev)
+        torch.cuda.synchronize()
+        dist.barrier()
+        for i in range(args.warmup):
+            flush()
+            runner(queries[i], step=i)
+        torch.cuda.synchronize()
+
+        # per step: events around the step, and on every rank the phase
+        # split (keys | exchange 1 | select | attend | exchange 2 | merge)
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(7)]
+              for _ in range(args.steps)]
+        clocks = ClockSampler(local)
+        clocks.start()
+        dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            st = args.warmup + i
+            flush()
+            e = ev[i]
+            e[0].record()
+            runner.candidates(queries[st], st)
+            e[1].record()
+            runner.exchange_keys()
+            e[2].record()
+            runner.plan()
+            e[3].record()
+            runner.execute()
+            e[4].record()
+            runner.exchange_partials()
+            e[5].record()
+            runner.merge()
+            e[6].record()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        clk = clocks.stop()
+        ph = np.array([[e[j].elapsed_time(e[j + 1]) for j in range(6)] for e in ev])
+        mine = torch.tensor([ph.sum()], dtype=torch.float64, device=dev)
+        dist.all_reduce(mine, op=dist.ReduceOp.MAX)
+        total_ms = float(mine.item())
+        value = shape.batch * args.steps / (total_ms / 1e3)
+        phase = {k: float(v) for k, v in zip(
+            ["keys", "exchange_keys", "select", "attend", "exchange_partials", "merge"],
+            ph.mean(axis=0))}
+
+        # end to end through the public call: pinned q in, merged out back
+        e2e = None
+        if not args.no_e2e:
+            q_host = queries[:args.steps].cpu().pin_memory()
+            out_host = torch.empty(shape.batch, shape.num_query_heads,
+                                   shape.head_dim).pin_memory()
+            q_dev = torch.empty_like(queries[0])
+            dist.barrier()
+            torch.cuda.synchronize()
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            for i in range(args.steps):
+                q_dev.copy_(q_host[i], non_blocking=True)
+                out = runner(q_dev, step=i)
+                out_host.copy_(out, non_blocking=True)
+            s1.record()
+            torch.cuda.synchronize()
+            t = torch.tensor([s0.elapsed_time(s1)], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e = {"value": shape.batch * args.steps / (float(t.item()) / 1e3),
+                   "unit": "tokens/s", "h2d_bytes_per_step": int(q_host[0].numel() * 4),
+                   "d2h_bytes_per_step": int(out_host.numel() * 4),
+                   "api": "santapp_b200.attention.ShardedDecodeStep (ctypes -> santa_shard_* "
+                          "C ABI, NCCL all-gathers)"}
+        peak, peak_kind = peaks()
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16" if shape.kv_dtype == torch.bfloat16 else "f32",
+            "data": "synthetic (seeded Gaussian-mixture keys per shard, N(0,1) values and "
+                    "queries)",
+            "config": {
+                "workload": f"{base.name}-per-gpu-seqshard{world}",
+                "query_heads": shape.num_query_heads, "kv_heads": shape.num_kv_heads,
+                "head_dim": shape.head_dim, "batch": shape.batch, "context": shape.context,
+                "clusters": shape.n_clusters, "topk_clusters": shape.topk_clusters,
+                "samples": shape.samples, "recent_window": shape.recent_window, "mode": "hybrid",
+                "parallelism": f"sequence shards x{world} (NCCL all-gather of top-k keys and "
+                               f"of (m, l, o) partials)",
+                "l2": "flushed before every step outside the events (256 MiB write + 256 MiB "
+                      "read of another buffer)",
+            },
+            "phase_ms": phase,
+            "timing": "CUDA events around each step on every rank, max over ranks of the sum",
+            "wall_s": wall,
+            "clocks": clk,
+            "gpu_launches": runner.kernels_per_call * args.steps,
+            "e2e": e2e,
+            "cpu_baseline": None,
+            "roofline": {"kernel": "decode_attend_gather_kernel", "bound": "hbm",
+                         "achieved": None, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": None, "traffic": None,
+                         "note": "per-kernel roofline is reported by the single-GPU run"},
+        }
+        return line if rank == 0 else None
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
 # reference arm: the CPU restatement on all host cores
 # ---------------------------------------------------------------------------
 
@@ -467,9 +613,10 @@ def main():
         if line is not None:
             print(json.dumps(line), flush=True)
         return
-    if world > 1 or args.gpus > 1:
-        from santapp_b200.parallel_bench import run_sharded
-        line = run_sharded(args, WORKLOADS, METRIC)
+    if world > 1:
+        line = run_sharded(args, rank, world)
+    elif args.gpus > 1:
+        raise SystemExit("--gpus N > 1 runs under torchrun (one process per GPU)")
     else:
         line = run_ours(args, rank, world)
     if line is not None and rank == 0:

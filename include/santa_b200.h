@@ -206,6 +206,86 @@ int santa_decode_select(const SantaGeometry *geo, const SantaDecodeParams *p, co
                         int32_t *n_exact, void *workspace, size_t workspace_bytes,
                         cudaStream_t stream);
 
+/* ---- sequence-sharded decode ------------------------------------------ */
+
+/* The reference decodes on one GPU (README.md:355): these entry points have
+ * no one-to-one counterpart there.  They split santa_decode in HYBRID mode
+ * (santapp.py:365-506 with the exact top-k clusters plus uniform samples of
+ * the rest) over contiguous shards of every sequence's clustered prefix, one
+ * shard per rank, around two small exchanges that the caller runs (NCCL
+ * all-gathers):
+ *
+ *   1. santa_shard_candidates: this shard's top-k cluster keys per
+ *      (sequence, query head).  Exchange 1 gathers them from every shard.
+ *   2. santa_shard_plan: every rank takes the same global top-k from the
+ *      gathered keys and selects the local clusters among them; samples
+ *      are drawn from this shard's non-selected tokens (the caller splits
+ *      the sample budget across shards in proportion to their token counts,
+ *      and each sample carries the weight n_rest_shard / samples_shard of
+ *      stratified sampling).
+ *   3. santa_shard_execute: the gather attention over the shard's rows,
+ *      written as an unnormalised partial per (sequence, query head).
+ *      Exchange 2 gathers the partials.
+ *   4. santa_merge_shards: LSE merge of the gathered partials into out, lse
+ *      and ess, identical on every rank.
+ *
+ * A cluster's global id is cluster_base + its row in this shard's summary;
+ * shards list their clusters in increasing global id, so the ranking (guess
+ * descending, lowest global id first on ties) is the one santa_decode applies
+ * to the concatenated summary.  The recent window [sample_end, n_total) lives
+ * on one shard (the caller gives the others n_total == sample_end).  bf16
+ * caches only; geometry, params, summary and workspace as for santa_decode
+ * (santa_decode_workspace_bytes). */
+#define SANTA_MAX_SHARDS 32
+#define SANTA_SHARD_MAX_KEYS 512 /* num_shards * topk_clusters */
+#define SANTA_PARTIAL_FLOATS(head_dim) ((head_dim) + 8)
+
+typedef struct SantaShard {
+    int32_t shard_index;         /* this rank's shard, < num_shards */
+    int32_t num_shards;          /* <= SANTA_MAX_SHARDS */
+    int32_t cluster_base;        /* global id of row 0 of this shard's summary */
+    int32_t reserved;
+    const uint64_t *candidates;  /* plan: [num_shards][B*Hq][topk_clusters] gathered keys */
+} SantaShard;
+
+/* Candidate keys: [B*Hq][topk_clusters] uint64, per row descending, key =
+ * (order-preserving bits of the fp32 guess) << 32 | (0xFFFFFFFF - global id),
+ * 0 where the shard has fewer clusters. */
+int santa_shard_candidates(const SantaGeometry *geo, const SantaDecodeParams *p, const float *q,
+                           const void *key_cache, const void *value_cache,
+                           const SantaSummary *summary, const SantaShard *shard, uint64_t *keys,
+                           void *workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* Selection and draws of this shard under the global top-k of
+ * shard->candidates; sample_a as for santa_decode (ranks in [0, n_rest) of
+ * this shard) when sample_source is SANTA_SAMPLES_INJECTED. */
+int santa_shard_plan(const SantaGeometry *geo, const SantaDecodeParams *p, const float *q,
+                     const void *key_cache, const void *value_cache, const SantaSummary *summary,
+                     const SantaShard *shard, const int32_t *sample_a, int32_t *n_exact,
+                     void *workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* partial: [B*Hq][SANTA_PARTIAL_FLOATS(head_dim)] fp32: m (log2 units), l,
+ * ms, e1, e2, samples, 0, 0, then o[head_dim] = sum 2^(lw - m) v; l = sum
+ * 2^(lw - m); ms, e1, e2 the same sums over the sample weights alone. */
+int santa_shard_execute(const SantaGeometry *geo, const SantaDecodeParams *p, const float *q,
+                        const void *key_cache, const void *value_cache,
+                        const SantaSummary *summary, float *partial, void *workspace,
+                        size_t workspace_bytes, cudaStream_t stream);
+
+/* Selection readout of santa_shard_plan (arguments of santa_decode_select). */
+int santa_shard_select(const SantaGeometry *geo, const SantaDecodeParams *p, const float *q,
+                       const void *key_cache, const void *value_cache,
+                       const SantaSummary *summary, const SantaShard *shard,
+                       const int32_t *sample_a, uint8_t *selected, int32_t *sample_rows,
+                       int32_t *n_exact, void *workspace, size_t workspace_bytes,
+                       cudaStream_t stream);
+
+/* partials: [num_shards][rows][SANTA_PARTIAL_FLOATS(head_dim)]; rows = B*Hq.
+ * out [rows][head_dim], lse [rows] (natural log) and ess [rows] (may be
+ * NULL) as santa_decode writes them. */
+int santa_merge_shards(int32_t rows, int32_t head_dim, int32_t num_shards, const float *partials,
+                       float *out, float *lse, float *ess, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

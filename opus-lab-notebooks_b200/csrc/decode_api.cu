@@ -98,6 +98,11 @@ static int prepare_decode(const SantaGeometry *geo, const SantaDecodeParams *p, 
     a->n_exact = nullptr;
     a->ess = nullptr;
     a->nsplit = nsplit;
+    a->cluster_base = 0;
+    a->num_shards = 1;
+    a->cand_out = nullptr;
+    a->shard_cands = nullptr;
+    a->part_out = nullptr;
     decode_ws_layout(BH, summary->max_groups, geo->group, p->samples,
                      attend_partial_slots(geo, nsplit), geo->head_dim, geo->sample_end,
                      (char *)workspace, &a->ws);
@@ -167,4 +172,108 @@ extern "C" int santa_decode_select(const SantaGeometry *geo, const SantaDecodePa
     st = launch_plan(a, stream);
     if (st) return st;
     return launch_expand(a, selected, sample_rows, stream);
+}
+
+// ---------------------------------------------------------------------------
+// sequence shards (HYBRID, bf16 caches)
+// ---------------------------------------------------------------------------
+static int check_shard(const SantaGeometry *geo, const SantaDecodeParams *p,
+                       const SantaShard *shard, bool need_candidates) {
+    if (!geo || !p || !shard) return SANTA_ERR_INVALID_ARGUMENT;
+    if (p->mode != SANTA_MODE_HYBRID || geo->kv_dtype != SANTA_DTYPE_BF16)
+        return SANTA_ERR_UNSUPPORTED;
+    if (shard->num_shards < 1 || shard->num_shards > SANTA_MAX_SHARDS) return SANTA_ERR_INVALID_ARGUMENT;
+    if (shard->shard_index < 0 || shard->shard_index >= shard->num_shards)
+        return SANTA_ERR_INVALID_ARGUMENT;
+    if (shard->cluster_base < 0) return SANTA_ERR_INVALID_ARGUMENT;
+    if (p->topk_clusters < 1 || (int64_t)p->topk_clusters * shard->num_shards > SANTA_SHARD_MAX_KEYS)
+        return SANTA_ERR_UNSUPPORTED;
+    if (need_candidates && !shard->candidates) return SANTA_ERR_INVALID_ARGUMENT;
+    return SANTA_OK;
+}
+
+static int prepare_shard(const SantaGeometry *geo, const SantaDecodeParams *p, const float *q,
+                         const void *key_cache, const void *value_cache,
+                         const SantaSummary *summary, const SantaShard *shard,
+                         const int32_t *sample_a, bool need_candidates, bool need_draws,
+                         void *workspace, size_t ws_bytes, DecodeArgs *a) {
+    int st = check_shard(geo, p, shard, need_candidates);
+    if (st) return st;
+    st = prepare_decode(geo, p, q, key_cache, value_cache, summary, sample_a, nullptr, need_draws,
+                        workspace, ws_bytes, a);
+    if (st) return st;
+    if ((int64_t)shard->cluster_base + summary->max_groups >= 0xFFFFFFFFll)
+        return SANTA_ERR_INVALID_ARGUMENT;
+    a->cluster_base = shard->cluster_base;
+    a->num_shards = shard->num_shards;
+    a->shard_cands = need_candidates ? shard->candidates : nullptr;
+    return SANTA_OK;
+}
+
+extern "C" int santa_shard_candidates(const SantaGeometry *geo, const SantaDecodeParams *p,
+                                      const float *q, const void *key_cache,
+                                      const void *value_cache, const SantaSummary *summary,
+                                      const SantaShard *shard, uint64_t *keys, void *workspace,
+                                      size_t workspace_bytes, cudaStream_t stream) {
+    if (!keys) return SANTA_ERR_INVALID_ARGUMENT;
+    DecodeArgs a;
+    int st = prepare_shard(geo, p, q, key_cache, value_cache, summary, shard, nullptr, false,
+                           false, workspace, workspace_bytes, &a);
+    if (st) return st;
+    a.cand_out = keys;
+    return launch_plan(a, stream);
+}
+
+extern "C" int santa_shard_plan(const SantaGeometry *geo, const SantaDecodeParams *p,
+                                const float *q, const void *key_cache, const void *value_cache,
+                                const SantaSummary *summary, const SantaShard *shard,
+                                const int32_t *sample_a, int32_t *n_exact, void *workspace,
+                                size_t workspace_bytes, cudaStream_t stream) {
+    DecodeArgs a;
+    int st = prepare_shard(geo, p, q, key_cache, value_cache, summary, shard, sample_a, true, true,
+                           workspace, workspace_bytes, &a);
+    if (st) return st;
+    a.n_exact = n_exact;
+    return launch_plan(a, stream);
+}
+
+extern "C" int santa_shard_execute(const SantaGeometry *geo, const SantaDecodeParams *p,
+                                   const float *q, const void *key_cache,
+                                   const void *value_cache, const SantaSummary *summary,
+                                   float *partial, void *workspace, size_t workspace_bytes,
+                                   cudaStream_t stream) {
+    if (!partial) return SANTA_ERR_INVALID_ARGUMENT;
+    if (!p || p->mode != SANTA_MODE_HYBRID || !geo || geo->kv_dtype != SANTA_DTYPE_BF16)
+        return SANTA_ERR_UNSUPPORTED;
+    DecodeArgs a;
+    int st = prepare_decode(geo, p, q, key_cache, value_cache, summary, nullptr, nullptr, false,
+                            workspace, workspace_bytes, &a);
+    if (st) return st;
+    a.part_out = partial;
+    return launch_execute(a, stream);
+}
+
+extern "C" int santa_shard_select(const SantaGeometry *geo, const SantaDecodeParams *p,
+                                  const float *q, const void *key_cache, const void *value_cache,
+                                  const SantaSummary *summary, const SantaShard *shard,
+                                  const int32_t *sample_a, uint8_t *selected,
+                                  int32_t *sample_rows, int32_t *n_exact, void *workspace,
+                                  size_t workspace_bytes, cudaStream_t stream) {
+    DecodeArgs a;
+    int st = prepare_shard(geo, p, q, key_cache, value_cache, summary, shard, sample_a, true, true,
+                           workspace, workspace_bytes, &a);
+    if (st) return st;
+    a.n_exact = n_exact;
+    st = launch_plan(a, stream);
+    if (st) return st;
+    return launch_expand(a, selected, sample_rows, stream);
+}
+
+extern "C" int santa_merge_shards(int32_t rows, int32_t head_dim, int32_t num_shards,
+                                  const float *partials, float *out, float *lse, float *ess,
+                                  cudaStream_t stream) {
+    if (rows <= 0 || num_shards < 1 || num_shards > SANTA_MAX_SHARDS) return SANTA_ERR_INVALID_ARGUMENT;
+    if (head_dim != 64 && head_dim != 128) return SANTA_ERR_UNSUPPORTED;
+    if (!partials || !out) return SANTA_ERR_INVALID_ARGUMENT;
+    return launch_merge_shards(rows, head_dim, num_shards, partials, out, lse, ess, stream);
 }

@@ -261,6 +261,21 @@ __device__ void merge_staged_to_output(const DecodeArgs &a, int bh, const float 
         if (i < g * D) {
             const int hh = i / D, dd = i - hh * D;
             const int64_t oh = (int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g + hh;
+            if (a.part_out) {  // sequence shard: the unnormalised partial
+                float *po = a.part_out + oh * PSTR;
+                po[8 + dd] = acc[k];
+                if (dd == 0) {
+                    po[0] = M[k];
+                    po[1] = L[k];
+                    po[2] = MS[k];
+                    po[3] = E1[k];
+                    po[4] = E2[k];
+                    po[5] = (float)a.ws.head_meta[((int64_t)bh * 8 + hh) * 2 + 1];
+                    po[6] = 0.f;
+                    po[7] = 0.f;
+                }
+                continue;
+            }
             a.out[oh * D + dd] = L[k] > 0.f ? acc[k] / L[k] : 0.f;
             if (dd == 0) {
                 if (a.lse) a.lse[oh] = L[k] > 0.f ? (M[k] + log2f(L[k])) * kLn2 : -INFINITY;
@@ -711,6 +726,12 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
             for (int i = tid; i < g * D; i += kGThreads) {
                 const int h = i / D, d = i - h * D;
                 const int64_t oh = (int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g + h;
+                if (a.part_out) {
+                    float *po = a.part_out + oh * PSTR;
+                    po[8 + d] = 0.f;
+                    if (d < 8) po[d] = (d == 0 || d == 2) ? -INFINITY : 0.f;
+                    continue;
+                }
                 a.out[oh * D + d] = 0.f;
                 if (d == 0) {
                     if (a.lse) a.lse[oh] = -INFINITY;

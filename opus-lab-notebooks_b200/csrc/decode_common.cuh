@@ -114,6 +114,12 @@ struct DecodeArgs {
     float *ess;
     int nsplit;   // SIMT attend: CTAs per segment
     DecodeWs ws;
+    // sequence shards (HYBRID): global cluster id = cluster_base + cluster row
+    int cluster_base;
+    int num_shards;
+    uint64_t *cand_out;           // select: write the local top-k keys and stop
+    const uint64_t *shard_cands;  // select: [num_shards][B*Hq][k] keys -> global top-k
+    float *part_out;              // attend: unnormalised partial per (b, query head)
 };
 
 // ---------------------------------------------------------------------------
@@ -369,5 +375,7 @@ int launch_execute(DecodeArgs &a, cudaStream_t stream);
 int launch_expand(DecodeArgs &a, uint8_t *selected, int32_t *sample_rows, cudaStream_t stream);
 int num_sms();
 int attend_partial_slots(const SantaGeometry *geo, int nsplit);
+int launch_merge_shards(int rows, int head_dim, int num_shards, const float *partials, float *out,
+                        float *lse, float *ess, cudaStream_t stream);
 
 }  // namespace santa

@@ -69,6 +69,8 @@ struct SelSmem {
     static_assert(CT_FLOATS >= SANTA_MAX_GROUP * MAXG,
                   "the centroid area also holds the guided CDF");
     static_assert(CT_FLOATS >= 3 * MAXG, "the centroid area also holds the union entries");
+    static_assert(CT_FLOATS * 4 >= SANTA_MAX_GROUP * SANTA_SHARD_MAX_KEYS * 8,
+                  "the centroid area also holds the gathered shard keys");
 };
 
 __device__ __forceinline__ void cp_async4(void *dst_smem, const void *src) {
@@ -222,6 +224,20 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
     __syncthreads();
 
     // ---- 3. ranking (TOPK / HYBRID): warp per query head, per-lane sorted keys ----
+    // key = order bits of the guess << 32 | ~(global cluster id): descending
+    // keys rank by guess, lowest id first on ties
+    const int cbase = a.cluster_base;
+    const int kk = a.p.topk_clusters;  // HYBRID: candidate keys per (b, query head)
+    uint64_t *cand_s = (uint64_t *)ct;  // sharded plan: [g][num_shards][kk], in the free tile area
+    if (a.shard_cands) {
+        const int NS = a.num_shards, per = NS * kk;
+        const int64_t rows = (int64_t)a.geo.batch * a.geo.num_kv_heads * g;
+        for (int i = tid; i < g * per; i += kSelThreads) {
+            const int h = i / per, r = (i - h * per) / kk, j = i - h * per - r * kk;
+            cand_s[i] = a.shard_cands[((int64_t)r * rows + (int64_t)bh * g + h) * kk + j];
+        }
+        __syncthreads();
+    }
     if ((mode == SANTA_MODE_TOPK || mode == SANTA_MODE_HYBRID) && warp < g) {
         const int h = warp;
         uint64_t key[KPL];
@@ -229,7 +245,7 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
         for (int j = 0; j < KPL; ++j) {
             const int c = lane + 32 * j;
             key[j] = c < n_groups ? (((uint64_t)float_order_key(guess_s[h * Gmax + c]) << 32) |
-                                     (uint64_t)(0xFFFFFFFFu - (uint32_t)c))
+                                     (uint64_t)(0xFFFFFFFFu - (uint32_t)(c + cbase)))
                                   : 0ull;
         }
         // bitonic sort, descending, entirely in registers
@@ -253,12 +269,47 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
         }
         const int kmax = (mode == SANTA_MODE_HYBRID) ? min(a.p.topk_clusters, n_groups) : n_groups;
         int nsel = 0, exact = 0;
-        while (nsel < kmax) {
+        if (a.shard_cands) {
+            // global k-th best key: k rounds of a merge of the shards'
+            // descending lists (lane r walks shard r's list; keys are unique)
+            const uint64_t *cl = cand_s + (int64_t)h * a.num_shards * kk;
+            int ptr = 0;
+            uint64_t thr = 1ull;  // fewer than k keys in all: every real key passes
+            for (int it = 0; it < kk; ++it) {
+                const uint64_t v = (lane < a.num_shards && ptr < kk) ? cl[lane * kk + ptr] : 0ull;
+                const uint32_t vh = (uint32_t)(v >> 32);
+                const uint32_t mh = __reduce_max_sync(0xffffffffu, vh);
+                const uint32_t ml = __reduce_max_sync(0xffffffffu, vh == mh ? (uint32_t)v : 0u);
+                if (mh == 0u && ml == 0u) break;
+                thr = ((uint64_t)mh << 32) | ml;
+                if (v == thr) ++ptr;
+            }
+            // local clusters at or above it: a prefix of every lane's sorted keys
+            int cnt = 0;
+#pragma unroll
+            for (int j = 0; j < KPL; ++j) cnt += (key[j] != 0ull && key[j] >= thr) ? 1 : 0;
+            int x = cnt;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, x, o);
+                if (lane >= o) x += y;
+            }
+            int pos = x - cnt;
+#pragma unroll
+            for (int j = 0; j < KPL; ++j)
+                if (j < cnt)
+                    gapcum[h * (2 * kcap + 1) + pos++] =
+                        (int)(0xFFFFFFFFu - (uint32_t)key[j]) - cbase;
+            nsel = __shfl_sync(0xffffffffu, x, 31);
+        }
+        while (!a.shard_cands && nsel < kmax) {
             const uint32_t bhi = (uint32_t)(key[0] >> 32);
             const uint32_t mhi = __reduce_max_sync(0xffffffffu, bhi);
             const uint32_t mlo = __reduce_max_sync(0xffffffffu, bhi == mhi ? (uint32_t)key[0] : 0u);
             if (mhi == 0u && mlo == 0u) break;  // no cluster left
-            const int c = (int)(0xFFFFFFFFu - mlo);
+            const int c = (int)(0xFFFFFFFFu - mlo) - cbase;
+            if (a.cand_out && lane == 0)
+                a.cand_out[((int64_t)bh * g + h) * kk + nsel] = ((uint64_t)mhi << 32) | mlo;
             if (lane == (c & 31)) {
 #pragma unroll
                 for (int j = 0; j + 1 < KPL; ++j) key[j] = key[j + 1];
@@ -293,6 +344,12 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
         }
     }
     __syncthreads();
+    if (a.cand_out) {  // shard candidates only: pad the key lists and stop
+        if (warp < g)
+            for (int j = head_sel[warp] + lane; j < kk; j += 32)
+                a.cand_out[((int64_t)bh * g + warp) * kk + j] = 0ull;
+        return;
+    }
 
     // ---- 4. union of the group's selections (ascending cluster order) ----
     int n_union = 0, U = 0;

@@ -1,0 +1,63 @@
+// SANTA++ decode over sequence shards: the LSE merge of the per-shard
+// partials gathered by exchange 2.
+//
+// Shard r's partial of one (sequence, query head) holds m_r (log2 units),
+// l_r = sum_j 2^(lw_j - m_r) and o_r = sum_j 2^(lw_j - m_r) v_j over the rows
+// the shard attended (its selected clusters, its samples with their
+// stratified weights, the recent window on the shard that holds it).  The
+// estimator over all shards is
+//   out = sum_r 2^(m_r - M) o_r / sum_r 2^(m_r - M) l_r,   M = max_r m_r,
+// the same self-normalised combine as santapp.py:472-506 over the union of
+// the shards' rows.  The ESS sums (santapp.py:481-485) merge the same way.
+#include "decode_common.cuh"
+
+#include <math.h>
+
+namespace santa {
+
+template <int D>
+__global__ void __launch_bounds__(D) merge_shards_kernel(int rows, int num_shards,
+                                                         const float *partials, float *out,
+                                                         float *lse, float *ess) {
+    constexpr int PS = D + 8;
+    const int row = blockIdx.x, d = threadIdx.x;
+    float M = -INFINITY, MS = -INFINITY;
+    for (int r = 0; r < num_shards; ++r) {
+        const float *p = partials + ((int64_t)r * rows + row) * PS;
+        if (p[1] > 0.f) M = fmaxf(M, p[0]);
+        if (p[3] > 0.f) MS = fmaxf(MS, p[2]);
+    }
+    float L = 0.f, acc = 0.f, E1 = 0.f, E2 = 0.f, ns = 0.f;
+    for (int r = 0; r < num_shards; ++r) {
+        const float *p = partials + ((int64_t)r * rows + row) * PS;
+        if (p[1] > 0.f) {
+            const float f = exp2f(p[0] - M);
+            L = fmaf(p[1], f, L);
+            acc = fmaf(p[8 + d], f, acc);
+        }
+        if (p[3] > 0.f) {
+            const float fe = exp2f(p[2] - MS);
+            E1 = fmaf(p[3], fe, E1);
+            E2 = fmaf(p[4], fe * fe, E2);
+        }
+        ns += p[5];
+    }
+    out[(int64_t)row * D + d] = L > 0.f ? acc / L : 0.f;
+    if (d == 0) {
+        if (lse) lse[row] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
+        if (ess) ess[row] = (ns > 0.f && E2 > 0.f) ? (E1 * E1 / E2) / ns : 0.f;
+    }
+}
+
+int launch_merge_shards(int rows, int head_dim, int num_shards, const float *partials, float *out,
+                        float *lse, float *ess, cudaStream_t stream) {
+    if (head_dim == 64)
+        merge_shards_kernel<64><<<rows, 64, 0, stream>>>(rows, num_shards, partials, out, lse, ess);
+    else
+        merge_shards_kernel<128>
+            <<<rows, 128, 0, stream>>>(rows, num_shards, partials, out, lse, ess);
+    SANTA_LAUNCH_CHECK();
+    return SANTA_OK;
+}
+
+}  // namespace santa

@@ -54,6 +54,19 @@ class SantaDecodeParams(ctypes.Structure):
                 ("seed", ctypes.c_uint64), ("step", ctypes.c_uint64), ("num_splits", _i32)]
 
 
+class SantaShard(ctypes.Structure):
+    _fields_ = [("shard_index", _i32), ("num_shards", _i32), ("cluster_base", _i32),
+                ("reserved", _i32), ("candidates", _vp)]
+
+
+MAX_SHARDS = 32
+SHARD_MAX_KEYS = 512
+
+
+def partial_floats(head_dim: int) -> int:
+    return head_dim + 8
+
+
 # Every symbol include/santa_b200.h declares, with its ctypes signature.
 _P = ctypes.POINTER
 SIGNATURES = {
@@ -81,6 +94,19 @@ SIGNATURES = {
     "santa_decode_select": (ctypes.c_int, [_P(SantaGeometry), _P(SantaDecodeParams), _vp, _vp,
                                            _vp, _P(SantaSummary), _vp, _vp, _vp, _vp, _vp, _vp,
                                            ctypes.c_size_t, _vp]),
+    "santa_shard_candidates": (ctypes.c_int, [_P(SantaGeometry), _P(SantaDecodeParams), _vp, _vp,
+                                              _vp, _P(SantaSummary), _P(SantaShard), _vp, _vp,
+                                              ctypes.c_size_t, _vp]),
+    "santa_shard_plan": (ctypes.c_int, [_P(SantaGeometry), _P(SantaDecodeParams), _vp, _vp, _vp,
+                                        _P(SantaSummary), _P(SantaShard), _vp, _vp, _vp,
+                                        ctypes.c_size_t, _vp]),
+    "santa_shard_execute": (ctypes.c_int, [_P(SantaGeometry), _P(SantaDecodeParams), _vp, _vp,
+                                           _vp, _P(SantaSummary), _vp, _vp, ctypes.c_size_t,
+                                           _vp]),
+    "santa_shard_select": (ctypes.c_int, [_P(SantaGeometry), _P(SantaDecodeParams), _vp, _vp,
+                                          _vp, _P(SantaSummary), _P(SantaShard), _vp, _vp, _vp,
+                                          _vp, _vp, ctypes.c_size_t, _vp]),
+    "santa_merge_shards": (ctypes.c_int, [_i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
 }
 
 _lock = threading.Lock()

@@ -1,0 +1,229 @@
+"""Sequence-sharded SANTA++ decode (hybrid estimator) over torch.distributed.
+
+The reference decodes on one GPU (santapp_ruler README.md:355).  For long
+contexts this module splits every sequence's clustered prefix ``[0,
+sample_end)`` into contiguous shards, one per rank (one process per GPU).
+Each shard clusters its own tokens, so a shard's summary lists its own
+clusters and the cluster with row ``c`` on shard ``r`` has the global id
+``cluster_base(r) + c``.  The recent window ``[sample_end, n_total)`` is
+held by the last shard.  A decode step is
+
+1. ``santa_shard_candidates``: each shard's top-k keys per (sequence, query
+   head) (guess = log n + c.q*scale as in santapp.py:397-400, ranked
+   descending with the lowest global id first on ties);
+2. exchange 1: an all-gather of the keys (``B*Hq*k`` uint64 per rank);
+3. ``santa_shard_plan``: every rank takes the same global top-k and selects
+   its local clusters among them; it draws its share of the uniform samples
+   from its own non-selected tokens (stratified: a sample of shard r weighs
+   ``n_rest_r / samples_r``);
+4. ``santa_shard_execute``: the gather attention over the shard's rows into
+   an unnormalised partial ``(m, l, o)`` per (sequence, query head);
+5. exchange 2: an all-gather of the partials (``B*Hq*(D+8)`` fp32 per rank);
+6. ``santa_merge_shards``: the LSE merge, identical on every rank.
+
+Both exchanges move a few hundred KB; the collectives are NCCL all-gathers
+on the ranks' own buffers (remote data lands in local memory before any
+kernel reads it).  ``ShardExchange`` holds the host logic (shard bounds,
+sample split, Philox seeds, exchange buffers and order) apart from the
+kernel calls, so that it can be checked on CPU ranks.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from .. import _lib
+from .santapp import ClusterSummary, _geometry, _require_cuda, decode_params
+
+__all__ = ["shard_bounds", "split_counts", "shard_seed", "ShardExchange", "ShardedDecodeStep"]
+
+_GOLDEN = 0x9E3779B97F4A7C15
+
+
+def shard_bounds(n: int, num_shards: int) -> list[tuple[int, int]]:
+    """Contiguous ``[start, end)`` shards of ``[0, n)``; sizes differ by at
+    most one, the larger ones first."""
+    if num_shards < 1 or n < num_shards:
+        raise ValueError(f"cannot split {n} tokens into {num_shards} non-empty shards")
+    base, extra = divmod(n, num_shards)
+    out, s = [], 0
+    for r in range(num_shards):
+        e = s + base + (1 if r < extra else 0)
+        out.append((s, e))
+        s = e
+    return out
+
+
+def split_counts(total: int, weights) -> list[int]:
+    """Integers proportional to ``weights`` that sum to ``total`` (largest
+    remainder; ties go to the lower index)."""
+    weights = [int(w) for w in weights]
+    wsum = sum(weights)
+    if wsum <= 0:
+        raise ValueError("weights must have a positive sum")
+    exact = [total * w / wsum for w in weights]
+    out = [int(math.floor(x)) for x in exact]
+    left = total - sum(out)
+    order = sorted(range(len(weights)), key=lambda i: (-(exact[i] - out[i]), i))
+    for i in order[:left]:
+        out[i] += 1
+    return out
+
+
+def shard_seed(seed: int, shard: int) -> int:
+    """Philox key of shard ``shard``: independent draw streams per shard."""
+    return (int(seed) + int(shard) * _GOLDEN) & 0xFFFFFFFFFFFFFFFF
+
+
+class ShardExchange:
+    """Exchange buffers and collectives of one rank (kernel calls elsewhere).
+
+    ``group`` is a torch.distributed process group (or None with
+    ``num_shards == 1``); the all-gathers run on the current stream."""
+
+    def __init__(self, *, rows: int, topk: int, head_dim: int, shard_index: int,
+                 num_shards: int, device, group=None):
+        if not 0 <= shard_index < num_shards:
+            raise ValueError("shard_index out of range")
+        if num_shards > _lib.MAX_SHARDS or topk * num_shards > _lib.SHARD_MAX_KEYS:
+            raise ValueError(f"{num_shards} shards x top-{topk} exceeds the candidate key limit "
+                             f"({_lib.SHARD_MAX_KEYS})")
+        self.rows, self.topk, self.head_dim = rows, topk, head_dim
+        self.shard_index, self.num_shards, self.group = shard_index, num_shards, group
+        pf = _lib.partial_floats(head_dim)
+        self.keys = torch.zeros(rows * topk, dtype=torch.int64, device=device)
+        self.all_keys = torch.zeros(num_shards, rows * topk, dtype=torch.int64, device=device)
+        self.partial = torch.zeros(rows, pf, dtype=torch.float32, device=device)
+        self.all_partials = torch.zeros(num_shards, rows, pf, dtype=torch.float32, device=device)
+
+    def _all_gather(self, out: torch.Tensor, inp: torch.Tensor) -> None:
+        if self.num_shards == 1:
+            out[0].copy_(inp)
+            return
+        import torch.distributed as dist
+        if not dist.is_initialized():
+            raise RuntimeError("sharded decode over several ranks needs torch.distributed")
+        dist.all_gather_into_tensor(out.view(-1), inp.reshape(-1), group=self.group)
+
+    def exchange_keys(self) -> torch.Tensor:
+        """Exchange 1: every shard's candidate keys, shard-major."""
+        self._all_gather(self.all_keys, self.keys)
+        return self.all_keys
+
+    def exchange_partials(self) -> torch.Tensor:
+        """Exchange 2: every shard's partials, shard-major."""
+        self._all_gather(self.all_partials, self.partial)
+        return self.all_partials
+
+
+class ShardedDecodeStep(ShardExchange):
+    """One rank's sequence shard of a hybrid SANTA++ decode step.
+
+    key_cache / value_cache: ``[B, Hkv, capacity, D]`` bf16 cache of this
+    shard's tokens (its old-prefix slice, plus the recent window on the last
+    shard); ``summary`` this shard's cluster summary (local cluster rows,
+    ``sample_end`` = the shard's old-prefix length); ``n_total`` the shard's
+    token count; ``samples`` this shard's share of the per-head sample budget
+    (``split_counts`` of the budget by shard token counts)."""
+
+    def __init__(self, key_cache: torch.Tensor, value_cache: torch.Tensor,
+                 summary: ClusterSummary, *, num_query_heads: int, n_total: int,
+                 topk_clusters: int, samples: int, shard_index: int, num_shards: int,
+                 cluster_base: int, group=None, scale: float | None = None, seed: int = 0,
+                 injected: bool = False):
+        _require_cuda("key_cache", key_cache)
+        _require_cuda("value_cache", value_cache)
+        if key_cache.dtype != torch.bfloat16:
+            raise ValueError("sharded decode runs on bf16 caches")
+        B, Hkv, _, D = key_cache.shape
+        super().__init__(rows=B * num_query_heads, topk=topk_clusters, head_dim=D,
+                         shard_index=shard_index, num_shards=num_shards,
+                         device=key_cache.device, group=group)
+        self.key_cache, self.value_cache, self.summary = key_cache, value_cache, summary
+        self.geo = _geometry(key_cache, num_query_heads, n_total, summary.sample_end)
+        self.scale = 1.0 / math.sqrt(D) if scale is None else scale
+        self.p = decode_params("hybrid", topk_clusters=topk_clusters, samples=samples,
+                               scale=self.scale, injected=injected,
+                               seed=shard_seed(seed, shard_index))
+        self.c = summary.as_c()
+        self.lib = _lib.load()
+        self.shard = _lib.SantaShard(shard_index, num_shards, int(cluster_base), 0,
+                                     self.all_keys.data_ptr())
+        nbytes = ctypes.c_size_t()
+        _lib.check("santa_decode_workspace_bytes", self.lib.santa_decode_workspace_bytes(
+            ctypes.byref(self.geo), ctypes.byref(self.p), summary.max_groups,
+            ctypes.byref(nbytes)))
+        self.ws_bytes = nbytes.value
+        dev = key_cache.device
+        self.ws = torch.empty(max(1, self.ws_bytes), dtype=torch.uint8, device=dev)
+        self.out = torch.empty(B, num_query_heads, D, dtype=torch.float32, device=dev)
+        self.lse = torch.empty(B, num_query_heads, dtype=torch.float32, device=dev)
+        self.ess = torch.empty(B, num_query_heads, dtype=torch.float32, device=dev)
+        self._q = None
+        self._refs = (ctypes.byref(self.geo), ctypes.byref(self.p), ctypes.byref(self.c),
+                      ctypes.byref(self.shard))
+
+    # ---- the kernel calls -------------------------------------------------
+    def candidates(self, q: torch.Tensor, step: int = 0, stream=None) -> torch.Tensor:
+        self.p.step = int(step) & 0xFFFFFFFFFFFFFFFF
+        self._q = q
+        g, p, c, s = self._refs
+        _lib.check("santa_shard_candidates", self.lib.santa_shard_candidates(
+            g, p, q.data_ptr(), self.key_cache.data_ptr(), self.value_cache.data_ptr(), c, s,
+            self.keys.data_ptr(), self.ws.data_ptr(), self.ws_bytes,
+            _lib.stream_handle(stream)))
+        return self.keys
+
+    def plan(self, sample_a: torch.Tensor | None = None, n_exact: torch.Tensor | None = None,
+             stream=None) -> None:
+        g, p, c, s = self._refs
+        _lib.check("santa_shard_plan", self.lib.santa_shard_plan(
+            g, p, self._q.data_ptr(), self.key_cache.data_ptr(), self.value_cache.data_ptr(),
+            c, s, _lib.ptr(sample_a), _lib.ptr(n_exact), self.ws.data_ptr(), self.ws_bytes,
+            _lib.stream_handle(stream)))
+
+    def execute(self, stream=None) -> torch.Tensor:
+        g, p, c, _ = self._refs
+        _lib.check("santa_shard_execute", self.lib.santa_shard_execute(
+            g, p, self._q.data_ptr(), self.key_cache.data_ptr(), self.value_cache.data_ptr(),
+            c, self.partial.data_ptr(), self.ws.data_ptr(), self.ws_bytes,
+            _lib.stream_handle(stream)))
+        return self.partial
+
+    def merge(self, stream=None) -> torch.Tensor:
+        _lib.check("santa_merge_shards", self.lib.santa_merge_shards(
+            self.rows, self.head_dim, self.num_shards, self.all_partials.data_ptr(),
+            self.out.data_ptr(), self.lse.data_ptr(), self.ess.data_ptr(),
+            _lib.stream_handle(stream)))
+        return self.out
+
+    def select(self, sample_a: torch.Tensor | None = None):
+        """Selection readout of the plan (after exchange 1): ``(selected
+        [B, Hq, G_local] uint8, sample_rows [B, Hq, samples] int32, n_exact)``."""
+        B, Hq = self.out.shape[:2]
+        dev = self.out.device
+        sel = torch.zeros(B, Hq, self.summary.max_groups, dtype=torch.uint8, device=dev)
+        rows = torch.full((B, Hq, max(1, self.p.samples)), -1, dtype=torch.int32, device=dev)
+        n_exact = torch.zeros(B, Hq, dtype=torch.int32, device=dev)
+        g, p, c, s = self._refs
+        _lib.check("santa_shard_select", self.lib.santa_shard_select(
+            g, p, self._q.data_ptr(), self.key_cache.data_ptr(), self.value_cache.data_ptr(),
+            c, s, _lib.ptr(sample_a), sel.data_ptr(), rows.data_ptr(), n_exact.data_ptr(),
+            self.ws.data_ptr(), self.ws_bytes, _lib.stream_handle(None)))
+        return sel, rows[..., : self.p.samples], n_exact
+
+    # ---- one decode step --------------------------------------------------
+    def __call__(self, q: torch.Tensor, step: int = 0, sample_a: torch.Tensor | None = None):
+        """The whole step on the current stream; returns ``out [B, Hq, D]``
+        (identical on every rank)."""
+        self.candidates(q, step)
+        self.exchange_keys()
+        self.plan(sample_a)
+        self.execute()
+        self.exchange_partials()
+        return self.merge()
+
+    kernels_per_call = 4  # candidates, select, attend, merge

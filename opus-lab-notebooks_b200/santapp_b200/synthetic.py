@@ -135,3 +135,63 @@ def tensor_digest(*tensors: torch.Tensor) -> str:
             t = t.view(torch.int16)
         h.update(t.numpy().tobytes())
     return h.hexdigest()
+
+
+@dataclass
+class ShardWorkload:
+    """One sequence shard of a decode workload (see ``make_shard_workload``)."""
+
+    keys: torch.Tensor        # [B, Hkv, n_total, D] this shard's tokens
+    values: torch.Tensor
+    labels: torch.Tensor      # [B, Hkv, sample_end] local cluster of each old token
+    queries: torch.Tensor     # [steps, B, Hq, D] fp32, identical on every shard
+    sample_end: int           # this shard's old-prefix tokens
+    n_total: int              # sample_end (+ the recent window on the last shard)
+    n_clusters: int           # this shard's clusters per (sequence, KV head)
+    cluster_base: int         # global id of its cluster 0
+    samples: int              # its share of the per-head sample budget
+
+
+def make_shard_workload(shape: DecodeShape, shard_index: int, num_shards: int, seed: int = 0,
+                        device: str | torch.device = "cpu") -> ShardWorkload:
+    """Shard ``shard_index`` of ``num_shards`` contiguous sequence shards.
+
+    The old prefix ``[0, sample_end)`` of every sequence is split into
+    contiguous shards; shard r holds its slice plus, on the last shard, the
+    recent window.  The Gaussian mixture's ``true_clusters`` components are
+    split across the shards too (a shard's tokens come from its own
+    components, which are its clusters), and so is the sample budget, in
+    proportion to the shards' token counts.  Each shard draws its cache from
+    its own generator (seed, shard); the queries come from a generator seeded
+    with ``seed`` alone, so every rank sees the same queries."""
+    from .attention.sharded import shard_bounds, split_counts
+    bounds = shard_bounds(shape.sample_end, num_shards)
+    sizes = [e - s for s, e in bounds]
+    clusters = split_counts(shape.true_clusters, [1] * num_shards)
+    if min(clusters) < 1:
+        raise ValueError("fewer mixture components than shards")
+    r = shard_index
+    old = sizes[r]
+    n_total = old + (shape.recent_window if r == num_shards - 1 else 0)
+    G = clusters[r]
+    B, H, D = shape.batch, shape.num_kv_heads, shape.head_dim
+    gen = torch.Generator(device=device)
+    gen.manual_seed(int(seed) * 1_000_003 + 1 + r)
+    f32 = torch.float32
+    centers = torch.randn(B, H, G, D, generator=gen, device=device, dtype=f32)
+    assign = torch.randint(0, G, (B, H, n_total), generator=gen, device=device)
+    keys = torch.gather(centers, 2, assign[..., None].expand(B, H, n_total, D))
+    keys.add_(torch.randn(B, H, n_total, D, generator=gen, device=device, dtype=f32),
+              alpha=shape.sigma)
+    values = torch.randn(B, H, n_total, D, generator=gen, device=device, dtype=f32)
+    qgen = torch.Generator(device=device)
+    qgen.manual_seed(int(seed))
+    queries = torch.randn(shape.steps, B, shape.num_query_heads, D, generator=qgen,
+                          device=device, dtype=f32)
+    if shape.query_scale != 1.0:
+        queries.mul_(shape.query_scale)
+    return ShardWorkload(
+        keys=keys.to(shape.kv_dtype), values=values.to(shape.kv_dtype),
+        labels=assign[:, :, :old].to(torch.int32).contiguous(), queries=queries,
+        sample_end=old, n_total=n_total, n_clusters=G, cluster_base=sum(clusters[:r]),
+        samples=split_counts(shape.samples, sizes)[r])

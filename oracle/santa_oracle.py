@@ -22,6 +22,10 @@ What it restates (reference = santapp-ruler-bench/src/santapp_ruler):
   santapp.py:397-401) and the recent window, plus uniform importance samples
   over the remaining old-prefix tokens with ``log r = -log(n_rest)`` (the
   uniform-mode weight of santapp.py:463-467 and the combine of 472-506).
+* ``decode_hybrid_sharded`` the same estimator over contiguous sequence
+  shards: one global top-k over all shards' clusters (``shard_topk``) and
+  the sample budget stratified over the shards (the reference itself is
+  single-GPU; this is the sharded decode's definition).
 * ``prefill_causal`` dense causal softmax attention (santapp.py:337-346 calls
   torch SDPA with is_causal=True).
 
@@ -482,6 +486,152 @@ def decode_hybrid(q, K, V, summary: Summary, sample_end, topk, ranks, scale) -> 
     out, lse, ess = _combine(q, K, V, scale, exact_idx, samp_idx, logr,
                              _recent(sample_end, K.shape[0]))
     return DecodeResult(out, lse, int(exact_idx.size), int(samp_idx.size), ess, sel, samp_idx)
+
+
+# ---------------------------------------------------------------------------
+# hybrid decode over sequence shards
+# ---------------------------------------------------------------------------
+
+def shard_topk(summaries, q, scale, k, bases) -> list:
+    """Global top-k over the clusters of all shards (cluster row c of shard r
+    has global id bases[r] + c): guess descending, lowest global id first on
+    ties, the ranking of select_topk over the concatenated clusters.  Returns
+    the selected local rows of every shard, ascending."""
+    keys = []
+    for r, s in enumerate(summaries):
+        gs = centroid_guess(s, q, scale)
+        keys += [(float(gs[c]), int(bases[r]) + c, r, c) for c in range(s.num_groups)]
+    keys.sort(key=lambda t: (-t[0], t[1]))
+    top = keys[:k]
+    return [np.array(sorted(c for (_, _, rr, c) in top if rr == r), np.int64)
+            for r in range(len(summaries))]
+
+
+def order_key(f) -> int:
+    """Order-preserving 32-bit image of an fp32 value (-0 taken as +0)."""
+    b = int(np.float32(np.float32(f) + np.float32(0.0)).view(np.uint32))
+    return (~b & 0xFFFFFFFF) if b & 0x80000000 else (b | 0x80000000)
+
+
+def shard_candidate_keys(summary: Summary, q, scale, k, base) -> np.ndarray:
+    """A shard's candidate keys for one query head, descending, 0-padded to
+    k: order_key(guess) << 32 | (0xFFFFFFFF - global id)."""
+    gs = centroid_guess(summary, q, scale)
+    keys = sorted(((order_key(gs[c]) << 32) | (0xFFFFFFFF - (int(base) + c))
+                   for c in range(summary.num_groups)), reverse=True)[:k]
+    return np.array(keys + [0] * (k - len(keys)), np.uint64)
+
+
+def keys_threshold(all_keys, k) -> int:
+    """k-th largest of the gathered keys (every real key when fewer)."""
+    real = sorted((int(x) for x in np.asarray(all_keys, np.uint64).ravel() if int(x)),
+                  reverse=True)
+    return real[k - 1] if len(real) >= k else 1
+
+
+def selected_by_threshold(summary: Summary, q, scale, thr, base) -> np.ndarray:
+    gs = centroid_guess(summary, q, scale)
+    return np.array([c for c in range(summary.num_groups)
+                     if ((order_key(gs[c]) << 32) | (0xFFFFFFFF - (int(base) + c))) >= thr],
+                    np.int64)
+
+
+def hybrid_shard_partial(q, K, V, summary: Summary, sample_end, n_total, selected, ranks, scale):
+    """Shard partial (m, l, ms, e1, e2, n_samples, o[D]) in log2 units,
+    float64: l = sum 2^(lw - m), o = sum 2^(lw - m) v over the shard's exact
+    rows, recent rows and stratified samples (lw in log2 units)."""
+    sel = np.asarray(selected, np.int64)
+    pos = (np.concatenate([np.arange(summary.starts[g], summary.starts[g] + summary.lengths[g])
+                           for g in sel]) if len(sel) else np.zeros(0, np.int64))
+    ex = summary.members[pos]
+    rec = _recent(sample_end, n_total)
+    idx = np.concatenate([ex, rec]).astype(np.int64)
+    lw = _scores(K, q, scale, idx) if idx.size else np.zeros(0)
+    rk = np.asarray(ranks, np.int64)
+    n_rest = int(sample_end - ex.size)
+    slw = np.zeros(0)
+    if n_rest > 0 and rk.size:
+        sidx = summary.members[hybrid_positions(summary, sel, rk)]
+        slw = _scores(K, q, scale, sidx) + math.log(n_rest) - math.log(rk.size)
+        idx = np.concatenate([idx, sidx])
+        lw = np.concatenate([lw, slw])
+    lw2, slw2 = lw / math.log(2.0), slw / math.log(2.0)
+    D = np.asarray(V).shape[1]
+    if lw2.size == 0:
+        return (-math.inf, 0.0, -math.inf, 0.0, 0.0, int(rk.size if n_rest > 0 else 0),
+                np.zeros(D))
+    m = lw2.max()
+    w = np.exp2(lw2 - m)
+    o = w @ np.asarray(V, np.float64)[idx]
+    ms, e1, e2 = -math.inf, 0.0, 0.0
+    if slw2.size:
+        ms = slw2.max()
+        we = np.exp2(slw2 - ms)
+        e1, e2 = float(we.sum()), float((we ** 2).sum())
+    return (float(m), float(w.sum()), float(ms), e1, e2, int(slw2.size), o)
+
+
+def merge_shard_partials(parts):
+    """LSE merge of hybrid_shard_partial results -> (out, lse, ess)."""
+    M = max((p[0] for p in parts if p[1] > 0), default=-math.inf)
+    L, o = 0.0, 0.0
+    for p in parts:
+        if p[1] > 0:
+            f = 2.0 ** (p[0] - M)
+            L += p[1] * f
+            o = o + p[6] * f
+    MS = max((p[2] for p in parts if p[3] > 0), default=-math.inf)
+    E1 = sum(p[3] * 2.0 ** (p[2] - MS) for p in parts if p[3] > 0)
+    E2 = sum(p[4] * 4.0 ** (p[2] - MS) for p in parts if p[3] > 0)
+    ns = sum(p[5] for p in parts)
+    out = o / L if L > 0 else np.zeros_like(parts[0][6])
+    lse = (M + math.log2(L)) * math.log(2.0) if L > 0 else -math.inf
+    ess = (E1 * E1 / E2) / ns if ns > 0 and E2 > 0 else 0.0
+    return out, lse, ess
+
+
+def decode_hybrid_sharded(q, shards, k, ranks, scale, bases) -> DecodeResult:
+    """The hybrid estimator with the sample budget stratified over shards.
+
+    shards[r] = (K_r, V_r, summary_r, sample_end_r, n_total_r): shard r's
+    token rows, its summary and its old-prefix / total lengths.  ranks[r] are
+    shard r's sample ranks in [0, n_rest_r); a sample of shard r weighs
+    n_rest_r / len(ranks[r]) (log r = log(S_r) - log(n_rest_r)).  Exact terms:
+    the global top-k clusters (shard_topk) and every shard's recent rows."""
+    sel = shard_topk([s[2] for s in shards], q, scale, k, bases)
+    terms_s, terms_v, samp_lw = [], [], []
+    n_exact = 0
+    for r, (K, V, summ, se, nt) in enumerate(shards):
+        sr = sel[r]
+        pos = (np.concatenate([np.arange(summ.starts[g], summ.starts[g] + summ.lengths[g])
+                               for g in sr]) if len(sr) else np.zeros(0, np.int64))
+        ex = summ.members[pos]
+        n_exact += ex.size
+        rec = _recent(se, nt)
+        for idx in (ex, rec):
+            if len(idx):
+                terms_s.append(_scores(K, q, scale, idx))
+                terms_v.append(np.asarray(V, np.float64)[idx])
+        rk = np.asarray(ranks[r], np.int64)
+        n_rest = int(se - ex.size)
+        if n_rest > 0 and rk.size:
+            sidx = summ.members[hybrid_positions(summ, sr, rk)]
+            lw = _scores(K, q, scale, sidx) + math.log(n_rest) - math.log(rk.size)
+            terms_s.append(lw)
+            terms_v.append(np.asarray(V, np.float64)[sidx])
+            samp_lw.append(lw)
+    s_all = np.concatenate(terms_s)
+    v_all = np.concatenate(terms_v)
+    m = s_all.max()
+    w = np.exp(s_all - m)
+    out = w @ v_all / w.sum()
+    ess = None
+    if samp_lw:
+        lw = np.concatenate(samp_lw)
+        nw = np.exp(lw - lw.max())
+        ess = float(nw.sum() ** 2 / (nw ** 2).sum() / lw.size)
+    return DecodeResult(out, float(m + math.log(w.sum())), n_exact,
+                        int(sum(len(x) for x in samp_lw)), ess, sel, None)
 
 
 # ---------------------------------------------------------------------------
