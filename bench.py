@@ -320,14 +320,15 @@ def run_ours(args, rank, world):
 
 
 def load_traffic(shape):
-    """Per-launch DRAM bytes of the attend kernel from the committed ncu summary."""
-    path = os.path.join(REPO, "profiles", f"decode_attend_{shape.name}.json")
+    """Per-launch DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of
+    the attend kernel, from the committed ncu summary of this workload (its
+    line ``dram_bytes_per_launch: N``)."""
+    import re
+    path = os.path.join(REPO, "profiles", f"decode_attend_gather_{shape.name}.md")
     if not os.path.exists(path):
         return None
-    try:
-        return float(json.load(open(path))["dram_bytes_per_launch"])
-    except (KeyError, ValueError):
-        return None
+    m = re.search(r"^dram_bytes_per_launch:\s*([0-9.eE+]+)", open(path).read(), re.M)
+    return float(m.group(1)) if m else None
 
 
 def run_e2e(args, shape, w, summ, runner):
