@@ -206,6 +206,60 @@ int santa_decode_select(const SantaGeometry *geo, const SantaDecodeParams *p, co
                         int32_t *n_exact, void *workspace, size_t workspace_bytes,
                         cudaStream_t stream);
 
+/* ---- MiniBatchKMeans (attention/minibatch_kmeans.py) -------------------- */
+
+/* The data-dependent arithmetic of SklearnLikeTorchMiniBatchKMeans.fit_predict
+ * (minibatch_kmeans.py:128-334); the caller keeps the reference's control flow
+ * and its numpy RandomState draws.  x is [n_rows, d] fp32 row-major; `rows`
+ * (int64, may be NULL) selects the rows an operation sees (x[rows[i]]), as
+ * the reference's x[batch_ids] / x[init_ids] / x[validation_ids].
+ * Defined arithmetic: dots are sequential fmaf chains over d; dist2 =
+ * max(0, fl32(fl32(|x|^2 + |c|^2) - 2 dot)); inertia and potentials are exact
+ * Q64.64 fixed-point sums, accumulated into two uint64 words (lo, hi) that the
+ * caller zeroes. d % 4 == 0 and d <= 512 for assign; k <= 4096. */
+
+/* out[i] = |x_i|^2 for n rows (_squared_distances' x^2 term, :58-66). */
+int santa_kmeans_sqnorm(const float *x, int64_t n, int32_t d, float *out, cudaStream_t stream);
+
+/* Nearest centre of every selected row, lowest index on ties (_assign, :68-71).
+ * xx: |x|^2 indexed like x; cc: |c|^2 of the k centres.  labels [n] int32,
+ * min_dist [n] (or NULL), inertia_fx [2] uint64 += fixed-point sum (or NULL). */
+int santa_kmeans_assign(const float *x, const int64_t *rows, const float *xx, int64_t n,
+                        int32_t d, const float *centers, const float *cc, int32_t k,
+                        int32_t *labels, float *min_dist, unsigned long long *inertia_fx,
+                        cudaStream_t stream);
+
+int santa_kmeans_update_workspace_bytes(int64_t nb, int32_t k, size_t *bytes);
+
+/* Mini-batch centre update (:226-239): batch counts, per-cluster sums in
+ * ascending batch order, new = (c * n + sum) / (n + bc) for clusters in the
+ * batch; counts updated in place, centers_new written, batch_counts [k] (or
+ * NULL).  Labels outside [0, k) are ignored. */
+int santa_kmeans_update(const float *x, const int64_t *rows, int64_t nb, int32_t d,
+                        const int32_t *labels, int32_t k, const float *centers, float *counts,
+                        float *centers_new, float *batch_counts, void *workspace,
+                        size_t workspace_bytes, cudaStream_t stream);
+
+/* Low-count reassignment (:241-267): centre clusters[i] <- selected row
+ * batch_rows[i], its count <- new_count. */
+int santa_kmeans_reassign(const float *x, const int64_t *rows, const int32_t *batch_rows,
+                          const int32_t *clusters, int32_t n_reassign, int32_t d,
+                          float *centers, float *counts, float new_count, cudaStream_t stream);
+
+int santa_kmeans_plusplus_workspace_bytes(int64_t n, int32_t trials, size_t *bytes);
+
+/* Greedy k-means++ over the n selected rows (_greedy_kmeans_plus_plus,
+ * :73-126): centre 0 = row first_id; centre c picks, among `trials`
+ * candidates found by searchsorted (fp64) of uniforms[(c-1)*trials + t] x
+ * potential in the fixed-point prefix sums of the closest distances, the one
+ * with the lowest potential (first on ties).  uniforms: device fp64
+ * [(k-1)*trials] in the reference's draw order.  centers [k, d]; chosen_ids
+ * [k] indices into the selected rows (or NULL). trials <= 16. */
+int santa_kmeans_plusplus(const float *x, const int64_t *rows, const float *xx, int64_t n,
+                          int32_t d, int32_t k, int32_t trials, int64_t first_id,
+                          const double *uniforms, float *centers, int64_t *chosen_ids,
+                          void *workspace, size_t workspace_bytes, cudaStream_t stream);
+
 /* ---- sequence-sharded decode ------------------------------------------ */
 
 /* The reference decodes on one GPU (README.md:355): these entry points have

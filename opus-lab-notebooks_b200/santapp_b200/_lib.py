@@ -107,6 +107,20 @@ SIGNATURES = {
                                           _vp, _P(SantaSummary), _P(SantaShard), _vp, _vp, _vp,
                                           _vp, _vp, ctypes.c_size_t, _vp]),
     "santa_merge_shards": (ctypes.c_int, [_i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "santa_kmeans_sqnorm": (ctypes.c_int, [_vp, ctypes.c_int64, _i32, _vp, _vp]),
+    "santa_kmeans_assign": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int64, _i32, _vp, _vp, _i32,
+                                           _vp, _vp, _vp, _vp]),
+    "santa_kmeans_update_workspace_bytes": (ctypes.c_int, [ctypes.c_int64, _i32,
+                                                           _P(ctypes.c_size_t)]),
+    "santa_kmeans_update": (ctypes.c_int, [_vp, _vp, ctypes.c_int64, _i32, _vp, _i32, _vp, _vp,
+                                           _vp, _vp, _vp, ctypes.c_size_t, _vp]),
+    "santa_kmeans_reassign": (ctypes.c_int, [_vp, _vp, _vp, _vp, _i32, _i32, _vp, _vp,
+                                             ctypes.c_float, _vp]),
+    "santa_kmeans_plusplus_workspace_bytes": (ctypes.c_int, [ctypes.c_int64, _i32,
+                                                             _P(ctypes.c_size_t)]),
+    "santa_kmeans_plusplus": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int64, _i32, _i32, _i32,
+                                             ctypes.c_int64, _vp, _vp, _vp, _vp,
+                                             ctypes.c_size_t, _vp]),
 }
 
 _lock = threading.Lock()
