@@ -206,6 +206,33 @@ int santa_decode_select(const SantaGeometry *geo, const SantaDecodeParams *p, co
                         int32_t *n_exact, void *workspace, size_t workspace_bytes,
                         cudaStream_t stream);
 
+/* ---- dense prefill (attention/santapp.py:320-346) ---------------------- */
+
+typedef struct SantaPrefillShape {
+    int32_t batch;
+    int32_t num_query_heads;  /* multiple of num_kv_heads (GQA) */
+    int32_t num_kv_heads;
+    int32_t seq_len;          /* T, a multiple of 8 */
+    int32_t head_dim;         /* 128 */
+    float scale;              /* softmax scale, 1/sqrt(head_dim) in the reference */
+    int32_t causal;           /* 1: key s attends only to queries t >= s */
+} SantaPrefillShape;
+
+/* Workspace: the transposed V ([B, Hkv, D, T] bf16). */
+int santa_prefill_workspace_bytes(const SantaPrefillShape *shape, size_t *bytes);
+
+/* Attention of every query position over the prompt, as the reference's
+ * prefill (sdpa_attention_forward -> torch scaled_dot_product_attention,
+ * is_causal=True, GQA by head // group).  q [B, Hq, T, D], k and v
+ * [B, Hkv, T, D], out [B, Hq, T, D], all bf16 and 16-byte aligned; lse
+ * [B, Hq, T] fp32 natural-log softmax denominators (or NULL).  tcgen05 MMAs
+ * with fp32 accumulation; P is rounded to bf16 before the P.V product.
+ * error_flag (device int32, zeroed by the caller) is set to 1 if a bounded
+ * wait inside the kernel gave up; the output is then undefined. */
+int santa_prefill(const SantaPrefillShape *shape, const void *q, const void *k, const void *v,
+                  void *out, float *lse, int32_t *error_flag, void *workspace,
+                  size_t workspace_bytes, cudaStream_t stream);
+
 /* ---- MiniBatchKMeans (attention/minibatch_kmeans.py) -------------------- */
 
 /* The data-dependent arithmetic of SklearnLikeTorchMiniBatchKMeans.fit_predict

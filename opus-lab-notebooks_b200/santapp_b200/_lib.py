@@ -67,6 +67,12 @@ def partial_floats(head_dim: int) -> int:
     return head_dim + 8
 
 
+class SantaPrefillShape(ctypes.Structure):
+    _fields_ = [("batch", _i32), ("num_query_heads", _i32), ("num_kv_heads", _i32),
+                ("seq_len", _i32), ("head_dim", _i32), ("scale", ctypes.c_float),
+                ("causal", _i32)]
+
+
 # Every symbol include/santa_b200.h declares, with its ctypes signature.
 _P = ctypes.POINTER
 SIGNATURES = {
@@ -107,6 +113,10 @@ SIGNATURES = {
                                           _vp, _P(SantaSummary), _P(SantaShard), _vp, _vp, _vp,
                                           _vp, _vp, ctypes.c_size_t, _vp]),
     "santa_merge_shards": (ctypes.c_int, [_i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "santa_prefill_workspace_bytes": (ctypes.c_int, [_P(SantaPrefillShape),
+                                                     _P(ctypes.c_size_t)]),
+    "santa_prefill": (ctypes.c_int, [_P(SantaPrefillShape), _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                     ctypes.c_size_t, _vp]),
     "santa_kmeans_sqnorm": (ctypes.c_int, [_vp, ctypes.c_int64, _i32, _vp, _vp]),
     "santa_kmeans_assign": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int64, _i32, _vp, _vp, _i32,
                                            _vp, _vp, _vp, _vp]),

@@ -1,0 +1,56 @@
+"""Dense causal prefill attention on the sm_100a tcgen05 kernel.
+
+Replaces the prefill branch of ``SantaPlusEngine._attention_forward``
+(santapp_ruler/attention/santapp.py:320-346): the reference calls
+``transformers.integrations.sdpa_attention.sdpa_attention_forward``, i.e.
+``torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True)``
+over ``[B, H, T, D]`` bf16 tensors with GQA (query head ``h`` reads KV head
+``h // (Hq // Hkv)``).  Here one call of ``santa_prefill`` (C ABI) does the
+same with tcgen05 MMAs accumulating in TMEM.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from .. import _lib
+from .santapp import _require_cuda
+
+__all__ = ["santa_prefill"]
+
+
+def santa_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, causal: bool = True,
+                  scale: float | None = None, out: torch.Tensor | None = None,
+                  return_lse: bool = False, stream=None):
+    """q ``[B, Hq, T, D]``, k / v ``[B, Hkv, T, D]`` bf16 CUDA tensors ->
+    out ``[B, Hq, T, D]`` bf16 (and the natural-log softmax denominators
+    ``[B, Hq, T]`` fp32 with ``return_lse``)."""
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _require_cuda(name, t)
+        if t.dtype != torch.bfloat16 or t.dim() != 4:
+            raise ValueError(f"{name} must be a [batch, heads, seq, head_dim] bf16 tensor")
+    B, Hq, T, D = q.shape
+    Hkv = k.shape[1]
+    if k.shape != (B, Hkv, T, D) or v.shape != k.shape:
+        raise ValueError("k and v must be [batch, kv_heads, seq, head_dim] matching q")
+    if Hq % Hkv:
+        raise ValueError("Query heads must be divisible by KV heads.")
+    shape = _lib.SantaPrefillShape(B, Hq, Hkv, T, D, 1.0 / math.sqrt(D) if scale is None
+                                   else float(scale), 1 if causal else 0)
+    lib = _lib.load()
+    nbytes = ctypes.c_size_t()
+    _lib.check("santa_prefill_workspace_bytes",
+               lib.santa_prefill_workspace_bytes(ctypes.byref(shape), ctypes.byref(nbytes)))
+    ws = torch.empty(nbytes.value, dtype=torch.uint8, device=q.device)
+    if out is None:
+        out = torch.empty_like(q)
+    lse = torch.empty(B, Hq, T, dtype=torch.float32, device=q.device) if return_lse else None
+    err = torch.zeros(1, dtype=torch.int32, device=q.device)
+    _lib.check("santa_prefill", lib.santa_prefill(
+        ctypes.byref(shape), q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+        _lib.ptr(lse), err.data_ptr(), ws.data_ptr(), nbytes.value, _lib.stream_handle(stream)))
+    out._santa_error_flag = err  # read by callers that check the kernel's bounded waits
+    return (out, lse) if return_lse else out
