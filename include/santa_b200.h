@@ -233,6 +233,25 @@ int santa_prefill(const SantaPrefillShape *shape, const void *q, const void *k, 
                   void *out, float *lse, int32_t *error_flag, void *workspace,
                   size_t workspace_bytes, cudaStream_t stream);
 
+/* ---- key fingerprints (attention/santapp.py:598-690) -------------------- */
+
+int santa_fingerprints_workspace_bytes(int32_t cols, size_t *bytes);
+
+/* Fingerprints of one (layer, KV head): out[n][h*P + p] =
+ * fl32(dot(key_n, q_h[probes[p]]) / divisor) for the group's `group` query
+ * heads (santapp.py:672-683), then, if normalize, the per-column population
+ * z-score (x - mean) / (std + 1e-6) (:684-691).  keys [n, d] (SANTA_DTYPE_F32
+ * or _BF16, upcast exactly); queries: rotated fp32 queries, head h of the group
+ * at queries + h * q_head_stride, [T, d] per head; probes [P] int64 positions;
+ * divisor = fl32(sqrt(d)).  Defined arithmetic: fmaf-chain dots, IEEE divide,
+ * column mean and variance as exact Q64.64 sums divided in fp64 then rounded
+ * to fp32, sqrt correctly rounded: results do not depend on reduction order. */
+int santa_fingerprints(const void *keys, int32_t key_dtype, int64_t n, int32_t d,
+                       const float *queries, int64_t q_head_stride, int32_t group,
+                       const int64_t *probes, int32_t n_probes, float divisor,
+                       int32_t normalize, float *out, void *workspace, size_t workspace_bytes,
+                       cudaStream_t stream);
+
 /* ---- MiniBatchKMeans (attention/minibatch_kmeans.py) -------------------- */
 
 /* The data-dependent arithmetic of SklearnLikeTorchMiniBatchKMeans.fit_predict

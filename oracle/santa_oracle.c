@@ -311,6 +311,48 @@ void or_cluster_means(const float *keys, const int32_t *labels, int64_t n, int d
     }
 }
 
+/* Key fingerprints (santapp.py:672-683): out[i][h*P + p] =
+ * fl32(dot(keys_i, q_h[probes[p]]) / divisor), q_h at q + h * q_stride. */
+void or_fingerprints(const float *keys, int64_t n, int d, const float *q, int64_t q_stride,
+                     int g, const int64_t *probes, int P, float divisor, float *out) {
+    const int cols = g * P;
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i)
+        for (int c = 0; c < cols; ++c) {
+            const int h = c / P, p = c % P;
+            const float dt = dot_fma(keys + i * d, q + (int64_t)h * q_stride + probes[p] * d, d);
+            out[i * cols + c] = dt / divisor;
+        }
+}
+
+/* Column z-score (santapp.py:684-691) with exact sums: mean = fl32(fl64(S)/n)
+ * of the exact signed fixed-point column sum S; var likewise over
+ * fl32(fl32(x - mean)^2); z = fl32(fl32(x - mean) / fl32(sqrt(var) + 1e-6)). */
+void or_zscore(float *f, int64_t n, int cols) {
+#pragma omp parallel for schedule(static)
+    for (int c = 0; c < cols; ++c) {
+        u128 s = 0;
+        for (int64_t i = 0; i < n; ++i) {
+            const float x = f[i * cols + c];
+            const u128 m = fx_of(fabsf(x));
+            s += (x < 0.0f) ? (u128)0 - m : m;
+        }
+        int neg = (int)(s >> 127);
+        u128 mag = neg ? (u128)0 - s : s;
+        double sd = fx_to_double(mag);
+        if (neg) sd = -sd;
+        const float mean = (float)(sd / (double)n);
+        u128 q = 0;
+        for (int64_t i = 0; i < n; ++i) {
+            const float dv = f[i * cols + c] - mean;
+            q += fx_of(dv * dv);
+        }
+        const float var = (float)(fx_to_double(q) / (double)n);
+        const float den = sqrtf(var) + 1e-6f;
+        for (int64_t i = 0; i < n; ++i) f[i * cols + c] = (f[i * cols + c] - mean) / den;
+    }
+}
+
 /* guess_g = fl32(log_n[g] + fl32(dot(c_g, q) * scale)) for G centroids. */
 void or_centroid_guess(const float *cent, const float *log_n, int G, int d,
                        const float *q, float scale, float *out) {

@@ -26,6 +26,8 @@ What it restates (reference = santapp-ruler-bench/src/santapp_ruler):
   shards: one global top-k over all shards' clusters (``shard_topk``) and
   the sample budget stratified over the shards (the reference itself is
   single-GPU; this is the sharded decode's definition).
+* ``fingerprints``   the clustering features of santapp.py:672-691 (key . probe
+  query / sqrt(d), then a per-column z-score) under defined arithmetic.
 * ``prefill_causal`` dense causal softmax attention (santapp.py:337-346 calls
   torch SDPA with is_causal=True).
 
@@ -85,6 +87,9 @@ def lib():
         L.or_centroid_guess.argtypes = [_f32p, _f32p, c_int, c_int, _f32p, c_float,
                                         _f32p]
         L.or_philox4x32.argtypes = [_u32p, _u32p, _u32p]
+        L.or_fingerprints.argtypes = [_f32p, i64, c_int, _f32p, i64, c_int, _i64p, c_int,
+                                      c_float, _f32p]
+        L.or_zscore.argtypes = [_f32p, i64, c_int]
         _lib = L
     return _lib
 
@@ -650,6 +655,26 @@ def philox_ranks(seed: int, step: int, b: int, h: int, n_samples: int, n_rest: i
             i = blk * 4 + j
             if i < n_samples:
                 out[i] = (int(w[j]) * int(n_rest)) >> 32
+    return out
+
+
+# ---------------------------------------------------------------------------
+# key fingerprints (santapp.py:598-690)
+# ---------------------------------------------------------------------------
+
+def fingerprints(keys, q_group, probes, normalize=True) -> np.ndarray:
+    """keys [N, D], q_group [g, T, D] rotated fp32 queries of the KV head's
+    query heads, probes [P] -> [N, g*P] (z-scored per column if normalize)."""
+    keys = _f32(keys)
+    q_group = _f32(q_group)
+    probes = np.ascontiguousarray(np.asarray(probes, np.int64))
+    n, d = keys.shape
+    g, T, _ = q_group.shape
+    out = np.empty((n, g * probes.size), np.float32)
+    lib().or_fingerprints(keys, n, d, q_group, T * d, g, probes, probes.size,
+                          np.float32(math.sqrt(d)), out)
+    if normalize:
+        lib().or_zscore(out, n, out.shape[1])
     return out
 
 
