@@ -206,25 +206,45 @@ int santa_decode_select(const SantaGeometry *geo, const SantaDecodeParams *p, co
                         int32_t *n_exact, void *workspace, size_t workspace_bytes,
                         cudaStream_t stream);
 
+/* ---- KV cache (attention/santapp.py:66-77, 234-283, 308-313) ---------- */
+
+/* RoPE of the new tokens' queries and keys (x*cos + rotate_half(x)*sin with
+ * every product and the sum rounded to bf16, as torch evaluates the
+ * reference's bf16 expression) and their append to the layer cache at
+ * [start, start + tokens) (LayerCache append, santapp.py:234-274).
+ * q [B, tokens, Hq, D], k and v [B, tokens, Hkv, D], cos and sin [B, tokens, D]
+ * (bf16, the projections' natural layout); caches [B, Hkv, capacity, D] bf16.
+ * Rotated queries out as [B, Hq, tokens, D] bf16 and/or fp32 (either may be
+ * NULL).  Trimming (santapp.py:276-283) is a host-side length change. */
+int santa_rope_append(int32_t batch, int32_t tokens, int32_t num_query_heads,
+                      int32_t num_kv_heads, int32_t head_dim, const void *q, const void *k,
+                      const void *v, const void *cos, const void *sin, void *key_cache,
+                      void *value_cache, int32_t capacity, int32_t start, void *q_rot_bf16,
+                      float *q_rot_f32, cudaStream_t stream);
+
 /* ---- dense prefill (attention/santapp.py:320-346) ---------------------- */
 
 typedef struct SantaPrefillShape {
     int32_t batch;
     int32_t num_query_heads;  /* multiple of num_kv_heads (GQA) */
     int32_t num_kv_heads;
-    int32_t seq_len;          /* T, a multiple of 8 */
+    int32_t seq_len;          /* T */
     int32_t head_dim;         /* 128 */
     float scale;              /* softmax scale, 1/sqrt(head_dim) in the reference */
     int32_t causal;           /* 1: key s attends only to queries t >= s */
+    int32_t kv_capacity;      /* tokens between the (batch, KV head) blocks of k
+                                 and v (a KV cache's capacity), >= seq_len;
+                                 0 = seq_len */
 } SantaPrefillShape;
 
-/* Workspace: the transposed V ([B, Hkv, D, T] bf16). */
+/* Workspace: the transposed V ([B, Hkv, D, T rounded up to 8] bf16). */
 int santa_prefill_workspace_bytes(const SantaPrefillShape *shape, size_t *bytes);
 
 /* Attention of every query position over the prompt, as the reference's
  * prefill (sdpa_attention_forward -> torch scaled_dot_product_attention,
  * is_causal=True, GQA by head // group).  q [B, Hq, T, D], k and v
- * [B, Hkv, T, D], out [B, Hq, T, D], all bf16 and 16-byte aligned; lse
+ * [B, Hkv, kv_capacity, D] (tokens [0, T) used), out [B, Hq, T, D], all bf16
+ * and 16-byte aligned; lse
  * [B, Hq, T] fp32 natural-log softmax denominators (or NULL).  tcgen05 MMAs
  * with fp32 accumulation; P is rounded to bf16 before the P.V product.
  * error_flag (device int32, zeroed by the caller) is set to 1 if a bounded

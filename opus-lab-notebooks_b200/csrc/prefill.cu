@@ -50,6 +50,8 @@ struct PrefillArgs {
     float *lse;               // [B, Hq, T] natural log, or null
     int32_t *err;             // error flag (a bounded wait gave up)
     int B, Hq, Hkv, T, n_tiles;
+    int64_t cap;              // tokens between consecutive (b, kv head) blocks of k
+    int Tp;                   // row stride of V^T: T rounded up to a multiple of 8
     float scale_log2;         // scale * log2(e)
     int causal;
 };
@@ -112,14 +114,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
     const uint32_t tlane = (uint32_t)(32 * (warp & 3)) << 16;
 
     const __nv_bfloat16 *qg = a.q + (((int64_t)b * a.Hq + h) * a.T + q0) * kPfD;
-    const __nv_bfloat16 *kg = a.k + ((int64_t)b * a.Hkv + kvh) * a.T * kPfD;
-    const __nv_bfloat16 *vg = a.vt + ((int64_t)b * a.Hkv + kvh) * kPfD * a.T;
+    const __nv_bfloat16 *kg = a.k + ((int64_t)b * a.Hkv + kvh) * a.cap * kPfD;
+    const __nv_bfloat16 *vg = a.vt + ((int64_t)b * a.Hkv + kvh) * kPfD * a.Tp;
 
     // prologue: Q, K_0 | V_0
     pf_load_tile(sQ, qg, kPfD, min(kPfRows, a.T - q0), kPfD, tid);
     pf_load_tile(sK0, kg, kPfD, min(kPfRows, a.T), kPfD, tid);
     pf_commit();
-    pf_load_tile(sV0, vg, a.T, kPfD, min(kPfRows, a.T), tid);
+    pf_load_tile(sV0, vg, a.Tp, kPfD, min(kPfRows, a.T), tid);
     pf_commit();
 
     const int qpos = q0 + row;
@@ -206,7 +208,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
         tc_fence_after();
         // prefetch V_{j+1} into the buffer V_{j-1} used
         if (j + 1 < nj && ok_o)
-            pf_load_tile(sV0 + (buf ^ 1) * kPfTile, vg + kv0 + kPfRows, a.T, kPfD,
+            pf_load_tile(sV0 + (buf ^ 1) * kPfTile, vg + kv0 + kPfRows, a.Tp, kPfD,
                          min(kPfRows, a.T - kv0 - kPfRows), tid);
         pf_commit();
         if (rescale && j > 0 && ok_o) {
@@ -305,22 +307,23 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
     if (warp == 0) tmem_dealloc(tS, 256);
 }
 
-// V [B, Hkv, T, D] -> V^T [B, Hkv, D, T], 32 x 32 tiles through shared memory
+// V [B, Hkv, cap, D] (tokens [0, T)) -> V^T [B, Hkv, D, Tp], 32 x 32 tiles;
+// columns [T, Tp) are zero (a partial key tile's masked columns multiply them)
 __global__ void prefill_transpose_v_kernel(const __nv_bfloat16 *v, __nv_bfloat16 *vt, int T,
-                                           int D) {
+                                           int Tp, int D, int64_t cap) {
     __shared__ __nv_bfloat16 tile[32][33];
     const int64_t mat = blockIdx.z;
     const int t0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
-    const __nv_bfloat16 *src = v + mat * (int64_t)T * D;
-    __nv_bfloat16 *dst = vt + mat * (int64_t)T * D;
+    const __nv_bfloat16 *src = v + mat * cap * D;
+    __nv_bfloat16 *dst = vt + mat * (int64_t)Tp * D;
     for (int i = threadIdx.y; i < 32; i += blockDim.y) {
         const int t = t0 + i, d = d0 + threadIdx.x;
-        if (t < T && d < D) tile[i][threadIdx.x] = src[(int64_t)t * D + d];
+        tile[i][threadIdx.x] = (t < T && d < D) ? src[(int64_t)t * D + d] : __float2bfloat16(0.f);
     }
     __syncthreads();
     for (int i = threadIdx.y; i < 32; i += blockDim.y) {
         const int d = d0 + i, t = t0 + threadIdx.x;
-        if (t < T && d < D) dst[(int64_t)d * T + t] = tile[threadIdx.x][i];
+        if (t < Tp && d < D) dst[(int64_t)d * Tp + t] = tile[threadIdx.x][i];
     }
 }
 
@@ -334,8 +337,8 @@ static int check_prefill(const SantaPrefillShape *s) {
         return SANTA_ERR_INVALID_ARGUMENT;
     if (s->num_query_heads % s->num_kv_heads) return SANTA_ERR_INVALID_ARGUMENT;
     if (s->head_dim != kPfD) return SANTA_ERR_UNSUPPORTED;
-    if (s->seq_len % 8) return SANTA_ERR_UNSUPPORTED;  // 16-byte rows of V^T
     if (!(s->scale > 0.f)) return SANTA_ERR_INVALID_ARGUMENT;
+    if (s->kv_capacity && s->kv_capacity < s->seq_len) return SANTA_ERR_INVALID_ARGUMENT;
     return SANTA_OK;
 }
 
@@ -343,7 +346,8 @@ extern "C" int santa_prefill_workspace_bytes(const SantaPrefillShape *shape, siz
     int st = check_prefill(shape);
     if (st) return st;
     if (!bytes) return SANTA_ERR_INVALID_ARGUMENT;
-    *bytes = (size_t)shape->batch * shape->num_kv_heads * shape->seq_len * shape->head_dim * 2 + 256;
+    const int64_t Tp = ((int64_t)shape->seq_len + 7) / 8 * 8;  // 16-byte rows of V^T
+    *bytes = (size_t)shape->batch * shape->num_kv_heads * Tp * shape->head_dim * 2 + 256;
     return SANTA_OK;
 }
 
@@ -360,9 +364,11 @@ extern "C" int santa_prefill(const SantaPrefillShape *shape, const void *q, cons
         return SANTA_ERR_UNSUPPORTED;
     const int T = shape->seq_len, D = shape->head_dim;
     __nv_bfloat16 *vt = (__nv_bfloat16 *)workspace;
-    dim3 tg((T + 31) / 32, (D + 31) / 32, shape->batch * shape->num_kv_heads);
+    const int Tp = (T + 7) / 8 * 8;
+    dim3 tg((Tp + 31) / 32, (D + 31) / 32, shape->batch * shape->num_kv_heads);
+    const int64_t cap = shape->kv_capacity ? shape->kv_capacity : T;
     prefill_transpose_v_kernel<<<tg, dim3(32, 8), 0, stream>>>((const __nv_bfloat16 *)v, vt, T,
-                                                                D);
+                                                                Tp, D, cap);
     SANTA_LAUNCH_CHECK();
     PrefillArgs a;
     a.q = (const __nv_bfloat16 *)q;
@@ -375,6 +381,8 @@ extern "C" int santa_prefill(const SantaPrefillShape *shape, const void *q, cons
     a.Hq = shape->num_query_heads;
     a.Hkv = shape->num_kv_heads;
     a.T = T;
+    a.cap = cap;
+    a.Tp = Tp;
     a.n_tiles = (T + kPfRows - 1) / kPfRows;
     a.scale_log2 = shape->scale * 1.4426950408889634f;
     a.causal = shape->causal ? 1 : 0;

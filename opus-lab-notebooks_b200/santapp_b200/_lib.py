@@ -70,7 +70,7 @@ def partial_floats(head_dim: int) -> int:
 class SantaPrefillShape(ctypes.Structure):
     _fields_ = [("batch", _i32), ("num_query_heads", _i32), ("num_kv_heads", _i32),
                 ("seq_len", _i32), ("head_dim", _i32), ("scale", ctypes.c_float),
-                ("causal", _i32)]
+                ("causal", _i32), ("kv_capacity", _i32)]
 
 
 # Every symbol include/santa_b200.h declares, with its ctypes signature.
@@ -113,6 +113,8 @@ SIGNATURES = {
                                           _vp, _P(SantaSummary), _P(SantaShard), _vp, _vp, _vp,
                                           _vp, _vp, ctypes.c_size_t, _vp]),
     "santa_merge_shards": (ctypes.c_int, [_i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "santa_rope_append": (ctypes.c_int, [_i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp,
+                                         _vp, _vp, _i32, _i32, _vp, _vp, _vp]),
     "santa_prefill_workspace_bytes": (ctypes.c_int, [_P(SantaPrefillShape),
                                                      _P(ctypes.c_size_t)]),
     "santa_prefill": (ctypes.c_int, [_P(SantaPrefillShape), _vp, _vp, _vp, _vp, _vp, _vp, _vp,

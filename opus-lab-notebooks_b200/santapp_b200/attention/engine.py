@@ -1,0 +1,353 @@
+"""Model-level SANTA++ engine on the sm_100a kernels.
+
+Host-side mirror of ``SantaPlusEngine`` (santapp_ruler/attention/
+santapp.py:145-926) for Qwen2 causal LMs, batched over sequences (the
+reference supports batch 1, :293-294):
+
+* ``patched()`` installs the same instance-level attention patch as the
+  reference (:201-227) and restores it afterwards;
+* ``_attention_forward`` (:285-363) runs the projections of the model, then
+  one fused kernel for RoPE and the cache append (``santa_rope_append``,
+  LayerCache :66-77 / :234-274), then
+    - prefill (query tokens == key tokens): the tcgen05 causal attention
+      ``santa_prefill`` over the cache in place,
+    - sparse decode (one query token): ``santa_decode`` for every (sequence,
+      query head) at once, in the configured mode,
+    - dense decode (the fidelity path): torch SDPA over the cache, as the
+      reference's dense branch does;
+* ``_dense_prefill_and_cluster`` (:542-722): prefill, then per (layer, KV
+  head, sequence) fingerprints (``build_fingerprints``), MiniBatchKMeans
+  (``SklearnLikeTorchMiniBatchKMeans``) and the cluster summary
+  (``build_summary``, batched over the layer);
+* ``generate`` (:794-908): prefill + clustering, trim the cache by one token,
+  re-feed the last prompt token, greedy decoding.
+
+Probe queries are captured inside the patched forward at the probe positions
+only (the reference keeps every layer's full q_proj output).
+"""
+
+from __future__ import annotations
+
+import contextlib
+import math
+import time
+import types
+from dataclasses import dataclass, field
+from typing import Any
+
+import numpy as np
+import torch
+
+from .. import _lib
+from .fingerprints import build_fingerprints, cluster_count, probe_positions
+from .kmeans import SklearnLikeTorchMiniBatchKMeans
+from .prefill import santa_prefill
+from .santapp import DecodeTrafficTracker, build_summary, santa_decode
+
+__all__ = ["KMeansConfig", "SantaB200Config", "LayerCache", "SantaGeneration", "SantaB200Engine"]
+
+_MISSING = object()
+
+
+@dataclass
+class KMeansConfig:
+    """MiniBatchKMeansConfig of santapp_ruler/config.py."""
+    batch_size: int = 4096
+    n_init: int = 1
+    max_iter: int = 100
+    tol: float = 0.0
+    max_no_improvement: int | None = 10
+    init_size: int | None = None
+    reassignment_ratio: float = 0.01
+    random_state: int = 0
+
+
+@dataclass
+class SantaB200Config:
+    """SantaPlusConfig (santapp_ruler/config.py:70-80) plus the hybrid
+    estimator's exact-cluster count and an optional fixed cluster count."""
+    mode: str = "guided"
+    group_size: int = 16
+    samples_per_head: int = 128
+    probe_queries: int = 64
+    recent_window: int = 64
+    probe_region_start_fraction: float = 0.75
+    probe_strategy: str = "end_quarter"
+    sample_seed: int = 0
+    kmeans: KMeansConfig = field(default_factory=KMeansConfig)
+    topk_clusters: int = 16
+    n_clusters: int | None = None
+
+
+@dataclass
+class LayerCache:
+    key: torch.Tensor     # [B, Hkv, capacity, D]
+    value: torch.Tensor
+    length: int
+
+    @property
+    def capacity(self) -> int:
+        return int(self.key.shape[2])
+
+    def view(self) -> tuple[torch.Tensor, torch.Tensor]:
+        return self.key[:, :, : self.length], self.value[:, :, : self.length]
+
+
+@dataclass(frozen=True)
+class SantaGeneration:
+    token_ids: list[list[int]]
+    metrics: dict[str, Any]
+
+
+def _patched_forward(attention, hidden_states, position_embeddings=None, attention_mask=None,
+                     *args, **kwargs):
+    del args, kwargs
+    return attention._santa_engine._attention_forward(attention, hidden_states,
+                                                      position_embeddings, attention_mask)
+
+
+class SantaB200Engine:
+    """Patch a loaded Qwen2 model only while running SANTA++ generation."""
+
+    def __init__(self, model: Any, config: SantaB200Config):
+        self.model = model
+        self.config = config
+        self.base_model = getattr(model, "model", None)
+        if self.base_model is None or not hasattr(self.base_model, "layers"):
+            raise TypeError("Expected a Hugging Face causal LM with model.layers.")
+        cfg = model.config
+        if getattr(cfg, "model_type", None) != "qwen2":
+            raise TypeError(f"Qwen2/Qwen2.5 models only, not {cfg.model_type!r}.")
+        if bool(getattr(cfg, "use_sliding_window", False)):
+            raise NotImplementedError("use_sliding_window=True is unsupported.")
+        self.num_layers = len(self.base_model.layers)
+        self.num_query_heads = int(cfg.num_attention_heads)
+        self.num_kv_heads = int(cfg.num_key_value_heads)
+        if self.num_query_heads % self.num_kv_heads:
+            raise ValueError("Query heads must be divisible by KV heads.")
+        self.group = self.num_query_heads // self.num_kv_heads
+        self.head_dim = int(getattr(cfg, "head_dim", None)
+                            or cfg.hidden_size // cfg.num_attention_heads)
+        self.mode = "dense"
+        self.sample_end = 0
+        self.cache_capacity = 0
+        self.cache: dict[int, LayerCache] = {}
+        self.summaries: dict[int, Any] = {}
+        self.traffic = DecodeTrafficTracker()
+        self._probe_idx: torch.Tensor | None = None
+        self._probe_q: dict[int, torch.Tensor] = {}
+        self._decode_step = 0
+        self._n_groups_host: dict[int, np.ndarray] = {}
+        self.track_traffic = True  # draw accounting needs a device->host read per layer call
+        self._lib = _lib.load()
+
+    # ---- patch ---------------------------------------------------------------
+    @contextlib.contextmanager
+    def patched(self):
+        originals, attns = [], []
+        try:
+            for layer_id, layer in enumerate(self.base_model.layers):
+                attn = layer.self_attn
+                originals.append(attn.__dict__.get("forward", _MISSING))
+                attns.append(attn)
+                attn._santa_engine = self
+                attn._santa_layer_id = layer_id
+                attn.forward = types.MethodType(_patched_forward, attn)
+            yield
+        finally:
+            for attn, orig in zip(attns, originals):
+                if orig is _MISSING:
+                    attn.__dict__.pop("forward", None)
+                else:
+                    attn.forward = orig
+                attn.__dict__.pop("_santa_engine", None)
+                attn.__dict__.pop("_santa_layer_id", None)
+
+    def clear(self) -> None:
+        self.cache.clear()
+        self.summaries.clear()
+        self._probe_q.clear()
+        self._n_groups_host.clear()
+        self.traffic = DecodeTrafficTracker()
+
+    def _trim_cache(self, length: int) -> None:
+        for layer_id, c in self.cache.items():
+            if c.length < length:
+                raise RuntimeError(f"Layer {layer_id} cache has only {c.length} tokens; "
+                                   f"cannot trim to {length}.")
+            c.length = length
+
+    # ---- attention -----------------------------------------------------------
+    def _attention_forward(self, attention, hidden_states, position_embeddings, attention_mask):
+        if position_embeddings is None:
+            raise RuntimeError("Qwen did not supply position_embeddings.")
+        B, Tn, _ = hidden_states.shape
+        Hq, Hkv, D = self.num_query_heads, self.num_kv_heads, self.head_dim
+        q = attention.q_proj(hidden_states)
+        k = attention.k_proj(hidden_states)
+        v = attention.v_proj(hidden_states)
+        if q.dtype != torch.bfloat16:
+            raise ValueError("the engine runs bf16 models")
+        cos, sin = position_embeddings
+        cos = cos.to(torch.bfloat16).expand(B, Tn, D).contiguous()
+        sin = sin.to(torch.bfloat16).expand(B, Tn, D).contiguous()
+        layer_id = int(attention._santa_layer_id)
+        cached = self.cache.get(layer_id)
+        if cached is None:
+            cap = max(self.cache_capacity, Tn)
+            cap = (cap + 7) // 8 * 8
+            kb = torch.empty(B, Hkv, cap, D, dtype=torch.bfloat16, device=q.device)
+            cached = LayerCache(kb, torch.empty_like(kb), 0)
+            self.cache[layer_id] = cached
+        start = cached.length
+        if start + Tn > cached.capacity:
+            raise RuntimeError(f"SANTA++ cache capacity exceeded in layer {layer_id}: need "
+                               f"{start + Tn}, allocated {cached.capacity}.")
+        sparse_decode = Tn == 1 and self.mode != "dense"
+        q_bf = None if sparse_decode else torch.empty(B, Hq, Tn, D, dtype=torch.bfloat16,
+                                                      device=q.device)
+        q_f32 = torch.empty(B, Hq, Tn, D, dtype=torch.float32, device=q.device) \
+            if sparse_decode else None
+        _lib.check("santa_rope_append", self._lib.santa_rope_append(
+            B, Tn, Hq, Hkv, D, q.contiguous().data_ptr(), k.contiguous().data_ptr(),
+            v.contiguous().data_ptr(), cos.data_ptr(), sin.data_ptr(), cached.key.data_ptr(),
+            cached.value.data_ptr(), cached.capacity, start, _lib.ptr(q_bf), _lib.ptr(q_f32),
+            _lib.stream_handle()))
+        cached.length = start + Tn
+        if sparse_decode:
+            res = santa_decode(q_f32[:, :, 0].contiguous(), cached.key, cached.value,
+                               self.summaries[layer_id], mode=self.config.mode,
+                               n_total=cached.length, sample_end=self.sample_end,
+                               topk_clusters=self.config.topk_clusters,
+                               token_budget=self.config.samples_per_head,
+                               samples=self.config.samples_per_head,
+                               scale=float(attention.scaling), seed=self.config.sample_seed,
+                               step=self._decode_step, with_stats=self.track_traffic)
+            if self.track_traffic:
+                if layer_id not in self._n_groups_host:
+                    self._n_groups_host[layer_id] = self.summaries[layer_id].n_groups.cpu().numpy()
+                self.traffic.record_step(
+                    mode=self.config.mode, n_total=cached.length, sample_end=self.sample_end,
+                    n_exact=res.n_exact.cpu().numpy(), samples=self.config.samples_per_head,
+                    n_groups=self._n_groups_host[layer_id], ess=res.ess.cpu().numpy())
+            out = res.out.to(torch.bfloat16).view(B, 1, Hq * D)
+        elif start == 0:
+            # prompt: causal attention of every position over the prompt
+            out = santa_prefill(q_bf, cached.key, cached.value, causal=True,
+                                scale=float(attention.scaling))
+            if self._probe_idx is not None:
+                self._probe_q[layer_id] = q_bf[:, :, self._probe_idx].float()
+            out = out.transpose(1, 2).reshape(B, Tn, Hq * D)
+        else:
+            # dense decode / continued prompt over the cache (fidelity path)
+            kf, vf = cached.view()
+            kf = kf.repeat_interleave(self.group, dim=1)
+            vf = vf.repeat_interleave(self.group, dim=1)
+            mask = None
+            if Tn > 1:
+                qa = torch.arange(start, start + Tn, device=q.device)[:, None]
+                mask = (torch.arange(cached.length, device=q.device)[None, :] <= qa)[None, None]
+            out = torch.nn.functional.scaled_dot_product_attention(
+                q_bf, kf, vf, attn_mask=mask, scale=float(attention.scaling))
+            out = out.transpose(1, 2).reshape(B, Tn, Hq * D)
+        return attention.o_proj(out.contiguous()), None
+
+    # ---- prefill and clustering ---------------------------------------------
+    @torch.inference_mode()
+    def _dense_prefill_and_cluster(self, input_ids: torch.Tensor, *, probe_seed: int):
+        B, T = input_ids.shape
+        sample_end = T - 1 - self.config.recent_window
+        if sample_end < 2:
+            raise ValueError(f"Prompt has {T} tokens, too short for recent_window="
+                             f"{self.config.recent_window}.")
+        self.sample_end = sample_end
+        self.mode = "dense"
+        probes = probe_positions(self.config.probe_strategy, T, self.config.probe_queries,
+                                 region_start_fraction=self.config.probe_region_start_fraction,
+                                 probe_seed=probe_seed)
+        self._probe_idx = torch.as_tensor(probes, dtype=torch.long, device=input_ids.device)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        try:
+            self.model(input_ids, use_cache=False, logits_to_keep=1)
+        finally:
+            self._probe_idx = None
+        torch.cuda.synchronize()
+        prefill_s = time.perf_counter() - t0
+        n_clusters = self.config.n_clusters or cluster_count(sample_end, self.config.group_size)
+        km = self.config.kmeans
+        P = len(probes)
+        t1 = time.perf_counter()
+        for layer_id in range(self.num_layers):
+            qp = self._probe_q.pop(layer_id)  # [B, Hq, P, D] fp32
+            cached = self.cache[layer_id]
+            labels = torch.empty(B, self.num_kv_heads, sample_end, dtype=torch.int32,
+                                 device=input_ids.device)
+            for b in range(B):
+                for kv in range(self.num_kv_heads):
+                    fp = build_fingerprints(cached.key[b, kv, :sample_end], qp[b].contiguous(),
+                                            kv, self.group, np.arange(P))
+                    est = SklearnLikeTorchMiniBatchKMeans(
+                        n_clusters, batch_size=km.batch_size, n_init=km.n_init,
+                        max_iter=km.max_iter, tol=km.tol,
+                        max_no_improvement=km.max_no_improvement, init_size=km.init_size,
+                        reassignment_ratio=km.reassignment_ratio,
+                        random_state=km.random_state)
+                    labels[b, kv] = est.fit_predict(fp).to(torch.int32)
+            self.summaries[layer_id] = build_summary(cached.key, cached.value, labels,
+                                                     n_clusters, sample_end=sample_end,
+                                                     n_total=cached.length)
+        torch.cuda.synchronize()
+        return prefill_s, time.perf_counter() - t1, sample_end, n_clusters
+
+    # ---- generation ------------------------------------------------------------
+    @torch.inference_mode()
+    def generate(self, input_ids: torch.Tensor, *, max_new_tokens: int,
+                 eos_token_ids: set[int] | None = None, stop_on_eos: bool = False,
+                 random_seed: int = 0) -> SantaGeneration:
+        if input_ids.ndim != 2:
+            raise ValueError("input_ids must be [batch, T]")
+        B, T = input_ids.shape
+        if T < 2:
+            raise ValueError("SANTA++ requires at least two prompt tokens.")
+        self.clear()
+        self.cache_capacity = T + max_new_tokens
+        t0 = time.perf_counter()
+        with self.patched():
+            prefill_s, cluster_s, sample_end, n_clusters = self._dense_prefill_and_cluster(
+                input_ids, probe_seed=random_seed)
+            self._trim_cache(T - 1)
+            self.mode = self.config.mode
+            self.traffic = DecodeTrafficTracker()
+            generated = [[] for _ in range(B)]
+            current = input_ids[:, -1:]
+            position = T - 1
+            done = torch.zeros(B, dtype=torch.bool, device=input_ids.device)
+            torch.cuda.synchronize()
+            t2 = time.perf_counter()
+            for step in range(max_new_tokens):
+                self._decode_step = step
+                out = self.model(current, position_ids=torch.full(
+                    (B, 1), position, dtype=torch.long, device=input_ids.device),
+                    use_cache=False, logits_to_keep=1)
+                current = out.logits[:, -1].argmax(dim=-1, keepdim=True)
+                ids = current[:, 0].tolist()
+                for b in range(B):
+                    generated[b].append(int(ids[b]))
+                position += 1
+                if stop_on_eos and eos_token_ids:
+                    done |= torch.tensor([i in eos_token_ids for i in ids], device=done.device)
+                    if bool(done.all()):
+                        break
+            torch.cuda.synchronize()
+            decode_s = time.perf_counter() - t2
+        metrics = {
+            "backend": "santapp_b200", "mode": self.config.mode, "batch": B,
+            "prompt_tokens": T, "generated_tokens": len(generated[0]),
+            "prefill_seconds": prefill_s, "clustering_seconds": cluster_s,
+            "decode_seconds": decode_s, "total_seconds": time.perf_counter() - t0,
+            "sampled_prefix_tokens": sample_end, "nominal_clusters_per_kv_head": n_clusters,
+            **self.traffic.as_dict(),
+        }
+        self.clear()
+        return SantaGeneration(token_ids=generated, metrics=metrics)

@@ -25,7 +25,8 @@ __all__ = ["santa_prefill"]
 def santa_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, causal: bool = True,
                   scale: float | None = None, out: torch.Tensor | None = None,
                   return_lse: bool = False, stream=None):
-    """q ``[B, Hq, T, D]``, k / v ``[B, Hkv, T, D]`` bf16 CUDA tensors ->
+    """q ``[B, Hq, T, D]``, k / v ``[B, Hkv, C, D]`` (C >= T: a cache whose first
+    T tokens are the prompt) bf16 CUDA tensors ->
     out ``[B, Hq, T, D]`` bf16 (and the natural-log softmax denominators
     ``[B, Hq, T]`` fp32 with ``return_lse``)."""
     for name, t in (("q", q), ("k", k), ("v", v)):
@@ -33,13 +34,14 @@ def santa_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, causal: 
         if t.dtype != torch.bfloat16 or t.dim() != 4:
             raise ValueError(f"{name} must be a [batch, heads, seq, head_dim] bf16 tensor")
     B, Hq, T, D = q.shape
-    Hkv = k.shape[1]
-    if k.shape != (B, Hkv, T, D) or v.shape != k.shape:
-        raise ValueError("k and v must be [batch, kv_heads, seq, head_dim] matching q")
+    Hkv, cap = k.shape[1], k.shape[2]
+    if k.shape != (B, Hkv, cap, D) or v.shape != k.shape or cap < T:
+        raise ValueError("k and v must be [batch, kv_heads, >= seq, head_dim] matching q "
+                         "(a KV cache whose first seq tokens are used)")
     if Hq % Hkv:
         raise ValueError("Query heads must be divisible by KV heads.")
     shape = _lib.SantaPrefillShape(B, Hq, Hkv, T, D, 1.0 / math.sqrt(D) if scale is None
-                                   else float(scale), 1 if causal else 0)
+                                   else float(scale), 1 if causal else 0, cap)
     lib = _lib.load()
     nbytes = ctypes.c_size_t()
     _lib.check("santa_prefill_workspace_bytes",

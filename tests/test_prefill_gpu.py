@@ -48,6 +48,7 @@ def test_single_tile_single_head():
 @pytest.mark.parametrize("B,Hq,Hkv,T,causal", [
     (1, 7, 1, 640, True),     # GQA 7, several tiles
     (2, 4, 2, 1000, True),    # ragged last tile (T % 128 != 0)
+    (1, 7, 1, 701, True),     # T % 8 != 0: padded V^T rows
     (1, 2, 1, 384, False),    # non-causal
 ])
 def test_prefill_matches_fp32_reference(B, Hq, Hkv, T, causal):
