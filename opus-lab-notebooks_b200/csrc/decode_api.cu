@@ -75,6 +75,8 @@ static int prepare_decode(const SantaGeometry *geo, const SantaDecodeParams *p, 
                           !summary->centroids || !summary->n_groups))
         return SANTA_ERR_INVALID_ARGUMENT;
     if (!summary->sorted_key || !summary->sorted_value) return SANTA_ERR_INVALID_ARGUMENT;
+    if (needs_summary && ((uintptr_t)summary->centroids & 15))  // 16-byte centroid copies
+        return SANTA_ERR_UNSUPPORTED;
     if ((p->mode == SANTA_MODE_UNIFORM || p->mode == SANTA_MODE_SANTA) && !summary->positions)
         return SANTA_ERR_INVALID_ARGUMENT;
     if (need_draws && p->sample_source == SANTA_SAMPLES_INJECTED && p->mode != SANTA_MODE_TOPK) {

@@ -18,8 +18,10 @@
 //      current one is scored.  A thread scores two centroids for one query
 //      head with two interleaved fmaf chains.
 //   2. Top-k: one warp per query head; every lane keeps its clusters' keys
-//      (orderable guess << 32 | ~index) sorted in registers, so extracting
-//      the next best cluster is two redux.sync steps and a register shift.
+//      (orderable guess << 32 | ~index) sorted in registers.  Hybrid with
+//      k <= 16 takes the 16 largest with a butterfly of bitonic merges; the
+//      budget walk and larger k extract the next best cluster with two
+//      redux.sync steps and a register shift per cluster.
 //   3. Union of the group's selections and its expanded row list.
 //   4. Draws: two warps per query head.
 #include "decode_common.cuh"
@@ -64,7 +66,10 @@ __device__ int sel_block_exclusive_scan(int v, int *sw, int *total) {
 template <int D, int KPL>
 struct SelSmem {
     static constexpr int ROWS = KPL == 8 ? 256 : kTileC;
-    static constexpr int CT_FLOATS = ROWS * (D + 1);
+    // whole-block variant: 16-byte rows (pitch D + 4) read as float4, which
+    // keeps 8 consecutive rows of a quarter warp on distinct bank groups
+    static constexpr int PITCH = KPL == 8 ? D + 4 : D + 1;
+    static constexpr int CT_FLOATS = ROWS * PITCH;
     static constexpr int MAXG = KPL * 32;
     static_assert(CT_FLOATS >= SANTA_MAX_GROUP * MAXG,
                   "the centroid area also holds the guided CDF");
@@ -76,6 +81,49 @@ struct SelSmem {
 __device__ __forceinline__ void cp_async4(void *dst_smem, const void *src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32(dst_smem)), "l"(src)
                  : "memory");
+}
+
+__device__ __forceinline__ uint64_t shfl_xor_u64(uint64_t v, int o) {
+    const uint32_t lo = __shfl_xor_sync(0xffffffffu, (uint32_t)v, o);
+    const uint32_t hi = __shfl_xor_sync(0xffffffffu, (uint32_t)(v >> 32), o);
+    return ((uint64_t)hi << 32) | lo;
+}
+
+// The 16 largest of the warp's 32 x 8 keys (every lane's 8 sorted
+// descending, 0 = none), sorted descending, in every lane.  Each butterfly
+// level merges the lane's list with its partner's: the elementwise maximum of
+// one list and the other reversed holds the 16 largest of both as a bitonic
+// sequence, which four half-cleaner stages sort.  Keys are unique (the low
+// word is the cluster id), so the result does not depend on the order of
+// the levels.
+__device__ __forceinline__ void warp_top16(const uint64_t (&k8)[8], uint64_t (&t)[16]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        t[i] = k8[i];
+        t[i + 8] = 0ull;
+    }
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        // entries i and 15 - i exchange with the partner together (two live
+        // temporaries instead of a copy of the partner's list)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint64_t a = shfl_xor_u64(t[15 - i], o), b = shfl_xor_u64(t[i], o);
+            t[i] = t[i] > a ? t[i] : a;
+            t[15 - i] = t[15 - i] > b ? t[15 - i] : b;
+        }
+#pragma unroll
+        for (int j = 8; j > 0; j >>= 1) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                if ((i & j) == 0) {
+                    const uint64_t x = t[i], y = t[i + j];
+                    t[i] = x > y ? x : y;
+                    t[i + j] = x > y ? y : x;
+                }
+            }
+        }
+    }
 }
 
 // KPL: keys per lane in the top-k extraction (clusters lane, lane+32, ...).
@@ -125,11 +173,12 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
     };
     if (uses_clusters) {
         if constexpr (KPL == 8) {
-            // the whole block (<= 256 rows) straight into shared memory, pitch
-            // D + 1 so that the scoring reads are bank-conflict free
-            for (int i = tid; i < Gmax * D; i += kSelThreads) {
-                const int r = i / D;
-                cp_async4(ct + r * (D + 1) + (i - r * D), cent + i);
+            // the whole block (<= 256 rows) straight into shared memory with
+            // 16-byte copies, rows D + 4 floats apart
+            constexpr int P = SelSmem<D, KPL>::PITCH;
+            for (int i = tid; i < Gmax * D / 4; i += kSelThreads) {
+                const int r = (4 * i) / D;
+                cp_async16(ct + r * P + (4 * i - r * D), cent + 4 * i);
             }
             for (int i = tid; i < Gmax; i += kSelThreads) {
                 cp_async4(starts_s + i, a.sum.starts + (int64_t)bh * Gmax + i);
@@ -166,14 +215,21 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
         const float *logn = a.sum.log_n + (int64_t)bh * Gmax;
         const int c = tid & 63, h = tid >> 6;  // 64 slots x 8 heads, 4 centroids a thread
         if (h < g) {
+            constexpr int P = SelSmem<D, KPL>::PITCH;
             const float *qh = qs + h * D;
             float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
-            for (int d = 0; d < D; ++d) {
-                const float qd = qh[d];
+            for (int d = 0; d < D; d += 4) {
+                const float4 q4 = *(const float4 *)(qh + d);
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    acc[k] = fmaf(ct[(c + 64 * k) * (D + 1) + d], qd, acc[k]);
+                for (int k = 0; k < 4; ++k) {
+                    // fmaf chain in ascending d, four dimensions per load
+                    const float4 c4 = *(const float4 *)(ct + (c + 64 * k) * P + d);
+                    acc[k] = fmaf(c4.x, q4.x, acc[k]);
+                    acc[k] = fmaf(c4.y, q4.y, acc[k]);
+                    acc[k] = fmaf(c4.z, q4.z, acc[k]);
+                    acc[k] = fmaf(c4.w, q4.w, acc[k]);
+                }
             }
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
@@ -302,7 +358,27 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
                         (int)(0xFFFFFFFFu - (uint32_t)key[j]) - cbase;
             nsel = __shfl_sync(0xffffffffu, x, 31);
         }
-        while (!a.shard_cands && nsel < kmax) {
+        bool ranked = false;
+        if constexpr (KPL == 8) {
+            // hybrid with k <= 16: one merge network instead of k extraction rounds
+            if (!a.shard_cands && mode == SANTA_MODE_HYBRID && kmax <= 16) {
+                uint64_t t[16];
+                warp_top16(key, t);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    if (j < kmax && t[j] != 0ull) {
+                        if (lane == j) {
+                            gapcum[h * (2 * kcap + 1) + j] =
+                                (int)(0xFFFFFFFFu - (uint32_t)t[j]) - cbase;
+                            if (a.cand_out) a.cand_out[((int64_t)bh * g + h) * kk + j] = t[j];
+                        }
+                        ++nsel;
+                    }
+                }
+                ranked = true;
+            }
+        }
+        while (!a.shard_cands && !ranked && nsel < kmax) {
             const uint32_t bhi = (uint32_t)(key[0] >> 32);
             const uint32_t mhi = __reduce_max_sync(0xffffffffu, bhi);
             const uint32_t mlo = __reduce_max_sync(0xffffffffu, bhi == mhi ? (uint32_t)key[0] : 0u);

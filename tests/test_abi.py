@@ -70,7 +70,7 @@ def test_workspace_queries_validate_arguments():
     assert lib.santa_decode_workspace_bytes(ctypes.byref(geo), ctypes.byref(p_bad), 256,
                                             ctypes.byref(n)) == _lib.SANTA_ERR_INVALID_ARGUMENT
     # a compute call without a workspace is refused before touching the device
-    s = _lib.SantaSummary(*([1] * 9), 256)
+    s = _lib.SantaSummary(*([256] * 9), 256)  # aligned dummy addresses, never dereferenced
     assert lib.santa_decode(ctypes.byref(geo), ctypes.byref(p), 1, 1, 1, ctypes.byref(s), None,
                             None, 1, 1, None, None, None, 0, None) == _lib.SANTA_ERR_WORKSPACE
 
