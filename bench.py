@@ -32,7 +32,9 @@ import torch  # noqa: E402
 
 from santapp_b200.synthetic import QWEN3_8B_128K, QWEN7B_32K, make_decode_workload  # noqa: E402
 
-WORKLOADS = {"qwen7b-32k": QWEN7B_32K, "qwen3-8b-128k": QWEN3_8B_128K}
+WORKLOADS = {"qwen7b-32k": QWEN7B_32K, "qwen3-8b-128k": QWEN3_8B_128K,
+             "qwen7b-prefill-32k": None}
+PREFILL_METRIC = "causal prefill attention TFLOP/s (tcgen05) and MiniBatchKMeans seconds per fit"
 METRIC = "SANTA++ decode attn tokens/s @32K-128K ctx; achieved HBM GB/s vs 8 TB/s peak"
 L2_FLUSH_BYTES = 256 << 20
 
@@ -43,7 +45,9 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="qwen7b-32k")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="qwen7b-32k",
+                    help="qwen7b-prefill-32k: prompt prefill + clustering of the Qwen2.5-7B "
+                         "shape (one GPU), not a decode step")
     ap.add_argument("--mode", default="hybrid")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -403,6 +407,78 @@ def cpu_baseline_sample(args, shape, w, summ):
 
 
 # ---------------------------------------------------------------------------
+# prefill + clustering of one layer (Qwen2.5-7B shape, 32K prompt)
+# ---------------------------------------------------------------------------
+
+def run_prefill(args):
+    """Causal prefill attention of one layer, [1, 28, 32768, 128] bf16 with 4
+    KV heads, through santa_prefill (tcgen05), then MiniBatchKMeans of each KV
+    head's 32704 prefix keys (k=256, minibatch 4096, 20 iterations, seed 0)
+    through SklearnLikeTorchMiniBatchKMeans.  Seeded N(0,1) Q/K/V; the keys are
+    the 256-component Gaussian mixture of the decode workloads."""
+    from santapp_b200.attention.kmeans import SklearnLikeTorchMiniBatchKMeans
+    from santapp_b200.attention.prefill import santa_prefill
+    from santapp_b200.synthetic import scaled_shape
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, Hq, Hkv, T, D = 1, 28, 4, 32768, 128
+    shape = scaled_shape(QWEN7B_32K, batch=1, steps=1)
+    w = make_decode_workload(shape, seed=args.seed, device=dev)
+    g = torch.Generator(device=dev).manual_seed(args.seed + 1)
+    q = torch.randn(B, Hq, T, D, device=dev, generator=g).to(torch.bfloat16)
+    k, v = w.keys, w.values
+    flops = 4.0 * Hq * D * T * (T + 1) / 2
+    out = santa_prefill(q, k, v)
+    flush = L2Flush(dev)
+    torch.cuda.synchronize()
+    ts = []
+    for i in range(args.warmup + args.steps):
+        flush()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        santa_prefill(q, k, v, out=out)
+        e1.record()
+        torch.cuda.synchronize()
+        if i >= args.warmup:
+            ts.append(e0.elapsed_time(e1))
+    err = int(out._santa_error_flag.item())
+    ms = float(np.mean(ts))
+    peaks_d = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json"))) \
+        if os.path.exists(os.path.join(REPO, "MEASURED_PEAKS.json")) else {}
+    peak = float(peaks_d.get("bf16_tflops", 1590.0))
+    tflops = flops / (ms / 1e3) / 1e12
+    # clustering: one fit per KV head, each timed with a host clock around the
+    # call (the fit synchronises every mini-batch, as the reference does)
+    fits = []
+    for kv in range(Hkv):
+        x = k[0, kv, :shape.sample_end].float()
+        est = SklearnLikeTorchMiniBatchKMeans(256, batch_size=4096, max_iter=20, random_state=0)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        est.fit_predict(x)
+        torch.cuda.synchronize()
+        fits.append((time.perf_counter() - t0, est.n_steps_))
+    return {
+        "metric": PREFILL_METRIC, "value": tflops, "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) queries, Gaussian-mixture keys, N(0,1) values)",
+        "config": {"workload": "qwen2.5-7b-prefill-ctx32768", "query_heads": Hq,
+                   "kv_heads": Hkv, "head_dim": D, "batch": B, "prompt": T, "causal": True,
+                   "kmeans": {"k": 256, "batch_size": 4096, "max_iter": 20, "rows": shape.sample_end,
+                              "features": D}},
+        "roofline": {"kernel": "prefill_fwd_kernel", "bound": "tensor", "achieved": tflops,
+                     "peak": peak, "peak_kind": "measured" if peaks_d else "fallback",
+                     "unit": "TFLOP/s", "frac": tflops / peak,
+                     "algorithmic_flops": flops},
+        "kmeans_seconds_per_fit": [round(f[0], 4) for f in fits],
+        "kmeans_steps_per_fit": [int(f[1]) for f in fits],
+        "error_flag": err,
+        "gpu_launches": 2 * args.steps,
+    }
+
+
+# ---------------------------------------------------------------------------
 # our arm on N GPUs: sequence shards
 # ---------------------------------------------------------------------------
 
@@ -443,7 +519,8 @@ def run_sharded(args, rank, world):
         torch.cuda.synchronize()
 
         # per step: events around the step, and on every rank the phase
-        # split (keys | exchange 1 | select | attend | exchange 2 | merge)
+        # split (keys | exchange 1 | select | attend | exchange 2 | merge);
+        # eager launches (the host runs ahead of the device)
         ev = [[torch.cuda.Event(enable_timing=True) for _ in range(7)]
               for _ in range(args.steps)]
         clocks = ClockSampler(local)
@@ -531,7 +608,8 @@ def run_sharded(args, rank, world):
                       "read of another buffer)",
             },
             "phase_ms": phase,
-            "timing": "CUDA events around each step on every rank, max over ranks of the sum",
+            "timing": "CUDA events around each step on every rank (eager launches), max over "
+                      "ranks of the sum",
             "wall_s": wall,
             "clocks": clk,
             "gpu_launches": runner.kernels_per_call * args.steps,
@@ -567,6 +645,8 @@ def run_reference(args, rank, world):
     if rank != 0:
         return None
     shape = WORKLOADS[args.workload]
+    if shape is None:
+        raise SystemExit("the reference arm times the decode workloads")
     from santapp_b200.synthetic import scaled_shape
     # one sequence's cache (its 4 KV heads) is enough to time per-token cost;
     # each step decodes that sequence's Hq heads across all host cores
@@ -618,6 +698,8 @@ def main():
         line = run_sharded(args, rank, world)
     elif args.gpus > 1:
         raise SystemExit("--gpus N > 1 runs under torchrun (one process per GPU)")
+    elif args.workload == "qwen7b-prefill-32k":
+        line = run_prefill(args)
     else:
         line = run_ours(args, rank, world)
     if line is not None and rank == 0:
