@@ -14,6 +14,17 @@
  *                              (SantaPlusEngine._approximate_attention), batched
  *                              over (batch, query head) as the decode branch of
  *                              _attention_forward does per head at :347-358
+ *   santa_prefill              santapp_ruler/attention/santapp.py:320-346
+ *                              (prefill branch -> sdpa_attention_forward)
+ *   santa_rope_append          santapp_ruler/attention/santapp.py:234-274, 308-313
+ *                              (_append_cache and the RoPE of _attention_forward)
+ *   santa_fingerprints         santapp_ruler/attention/santapp.py:598-691
+ *   santa_kmeans_*             santapp_ruler/attention/minibatch_kmeans.py:58-267
+ *                              (_squared_distances, _assign, _greedy_kmeans_plus_plus,
+ *                              the mini-batch update and reassignment of fit_predict)
+ *   santa_shard_*, santa_merge_shards
+ *                              no counterpart (the reference is single-GPU):
+ *                              santa_decode over sequence shards
  */
 #ifndef SANTA_B200_H
 #define SANTA_B200_H
