@@ -56,6 +56,8 @@ def parse_args():
                     help="skip the host-side extras (byte accounting, e2e, CPU baseline)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="bound on the CPU-baseline sample")
+    ap.add_argument("--transport", choices=["nccl", "p2p"], default="nccl",
+                    help="N > 1: NCCL all-gathers, or the kernels' own peer-memory exchange")
     return ap.parse_args()
 
 
@@ -508,7 +510,8 @@ def run_sharded(args, rank, world):
         runner = ShardedDecodeStep(p.keys, p.values, summ, num_query_heads=shape.num_query_heads,
                                    n_total=p.n_total, topk_clusters=shape.topk_clusters,
                                    samples=p.samples, shard_index=rank, num_shards=world,
-                                   cluster_base=p.cluster_base, seed=args.seed)
+                                   cluster_base=p.cluster_base, seed=args.seed,
+                                   transport=args.transport)
         queries = p.queries
         flush = L2Flush(dev)
         torch.cuda.synchronize()
@@ -519,35 +522,55 @@ def run_sharded(args, rank, world):
         torch.cuda.synchronize()
 
         # per step: events around the step, and on every rank the phase
-        # split (keys | exchange 1 | select | attend | exchange 2 | merge);
-        # eager launches (the host runs ahead of the device)
-        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(7)]
+        # split (keys | exchange 1 | select | attend | exchange 2 | merge).
+        # NCCL transport: eager launches.  Peer-memory transport: the step is
+        # four kernels of this library and no library collective, captured in
+        # one CUDA graph per step (epoch baked in) with event-record nodes.
+        use_graphs = runner.p2p is not None
+        ev = [[torch.cuda.Event(enable_timing=True, external=use_graphs) for _ in range(7)]
               for _ in range(args.steps)]
+
+        def one_step(i, e, stream=None):
+            st = args.warmup + i
+            e[0].record(stream)
+            runner.candidates(queries[st], st, stream=stream)
+            e[1].record(stream)
+            runner.exchange_keys()
+            e[2].record(stream)
+            runner.plan(stream=stream)
+            e[3].record(stream)
+            runner.execute(stream=stream)
+            e[4].record(stream)
+            runner.exchange_partials()
+            e[5].record(stream)
+            runner.merge(stream=stream)
+            e[6].record(stream)
+
+        graphs = []
+        if use_graphs:
+            cap = torch.cuda.Stream()
+            with torch.cuda.stream(cap):
+                for i in range(args.steps):
+                    gph = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(gph, stream=cap):
+                        one_step(i, ev[i], cap)
+                    graphs.append(gph)
+            torch.cuda.synchronize()
         clocks = ClockSampler(local)
         clocks.start()
         dist.barrier()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         for i in range(args.steps):
-            st = args.warmup + i
             flush()
-            e = ev[i]
-            e[0].record()
-            runner.candidates(queries[st], st)
-            e[1].record()
-            runner.exchange_keys()
-            e[2].record()
-            runner.plan()
-            e[3].record()
-            runner.execute()
-            e[4].record()
-            runner.exchange_partials()
-            e[5].record()
-            runner.merge()
-            e[6].record()
+            if graphs:
+                graphs[i].replay()
+            else:
+                one_step(i, ev[i])
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
         clk = clocks.stop()
+        del graphs
         ph = np.array([[e[j].elapsed_time(e[j + 1]) for j in range(6)] for e in ev])
         mine = torch.tensor([ph.sum()], dtype=torch.float64, device=dev)
         dist.all_reduce(mine, op=dist.ReduceOp.MAX)
@@ -602,14 +625,17 @@ def run_sharded(args, rank, world):
                 "head_dim": shape.head_dim, "batch": shape.batch, "context": shape.context,
                 "clusters": shape.n_clusters, "topk_clusters": shape.topk_clusters,
                 "samples": shape.samples, "recent_window": shape.recent_window, "mode": "hybrid",
-                "parallelism": f"sequence shards x{world} (NCCL all-gather of top-k keys and "
-                               f"of (m, l, o) partials)",
+                "parallelism": (f"sequence shards x{world} (NCCL all-gather of top-k keys and "
+                                f"of (m, l, o) partials)" if args.transport == "nccl" else
+                                f"sequence shards x{world} (top-k keys and (m, l, o) partials "
+                                f"stored by the kernels into every rank's buffer over NVLink)"),
                 "l2": "flushed before every step outside the events (256 MiB write + 256 MiB "
                       "read of another buffer)",
             },
             "phase_ms": phase,
-            "timing": "CUDA events around each step on every rank (eager launches), max over "
-                      "ranks of the sum",
+            "timing": ("CUDA events around each step on every rank, max over ranks of the sum; "
+                       + ("one CUDA graph per step (this library's four kernels)"
+                          if runner.p2p is not None else "eager launches")),
             "wall_s": wall,
             "clocks": clk,
             "gpu_launches": runner.kernels_per_call * args.steps,
@@ -620,8 +646,16 @@ def run_sharded(args, rank, world):
                          "frac": None, "traffic": None,
                          "note": "per-kernel roofline is reported by the single-GPU run"},
         }
+        if runner.p2p is not None:
+            bad = torch.tensor([int(runner.p2p_error.item())], device=dev)
+            dist.all_reduce(bad, op=dist.ReduceOp.MAX)
+            line["p2p_wait_timeouts"] = int(bad.item())
         return line if rank == 0 else None
     finally:
+        dist.barrier()
+        if "runner" in locals():
+            torch.cuda.synchronize()
+            runner.close()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -371,12 +371,48 @@ int santa_kmeans_plusplus(const float *x, const int64_t *rows, const float *xx, 
 #define SANTA_SHARD_MAX_KEYS 512 /* num_shards * topk_clusters */
 #define SANTA_PARTIAL_FLOATS(head_dim) ((head_dim) + 8)
 
+/* Peer-memory exchange (optional): every rank allocates one exchange buffer
+ * (santa_p2p_alloc, santa_p2p_buffer_bytes), shares its IPC handle, maps the
+ * others' (santa_p2p_ipc_open) and passes the table of all ranks' buffers as
+ * mapped in this process.  The kernels then write candidate keys and partials
+ * straight into every rank's buffer and signal a per-rank flag; the consuming
+ * kernels wait for the flags (bounded: error_flag is set to 1 if a peer never
+ * signals within ~2 s) instead of the caller running two all-gathers.  epoch =
+ * the step number + 1, increasing per step; the same epoch for the
+ * candidates, plan, execute and merge calls of one step. */
+typedef struct SantaP2P {
+    void *const *peer_buffers;   /* device array [num_shards] of buffers (own at shard_index) */
+    void *local_buffer;          /* this rank's buffer */
+    uint64_t epoch;
+    int32_t *error_flag;         /* device int32 */
+    int32_t rows;                /* B * Hq */
+    int32_t keys_per_row;        /* topk_clusters */
+    int32_t partial_floats;      /* SANTA_PARTIAL_FLOATS(head_dim) */
+    int32_t reserved;
+} SantaP2P;
+
+#define SANTA_IPC_HANDLE_BYTES 64
+
+int santa_p2p_buffer_bytes(int32_t num_shards, int32_t rows, int32_t keys_per_row,
+                           int32_t head_dim, size_t *bytes);
+/* cudaMalloc'd exchange buffer, zeroed (flags start at epoch 0). */
+int santa_p2p_alloc(size_t bytes, void **buffer);
+int santa_p2p_free(void *buffer);
+int santa_p2p_ipc_handle(void *buffer, void *handle);
+int santa_p2p_ipc_open(const void *handle, void **mapped);
+int santa_p2p_ipc_close(void *mapped);
+/* 8 bytes at a device address (own or mapped peer buffer), for set-up checks. */
+int santa_p2p_peek(const void *address, uint64_t *value);
+int santa_p2p_poke(void *address, uint64_t value);
+
 typedef struct SantaShard {
     int32_t shard_index;         /* this rank's shard, < num_shards */
     int32_t num_shards;          /* <= SANTA_MAX_SHARDS */
     int32_t cluster_base;        /* global id of row 0 of this shard's summary */
     int32_t reserved;
-    const uint64_t *candidates;  /* plan: [num_shards][B*Hq][topk_clusters] gathered keys */
+    const uint64_t *candidates;  /* plan: [num_shards][B*Hq][topk_clusters] gathered keys
+                                    (ignored with p2p: they are in the exchange buffer) */
+    const SantaP2P *p2p;         /* NULL: the caller exchanges keys and partials */
 } SantaShard;
 
 /* Candidate keys: [B*Hq][topk_clusters] uint64, per row descending, key =
@@ -400,8 +436,8 @@ int santa_shard_plan(const SantaGeometry *geo, const SantaDecodeParams *p, const
  * 2^(lw - m); ms, e1, e2 the same sums over the sample weights alone. */
 int santa_shard_execute(const SantaGeometry *geo, const SantaDecodeParams *p, const float *q,
                         const void *key_cache, const void *value_cache,
-                        const SantaSummary *summary, float *partial, void *workspace,
-                        size_t workspace_bytes, cudaStream_t stream);
+                        const SantaSummary *summary, const SantaShard *shard, float *partial,
+                        void *workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /* Selection readout of santa_shard_plan (arguments of santa_decode_select). */
 int santa_shard_select(const SantaGeometry *geo, const SantaDecodeParams *p, const float *q,
@@ -411,11 +447,13 @@ int santa_shard_select(const SantaGeometry *geo, const SantaDecodeParams *p, con
                        int32_t *n_exact, void *workspace, size_t workspace_bytes,
                        cudaStream_t stream);
 
-/* partials: [num_shards][rows][SANTA_PARTIAL_FLOATS(head_dim)]; rows = B*Hq.
+/* partials: [num_shards][rows][SANTA_PARTIAL_FLOATS(head_dim)]; rows = B*Hq
+ * (with p2p: NULL, read from the exchange buffer after the peers' flags).
  * out [rows][head_dim], lse [rows] (natural log) and ess [rows] (may be
  * NULL) as santa_decode writes them. */
 int santa_merge_shards(int32_t rows, int32_t head_dim, int32_t num_shards, const float *partials,
-                       float *out, float *lse, float *ess, cudaStream_t stream);
+                       const SantaP2P *p2p, int32_t shard_index, float *out, float *lse,
+                       float *ess, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

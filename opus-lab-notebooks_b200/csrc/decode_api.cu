@@ -6,6 +6,8 @@
 // stream-ordered halves, santa_decode_select reads the selection out.
 #include "decode_common.cuh"
 
+#include <string.h>
+
 using namespace santa;
 
 extern "C" int santa_check_geometry(const SantaGeometry *geo);
@@ -105,6 +107,7 @@ static int prepare_decode(const SantaGeometry *geo, const SantaDecodeParams *p, 
     a->cand_out = nullptr;
     a->shard_cands = nullptr;
     a->part_out = nullptr;
+    memset(&a->p2p, 0, sizeof(a->p2p));
     decode_ws_layout(BH, summary->max_groups, geo->group, p->samples,
                      attend_partial_slots(geo, nsplit), geo->head_dim, geo->sample_end,
                      (char *)workspace, &a->ws);
@@ -179,6 +182,28 @@ extern "C" int santa_decode_select(const SantaGeometry *geo, const SantaDecodePa
 // ---------------------------------------------------------------------------
 // sequence shards (HYBRID, bf16 caches)
 // ---------------------------------------------------------------------------
+static int bind_p2p(const SantaGeometry *geo, const SantaDecodeParams *p,
+                    const SantaShard *shard, DecodeArgs *a) {
+    memset(&a->p2p, 0, sizeof(a->p2p));
+    const SantaP2P *c = shard->p2p;
+    if (!c) return SANTA_OK;
+    if (!c->peer_buffers || !c->local_buffer || !c->error_flag || c->epoch == 0)
+        return SANTA_ERR_INVALID_ARGUMENT;
+    if (c->rows != geo->batch * geo->num_kv_heads * geo->group ||
+        c->keys_per_row != p->topk_clusters || c->partial_floats != geo->head_dim + 8)
+        return SANTA_ERR_INVALID_ARGUMENT;
+    a->p2p.peers = c->peer_buffers;
+    a->p2p.local = (unsigned char *)c->local_buffer;
+    a->p2p.epoch = c->epoch;
+    a->p2p.err = c->error_flag;
+    a->p2p.rank = shard->shard_index;
+    a->p2p.n = shard->num_shards;
+    a->p2p.rows = c->rows;
+    a->p2p.kk = c->keys_per_row;
+    a->p2p.pf = c->partial_floats;
+    return SANTA_OK;
+}
+
 static int check_shard(const SantaGeometry *geo, const SantaDecodeParams *p,
                        const SantaShard *shard, bool need_candidates) {
     if (!geo || !p || !shard) return SANTA_ERR_INVALID_ARGUMENT;
@@ -190,7 +215,7 @@ static int check_shard(const SantaGeometry *geo, const SantaDecodeParams *p,
     if (shard->cluster_base < 0) return SANTA_ERR_INVALID_ARGUMENT;
     if (p->topk_clusters < 1 || (int64_t)p->topk_clusters * shard->num_shards > SANTA_SHARD_MAX_KEYS)
         return SANTA_ERR_UNSUPPORTED;
-    if (need_candidates && !shard->candidates) return SANTA_ERR_INVALID_ARGUMENT;
+    if (need_candidates && !shard->candidates && !shard->p2p) return SANTA_ERR_INVALID_ARGUMENT;
     return SANTA_OK;
 }
 
@@ -209,6 +234,13 @@ static int prepare_shard(const SantaGeometry *geo, const SantaDecodeParams *p, c
     a->cluster_base = shard->cluster_base;
     a->num_shards = shard->num_shards;
     a->shard_cands = need_candidates ? shard->candidates : nullptr;
+    st = bind_p2p(geo, p, shard, a);
+    if (st) return st;
+    if (need_candidates && a->p2p.peers) {  // the gathered keys live in the exchange buffer
+        const size_t per = (size_t)a->p2p.rows * a->p2p.kk;
+        a->shard_cands = (const uint64_t *)(a->p2p.local + kP2PKeys) +
+                         (size_t)(a->p2p.epoch & 1) * a->p2p.n * per;
+    }
     return SANTA_OK;
 }
 
@@ -242,14 +274,16 @@ extern "C" int santa_shard_plan(const SantaGeometry *geo, const SantaDecodeParam
 extern "C" int santa_shard_execute(const SantaGeometry *geo, const SantaDecodeParams *p,
                                    const float *q, const void *key_cache,
                                    const void *value_cache, const SantaSummary *summary,
-                                   float *partial, void *workspace, size_t workspace_bytes,
-                                   cudaStream_t stream) {
-    if (!partial) return SANTA_ERR_INVALID_ARGUMENT;
-    if (!p || p->mode != SANTA_MODE_HYBRID || !geo || geo->kv_dtype != SANTA_DTYPE_BF16)
-        return SANTA_ERR_UNSUPPORTED;
+                                   const SantaShard *shard, float *partial, void *workspace,
+                                   size_t workspace_bytes, cudaStream_t stream) {
+    if (!partial || !shard) return SANTA_ERR_INVALID_ARGUMENT;
+    int st = check_shard(geo, p, shard, false);
+    if (st) return st;
     DecodeArgs a;
-    int st = prepare_decode(geo, p, q, key_cache, value_cache, summary, nullptr, nullptr, false,
-                            workspace, workspace_bytes, &a);
+    st = prepare_decode(geo, p, q, key_cache, value_cache, summary, nullptr, nullptr, false,
+                        workspace, workspace_bytes, &a);
+    if (st) return st;
+    st = bind_p2p(geo, p, shard, &a);
     if (st) return st;
     a.part_out = partial;
     return launch_execute(a, stream);
@@ -272,10 +306,28 @@ extern "C" int santa_shard_select(const SantaGeometry *geo, const SantaDecodePar
 }
 
 extern "C" int santa_merge_shards(int32_t rows, int32_t head_dim, int32_t num_shards,
-                                  const float *partials, float *out, float *lse, float *ess,
+                                  const float *partials, const SantaP2P *p2p,
+                                  int32_t shard_index, float *out, float *lse, float *ess,
                                   cudaStream_t stream) {
     if (rows <= 0 || num_shards < 1 || num_shards > SANTA_MAX_SHARDS) return SANTA_ERR_INVALID_ARGUMENT;
     if (head_dim != 64 && head_dim != 128) return SANTA_ERR_UNSUPPORTED;
-    if (!partials || !out) return SANTA_ERR_INVALID_ARGUMENT;
-    return launch_merge_shards(rows, head_dim, num_shards, partials, out, lse, ess, stream);
+    if ((!partials && !p2p) || !out) return SANTA_ERR_INVALID_ARGUMENT;
+    P2PArgs c;
+    memset(&c, 0, sizeof(c));
+    if (p2p) {
+        if (!p2p->peer_buffers || !p2p->local_buffer || !p2p->error_flag || p2p->epoch == 0 ||
+            p2p->rows != rows || p2p->partial_floats != head_dim + 8 || shard_index < 0 ||
+            shard_index >= num_shards)
+            return SANTA_ERR_INVALID_ARGUMENT;
+        c.peers = p2p->peer_buffers;
+        c.local = (unsigned char *)p2p->local_buffer;
+        c.epoch = p2p->epoch;
+        c.err = p2p->error_flag;
+        c.rank = shard_index;
+        c.n = num_shards;
+        c.rows = rows;
+        c.kk = p2p->keys_per_row;
+        c.pf = p2p->partial_floats;
+    }
+    return launch_merge_shards(rows, head_dim, num_shards, partials, c, out, lse, ess, stream);
 }

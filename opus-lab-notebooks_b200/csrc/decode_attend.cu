@@ -262,17 +262,21 @@ __device__ void merge_staged_to_output(const DecodeArgs &a, int bh, const float 
             const int hh = i / D, dd = i - hh * D;
             const int64_t oh = (int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g + hh;
             if (a.part_out) {  // sequence shard: the unnormalised partial
-                float *po = a.part_out + oh * PSTR;
-                po[8 + dd] = acc[k];
-                if (dd == 0) {
-                    po[0] = M[k];
-                    po[1] = L[k];
-                    po[2] = MS[k];
-                    po[3] = E1[k];
-                    po[4] = E2[k];
-                    po[5] = (float)a.ws.head_meta[((int64_t)bh * 8 + hh) * 2 + 1];
-                    po[6] = 0.f;
-                    po[7] = 0.f;
+                const int nr = a.p2p.peers ? a.p2p.n : 1;
+                for (int r = 0; r < nr; ++r) {  // every rank's buffer, or part_out
+                    float *po = (a.p2p.peers ? p2p_part_slot(a.p2p, a.p2p.peers[r], a.p2p.rank)
+                                             : a.part_out) + oh * PSTR;
+                    po[8 + dd] = acc[k];
+                    if (dd == 0) {
+                        po[0] = M[k];
+                        po[1] = L[k];
+                        po[2] = MS[k];
+                        po[3] = E1[k];
+                        po[4] = E2[k];
+                        po[5] = (float)a.ws.head_meta[((int64_t)bh * 8 + hh) * 2 + 1];
+                        po[6] = 0.f;
+                        po[7] = 0.f;
+                    }
                 }
                 continue;
             }
@@ -727,9 +731,13 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
                 const int h = i / D, d = i - h * D;
                 const int64_t oh = (int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g + h;
                 if (a.part_out) {
-                    float *po = a.part_out + oh * PSTR;
-                    po[8 + d] = 0.f;
-                    if (d < 8) po[d] = (d == 0 || d == 2) ? -INFINITY : 0.f;
+                    const int nr = a.p2p.peers ? a.p2p.n : 1;
+                    for (int r = 0; r < nr; ++r) {
+                        float *po = (a.p2p.peers ? p2p_part_slot(a.p2p, a.p2p.peers[r], a.p2p.rank)
+                                                 : a.part_out) + oh * PSTR;
+                        po[8 + d] = 0.f;
+                        if (d < 8) po[d] = (d == 0 || d == 2) ? -INFINITY : 0.f;
+                    }
                     continue;
                 }
                 a.out[oh * D + d] = 0.f;

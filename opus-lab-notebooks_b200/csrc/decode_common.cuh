@@ -99,6 +99,35 @@ inline size_t decode_ws_layout(int BH, int G, int g, int S, int n_slots, int D, 
     return off;
 }
 
+// ---------------------------------------------------------------------------
+// peer-memory exchange between sequence shards (one buffer per rank, mapped
+// into every other rank's address space):
+//   [0, 512)      flags  u64 [2 exchanges][32 ranks]: last epoch rank r signalled
+//   [512, 1024)   unused (set-up marker at 768)
+//   [1024, ...)   keys   u64 [2 parities][n ranks][rows * kk]
+//   parts         f32    [2 parities][n ranks][rows][pf]
+// Epoch e (the step number + 1, increasing) uses parity e & 1, so a rank one
+// step ahead never overwrites what a slower peer still reads (a rank cannot
+// get two steps ahead: its next use of a parity waits for the peers' flags of
+// the step in between).  The producing kernels (candidates, attention) only
+// store; the consuming kernels (threshold selection, shard merge) raise this
+// rank's flag for the epoch and wait for every rank's.
+// ---------------------------------------------------------------------------
+struct P2PArgs {
+    void *const *peers;      // device array [n]: every rank's buffer as mapped here
+    unsigned char *local;    // this rank's buffer
+    unsigned long long epoch;
+    int32_t *err;            // set to 1 when a wait for a peer gave up
+    int rank, n, rows, kk, pf;
+};
+constexpr size_t kP2PFlags = 0, kP2PKeys = 1024;
+__host__ __device__ inline size_t p2p_parts_offset(int n, int rows, int kk) {
+    return (kP2PKeys + (size_t)2 * n * rows * kk * 8 + 255) / 256 * 256;
+}
+__host__ __device__ inline size_t p2p_buffer_bytes(int n, int rows, int kk, int pf) {
+    return p2p_parts_offset(n, rows, kk) + (size_t)2 * n * rows * pf * 4;
+}
+
 struct DecodeArgs {
     SantaGeometry geo;
     SantaDecodeParams p;
@@ -120,7 +149,56 @@ struct DecodeArgs {
     uint64_t *cand_out;           // select: write the local top-k keys and stop
     const uint64_t *shard_cands;  // select: [num_shards][B*Hq][k] keys -> global top-k
     float *part_out;              // attend: unnormalised partial per (b, query head)
+    P2PArgs p2p;                  // peers == nullptr: the caller exchanges
 };
+
+__device__ __forceinline__ uint64_t *p2p_key_slot(const P2PArgs &c, void *base, int r) {
+    return (uint64_t *)((unsigned char *)base + kP2PKeys) +
+           ((size_t)((c.epoch & 1) * c.n + r) * c.rows * c.kk);
+}
+__device__ __forceinline__ float *p2p_part_slot(const P2PArgs &c, void *base, int r) {
+    return (float *)((unsigned char *)base + p2p_parts_offset(c.n, c.rows, c.kk)) +
+           ((size_t)((c.epoch & 1) * c.n + r) * c.rows * c.pf);
+}
+__device__ __forceinline__ unsigned long long p2p_ld_acquire(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void p2p_st_release(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
+}
+// one thread: wait (at most ~2 s) until every rank signalled exchange ex for
+// this epoch; false (and the error flag set) if one never did
+__device__ inline bool p2p_wait(const P2PArgs &c, int ex) {
+    const unsigned long long *fl = (const unsigned long long *)(c.local + kP2PFlags) + ex * 32;
+    uint64_t t0 = 0;
+    asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t0));
+    for (int r = 0; r < c.n; ++r) {
+        for (uint32_t i = 0;; ++i) {
+            if (p2p_ld_acquire(fl + r) >= c.epoch) break;
+            if ((i & 63u) == 63u) {
+                uint64_t t;
+                asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+                if (t - t0 > 2000000000ull) {
+                    atomicExch(c.err, 1);
+                    return false;
+                }
+            }
+        }
+    }
+    return true;
+}
+// one thread, at the start of the kernel that consumes exchange ex: this
+// rank's contribution was stored by the previous kernel on the stream, which
+// has completed, so the flag can go up now (every consuming CTA raises it;
+// the stores are idempotent, and no CTA depends on another being resident)
+__device__ inline void p2p_publish(const P2PArgs &c, int ex) {
+    for (int r = 0; r < c.n; ++r)
+        p2p_st_release((unsigned long long *)((unsigned char *)c.peers[r] + kP2PFlags) +
+                           ex * 32 + c.rank,
+                       c.epoch);
+}
 
 // ---------------------------------------------------------------------------
 // row resolution: virtual row v of segment bh -> K/V row addresses + weights
@@ -375,7 +453,8 @@ int launch_execute(DecodeArgs &a, cudaStream_t stream);
 int launch_expand(DecodeArgs &a, uint8_t *selected, int32_t *sample_rows, cudaStream_t stream);
 int num_sms();
 int attend_partial_slots(const SantaGeometry *geo, int nsplit);
-int launch_merge_shards(int rows, int head_dim, int num_shards, const float *partials, float *out,
-                        float *lse, float *ess, cudaStream_t stream);
+int launch_merge_shards(int rows, int head_dim, int num_shards, const float *partials,
+                        const P2PArgs &c, float *out, float *lse, float *ess,
+                        cudaStream_t stream);
 
 }  // namespace santa

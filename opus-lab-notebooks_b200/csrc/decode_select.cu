@@ -126,6 +126,15 @@ __device__ __forceinline__ void warp_top16(const uint64_t (&k8)[8], uint64_t (&t
     }
 }
 
+// a candidate key: into every rank's buffer (peer exchange) or cand_out
+__device__ __forceinline__ void store_key(const DecodeArgs &a, int64_t idx, uint64_t key) {
+    if (a.p2p.peers) {
+        for (int r = 0; r < a.p2p.n; ++r) p2p_key_slot(a.p2p, a.p2p.peers[r], a.p2p.rank)[idx] = key;
+    } else {
+        a.cand_out[idx] = key;
+    }
+}
+
 // KPL: keys per lane in the top-k extraction (clusters lane, lane+32, ...).
 template <int D, int KPL>
 __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a) {
@@ -286,6 +295,13 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
     const int kk = a.p.topk_clusters;  // HYBRID: candidate keys per (b, query head)
     uint64_t *cand_s = (uint64_t *)ct;  // sharded plan: [g][num_shards][kk], in the free tile area
     if (a.shard_cands) {
+        if (a.p2p.peers) {  // the peers' keys arrive through peer memory
+            if (tid == 0) {
+                p2p_publish(a.p2p, 0);
+                p2p_wait(a.p2p, 0);
+            }
+            __syncthreads();
+        }
         const int NS = a.num_shards, per = NS * kk;
         const int64_t rows = (int64_t)a.geo.batch * a.geo.num_kv_heads * g;
         for (int i = tid; i < g * per; i += kSelThreads) {
@@ -370,7 +386,7 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
                         if (lane == j) {
                             gapcum[h * (2 * kcap + 1) + j] =
                                 (int)(0xFFFFFFFFu - (uint32_t)t[j]) - cbase;
-                            if (a.cand_out) a.cand_out[((int64_t)bh * g + h) * kk + j] = t[j];
+                            if (a.cand_out) store_key(a, ((int64_t)bh * g + h) * kk + j, t[j]);
                         }
                         ++nsel;
                     }
@@ -385,7 +401,7 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
             if (mhi == 0u && mlo == 0u) break;  // no cluster left
             const int c = (int)(0xFFFFFFFFu - mlo) - cbase;
             if (a.cand_out && lane == 0)
-                a.cand_out[((int64_t)bh * g + h) * kk + nsel] = ((uint64_t)mhi << 32) | mlo;
+                store_key(a, ((int64_t)bh * g + h) * kk + nsel, ((uint64_t)mhi << 32) | mlo);
             if (lane == (c & 31)) {
 #pragma unroll
                 for (int j = 0; j + 1 < KPL; ++j) key[j] = key[j + 1];
@@ -423,7 +439,7 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
     if (a.cand_out) {  // shard candidates only: pad the key lists and stop
         if (warp < g)
             for (int j = head_sel[warp] + lane; j < kk; j += 32)
-                a.cand_out[((int64_t)bh * g + warp) * kk + j] = 0ull;
+                store_key(a, ((int64_t)bh * g + warp) * kk + j, 0ull);
         return;
     }
 

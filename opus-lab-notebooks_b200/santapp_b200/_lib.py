@@ -54,9 +54,18 @@ class SantaDecodeParams(ctypes.Structure):
                 ("seed", ctypes.c_uint64), ("step", ctypes.c_uint64), ("num_splits", _i32)]
 
 
+class SantaP2P(ctypes.Structure):
+    _fields_ = [("peer_buffers", _vp), ("local_buffer", _vp), ("epoch", ctypes.c_uint64),
+                ("error_flag", _vp), ("rows", _i32), ("keys_per_row", _i32),
+                ("partial_floats", _i32), ("reserved", _i32)]
+
+
+IPC_HANDLE_BYTES = 64
+
+
 class SantaShard(ctypes.Structure):
     _fields_ = [("shard_index", _i32), ("num_shards", _i32), ("cluster_base", _i32),
-                ("reserved", _i32), ("candidates", _vp)]
+                ("reserved", _i32), ("candidates", _vp), ("p2p", _vp)]
 
 
 MAX_SHARDS = 32
@@ -107,12 +116,21 @@ SIGNATURES = {
                                         _P(SantaSummary), _P(SantaShard), _vp, _vp, _vp,
                                         ctypes.c_size_t, _vp]),
     "santa_shard_execute": (ctypes.c_int, [_P(SantaGeometry), _P(SantaDecodeParams), _vp, _vp,
-                                           _vp, _P(SantaSummary), _vp, _vp, ctypes.c_size_t,
-                                           _vp]),
+                                           _vp, _P(SantaSummary), _P(SantaShard), _vp, _vp,
+                                           ctypes.c_size_t, _vp]),
     "santa_shard_select": (ctypes.c_int, [_P(SantaGeometry), _P(SantaDecodeParams), _vp, _vp,
                                           _vp, _P(SantaSummary), _P(SantaShard), _vp, _vp, _vp,
                                           _vp, _vp, ctypes.c_size_t, _vp]),
-    "santa_merge_shards": (ctypes.c_int, [_i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "santa_merge_shards": (ctypes.c_int, [_i32, _i32, _i32, _vp, _vp, _i32, _vp, _vp, _vp,
+                                          _vp]),
+    "santa_p2p_buffer_bytes": (ctypes.c_int, [_i32, _i32, _i32, _i32, _P(ctypes.c_size_t)]),
+    "santa_p2p_alloc": (ctypes.c_int, [ctypes.c_size_t, _P(_vp)]),
+    "santa_p2p_free": (ctypes.c_int, [_vp]),
+    "santa_p2p_ipc_handle": (ctypes.c_int, [_vp, _vp]),
+    "santa_p2p_ipc_open": (ctypes.c_int, [_vp, _P(_vp)]),
+    "santa_p2p_ipc_close": (ctypes.c_int, [_vp]),
+    "santa_p2p_peek": (ctypes.c_int, [_vp, _P(ctypes.c_uint64)]),
+    "santa_p2p_poke": (ctypes.c_int, [_vp, ctypes.c_uint64]),
     "santa_rope_append": (ctypes.c_int, [_i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp,
                                          _vp, _vp, _i32, _i32, _vp, _vp, _vp]),
     "santa_prefill_workspace_bytes": (ctypes.c_int, [_P(SantaPrefillShape),

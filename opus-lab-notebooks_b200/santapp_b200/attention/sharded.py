@@ -21,9 +21,13 @@ held by the last shard.  A decode step is
 5. exchange 2: an all-gather of the partials (``B*Hq*(D+8)`` fp32 per rank);
 6. ``santa_merge_shards``: the LSE merge, identical on every rank.
 
-Both exchanges move a few hundred KB; the collectives are NCCL all-gathers
-on the ranks' own buffers (remote data lands in local memory before any
-kernel reads it).  ``ShardExchange`` holds the host logic (shard bounds,
+Both exchanges move a few hundred KB.  With ``transport="nccl"`` they are
+NCCL all-gathers on the ranks' own buffers; with ``transport="p2p"`` the
+producing kernels store keys and partials straight into every rank's
+exchange buffer (mapped through CUDA IPC) and raise a per-rank flag that the
+consuming kernels wait for (bounded; ``p2p_error`` is set if a peer never
+signals).  Either way remote data lands in local memory before a kernel
+reads it; no TMA or multicast is involved.  ``ShardExchange`` holds the host logic (shard bounds,
 sample split, Philox seeds, exchange buffers and order) apart from the
 kernel calls, so that it can be checked on CPU ranks.
 """
@@ -133,7 +137,7 @@ class ShardedDecodeStep(ShardExchange):
                  summary: ClusterSummary, *, num_query_heads: int, n_total: int,
                  topk_clusters: int, samples: int, shard_index: int, num_shards: int,
                  cluster_base: int, group=None, scale: float | None = None, seed: int = 0,
-                 injected: bool = False):
+                 injected: bool = False, transport: str = "nccl"):
         _require_cuda("key_cache", key_cache)
         _require_cuda("value_cache", value_cache)
         if key_cache.dtype != torch.bfloat16:
@@ -151,7 +155,14 @@ class ShardedDecodeStep(ShardExchange):
         self.c = summary.as_c()
         self.lib = _lib.load()
         self.shard = _lib.SantaShard(shard_index, num_shards, int(cluster_base), 0,
-                                     self.all_keys.data_ptr())
+                                     self.all_keys.data_ptr(), None)
+        if transport not in ("nccl", "p2p"):
+            raise ValueError(f"unknown transport {transport!r}")
+        self.transport = transport
+        self.epoch = 0
+        self.p2p = None
+        self._p2p_buffers: list[int] = []  # every rank's buffer as mapped here
+        self._p2p_owned = False
         nbytes = ctypes.c_size_t()
         _lib.check("santa_decode_workspace_bytes", self.lib.santa_decode_workspace_bytes(
             ctypes.byref(self.geo), ctypes.byref(self.p), summary.max_groups,
@@ -165,11 +176,86 @@ class ShardedDecodeStep(ShardExchange):
         self._q = None
         self._refs = (ctypes.byref(self.geo), ctypes.byref(self.p), ctypes.byref(self.c),
                       ctypes.byref(self.shard))
+        if transport == "p2p" and num_shards > 1:
+            self._p2p_setup(group)
+
+    # ---- peer-memory exchange (transport="p2p") -----------------------------
+    def p2p_buffer_bytes(self) -> int:
+        n = ctypes.c_size_t()
+        _lib.check("santa_p2p_buffer_bytes", self.lib.santa_p2p_buffer_bytes(
+            self.num_shards, self.rows, self.topk, self.head_dim, ctypes.byref(n)))
+        return n.value
+
+    def bind_p2p(self, buffers: list[int], *, owned: bool = False) -> None:
+        """Use the exchange buffers ``buffers`` (device addresses of every
+        rank's buffer as mapped in this process, own one at shard_index)."""
+        dev = self.out.device
+        self._p2p_buffers = list(buffers)
+        self._p2p_owned = owned
+        self._peer_table = torch.tensor(buffers, dtype=torch.int64, device=dev)
+        self.p2p_error = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.p2p = _lib.SantaP2P(self._peer_table.data_ptr(), buffers[self.shard_index], 0,
+                                 self.p2p_error.data_ptr(), self.rows, self.topk,
+                                 _lib.partial_floats(self.head_dim), 0)
+        self.shard.p2p = ctypes.addressof(self.p2p)
+        self.transport = "p2p"
+
+    def _p2p_setup(self, group) -> None:
+        """Allocate this rank's exchange buffer, share its IPC handle through
+        the process group, map the peers' buffers and check each mapping by
+        reading a marker its owner wrote."""
+        import torch.distributed as dist
+        lib, dev = self.lib, self.out.device
+        own = ctypes.c_void_p()
+        _lib.check("santa_p2p_alloc", lib.santa_p2p_alloc(self.p2p_buffer_bytes(),
+                                                          ctypes.byref(own)))
+        handle = (ctypes.c_uint8 * _lib.IPC_HANDLE_BYTES)()
+        _lib.check("santa_p2p_ipc_handle", lib.santa_p2p_ipc_handle(own, handle))
+        mine = torch.tensor(bytearray(handle), dtype=torch.uint8, device=dev)
+        every = torch.empty(self.num_shards * _lib.IPC_HANDLE_BYTES, dtype=torch.uint8,
+                            device=dev)
+        dist.all_gather_into_tensor(every, mine, group=group)
+        every = every.cpu().numpy().reshape(self.num_shards, _lib.IPC_HANDLE_BYTES)
+        marker_off = 768  # unused bytes of the counter block
+        _lib.check("santa_p2p_poke", lib.santa_p2p_poke(own.value + marker_off,
+                                                        0x5A5A0000 + self.shard_index))
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=group)
+        buffers = []
+        for r in range(self.num_shards):
+            if r == self.shard_index:
+                buffers.append(own.value)
+                continue
+            mapped = ctypes.c_void_p()
+            h = (ctypes.c_uint8 * _lib.IPC_HANDLE_BYTES)(*every[r].tolist())
+            _lib.check("santa_p2p_ipc_open", lib.santa_p2p_ipc_open(h, ctypes.byref(mapped)))
+            seen = ctypes.c_uint64()
+            _lib.check("santa_p2p_peek", lib.santa_p2p_peek(mapped.value + marker_off,
+                                                            ctypes.byref(seen)))
+            if seen.value != 0x5A5A0000 + r:
+                raise RuntimeError(f"exchange buffer of rank {r} is not mapped correctly")
+            buffers.append(mapped.value)
+        dist.barrier(group=group)
+        self.bind_p2p(buffers, owned=True)
+
+    def close(self) -> None:
+        """Unmap the peers' exchange buffers and free this rank's."""
+        if self._p2p_owned and self._p2p_buffers:
+            for r, ptr in enumerate(self._p2p_buffers):
+                if r == self.shard_index:
+                    self.lib.santa_p2p_free(ctypes.c_void_p(ptr))
+                else:
+                    self.lib.santa_p2p_ipc_close(ctypes.c_void_p(ptr))
+        self._p2p_buffers = []
+        self._p2p_owned = False
 
     # ---- the kernel calls -------------------------------------------------
     def candidates(self, q: torch.Tensor, step: int = 0, stream=None) -> torch.Tensor:
         self.p.step = int(step) & 0xFFFFFFFFFFFFFFFF
         self._q = q
+        self.epoch += 1
+        if self.p2p is not None:
+            self.p2p.epoch = self.epoch
         g, p, c, s = self._refs
         _lib.check("santa_shard_candidates", self.lib.santa_shard_candidates(
             g, p, q.data_ptr(), self.key_cache.data_ptr(), self.value_cache.data_ptr(), c, s,
@@ -186,19 +272,31 @@ class ShardedDecodeStep(ShardExchange):
             _lib.stream_handle(stream)))
 
     def execute(self, stream=None) -> torch.Tensor:
-        g, p, c, _ = self._refs
+        g, p, c, s = self._refs
         _lib.check("santa_shard_execute", self.lib.santa_shard_execute(
             g, p, self._q.data_ptr(), self.key_cache.data_ptr(), self.value_cache.data_ptr(),
-            c, self.partial.data_ptr(), self.ws.data_ptr(), self.ws_bytes,
+            c, s, self.partial.data_ptr(), self.ws.data_ptr(), self.ws_bytes,
             _lib.stream_handle(stream)))
         return self.partial
 
     def merge(self, stream=None) -> torch.Tensor:
+        p2p = ctypes.byref(self.p2p) if self.p2p is not None else None
         _lib.check("santa_merge_shards", self.lib.santa_merge_shards(
-            self.rows, self.head_dim, self.num_shards, self.all_partials.data_ptr(),
+            self.rows, self.head_dim, self.num_shards,
+            None if p2p is not None else self.all_partials.data_ptr(), p2p, self.shard_index,
             self.out.data_ptr(), self.lse.data_ptr(), self.ess.data_ptr(),
             _lib.stream_handle(stream)))
         return self.out
+
+    def exchange_keys(self) -> torch.Tensor:
+        if self.p2p is not None:
+            return self.all_keys  # the kernels exchanged them through peer memory
+        return super().exchange_keys()
+
+    def exchange_partials(self) -> torch.Tensor:
+        if self.p2p is not None:
+            return self.all_partials
+        return super().exchange_partials()
 
     def select(self, sample_a: torch.Tensor | None = None):
         """Selection readout of the plan (after exchange 1): ``(selected

@@ -25,7 +25,7 @@ SH = scaled_shape(QWEN7B_32K, name="shard-gpu", batch=2, context=3000, true_clus
 
 
 class Shards:
-    def __init__(self, shape, n, injected, seed=0):
+    def __init__(self, shape, n, injected, seed=0, p2p=False):
         self.shape, self.n = shape, n
         self.parts = [make_shard_workload(shape, r, n, seed=seed) for r in range(n)]
         self.steps = []
@@ -37,6 +37,19 @@ class Shards:
                 kc, vc, summ, num_query_heads=shape.num_query_heads, n_total=p.n_total,
                 topk_clusters=shape.topk_clusters, samples=p.samples, shard_index=r,
                 num_shards=n, cluster_base=p.cluster_base, seed=seed, injected=injected))
+        self.p2p = p2p
+        self.buffers = []
+        if p2p:  # one exchange buffer per shard, all on this device
+            import ctypes
+            from santapp_b200 import _lib
+            lib = _lib.load()
+            nbytes = self.steps[0].p2p_buffer_bytes()
+            for _ in range(n):
+                ptr = ctypes.c_void_p()
+                _lib.check("alloc", lib.santa_p2p_alloc(nbytes, ctypes.byref(ptr)))
+                self.buffers.append(ptr.value)
+            for st in self.steps:
+                st.bind_p2p(self.buffers)
         self.osum = {}
         for r, p in enumerate(self.parts):
             for b in range(shape.batch):
@@ -45,15 +58,42 @@ class Shards:
                     self.osum[(r, b, kv)] = O.build_summary(K[:p.sample_end],
                                                             p.labels[b, kv].numpy(), p.n_clusters)
 
+    def _raise_flags(self, ex):
+        """Emulated ranks share one stream, so no kernel may wait for another:
+        after the producing kernels finished, the host raises every shard's
+        flag in every buffer; the consuming kernels then find them up."""
+        import ctypes
+        from santapp_b200 import _lib
+        torch.cuda.synchronize()
+        lib = _lib.load()
+        epoch = self.steps[0].epoch
+        for buf in self.buffers:
+            for r in range(self.n):
+                _lib.check("poke", lib.santa_p2p_poke(ctypes.c_void_p(buf + (ex * 32 + r) * 8),
+                                                      epoch))
+
     def exchange_keys(self):
+        if self.p2p:  # the kernels wrote every shard's keys into every buffer
+            self._raise_flags(0)
+            return
         for st in self.steps:
             for r, src in enumerate(self.steps):
                 st.all_keys[r].copy_(src.keys)
 
     def exchange_partials(self):
+        if self.p2p:
+            self._raise_flags(1)
+            return
         for st in self.steps:
             for r, src in enumerate(self.steps):
                 st.all_partials[r].copy_(src.partial)
+
+    def close(self):
+        import ctypes
+        from santapp_b200 import _lib
+        for ptr in self.buffers:
+            _lib.load().santa_p2p_free(ctypes.c_void_p(ptr))
+        self.buffers = []
 
     def run(self, step, ranks=None):
         q = self.parts[0].queries[step].cuda().contiguous()
@@ -198,3 +238,27 @@ def test_shard_api_rejects_unsupported():
         ShardedDecodeStep(kc.float(), vc.float(), summ, num_query_heads=sh.num_query_heads,
                           n_total=p.n_total, topk_clusters=4, samples=8, shard_index=0,
                           num_shards=2, cluster_base=0)
+
+
+@pytest.mark.parametrize("n", [2, 3])
+def test_sharded_peer_memory_exchange_matches_oracle(n):
+    """The kernels' own exchange (keys and partials stored into every
+    shard's buffer, flags awaited) gives the same result as the host-side
+    exchange.  The emulated shards run on one stream, so the host raises the
+    flags between the producing and the consuming kernels and no wait is
+    ever outstanding."""
+    sh = scaled_shape(SH, steps=3)
+    obj = Shards(sh, n, injected=False, seed=5, p2p=True)
+    ref = Shards(sh, n, injected=False, seed=5)
+    for step in range(3):  # both parities of the exchange buffers
+        q, sels, outs = obj.run(step)
+        _, _, outs_ref = ref.run(step)
+        for out in outs:
+            assert torch.equal(out, outs_ref[0])
+        assert all(int(st.p2p_error.item()) == 0 for st in obj.steps)
+
+    def ranks_of(b, h, osel, osums):
+        return _oracle_ranks(sh, obj.parts, osums, osel, b, h, seed=5, step=2)
+
+    _check(obj, q, sels, outs, ranks_of)
+    obj.close()
