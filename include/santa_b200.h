@@ -217,6 +217,16 @@ int santa_decode_select(const SantaGeometry *geo, const SantaDecodeParams *p, co
                         int32_t *n_exact, void *workspace, size_t workspace_bytes,
                         cudaStream_t stream);
 
+/* Injected draws out of range: *segments = the number of (batch, KV head)
+ * segments whose last selection in this workspace (santa_decode, _plan,
+ * _select or a shard entry point with SANTA_SAMPLES_INJECTED) met a draw
+ * outside the range documented at santa_decode; such a draw is clamped into
+ * range.  The selection kernel clears and sets one flag per segment at the
+ * start of the workspace; this call synchronises the stream and reads them
+ * (host-blocking, for parity runs). */
+int santa_decode_bad_draws(const SantaGeometry *geo, const void *workspace,
+                           size_t workspace_bytes, int32_t *segments, cudaStream_t stream);
+
 /* ---- KV cache (attention/santapp.py:66-77, 234-283, 308-313) ---------- */
 
 /* RoPE of the new tokens' queries and keys (x*cos + rotate_half(x)*sin with

@@ -6,6 +6,7 @@
 // stream-ordered halves, santa_decode_select reads the selection out.
 #include "decode_common.cuh"
 
+#include <stdlib.h>
 #include <string.h>
 
 using namespace santa;
@@ -125,6 +126,29 @@ extern "C" int santa_decode_plan(const SantaGeometry *geo, const SantaDecodePara
     if (st) return st;
     a.n_exact = n_exact;
     return launch_plan(a, stream);
+}
+
+extern "C" int santa_decode_bad_draws(const SantaGeometry *geo, const void *workspace,
+                                      size_t workspace_bytes, int32_t *segments,
+                                      cudaStream_t stream) {
+    if (!geo || !workspace || !segments) return SANTA_ERR_INVALID_ARGUMENT;
+    const int64_t BH = (int64_t)geo->batch * geo->num_kv_heads;
+    if (geo->batch <= 0 || geo->num_kv_heads <= 0) return SANTA_ERR_INVALID_ARGUMENT;
+    if (workspace_bytes < (size_t)BH * 4) return SANTA_ERR_WORKSPACE;
+    int32_t *h = (int32_t *)malloc((size_t)BH * 4);
+    if (!h) return SANTA_ERR_INVALID_ARGUMENT;
+    cudaError_t e = cudaMemcpyAsync(h, workspace, (size_t)BH * 4, cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) {
+        free(h);
+        santa_set_cuda_error(e);
+        return SANTA_ERR_CUDA;
+    }
+    int32_t n = 0;
+    for (int64_t i = 0; i < BH; ++i) n += h[i] != 0 ? 1 : 0;
+    free(h);
+    *segments = n;
+    return SANTA_OK;
 }
 
 extern "C" int santa_decode_execute(const SantaGeometry *geo, const SantaDecodeParams *p,

@@ -1,10 +1,12 @@
 // Shared definitions of the SANTA++ decode kernels (selection + attention).
 //
 // A decode step is two launches:
-//   select  one CTA per (batch, KV head) = segment bh: centroid guesses for
-//           the GQA group, ranking, top-k / budget walk, the union of the
-//           group's selections and the importance samples.  It writes a work
-//           list for the segment into the workspace.
+//   select  per (batch, KV head) = segment bh: centroid guesses for the GQA
+//           group, ranking, top-k / budget walk, the union of the group's
+//           selections and the importance samples; one CTA per segment, or
+//           (hybrid, k <= 32) a cluster of one CTA per query head
+//           (decode_select_group.cu).  It writes a work list for the segment
+//           into the workspace.
 //   attend  streams the rows of every segment's work list (selected clusters
 //           of the cluster-sorted copy, the exact recent window of the cache,
 //           sampled rows) with an online softmax per query head, and merges
@@ -35,13 +37,11 @@ constexpr uint32_t kAbsBit = 1u << 27;
 constexpr int kMaskSample = 256;
 constexpr int kMaskAbs = 512;
 
-// error flags in DecodeWs::flag
-constexpr int kFlagBadDraw = 0;     // an injected draw was out of range (clamped)
-constexpr int kFlagWaitTimeout = 1; // an mbarrier wait hit its time limit
 
 struct DecodeWs {
     int32_t *counters;   // [BH] CTAs finished per segment (last one merges)
-    int32_t *flag;       // [4] error flags, see kFlag*
+    int32_t *flag;       // [BH] 1 = an injected draw of the segment was out of range
+                         // (clamped); cleared by the segment's selection kernel
     int32_t *meta;       // [BH][8]: 0 n_union, 1 U, 2 R, 3 n_samples, 4 total rows
     int32_t *head_meta;  // [BH][8][2]: n_exact, n_samples
     int32_t *u_start;    // [BH][G] sorted-row start of each union entry
@@ -68,8 +68,8 @@ inline size_t decode_ws_layout(int BH, int G, int g, int S, int n_slots, int D, 
         return o;
     };
     const int gs = g * (S > 0 ? S : 1);
+    size_t o_flag = take((size_t)BH * 4);  // first: santa_decode_bad_draws reads it
     size_t o_cnt = take((size_t)BH * 4);
-    size_t o_flag = take(16);
     size_t o_meta = take((size_t)BH * 8 * 4);
     size_t o_hm = take((size_t)BH * 16 * 4);
     size_t o_us = take((size_t)BH * G * 4);
@@ -451,6 +451,9 @@ __device__ __forceinline__ void cp_async_mbar_arrive(uint64_t *bar) {
 int launch_plan(DecodeArgs &a, cudaStream_t stream);
 int launch_execute(DecodeArgs &a, cudaStream_t stream);
 int launch_expand(DecodeArgs &a, uint8_t *selected, int32_t *sample_rows, cudaStream_t stream);
+// hybrid selection on a thread-block cluster (decode_select_group.cu)
+bool select_group_supported(const DecodeArgs &a);
+int launch_select_group(DecodeArgs &a, cudaStream_t stream);
 int num_sms();
 int attend_partial_slots(const SantaGeometry *geo, int nsplit);
 int launch_merge_shards(int rows, int head_dim, int num_shards, const float *partials,

@@ -208,7 +208,10 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
         }
     }
     for (int i = tid; i < Gmax; i += kSelThreads) mask_s[i] = 0;
-    if (tid == 0) a.ws.counters[bh] = 0;  // arrival counter of the attention merge
+    if (tid == 0) {
+        a.ws.counters[bh] = 0;  // arrival counter of the attention merge
+        a.ws.flag[bh] = 0;      // set by the draws below (after block barriers)
+    }
     if (tid < 8) {
         head_sel[tid] = 0;
         head_exact[tid] = 0;
@@ -600,7 +603,7 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
                 if (a.p.sample_source == SANTA_SAMPLES_INJECTED) {
                     int v = a.sample_a[inj + i];
                     if (v < 0 || v >= n_rest) {
-                        atomicExch(a.ws.flag + kFlagBadDraw, 1);
+                        a.ws.flag[bh] = 1;
                         v = min(max(v, 0), n_rest - 1);
                     }
                     r = (uint32_t)v;
@@ -631,11 +634,11 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
                     grp = a.sample_a[inj + i];
                     within = a.sample_b[inj + i];
                     if (grp < 0 || grp >= n_groups) {
-                        atomicExch(a.ws.flag + kFlagBadDraw, 1);
+                        a.ws.flag[bh] = 1;
                         grp = min(max(grp, 0), n_groups - 1);
                     }
                     if (within < 0 || within >= len_s[grp]) {
-                        atomicExch(a.ws.flag + kFlagBadDraw, 1);
+                        a.ws.flag[bh] = 1;
                         within = min(max(within, 0), len_s[grp] - 1);
                     }
                 } else {
@@ -669,7 +672,7 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
                 if (a.p.sample_source == SANTA_SAMPLES_INJECTED) {
                     t = a.sample_a[inj + i];
                     if (t < 0 || t >= sample_end) {
-                        atomicExch(a.ws.flag + kFlagBadDraw, 1);
+                        a.ws.flag[bh] = 1;
                         t = min(max(t, 0), sample_end - 1);
                     }
                 } else {
@@ -830,7 +833,6 @@ static int launch_select(DecodeArgs &a, cudaStream_t stream) {
 template <int D>
 static int launch_plan_d(DecodeArgs &a, cudaStream_t stream) {
     const int BH = a.geo.batch * a.geo.num_kv_heads;
-    SANTA_CUDA_CHECK(cudaMemsetAsync(a.ws.flag, 0, 16, stream));
     if (a.p.mode == SANTA_MODE_SANTA) {
         if (a.geo.kv_dtype == SANTA_DTYPE_BF16)
             decode_old_lse_kernel<D, __nv_bfloat16><<<BH, 256, 0, stream>>>(a);
@@ -838,6 +840,7 @@ static int launch_plan_d(DecodeArgs &a, cudaStream_t stream) {
             decode_old_lse_kernel<D, float><<<BH, 256, 0, stream>>>(a);
         SANTA_LAUNCH_CHECK();
     }
+    if (select_group_supported(a)) return launch_select_group(a, stream);
     return a.sum.max_groups <= 256 ? launch_select<D, 8>(a, stream) : launch_select<D, 32>(a, stream);
 }
 

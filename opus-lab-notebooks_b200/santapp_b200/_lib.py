@@ -106,6 +106,8 @@ SIGNATURES = {
     "santa_decode_static_scratch": (ctypes.c_int, [_P(SantaGeometry), _P(SantaDecodeParams), _vp,
                                                    _vp, _vp, _P(SantaSummary), _vp, _vp, _vp,
                                                    _vp, _vp, _vp, _vp]),
+    "santa_decode_bad_draws": (ctypes.c_int, [_P(SantaGeometry), _vp, ctypes.c_size_t,
+                                              _P(ctypes.c_int32), _vp]),
     "santa_decode_select": (ctypes.c_int, [_P(SantaGeometry), _P(SantaDecodeParams), _vp, _vp,
                                            _vp, _P(SantaSummary), _vp, _vp, _vp, _vp, _vp, _vp,
                                            ctypes.c_size_t, _vp]),

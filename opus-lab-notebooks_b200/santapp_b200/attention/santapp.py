@@ -203,6 +203,16 @@ class DecodeWorkspace:
 _default_ws: dict = {}
 
 
+def _check_injected_draws(lib, geo, ws: torch.Tensor, nbytes: int, stream=None) -> None:
+    """Raise if an injected draw was out of range (the kernel clamps it)."""
+    n = ctypes.c_int32()
+    _lib.check("santa_decode_bad_draws", lib.santa_decode_bad_draws(
+        ctypes.byref(geo), ws.data_ptr(), nbytes, ctypes.byref(n), _lib.stream_handle(stream)))
+    if n.value:
+        raise ValueError(f"injected sample draws out of range in {n.value} (batch, KV head) "
+                         "segments")
+
+
 def decode_params(mode: str, *, topk_clusters: int = 0, token_budget: int = 0, samples: int = 0,
                   scale: float, injected: bool = False, seed: int = 0, step: int = 0,
                   num_splits: int = 0) -> _lib.SantaDecodeParams:
@@ -271,6 +281,8 @@ def santa_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Te
         value_cache.data_ptr(), ctypes.byref(c), _lib.ptr(sample_a), _lib.ptr(sample_b),
         out.data_ptr(), lse.data_ptr(), _lib.ptr(n_exact), _lib.ptr(ess), ws.data_ptr(),
         nbytes.value, _lib.stream_handle(stream)))
+    if injected:
+        _check_injected_draws(lib, geo, ws, nbytes.value, stream)
     return DecodeResult(out, lse, n_exact, ess)
 
 
@@ -322,6 +334,8 @@ class DecodeStep:
             g, p, q.data_ptr(), self.key_cache.data_ptr(), self.value_cache.data_ptr(), c,
             _lib.ptr(sample_a), _lib.ptr(sample_b), _lib.ptr(self.n_exact), self.ws.data_ptr(),
             self.ws_bytes, _lib.stream_handle(stream)))
+        if sample_a is not None:
+            _check_injected_draws(self.lib, self.geo, self.ws, self.ws_bytes, stream)
 
     def execute(self, stream=None) -> torch.Tensor:
         g, p, c = self._refs
@@ -377,6 +391,8 @@ def santa_decode_select(q: torch.Tensor, key_cache: torch.Tensor, value_cache: t
         value_cache.data_ptr(), ctypes.byref(c), _lib.ptr(sample_a), _lib.ptr(sample_b),
         selected.data_ptr(), rows.data_ptr(), n_exact.data_ptr(), ws.data_ptr(), nbytes.value,
         _lib.stream_handle(stream)))
+    if sample_a is not None:
+        _check_injected_draws(lib, geo, ws, nbytes.value, stream)
     return selected, rows[..., :samples], n_exact
 
 

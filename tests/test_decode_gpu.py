@@ -13,8 +13,8 @@ import torch
 
 from oracle import santa_oracle as O
 from santapp_b200.attention import santapp as S
-from santapp_b200.synthetic import (QWEN05B_4K, QWEN7B_32K, make_decode_workload, scaled_shape,
-                                    tensor_digest)
+from santapp_b200.synthetic import (QWEN05B_4K, QWEN7B_32K, QWEN3_8B_128K, make_decode_workload,
+                                    scaled_shape, tensor_digest)
 
 pytestmark = pytest.mark.gpu
 
@@ -249,6 +249,24 @@ def test_hybrid_injected_matches_oracle(cases, prefix):
         assert int(n_exact[b, h]) == r.n_exact
 
 
+@pytest.mark.parametrize("mode", ["hybrid", "uniform"])
+def test_out_of_range_injected_draws_raise(cases, mode):
+    """An injected draw outside its range is clamped by the kernel, flagged for
+    its segment and reported as ValueError; the next valid call is clean (the
+    selection kernel clears the flags)."""
+    case = cases["qwen7b_"]
+    sh = case.shape
+    kw = dict(mode=mode, n_total=sh.context, topk_clusters=sh.topk_clusters, samples=sh.samples)
+    a = torch.zeros(sh.batch, sh.num_query_heads, sh.samples, dtype=torch.int32, device="cuda")
+    a[-1, -1, 3] = sh.sample_end + 5  # beyond n_rest and beyond sample_end
+    with pytest.raises(ValueError, match="out of range"):
+        S.santa_decode(case.q(), case.kc, case.vc, case.summary, sample_a=a, **kw)
+    with pytest.raises(ValueError, match="out of range"):
+        S.santa_decode_select(case.q(), case.kc, case.vc, case.summary, sample_a=a, **kw)
+    a[-1, -1, 3] = 0
+    S.santa_decode(case.q(), case.kc, case.vc, case.summary, sample_a=a, **kw)
+
+
 def test_hybrid_device_sampler_matches_philox_oracle(cases):
     case = cases["qwen7b_"]
     sh = case.shape
@@ -411,3 +429,59 @@ def test_many_clusters_selection_bit_exact(mode):
             assert np.array_equal(sel[0, h], want), (kv, hh)
             assert int(n_exact[0, h]) == int(o.lengths[chosen].sum())
             assert np.abs(out[0, h] - r.out).max() < 2e-2
+
+
+@pytest.mark.parametrize("name,changes", [
+    # Qwen3-8B group of 4 with 1024 clusters and top-32 (the 128K selection)
+    ("g4-1024c-k32", dict(base=QWEN3_8B_128K, batch=2, context=24576, samples=512)),
+    # cluster counts that are not a multiple of the 32-key batches
+    ("g7-600c-k32", dict(batch=1, context=8192, true_clusters=600, n_clusters=600,
+                         topk_clusters=32, samples=96)),
+    # empty clusters: fewer non-empty groups than summary rows
+    ("g7-empty-k20", dict(batch=2, context=4096, true_clusters=80, n_clusters=96,
+                          topk_clusters=20, samples=128)),
+    # one query head per KV head (cluster of one CTA) and a full group of 8
+    ("g1-d64", dict(num_query_heads=4, num_kv_heads=4, head_dim=64, batch=2, context=4096,
+                    true_clusters=64, n_clusters=64, topk_clusters=8, samples=64)),
+    ("g8-k1", dict(num_query_heads=16, num_kv_heads=2, batch=2, context=4096, true_clusters=40,
+                   n_clusters=40, topk_clusters=1, samples=32)),
+])
+def test_hybrid_selection_shapes_bit_exact(name, changes):
+    """The hybrid selection (one CTA per query head, a cluster per KV head)
+    across group sizes, cluster counts and k: selected sets, n_exact and
+    sample rows bit-exact, outputs within the bf16 tolerance."""
+    changes = dict(changes)
+    base = changes.pop("base", QWEN7B_32K)
+    sh = scaled_shape(base, name=name, steps=1, **changes)
+    w = make_decode_workload(sh, seed=5)
+    kc, vc = w.keys.cuda(), w.values.cuda()
+    labels = w.labels[:, :, :sh.sample_end]
+    summ = S.build_summary(kc, vc, labels.cuda(), sh.n_clusters, sample_end=sh.sample_end,
+                           n_total=sh.context)
+    q = w.queries[0].cuda()
+    kw = dict(mode="hybrid", n_total=sh.context, topk_clusters=sh.topk_clusters,
+              samples=sh.samples, seed=9, step=2)
+    sel, rows, n_exact = S.santa_decode_select(q, kc, vc, summ, **kw)
+    res = S.santa_decode(q, kc, vc, summ, **kw)
+    sel, rows, out = sel.cpu().numpy(), rows.cpu().numpy(), res.out.cpu().numpy()
+    n_exact = n_exact.cpu().numpy()
+    for b in range(sh.batch):
+        for kv in range(sh.num_kv_heads):
+            K = w.keys[b, kv].float().numpy()
+            V = w.values[b, kv].float().numpy()
+            o = O.build_summary(K[:sh.sample_end], labels[b, kv].numpy(), sh.n_clusters)
+            for hh in range(sh.group):
+                h = kv * sh.group + hh
+                qh = w.queries[0, b, h].numpy()
+                chosen = O.select_topk(O.centroid_guess(o, qh, sh.scale), sh.topk_clusters)
+                want = np.zeros(sh.n_clusters, np.uint8)
+                want[chosen] = 1
+                assert np.array_equal(sel[b, h], want), (b, kv, hh)
+                assert int(n_exact[b, h]) == int(o.lengths[chosen].sum())
+                n_rest = sh.sample_end - int(o.lengths[chosen].sum())
+                ranks = O.philox_ranks(9, 2, b, h, sh.samples, n_rest)
+                assert np.array_equal(rows[b, h], O.hybrid_positions(o, chosen, ranks))
+                if (b + kv + hh) % 3 == 0:
+                    r = O.decode_hybrid(qh, K, V, o, sh.sample_end, sh.topk_clusters, ranks,
+                                        sh.scale)
+                    assert np.abs(out[b, h] - r.out).max() < 2e-2
