@@ -8,26 +8,35 @@
 //
 //   out[b, h, t] = sum_{s <= t} softmax_s(q_t . k_s * scale) v_s
 //
-// Kernel (one CTA of 8 warps per (128-query tile, query head); the heaviest
-// causal tiles are scheduled first):
-//   * Q, K and V^T tiles live in shared memory in the canonical K-major
-//     128-byte-swizzle layout (two 64-element halves of the 128 dims; rows in
-//     1024-byte atoms of 8), so every MMA operand uses one descriptor form.
-//     V is transposed once into the workspace so that the P.V product's B
-//     operand (K = keys, N = dims) is K-major too.
-//   * S = Q K^T: 8 tcgen05.mma (M=128, N=128, K=16) into TMEM columns
-//     [0, 128); O += P V^T: 8 more into columns [128, 256).  One thread issues
-//     them and commits to an mbarrier; every wait is bounded.
-//   * Softmax: warp w reads TMEM lanes 32*(w%4).. (its 32 query rows) and
-//     columns 64*(w/4).. (half of the keys) with tcgen05.ld, so a query row
-//     is owned by two threads that exchange their row maxima through shared
-//     memory.  The running maximum is updated lazily: O (in TMEM) and l are
-//     rescaled only when the maximum grows by more than 8 (log2 units), so
-//     p <= 2^8 and most tiles skip the TMEM round trip.  P is written to
-//     shared memory as bf16 in the same swizzled layout (A operand of P.V).
-//   * K and V^T tiles are double-buffered with 16-byte cp.async; the next K
-//     tile streams in during the S MMA and softmax, the next V^T tile during
-//     the P.V MMA.
+// Two launches:
+//   prefill_image_kernel  writes every 128-key tile of K and of V^T as the
+//       exact 32 KB shared-memory image the MMAs read (K-major, 128-byte
+//       swizzle, two 64-element halves), zero-filled past T, so one bulk copy
+//       moves a tile;
+//   prefill_fwd_kernel    one CTA per (pair of 128-query tiles, query head),
+//       heaviest causal pairs first, warp-specialised:
+//         warps 0-3 / 4-7  softmax of query tile 0 / 1: a thread owns one
+//                          query row (= TMEM lane) and reads its 128 scores
+//                          from TMEM, so row maxima and sums need no
+//                          exchange; P (bf16) goes back into the score
+//                          columns of TMEM;
+//         warp 8           one thread issues every tcgen05.mma:
+//                            S_t = Q_t K_j^T   (smem x smem -> TMEM cols S_t)
+//                            O_t += P_t V_j    (TMEM x smem -> TMEM cols O_t)
+//                          in the order S0(j) S1(j) PV0(j) S0(j+1) PV1(j)
+//                          S1(j+1) ..., so the tensor core runs one tile's
+//                          products while the other tile's softmax runs;
+//         warp 9           one thread streams K_j and V^T_j (two stages,
+//                          one 32 KB bulk copy each).
+//       TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
+//       The running maximum is updated lazily: O and l are rescaled only
+//       when the maximum grows by more than 8 (log2 units), so p <= 2^8.
+//       tcgen05.commit orders everything: the commit after S_t(j+1) fires
+//       only when PV_t(j) (issued before it) has finished, so the softmax of
+//       tile t may rescale O_t as soon as it sees its next scores.
+//       Every mbarrier wait is bounded; a wait that gives up sets the error
+//       flag, every role stops, and the MMAs in flight drain before TMEM is
+//       released.
 #include "decode_common.cuh"
 #include "tcgen05.cuh"
 
@@ -35,295 +44,355 @@
 
 namespace santa {
 
-constexpr int kPfD = 128;            // head dim
-constexpr int kPfRows = 128;         // query rows per CTA = keys per tile
-constexpr int kPfThreads = 256;
-constexpr int kPfTile = 32768;       // bytes of one 128 x 128 bf16 tile
-constexpr int kPfHalf = 16384;       // one 64-element half of a tile
+constexpr int kPfD = 128;             // head dim
+constexpr int kPfRows = 128;          // query rows per tile = keys per KV tile
+constexpr int kPfThreads = 320;       // 2 softmax warpgroups + MMA warp + load warp
+constexpr int kPfMmaWarp = 8;  // warp 9 loads K / V^T
+constexpr int kPfTile = 32768;        // bytes of one 128 x 128 bf16 tile image
+constexpr int kPfHalf = 16384;        // one 64-element half of a tile
 constexpr uint32_t kIdesc = umma_idesc_bf16(128, 128);
 
+// byte offset of 16-byte chunk ch (of 16 along the 128-element row) of row r
+// in a tile image (K-major, 128-byte swizzle, 8-row atoms 1024 bytes apart)
+__host__ __device__ __forceinline__ uint32_t pf_img_off(int r, int ch) {
+    return (uint32_t)((ch >> 3) * kPfHalf + (r >> 3) * 1024 + (r & 7) * 128 +
+                      (((ch & 7) ^ (r & 7)) << 4));
+}
+
 struct PrefillArgs {
-    const __nv_bfloat16 *q;   // [B, Hq, T, D]
-    const __nv_bfloat16 *k;   // [B, Hkv, T, D]
-    const __nv_bfloat16 *vt;  // [B, Hkv, D, T] (transposed V)
-    __nv_bfloat16 *out;       // [B, Hq, T, D]
-    float *lse;               // [B, Hq, T] natural log, or null
-    int32_t *err;             // error flag (a bounded wait gave up)
-    int B, Hq, Hkv, T, n_tiles;
-    int64_t cap;              // tokens between consecutive (b, kv head) blocks of k
-    int Tp;                   // row stride of V^T: T rounded up to a multiple of 8
-    float scale_log2;         // scale * log2(e)
+    const __nv_bfloat16 *q;     // [B, Hq, T, D]
+    const unsigned char *kimg;  // [B, Hkv, n_tiles] 32 KB tile images of K
+    const unsigned char *vimg;  // [B, Hkv, n_tiles] 32 KB tile images of V^T
+    __nv_bfloat16 *out;         // [B, Hq, T, D]
+    float *lse;                 // [B, Hq, T] natural log, or null
+    int32_t *err;               // error flag (a bounded wait gave up)
+    int B, Hq, Hkv, T, n_tiles, n_pairs;
+    float scale_log2;           // scale * log2(e)
     int causal;
 };
 
-// one 128-row x 128-column bf16 tile from a row-major matrix into the
-// swizzled K-major layout; rows >= rows_ok and columns >= cols_ok read as 0
-__device__ __forceinline__ void pf_load_tile(uint32_t dst, const __nv_bfloat16 *src, int64_t ld,
-                                             int rows_ok, int cols_ok, int tid) {
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-        const int ci = tid + it * kPfThreads;  // 16-byte chunk: 16 per row
-        const int row = ci >> 4, ch = ci & 15;
-        const int half = ch >> 3, c = ch & 7;
-        const uint32_t d = dst + half * kPfHalf + (row >> 3) * 1024 + (row & 7) * 128 +
-                           ((c ^ (row & 7)) << 4);
-        const bool ok = row < rows_ok && ch * 8 < cols_ok;
-        const __nv_bfloat16 *s = src + (ok ? (int64_t)row * ld + ch * 8 : 0);
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(s),
-                     "r"(ok ? 16 : 0)
-                     : "memory");
-    }
+// 2^x with the MUFU instruction (PTX ex2.approx.ftz.f32: relative error
+// about 2^-22, subnormal results flushed to zero); p is rounded to bf16
+// right after, so the approximation is far below the output precision
+__device__ __forceinline__ float pf_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+    return y;
 }
 
-__device__ __forceinline__ void pf_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void pf_wait() {
-    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+__device__ __forceinline__ void bulk_g2s_u32(uint32_t dst, const void *src, uint32_t bytes,
+                                             uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+            dst),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
 }
 
 __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs a) {
     extern __shared__ __align__(16) unsigned char pf_raw[];
     unsigned char *base = (unsigned char *)(((uintptr_t)pf_raw + 1023) & ~(uintptr_t)1023);
-    const uint32_t sQ = smem_u32(base);
-    const uint32_t sK0 = sQ + kPfTile, sV0 = sQ + 3 * kPfTile, sP = sQ + 5 * kPfTile;
-    __shared__ __align__(8) uint64_t mbar[2];  // 0: S done, 1: P.V done
+    const uint32_t sQ = smem_u32(base);              // Q tile t at sQ + t * kPfTile
+    const uint32_t sK = sQ + 2 * kPfTile;            // K stage s at sK + s * kPfTile
+    const uint32_t sV = sK + 2 * kPfTile;            // V^T stage s at sV + s * kPfTile
+    __shared__ __align__(8) uint64_t bar_k[2], bar_v[2], bar_free[2], bar_s[2], bar_p[2];
+    __shared__ __align__(8) uint64_t bar_q, bar_o, bar_drain;
     __shared__ uint32_t s_tmem;
-    __shared__ float red_m[kPfRows][2], red_l[kPfRows][2];
+    __shared__ volatile int s_abort;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int row = 32 * (warp & 3) + lane;   // query row of this thread (TMEM lane)
-    const int hv = warp >> 2;                  // key / dim half of this thread
     const int bh = blockIdx.x % (a.B * a.Hq);
-    const int tile = a.n_tiles - 1 - blockIdx.x / (a.B * a.Hq);
+    const int pair = a.n_pairs - 1 - blockIdx.x / (a.B * a.Hq);
     const int b = bh / a.Hq, h = bh - b * a.Hq;
     const int kvh = h / (a.Hq / a.Hkv);
-    const int q0 = tile * kPfRows;
-    const int nj = a.causal ? tile + 1 : a.n_tiles;
+    const int qt0 = 2 * pair;
+    // KV tiles per query tile (tile 1 may lie past T: its rows are computed
+    // on zero queries and never stored)
+    const int nj0 = a.causal ? min(qt0 + 1, a.n_tiles) : a.n_tiles;
+    const int nj = a.causal ? min(qt0 + 2, a.n_tiles) : a.n_tiles;  // tile 1, >= nj0
 
-    if (warp == 0) tmem_alloc(smem_u32(&s_tmem), 256);
+    if (warp == kPfMmaWarp) tmem_alloc(smem_u32(&s_tmem), 512);
     if (tid == 0) {
-        mbar_init(&mbar[0], 1);
-        mbar_init(&mbar[1], 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&bar_k[s], 1);
+            mbar_init(&bar_v[s], 1);
+            mbar_init(&bar_free[s], 1);
+            mbar_init(&bar_s[s], 1);
+            mbar_init(&bar_p[s], 128);
+        }
+        mbar_init(&bar_q, 256);
+        mbar_init(&bar_o, 1);
+        mbar_init(&bar_drain, 1);
+        s_abort = 0;
         mbar_fence_init();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 0) tmem_relinquish();
-    const uint32_t tS = s_tmem, tO = s_tmem + 128;
-    const uint32_t tlane = (uint32_t)(32 * (warp & 3)) << 16;
+    if (warp == kPfMmaWarp) tmem_relinquish();
+    const uint32_t tmem = s_tmem;
 
-    const __nv_bfloat16 *qg = a.q + (((int64_t)b * a.Hq + h) * a.T + q0) * kPfD;
-    const __nv_bfloat16 *kg = a.k + ((int64_t)b * a.Hkv + kvh) * a.cap * kPfD;
-    const __nv_bfloat16 *vg = a.vt + ((int64_t)b * a.Hkv + kvh) * kPfD * a.Tp;
-
-    // prologue: Q, K_0 | V_0
-    pf_load_tile(sQ, qg, kPfD, min(kPfRows, a.T - q0), kPfD, tid);
-    pf_load_tile(sK0, kg, kPfD, min(kPfRows, a.T), kPfD, tid);
-    pf_commit();
-    pf_load_tile(sV0, vg, a.Tp, kPfD, min(kPfRows, a.T), tid);
-    pf_commit();
-
-    const int qpos = q0 + row;
-    float m_used = -INFINITY, l_part = 0.f;
-    bool failed = false;  // block-uniform: decided at block barriers only
-    int j_fail = 0, n_pv = 0;
-    for (int j = 0; j < nj; ++j) {
-        const int buf = j & 1;
-        const int kv0 = j * kPfRows;
-        // K_j (and Q) landed; groups after it: V_j
-        pf_wait<1>();
-        fence_proxy_async_smem();
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-            const uint32_t sK = sK0 + buf * kPfTile;
-#pragma unroll
-            for (int kk = 0; kk < kPfD / 16; ++kk) {
-                const uint32_t off = (kk >> 2) * kPfHalf + (kk & 3) * 32;
-                umma_bf16_ss(tS, umma_desc_sw128(sQ + off), umma_desc_sw128(sK + off), kIdesc,
-                             kk > 0);
-            }
-            umma_commit(smem_u32(&mbar[0]));
-        }
-        // prefetch K_{j+1} into the other buffer (its S MMA finished last iteration)
-        if (j + 1 < nj)
-            pf_load_tile(sK0 + (buf ^ 1) * kPfTile, kg + (int64_t)(kv0 + kPfRows) * kPfD, kPfD,
-                         min(kPfRows, a.T - kv0 - kPfRows), kPfD, tid);
-        pf_commit();
-
-        const bool ok_s = mbar_wait(&mbar[0], j & 1);
-        tc_fence_after();
-        // ---- S row: 64 keys of this thread's half ----
-        float s[64];
+    if (warp < 8) {
+        // ---------------- softmax warpgroup t ----------------
+        const int t = warp >> 2;
+        const int row = 32 * (warp & 3) + lane;  // TMEM lane = query row in the tile
+        const int qtile = qt0 + t;
+        const int qpos = qtile * kPfRows + row;
+        // this thread's query row into the swizzled Q tile (zeros past T)
         {
-            uint32_t r[16];
+            const bool ok = qpos < a.T;
+            const __nv_bfloat16 *qg =
+                a.q + (((int64_t)b * a.Hq + h) * a.T + (ok ? qpos : 0)) * kPfD;
+            const uint32_t dst = sQ + t * kPfTile;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                tmem_ld_x16(tS + tlane + 64 * hv + 16 * c, r);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 16; ++i) s[16 * c + i] = __uint_as_float(r[i]);
-            }
-        }
-        float mx = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-            const int kpos = kv0 + 64 * hv + i;
-            const bool on = kpos < a.T && (!a.causal || kpos <= qpos);
-            s[i] = on ? s[i] * a.scale_log2 : -INFINITY;
-            mx = fmaxf(mx, s[i]);
-        }
-        red_m[row][hv] = mx;
-        tc_fence_before();
-        if (__syncthreads_or(!ok_s)) {
-            failed = true;
-            j_fail = j;
-            break;
-        }
-        const float m_tile = fmaxf(red_m[row][0], red_m[row][1]);
-        const float m_new = fmaxf(m_used, m_tile);
-        float alpha = 1.f;
-        bool rescale = false;
-        if (m_used == -INFINITY) {
-            m_used = m_new;
-        } else if (m_new > m_used + 8.0f) {
-            alpha = exp2f(m_used - m_new);
-            m_used = m_new;
-            rescale = true;
-        }
-        uint32_t pk[32];
-        float lsum = 0.f;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            const float p0 = m_used == -INFINITY ? 0.f : exp2f(s[2 * i] - m_used);
-            const float p1 = m_used == -INFINITY ? 0.f : exp2f(s[2 * i + 1] - m_used);
-            lsum += p0 + p1;
-            pk[i] = pack_bf16(p0, p1);
-        }
-        l_part = l_part * alpha + lsum;
-
-        // the previous P.V MMA has read P and V_{j-1}, and O is settled
-        const bool ok_o = j == 0 || mbar_wait(&mbar[1], (j - 1) & 1);
-        tc_fence_after();
-        // prefetch V_{j+1} into the buffer V_{j-1} used
-        if (j + 1 < nj && ok_o)
-            pf_load_tile(sV0 + (buf ^ 1) * kPfTile, vg + kv0 + kPfRows, a.Tp, kPfD,
-                         min(kPfRows, a.T - kv0 - kPfRows), tid);
-        pf_commit();
-        if (rescale && j > 0 && ok_o) {
-            uint32_t r[16];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const uint32_t ta = tO + tlane + 64 * hv + 16 * c;
-                tmem_ld_x16(ta, r);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-                tmem_st_x16(ta, r);
-            }
-            tmem_wait_st();
-        }
-        // P (bf16) -> swizzled A operand, keys 64*hv .. 64*hv+63 = half hv
-        if (ok_o) {
-            const uint32_t prow = sP + hv * kPfHalf + (row >> 3) * 1024 + (row & 7) * 128;
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                const uint32_t d = prow + ((c ^ (row & 7)) << 4);
-                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(d),
-                             "r"(pk[4 * c]), "r"(pk[4 * c + 1]), "r"(pk[4 * c + 2]),
-                             "r"(pk[4 * c + 3])
+            for (int ch = 0; ch < 16; ++ch)
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(
+                                 dst + pf_img_off(row, ch)),
+                             "l"(qg + ch * 8), "r"(ok ? 16 : 0)
                              : "memory");
+            asm volatile("cp.async.commit_group;\n" ::: "memory");
+            asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+            fence_proxy_async_smem();
+            mbar_arrive(&bar_q);
+        }
+        const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+        const uint32_t tS = tmem + lane_off + (uint32_t)(t * 128);
+        const uint32_t tO = tmem + lane_off + (uint32_t)(256 + t * 128);
+        const int njt = t ? nj : nj0;
+        float m_used = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < njt; ++j) {
+            if (s_abort || !mbar_wait(&bar_s[t], (uint32_t)(j & 1))) {
+                ok = false;
+                break;
             }
-        }
-        // V_j landed; groups after it: K_{j+1}, V_{j+1}
-        pf_wait<2>();
-        fence_proxy_async_smem();
-        tc_fence_before();
-        if (__syncthreads_or(!ok_o)) {
-            failed = true;
-            j_fail = j;
-            break;
-        }
-        if (tid == 0) {
             tc_fence_after();
-            const uint32_t sV = sV0 + buf * kPfTile;
+            // keys [0, lim) of this tile are visible to this row; only the
+            // diagonal tile (causal) and the ragged last tile mask anything,
+            // so the other tiles take the compare-free path
+            const int kv0 = j * kPfRows;
+            const bool masked = (a.causal && j == qtile) || kv0 + kPfRows > a.T;
+            const int lim = (a.causal ? min(a.T, qpos + 1) : a.T) - kv0;
+            // pass 1: row maximum over the 128 scores (32 columns at a time)
+            float mx = -INFINITY;
 #pragma unroll
-            for (int kk = 0; kk < kPfRows / 16; ++kk) {
-                const uint32_t off = (kk >> 2) * kPfHalf + (kk & 3) * 32;
-                umma_bf16_ss(tO, umma_desc_sw128(sP + off), umma_desc_sw128(sV + off), kIdesc,
-                             (j > 0 || kk > 0) ? 1u : 0u);
+            for (int c = 0; c < 4; ++c) {
+                uint32_t r[32];
+                tmem_ld_x32(tS + 32 * c, r);
+                tmem_wait_ld();
+                if (masked) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        mx = fmaxf(mx, 32 * c + i < lim ? __uint_as_float(r[i]) : -INFINITY);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(r[i]));
+                }
             }
-            umma_commit(smem_u32(&mbar[1]));
-        }
-        n_pv = j + 1;
-    }
-    pf_wait<0>();
-    if (!failed && nj > 0) {
-        const bool ok = mbar_wait(&mbar[1], (nj - 1) & 1);
-        tc_fence_after();
-        if (__syncthreads_or(!ok)) {
-            failed = true;
-            j_fail = nj;
-        }
-    }
-    if (failed) {
-        // record it, and let the MMAs already issued finish (bounded) before
-        // TMEM is released
-        if (tid == 0) atomicExch(a.err, 1);
-        if (j_fail < nj) mbar_wait(&mbar[0], j_fail & 1);
-        if (n_pv > 0) mbar_wait(&mbar[1], (n_pv - 1) & 1);
-    }
-    // ---- epilogue: O / l ----
-    red_l[row][hv] = l_part;
-    tc_fence_after();
-    __syncthreads();
-    if (!failed) {
-        const float l = red_l[row][0] + red_l[row][1];
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        uint32_t r[16];
-        __nv_bfloat16 *og = a.out + (((int64_t)b * a.Hq + h) * a.T + qpos) * kPfD + 64 * hv;
+            mx *= a.scale_log2;
+            const float m_new = fmaxf(m_used, mx);
+            if (m_used == -INFINITY) {
+                m_used = m_new;
+            } else if (m_new > m_used + 8.0f) {
+                // PV(j-1) of this tile has finished (it was issued before
+                // S(j), whose commit this thread waited for)
+                const float alpha = pf_exp2(m_used - m_new);
+                m_used = m_new;
+                l *= alpha;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            tmem_ld_x16(tO + tlane + 64 * hv + 16 * c, r);
-            tmem_wait_ld();
-            if (qpos < a.T) {
-                uint32_t o[8];
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t r[32];
+                    tmem_ld_x32(tO + 32 * c, r);
+                    tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    o[i] = pack_bf16(__uint_as_float(r[2 * i]) * inv,
-                                     __uint_as_float(r[2 * i + 1]) * inv);
-                uint4 *dst = (uint4 *)(og + 16 * c);
-                dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-                dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+                    for (int i = 0; i < 32; ++i)
+                        r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+                    tmem_st_x32(tO + 32 * c, r);
+                }
+            }
+            // pass 2: p = 2^(s * scale - m) as bf16 pairs (two keys per
+            // column) over the first 64 score columns: the P columns of
+            // score chunk c, [16 c, 16 c + 16), lie below every score column
+            // still to be read
+            const float neg = m_used == -INFINITY ? 0.f : -m_used;
+            float ls = 0.f;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t r[32], pk[16];
+                tmem_ld_x32(tS + 32 * c, r);
+                tmem_wait_ld();
+                if (masked) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (32 * c + i >= lim) r[i] = __float_as_uint(-INFINITY);
+                }
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float p0 = pf_exp2(fmaf(__uint_as_float(r[2 * i]), a.scale_log2, neg));
+                    const float p1 =
+                        pf_exp2(fmaf(__uint_as_float(r[2 * i + 1]), a.scale_log2, neg));
+                    ls += p0 + p1;
+                    pk[i] = pack_bf16(p0, p1);
+                }
+                tmem_st_x16(tS + 16 * c, pk);
+            }
+            l += ls;
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&bar_p[t]);
+        }
+        if (!ok) {
+            s_abort = 1;
+            atomicExch(a.err, 1);
+        }
+        // ---- epilogue: O / l ----
+        if (ok && !s_abort && mbar_wait(&bar_o, 0)) {
+            tc_fence_after();
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            __nv_bfloat16 *og = a.out + (((int64_t)b * a.Hq + h) * a.T + qpos) * kPfD;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t r[32];
+                tmem_ld_x32(tO + 32 * c, r);
+                tmem_wait_ld();
+                if (qpos < a.T) {
+                    uint32_t o[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        o[i] = pack_bf16(__uint_as_float(r[2 * i]) * inv,
+                                         __uint_as_float(r[2 * i + 1]) * inv);
+                    uint4 *dst = (uint4 *)(og + 32 * c);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        dst[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+                }
+            }
+            if (a.lse && qpos < a.T)
+                a.lse[((int64_t)b * a.Hq + h) * a.T + qpos] =
+                    l > 0.f ? (m_used + log2f(l)) * kLn2 : -INFINITY;
+        } else if (ok) {
+            s_abort = 1;
+            atomicExch(a.err, 1);
+        }
+    } else if (warp == kPfMmaWarp) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            bool ok = mbar_wait(&bar_q, 0);
+            tc_fence_after();
+            auto s_mma = [&](int t, int j) -> bool {
+                const int st = j & 1;
+                if (s_abort || !mbar_wait(&bar_k[st], (uint32_t)((j >> 1) & 1))) return false;
+                tc_fence_after();
+                const uint32_t q0 = sQ + t * kPfTile, k0 = sK + st * kPfTile;
+#pragma unroll
+                for (int kk = 0; kk < kPfD / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * kPfHalf + (kk & 3) * 32;
+                    umma_bf16_ss(tmem + t * 128, umma_desc_sw128(q0 + off),
+                                 umma_desc_sw128(k0 + off), kIdesc, kk > 0);
+                }
+                umma_commit(smem_u32(&bar_s[t]));
+                return true;
+            };
+            auto pv_mma = [&](int t, int j) -> bool {
+                const int st = j & 1;
+                if (s_abort || !mbar_wait(&bar_v[st], (uint32_t)((j >> 1) & 1)) ||
+                    !mbar_wait(&bar_p[t], (uint32_t)(j & 1)))
+                    return false;
+                tc_fence_after();
+                const uint32_t v0 = sV + st * kPfTile;
+#pragma unroll
+                for (int kk = 0; kk < kPfRows / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * kPfHalf + (kk & 3) * 32;
+                    umma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
+                                 umma_desc_sw128(v0 + off), kIdesc, (j > 0 || kk > 0) ? 1u : 0u);
+                }
+                return true;
+            };
+            if (ok && nj0 > 0) ok = s_mma(0, 0);
+            if (ok) ok = s_mma(1, 0);
+            for (int j = 0; ok && j < nj; ++j) {
+                if (j < nj0) {
+                    ok = pv_mma(0, j);
+                    if (ok && j + 1 < nj0) ok = s_mma(0, j + 1);
+                }
+                if (ok) ok = pv_mma(1, j);
+                if (ok) umma_commit(smem_u32(&bar_free[j & 1]));  // stage j & 1 read
+                if (ok && j + 1 < nj) ok = s_mma(1, j + 1);
+            }
+            if (ok) {
+                umma_commit(smem_u32(&bar_o));
+            } else {
+                s_abort = 1;
+                atomicExch(a.err, 1);
+            }
+            // every MMA issued so far has finished before TMEM is released
+            umma_commit(smem_u32(&bar_drain));
+            if (!mbar_wait(&bar_drain, 0)) atomicExch(a.err, 1);
+        }
+    } else {
+        // ---------------- K / V^T loads ----------------
+        if (lane == 0) {
+            const size_t tile0 = ((size_t)b * a.Hkv + kvh) * a.n_tiles;
+            int issued = 0;
+            for (int j = 0; j < nj; ++j) {
+                const int st = j & 1;
+                if (j >= 2 && (s_abort || !mbar_wait(&bar_free[st], (uint32_t)(((j >> 1) - 1) & 1)))) {
+                    s_abort = 1;
+                    atomicExch(a.err, 1);
+                    break;
+                }
+                mbar_arrive_expect_tx(&bar_k[st], kPfTile);
+                bulk_g2s_u32(sK + st * kPfTile, a.kimg + (tile0 + j) * kPfTile, kPfTile, &bar_k[st]);
+                mbar_arrive_expect_tx(&bar_v[st], kPfTile);
+                bulk_g2s_u32(sV + st * kPfTile, a.vimg + (tile0 + j) * kPfTile, kPfTile, &bar_v[st]);
+                issued = j + 1;
+            }
+            // the last copies into each stage have landed before the CTA ends
+            for (int j = max(0, issued - 2); j < issued; ++j) {
+                mbar_wait(&bar_k[j & 1], (uint32_t)((j >> 1) & 1));
+                mbar_wait(&bar_v[j & 1], (uint32_t)((j >> 1) & 1));
             }
         }
-        if (a.lse && hv == 0 && qpos < a.T)
-            a.lse[((int64_t)b * a.Hq + h) * a.T + qpos] =
-                l > 0.f ? (m_used + log2f(l)) * kLn2 : -INFINITY;
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tS, 256);
+    tc_fence_after();
+    if (warp == kPfMmaWarp) tmem_dealloc(tmem, 512);
 }
 
-// V [B, Hkv, cap, D] (tokens [0, T)) -> V^T [B, Hkv, D, Tp], 32 x 32 tiles;
-// columns [T, Tp) are zero (a partial key tile's masked columns multiply them)
-__global__ void prefill_transpose_v_kernel(const __nv_bfloat16 *v, __nv_bfloat16 *vt, int T,
-                                           int Tp, int D, int64_t cap) {
-    __shared__ __nv_bfloat16 tile[32][33];
-    const int64_t mat = blockIdx.z;
-    const int t0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
-    const __nv_bfloat16 *src = v + mat * cap * D;
-    __nv_bfloat16 *dst = vt + mat * (int64_t)Tp * D;
-    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-        const int t = t0 + i, d = d0 + threadIdx.x;
-        tile[i][threadIdx.x] = (t < T && d < D) ? src[(int64_t)t * D + d] : __float2bfloat16(0.f);
+// K [B, Hkv, cap, D] and V (tokens [0, T)) -> the tile images of K and V^T
+// (pf_img_off layout, zeros past T).  One CTA per (128-key tile, b * kv head).
+__global__ void __launch_bounds__(256) prefill_image_kernel(const __nv_bfloat16 *k,
+                                                            const __nv_bfloat16 *v,
+                                                            unsigned char *kimg,
+                                                            unsigned char *vimg, int T,
+                                                            int n_tiles, int64_t cap) {
+    __shared__ __align__(16) __nv_bfloat16 vs[kPfRows][kPfD + 8];
+    const int j = blockIdx.x, bh = blockIdx.y, tid = threadIdx.x;
+    const int64_t src0 = ((int64_t)bh * cap + (int64_t)j * kPfRows) * kPfD;
+    unsigned char *ki = kimg + ((size_t)bh * n_tiles + j) * kPfTile;
+    unsigned char *vi = vimg + ((size_t)bh * n_tiles + j) * kPfTile;
+    for (int idx = tid; idx < kPfRows * 16; idx += 256) {
+        const int r = idx >> 4, ch = idx & 15;
+        const bool ok = j * kPfRows + r < T;
+        const uint4 kv = ok ? *(const uint4 *)(k + src0 + (int64_t)r * kPfD + ch * 8)
+                            : make_uint4(0, 0, 0, 0);
+        *(uint4 *)(ki + pf_img_off(r, ch)) = kv;
+        const uint4 vv = ok ? *(const uint4 *)(v + src0 + (int64_t)r * kPfD + ch * 8)
+                            : make_uint4(0, 0, 0, 0);
+        *(uint4 *)(&vs[r][ch * 8]) = vv;
     }
     __syncthreads();
-    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-        const int d = d0 + i, t = t0 + threadIdx.x;
-        if (t < Tp && d < D) dst[(int64_t)d * Tp + t] = tile[threadIdx.x][i];
+    // V^T: row = dim d, 16-byte chunk ch = keys 8 ch .. 8 ch + 7
+    for (int idx = tid; idx < kPfD * 16; idx += 256) {
+        const int d = idx & (kPfD - 1), ch = idx >> 7;
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const __nv_bfloat16 lo = vs[8 * ch + 2 * e][d], hi = vs[8 * ch + 2 * e + 1][d];
+            w[e] = (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
+        }
+        *(uint4 *)(vi + pf_img_off(d, ch)) = make_uint4(w[0], w[1], w[2], w[3]);
     }
 }
 
@@ -346,8 +415,8 @@ extern "C" int santa_prefill_workspace_bytes(const SantaPrefillShape *shape, siz
     int st = check_prefill(shape);
     if (st) return st;
     if (!bytes) return SANTA_ERR_INVALID_ARGUMENT;
-    const int64_t Tp = ((int64_t)shape->seq_len + 7) / 8 * 8;  // 16-byte rows of V^T
-    *bytes = (size_t)shape->batch * shape->num_kv_heads * Tp * shape->head_dim * 2 + 256;
+    const size_t n_tiles = ((size_t)shape->seq_len + kPfRows - 1) / kPfRows;
+    *bytes = 2 * (size_t)shape->batch * shape->num_kv_heads * n_tiles * kPfTile + 256;
     return SANTA_OK;
 }
 
@@ -362,18 +431,19 @@ extern "C" int santa_prefill(const SantaPrefillShape *shape, const void *q, cons
     if (!workspace || workspace_bytes < need) return SANTA_ERR_WORKSPACE;
     if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out | (uintptr_t)workspace) & 15)
         return SANTA_ERR_UNSUPPORTED;
-    const int T = shape->seq_len, D = shape->head_dim;
-    __nv_bfloat16 *vt = (__nv_bfloat16 *)workspace;
-    const int Tp = (T + 7) / 8 * 8;
-    dim3 tg((Tp + 31) / 32, (D + 31) / 32, shape->batch * shape->num_kv_heads);
+    const int T = shape->seq_len;
+    const int n_tiles = (T + kPfRows - 1) / kPfRows;
+    const int BHkv = shape->batch * shape->num_kv_heads;
     const int64_t cap = shape->kv_capacity ? shape->kv_capacity : T;
-    prefill_transpose_v_kernel<<<tg, dim3(32, 8), 0, stream>>>((const __nv_bfloat16 *)v, vt, T,
-                                                                Tp, D, cap);
+    unsigned char *kimg = (unsigned char *)workspace;
+    unsigned char *vimg = kimg + (size_t)BHkv * n_tiles * kPfTile;
+    prefill_image_kernel<<<dim3(n_tiles, BHkv), 256, 0, stream>>>(
+        (const __nv_bfloat16 *)k, (const __nv_bfloat16 *)v, kimg, vimg, T, n_tiles, cap);
     SANTA_LAUNCH_CHECK();
     PrefillArgs a;
     a.q = (const __nv_bfloat16 *)q;
-    a.k = (const __nv_bfloat16 *)k;
-    a.vt = vt;
+    a.kimg = kimg;
+    a.vimg = vimg;
     a.out = (__nv_bfloat16 *)out;
     a.lse = lse;
     a.err = error_flag;
@@ -381,9 +451,8 @@ extern "C" int santa_prefill(const SantaPrefillShape *shape, const void *q, cons
     a.Hq = shape->num_query_heads;
     a.Hkv = shape->num_kv_heads;
     a.T = T;
-    a.cap = cap;
-    a.Tp = Tp;
-    a.n_tiles = (T + kPfRows - 1) / kPfRows;
+    a.n_tiles = n_tiles;
+    a.n_pairs = (n_tiles + 1) / 2;
     a.scale_log2 = shape->scale * 1.4426950408889634f;
     a.causal = shape->causal ? 1 : 0;
     const size_t smem = 6 * (size_t)kPfTile + 1024;
@@ -394,7 +463,7 @@ extern "C" int santa_prefill(const SantaPrefillShape *shape, const void *q, cons
                                               (int)smem));
         attr = true;
     }
-    const unsigned grid = (unsigned)a.n_tiles * a.B * a.Hq;
+    const unsigned grid = (unsigned)a.n_pairs * a.B * a.Hq;
     prefill_fwd_kernel<<<grid, kPfThreads, smem, stream>>>(a);
     SANTA_LAUNCH_CHECK();
     return SANTA_OK;
