@@ -258,7 +258,8 @@ typedef struct SantaPrefillShape {
                                  0 = seq_len */
 } SantaPrefillShape;
 
-/* Workspace: the transposed V ([B, Hkv, D, T rounded up to 8] bf16). */
+/* Workspace: the 32 KB shared-memory images of every 128-token tile of K and
+ * of V^T (2 * B * Hkv * ceil(T / 128) * 32768 bytes). */
 int santa_prefill_workspace_bytes(const SantaPrefillShape *shape, size_t *bytes);
 
 /* Attention of every query position over the prompt, as the reference's

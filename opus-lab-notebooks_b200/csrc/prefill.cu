@@ -28,6 +28,11 @@
 //                          products while the other tile's softmax runs;
 //         warp 9           one thread streams K_j and V^T_j (two stages,
 //                          one 32 KB bulk copy each).
+//       The two softmax warpgroups take turns for their exp2 pass (an
+//       mbarrier token), so one tile's exponentials run beside the other
+//       tile's MMAs rather than beside its exponentials; exp2 is the MUFU
+//       ex2.approx instruction and row maxima and sums use eight independent
+//       partial accumulators (no serial fmax / fadd chains).
 //       TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
 //       The running maximum is updated lazily: O and l are rescaled only
 //       when the maximum grows by more than 8 (log2 units), so p <= 2^8.
@@ -96,7 +101,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
     const uint32_t sK = sQ + 2 * kPfTile;            // K stage s at sK + s * kPfTile
     const uint32_t sV = sK + 2 * kPfTile;            // V^T stage s at sV + s * kPfTile
     __shared__ __align__(8) uint64_t bar_k[2], bar_v[2], bar_free[2], bar_s[2], bar_p[2];
-    __shared__ __align__(8) uint64_t bar_q, bar_o, bar_drain;
+    __shared__ __align__(8) uint64_t bar_q, bar_o, bar_drain, bar_tok[2];
     __shared__ uint32_t s_tmem;
     __shared__ volatile int s_abort;
 
@@ -121,6 +126,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
             mbar_init(&bar_p[s], 128);
         }
         mbar_init(&bar_q, 256);
+        mbar_init(&bar_tok[0], 128);
+        mbar_init(&bar_tok[1], 128);
         mbar_init(&bar_o, 1);
         mbar_init(&bar_drain, 1);
         s_abort = 0;
@@ -161,6 +168,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
         const int njt = t ? nj : nj0;
         float m_used = -INFINITY, l = 0.f;
         bool ok = true;
+        // the exp2 passes of the two tiles take turns (bar_tok[t] = tile t
+        // may start its pass 2), so one tile's exponentials overlap the other
+        // tile's MMAs instead of sharing the MUFU with its exponentials
+        if (t == 1) mbar_arrive(&bar_tok[0]);
         for (int j = 0; j < njt; ++j) {
             if (s_abort || !mbar_wait(&bar_s[t], (uint32_t)(j & 1))) {
                 ok = false;
@@ -174,21 +185,32 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
             const bool masked = (a.causal && j == qtile) || kv0 + kPfRows > a.T;
             const int lim = (a.causal ? min(a.T, qpos + 1) : a.T) - kv0;
             // pass 1: row maximum over the 128 scores (32 columns at a time)
-            float mx = -INFINITY;
+            // eight independent partial maxima (no serial fmax chain)
+            float mp[8];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t r[32];
-                tmem_ld_x32(tS + 32 * c, r);
+            for (int e = 0; e < 8; ++e) mp[e] = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                uint32_t r0[32], r1[32];
+                tmem_ld_x32(tS + 64 * c, r0);
+                tmem_ld_x32(tS + 64 * c + 32, r1);
                 tmem_wait_ld();
                 if (masked) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        mx = fmaxf(mx, 32 * c + i < lim ? __uint_as_float(r[i]) : -INFINITY);
+                    for (int i = 0; i < 32; ++i) {
+                        const float v0 = 64 * c + i < lim ? __uint_as_float(r0[i]) : -INFINITY;
+                        const float v1 = 64 * c + 32 + i < lim ? __uint_as_float(r1[i]) : -INFINITY;
+                        mp[i & 7] = fmaxf(mp[i & 7], fmaxf(v0, v1));
+                    }
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(r[i]));
+                    for (int i = 0; i < 32; ++i)
+                        mp[i & 7] = fmaxf(mp[i & 7],
+                                          fmaxf(__uint_as_float(r0[i]), __uint_as_float(r1[i])));
                 }
             }
+            float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
             mx *= a.scale_log2;
             const float m_new = fmaxf(m_used, mx);
             if (m_used == -INFINITY) {
@@ -210,12 +232,19 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
                     tmem_st_x32(tO + 32 * c, r);
                 }
             }
+            // (tile 1's extra last iteration has no tile-0 turn to alternate with)
+            if (j < nj0 && (s_abort || !mbar_wait(&bar_tok[t], (uint32_t)(j & 1)))) {
+                ok = false;
+                break;
+            }
             // pass 2: p = 2^(s * scale - m) as bf16 pairs (two keys per
             // column) over the first 64 score columns: the P columns of
             // score chunk c, [16 c, 16 c + 16), lie below every score column
             // still to be read
             const float neg = m_used == -INFINITY ? 0.f : -m_used;
-            float ls = 0.f;
+            float lp[8];  // eight independent partial row sums
+#pragma unroll
+            for (int e = 0; e < 8; ++e) lp[e] = 0.f;
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 uint32_t r[32], pk[16];
@@ -231,12 +260,16 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
                     const float p0 = pf_exp2(fmaf(__uint_as_float(r[2 * i]), a.scale_log2, neg));
                     const float p1 =
                         pf_exp2(fmaf(__uint_as_float(r[2 * i + 1]), a.scale_log2, neg));
-                    ls += p0 + p1;
+                    lp[i & 7] += p0 + p1;
                     pk[i] = pack_bf16(p0, p1);
                 }
                 tmem_st_x16(tS + 16 * c, pk);
             }
-            l += ls;
+            l += ((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7]));
+            // the other tile's turn, while it has a turn left: nj0
+            // completions of each token, never two ahead of the waiter (a
+            // tile's next hand-over comes after it waited for the other's)
+            if (t == 0 || j + 1 < nj0) mbar_arrive(&bar_tok[1 - t]);
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(&bar_p[t]);
