@@ -51,8 +51,9 @@ namespace santa {
 
 constexpr int kPfD = 128;             // head dim
 constexpr int kPfRows = 128;          // query rows per tile = keys per KV tile
-constexpr int kPfThreads = 320;       // 2 softmax warpgroups + MMA warp + load warp
-constexpr int kPfMmaWarp = 8;  // warp 9 loads K / V^T
+constexpr int kPfSoftmaxWarps = 16;   // 2 warpgroups per query tile (one per score half)
+constexpr int kPfThreads = 32 * (kPfSoftmaxWarps + 2);  // + MMA warp + load warp
+constexpr int kPfMmaWarp = kPfSoftmaxWarps;  // the next warp loads K / V^T
 constexpr int kPfTile = 32768;        // bytes of one 128 x 128 bf16 tile image
 constexpr int kPfHalf = 16384;        // one 64-element half of a tile
 constexpr uint32_t kIdesc = umma_idesc_bf16(128, 128);
@@ -83,6 +84,18 @@ __device__ __forceinline__ float pf_exp2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
     return y;
+}
+
+// named barrier over n threads (whole warps) that also ORs a predicate
+__device__ __forceinline__ bool bar_red_or(int id, int n, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, %2, %3, p;\n"
+        " selp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(id), "r"(n)
+        : "memory");
+    return r != 0;
 }
 
 __device__ __forceinline__ void bulk_g2s_u32(uint32_t dst, const void *src, uint32_t bytes,
@@ -123,11 +136,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
             mbar_init(&bar_v[s], 1);
             mbar_init(&bar_free[s], 1);
             mbar_init(&bar_s[s], 1);
-            mbar_init(&bar_p[s], 128);
+            mbar_init(&bar_p[s], 256);
         }
-        mbar_init(&bar_q, 256);
-        mbar_init(&bar_tok[0], 128);
-        mbar_init(&bar_tok[1], 128);
+        mbar_init(&bar_q, 512);
+        mbar_init(&bar_tok[0], 256);
+        mbar_init(&bar_tok[1], 256);
         mbar_init(&bar_o, 1);
         mbar_init(&bar_drain, 1);
         s_abort = 0;
@@ -139,32 +152,44 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
     if (warp == kPfMmaWarp) tmem_relinquish();
     const uint32_t tmem = s_tmem;
 
-    if (warp < 8) {
-        // ---------------- softmax warpgroup t ----------------
-        const int t = warp >> 2;
+    if (warp < kPfSoftmaxWarps) {
+        // ---------------- softmax: tile t, score half hf ----------------
+        // warpgroup (t, hf) owns score columns [64 hf, 64 hf + 64) of every
+        // row of tile t; the two halves of a tile exchange row maxima through
+        // shared memory at a named barrier (id 1 + t) and their row sums once
+        // at the end.  The named barriers carry every thread's wait outcome
+        // (bar.red.or), so a timed-out wait ends both halves together.
+        // row maxima, double-buffered by iteration parity (a half writes
+        // buffer j & 1 only after the barrier of iteration j - 1, which the
+        // other half passes only after reading it), and the row sums
+        __shared__ float s_red[2][2][2][kPfRows], s_l[2][2][kPfRows];
+        const int t = warp >> 3, hf = (warp >> 2) & 1;
         const int row = 32 * (warp & 3) + lane;  // TMEM lane = query row in the tile
         const int qtile = qt0 + t;
         const int qpos = qtile * kPfRows + row;
-        // this thread's query row into the swizzled Q tile (zeros past T)
+        const int bar_id = 1 + t;
+        // this thread's half of its query row into the swizzled Q tile
         {
             const bool ok = qpos < a.T;
             const __nv_bfloat16 *qg =
                 a.q + (((int64_t)b * a.Hq + h) * a.T + (ok ? qpos : 0)) * kPfD;
             const uint32_t dst = sQ + t * kPfTile;
 #pragma unroll
-            for (int ch = 0; ch < 16; ++ch)
+            for (int c = 0; c < 8; ++c) {
+                const int ch = 8 * hf + c;
                 asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(
                                  dst + pf_img_off(row, ch)),
                              "l"(qg + ch * 8), "r"(ok ? 16 : 0)
                              : "memory");
+            }
             asm volatile("cp.async.commit_group;\n" ::: "memory");
             asm volatile("cp.async.wait_group 0;\n" ::: "memory");
             fence_proxy_async_smem();
             mbar_arrive(&bar_q);
         }
         const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
-        const uint32_t tS = tmem + lane_off + (uint32_t)(t * 128);
-        const uint32_t tO = tmem + lane_off + (uint32_t)(256 + t * 128);
+        const uint32_t tS = tmem + lane_off + (uint32_t)(t * 128 + 64 * hf);  // my score half
+        const uint32_t tO = tmem + lane_off + (uint32_t)(256 + t * 128 + 64 * hf);  // my O half
         const int njt = t ? nj : nj0;
         float m_used = -INFINITY, l = 0.f;
         bool ok = true;
@@ -173,33 +198,27 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
         // tile's MMAs instead of sharing the MUFU with its exponentials
         if (t == 1) mbar_arrive(&bar_tok[0]);
         for (int j = 0; j < njt; ++j) {
-            if (s_abort || !mbar_wait(&bar_s[t], (uint32_t)(j & 1))) {
-                ok = false;
-                break;
-            }
+            bool wok = !s_abort && mbar_wait(&bar_s[t], (uint32_t)(j & 1));
             tc_fence_after();
             // keys [0, lim) of this tile are visible to this row; only the
-            // diagonal tile (causal) and the ragged last tile mask anything,
-            // so the other tiles take the compare-free path
+            // diagonal tile (causal) and the ragged last tile mask anything
             const int kv0 = j * kPfRows;
             const bool masked = (a.causal && j == qtile) || kv0 + kPfRows > a.T;
-            const int lim = (a.causal ? min(a.T, qpos + 1) : a.T) - kv0;
-            // pass 1: row maximum over the 128 scores (32 columns at a time)
-            // eight independent partial maxima (no serial fmax chain)
+            const int lim = (a.causal ? min(a.T, qpos + 1) : a.T) - kv0 - 64 * hf;
+            // pass 1: maximum over my 64 scores (eight partial maxima)
             float mp[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) mp[e] = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
+            if (wok) {
                 uint32_t r0[32], r1[32];
-                tmem_ld_x32(tS + 64 * c, r0);
-                tmem_ld_x32(tS + 64 * c + 32, r1);
+                tmem_ld_x32(tS, r0);
+                tmem_ld_x32(tS + 32, r1);
                 tmem_wait_ld();
                 if (masked) {
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
-                        const float v0 = 64 * c + i < lim ? __uint_as_float(r0[i]) : -INFINITY;
-                        const float v1 = 64 * c + 32 + i < lim ? __uint_as_float(r1[i]) : -INFINITY;
+                        const float v0 = i < lim ? __uint_as_float(r0[i]) : -INFINITY;
+                        const float v1 = 32 + i < lim ? __uint_as_float(r1[i]) : -INFINITY;
                         mp[i & 7] = fmaxf(mp[i & 7], fmaxf(v0, v1));
                     }
                 } else {
@@ -209,9 +228,18 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
                                           fmaxf(__uint_as_float(r0[i]), __uint_as_float(r1[i])));
                 }
             }
-            float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
-                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
-            mx *= a.scale_log2;
+            s_red[j & 1][t][hf][row] = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+            // my turn for the exp pass (tile 1's extra last iteration has no
+            // turn to wait for); its outcome joins the barrier's OR so both
+            // halves leave together
+            if (wok && j < nj0) wok = !s_abort && mbar_wait(&bar_tok[t], (uint32_t)(j & 1));
+            if (bar_red_or(bar_id, 256, !wok)) {
+                ok = false;
+                break;
+            }
+            const float mx =
+                fmaxf(s_red[j & 1][t][0][row], s_red[j & 1][t][1][row]) * a.scale_log2;
             const float m_new = fmaxf(m_used, mx);
             if (m_used == -INFINITY) {
                 m_used = m_new;
@@ -222,7 +250,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
                 m_used = m_new;
                 l *= alpha;
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
+                for (int c = 0; c < 2; ++c) {
                     uint32_t r[32];
                     tmem_ld_x32(tO + 32 * c, r);
                     tmem_wait_ld();
@@ -232,21 +260,15 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
                     tmem_st_x32(tO + 32 * c, r);
                 }
             }
-            // (tile 1's extra last iteration has no tile-0 turn to alternate with)
-            if (j < nj0 && (s_abort || !mbar_wait(&bar_tok[t], (uint32_t)(j & 1)))) {
-                ok = false;
-                break;
-            }
             // pass 2: p = 2^(s * scale - m) as bf16 pairs (two keys per
-            // column) over the first 64 score columns: the P columns of
-            // score chunk c, [16 c, 16 c + 16), lie below every score column
-            // still to be read
+            // column) over my own first 32 score columns: the P columns of
+            // chunk c, [16 c, 16 c + 16), lie below every column still to be read
             const float neg = m_used == -INFINITY ? 0.f : -m_used;
-            float lp[8];  // eight independent partial row sums
+            float lp[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) lp[e] = 0.f;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 uint32_t r[32], pk[16];
                 tmem_ld_x32(tS + 32 * c, r);
                 tmem_wait_ld();
@@ -278,13 +300,16 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
             s_abort = 1;
             atomicExch(a.err, 1);
         }
-        // ---- epilogue: O / l ----
-        if (ok && !s_abort && mbar_wait(&bar_o, 0)) {
+        // ---- epilogue: O / (l of both halves) ----
+        const bool eok = ok && !s_abort && mbar_wait(&bar_o, 0);
+        s_l[t][hf][row] = l;
+        if (!bar_red_or(bar_id, 256, !eok)) {
             tc_fence_after();
-            const float inv = l > 0.f ? 1.f / l : 0.f;
-            __nv_bfloat16 *og = a.out + (((int64_t)b * a.Hq + h) * a.T + qpos) * kPfD;
+            const float lt = s_l[t][0][row] + s_l[t][1][row];
+            const float inv = lt > 0.f ? 1.f / lt : 0.f;
+            __nv_bfloat16 *og = a.out + (((int64_t)b * a.Hq + h) * a.T + qpos) * kPfD + 64 * hf;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 uint32_t r[32];
                 tmem_ld_x32(tO + 32 * c, r);
                 tmem_wait_ld();
@@ -300,10 +325,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
                         dst[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
                 }
             }
-            if (a.lse && qpos < a.T)
+            if (a.lse && hf == 0 && qpos < a.T)
                 a.lse[((int64_t)b * a.Hq + h) * a.T + qpos] =
-                    l > 0.f ? (m_used + log2f(l)) * kLn2 : -INFINITY;
-        } else if (ok) {
+                    lt > 0.f ? (m_used + log2f(lt)) * kLn2 : -INFINITY;
+        } else {
             s_abort = 1;
             atomicExch(a.err, 1);
         }
@@ -336,7 +361,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
 #pragma unroll
                 for (int kk = 0; kk < kPfRows / 16; ++kk) {
                     const uint32_t off = (kk >> 2) * kPfHalf + (kk & 3) * 32;
-                    umma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
+                    // P of keys 0-63 in columns [0, 32), of keys 64-127 in
+                    // [64, 96): each score half wrote P over its own columns
+                    umma_bf16_ts(tmem + 256 + t * 128,
+                                 tmem + t * 128 + (kk < 4 ? kk * 8 : 64 + (kk - 4) * 8),
                                  umma_desc_sw128(v0 + off), kIdesc, (j > 0 || kk > 0) ? 1u : 0u);
                 }
                 return true;
