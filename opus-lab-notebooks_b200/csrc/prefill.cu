@@ -15,18 +15,19 @@
 //       moves a tile;
 //   prefill_fwd_kernel    one CTA per (pair of 128-query tiles, query head),
 //       heaviest causal pairs first, warp-specialised:
-//         warps 0-3 / 4-7  softmax of query tile 0 / 1: a thread owns one
-//                          query row (= TMEM lane) and reads its 128 scores
-//                          from TMEM, so row maxima and sums need no
-//                          exchange; P (bf16) goes back into the score
-//                          columns of TMEM;
-//         warp 8           one thread issues every tcgen05.mma:
+//         warps 0-7 / 8-15 softmax of query tile 0 / 1, two warpgroups per
+//                          tile: a thread owns one query row (= TMEM lane)
+//                          and one half (64) of its scores; the halves
+//                          exchange row maxima at a named barrier and row
+//                          sums once at the end; P (bf16) goes back into
+//                          each half's own score columns of TMEM;
+//         warp 16          one thread issues every tcgen05.mma:
 //                            S_t = Q_t K_j^T   (smem x smem -> TMEM cols S_t)
 //                            O_t += P_t V_j    (TMEM x smem -> TMEM cols O_t)
 //                          in the order S0(j) S1(j) PV0(j) S0(j+1) PV1(j)
 //                          S1(j+1) ..., so the tensor core runs one tile's
 //                          products while the other tile's softmax runs;
-//         warp 9           one thread streams K_j and V^T_j (two stages,
+//         warp 17          one thread streams K_j and V^T_j (two stages,
 //                          one 32 KB bulk copy each).
 //       The two softmax warpgroups take turns for their exp2 pass (an
 //       mbarrier token), so one tile's exponentials run beside the other
