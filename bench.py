@@ -335,33 +335,36 @@ def load_traffic(shape):
 
 
 def run_e2e(args, shape, w, summ, runner):
-    """Through the public santa_decode API with host buffers: per step copy
-    the queries host->device from pinned memory, decode, read the output back."""
+    """Through the public decode API with host buffers, the way a serving
+    loop calls it: a DecodeStep bound once to the cache and summary (what
+    the model-level engine uses), then per step the queries copied
+    host->device from pinned memory, santa_decode_plan + santa_decode_execute
+    (C ABI) and the output read back into pinned memory, synchronised."""
     from santapp_b200.attention import santapp as S
     steps = args.steps
     q_host = w.queries[:steps].cpu().pin_memory()
     out_host = torch.empty(shape.batch, shape.num_query_heads, shape.head_dim).pin_memory()
     q_dev = torch.empty_like(w.queries[0])
-    ws = S.DecodeWorkspace()
-    kw = dict(mode=args.mode, n_total=shape.context, topk_clusters=shape.topk_clusters,
-              samples=shape.samples, seed=args.seed, workspace=ws)
+    step_api = S.DecodeStep(w.keys, w.values, summ, num_query_heads=shape.num_query_heads,
+                            mode=args.mode, n_total=shape.context,
+                            topk_clusters=shape.topk_clusters, samples=shape.samples,
+                            seed=args.seed)
     for i in range(2):
         q_dev.copy_(q_host[i], non_blocking=True)
-        r = S.santa_decode(q_dev, w.keys, w.values, summ, step=i, **kw)
-        out_host.copy_(r.out, non_blocking=True)
+        out_host.copy_(step_api(q_dev, step=i), non_blocking=True)
         torch.cuda.current_stream().synchronize()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for i in range(steps):
         q_dev.copy_(q_host[i], non_blocking=True)
-        r = S.santa_decode(q_dev, w.keys, w.values, summ, step=i, **kw)
-        out_host.copy_(r.out, non_blocking=True)
+        out_host.copy_(step_api(q_dev, step=i), non_blocking=True)
         torch.cuda.current_stream().synchronize()
     dt = time.perf_counter() - t0
     return {"value": shape.batch * steps / dt, "unit": "tokens/s",
             "h2d_bytes_per_step": int(q_host[0].numel() * 4),
             "d2h_bytes_per_step": int(out_host.numel() * 4),
-            "api": "santapp_b200.attention.santa_decode (ctypes -> santa_decode C ABI)"}
+            "api": "santapp_b200.attention.DecodeStep (ctypes -> santa_decode_plan / "
+                   "santa_decode_execute C ABI)"}
 
 
 def _oracle_inputs(shape, w, summ, pairs):

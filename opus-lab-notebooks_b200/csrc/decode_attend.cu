@@ -171,6 +171,10 @@ constexpr int kGStages = 3;   // cp.async ring depth per warp
 constexpr int kGThreads = 32 * kGW;
 constexpr int kCostRow = 2;     // balancing cost of a union or recent-window row
 constexpr int kCostSample = 3;  // balancing cost of a sampled (scattered) row
+// balancing cost of starting a segment (ring drain, CTA fold, pipeline refill:
+// ~2 us, about 128 streamed rows); charged before the segment's first row, so
+// the CTA whose share covers a segment boundary takes fewer rows
+constexpr int kCostSegment = 256;
 
 template <int D>
 struct GatherGeom {
@@ -189,29 +193,68 @@ inline size_t gather_smem_bytes(int BH) {
     return 128 + (size_t)kGW * GatherGeom<D>::WARP + ((size_t)BH + 1) * 4;
 }
 
+// One merged output element (head hh, dim dd) of segment bh: out / lse / ess,
+// or the unnormalised partial for a sequence shard (ns: the head's sample
+// count, used where dd == 0).
+template <int D>
+__device__ __forceinline__ void write_merged(const DecodeArgs &a, int bh, int hh, int dd, float acc,
+                                             float M, float L, float MS, float E1, float E2,
+                                             int ns) {
+    const int g = a.geo.group, PSTR = partial_stride(D);
+    const int b = bh / a.geo.num_kv_heads, kv = bh - b * a.geo.num_kv_heads;
+    const int64_t oh = (int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g + hh;
+    if (a.part_out) {  // sequence shard: the unnormalised partial
+        const int nr = a.p2p.peers ? a.p2p.n : 1;
+        for (int r = 0; r < nr; ++r) {  // every rank's buffer, or part_out
+            float *po = (a.p2p.peers ? p2p_part_slot(a.p2p, a.p2p.peers[r], a.p2p.rank)
+                                     : a.part_out) + oh * PSTR;
+            po[8 + dd] = acc;
+            if (dd == 0) {
+                po[0] = M;
+                po[1] = L;
+                po[2] = MS;
+                po[3] = E1;
+                po[4] = E2;
+                po[5] = (float)ns;
+                po[6] = 0.f;
+                po[7] = 0.f;
+            }
+        }
+        return;
+    }
+    a.out[oh * D + dd] = L > 0.f ? acc / L : 0.f;
+    if (dd == 0) {
+        if (a.lse) a.lse[oh] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
+        if (a.ess) a.ess[oh] = (ns > 0 && E2 > 0.f) ? (E1 * E1 / E2) / (float)ns : 0.f;
+    }
+}
+
 // LSE merge of `count` partials (header m, l, ms, e1, e2 at [0, 5), values
 // at [8, 8 + D) per head, heads PSTR floats apart) that lie `wstride` floats
 // apart from `src`, into out / lse / ess of segment bh.  The whole CTA
 // (kGThreads threads) calls it.  Up to 32 partials at a time are staged into
-// `stage` with one batch of 16-byte cp.async; lane s of every warp computes
-// partial s's factor for the warp's head and the FMA pass broadcasts it by
-// shuffle (a warp's 32 output elements belong to one head), so no block
-// barrier separates the factors from the sums.
+// `stage` with one batch of 16-byte cp.async; one thread per head then
+// computes that head's factors for the batch (a short sequential loop, no
+// warp reductions on the critical path) into shared memory, and after one
+// barrier every thread runs the FMA pass over its output elements.
 template <int D>
 __device__ void merge_staged_to_output(const DecodeArgs &a, int bh, const float *src, int count,
                                        int wstride, float *stage, int stage_floats) {
     constexpr int NT = kGThreads;
     constexpr int OPT = (SANTA_MAX_GROUP * D + NT - 1) / NT;
-    static_assert(D % 32 == 0, "a warp's output elements must share one head");
+    __shared__ float s_f[SANTA_MAX_GROUP][32], s_r[SANTA_MAX_GROUP];
+    __shared__ float s_M[SANTA_MAX_GROUP], s_L[SANTA_MAX_GROUP], s_MS[SANTA_MAX_GROUP];
+    __shared__ float s_E1[SANTA_MAX_GROUP], s_E2[SANTA_MAX_GROUP];
     const int g = a.geo.group, PSTR = partial_stride(D);
-    const int tid = threadIdx.x, lane = tid & 31;
+    const int tid = threadIdx.x;
     const int cap = min(32, stage_floats / wstride);
-    float M[OPT], L[OPT], acc[OPT], MS[OPT], E1[OPT], E2[OPT];
+    float acc[OPT];
 #pragma unroll
-    for (int k = 0; k < OPT; ++k) {
-        M[k] = -INFINITY;
-        MS[k] = -INFINITY;
-        L[k] = acc[k] = E1[k] = E2[k] = 0.f;
+    for (int k = 0; k < OPT; ++k) acc[k] = 0.f;
+    if (tid < g) {
+        s_M[tid] = -INFINITY;
+        s_MS[tid] = -INFINITY;
+        s_L[tid] = s_E1[tid] = s_E2[tid] = 0.f;
     }
     for (int s0 = 0; s0 < count; s0 += cap) {
         const int n = min(cap, count - s0);
@@ -221,74 +264,141 @@ __device__ void merge_staged_to_output(const DecodeArgs &a, int bh, const float 
         asm volatile("cp.async.commit_group;\n" ::: "memory");
         asm volatile("cp.async.wait_group 0;\n" ::: "memory");
         __syncthreads();
-        float f[OPT];
-        int col[OPT];
+        if (tid < g) {  // this batch's factors of head tid
+            const int hh = tid;
+            float Mn = s_M[hh], MSn = s_MS[hh];
+            for (int s = 0; s < n; ++s) {
+                const float *hs = stage + s * wstride + hh * PSTR;
+                if (hs[1] > 0.f) Mn = fmaxf(Mn, hs[0]);
+                if (hs[3] > 0.f) MSn = fmaxf(MSn, hs[2]);
+            }
+            const float r = s_M[hh] == -INFINITY ? 0.f : exp2f(s_M[hh] - Mn);
+            const float re = s_MS[hh] == -INFINITY ? 0.f : exp2f(s_MS[hh] - MSn);
+            float L = s_L[hh] * r, E1 = s_E1[hh] * re, E2 = s_E2[hh] * re * re;
+            for (int s = 0; s < n; ++s) {
+                const float *hs = stage + s * wstride + hh * PSTR;
+                const float f = hs[1] > 0.f ? exp2f(hs[0] - Mn) : 0.f;
+                s_f[hh][s] = f;
+                L = fmaf(hs[1], f, L);
+                if (hs[3] > 0.f) {
+                    const float fe = exp2f(hs[2] - MSn);
+                    E1 = fmaf(hs[3], fe, E1);
+                    E2 = fmaf(hs[4], fe * fe, E2);
+                }
+            }
+            s_r[hh] = r;
+            s_M[hh] = Mn;
+            s_MS[hh] = MSn;
+            s_L[hh] = L;
+            s_E1[hh] = E1;
+            s_E2[hh] = E2;
+        }
+        __syncthreads();
 #pragma unroll
         for (int k = 0; k < OPT; ++k) {
-            const int i = min(tid + k * NT, g * D - 1);
-            const int hh = i / D;  // warp-uniform
-            col[k] = hh * PSTR + 8 + (i - hh * D);
-            const float *hs = stage + min(lane, n - 1) * wstride + hh * PSTR;
-            const bool have = lane < n;
-            const float m = have ? hs[0] : -INFINITY, l = have ? hs[1] : 0.f;
-            const float ms = have ? hs[2] : -INFINITY, e1 = have ? hs[3] : 0.f;
-            const float e2 = have ? hs[4] : 0.f;
-            const float Mn = fmaxf(M[k], warp_max(l > 0.f ? m : -INFINITY));
-            f[k] = l > 0.f ? exp2f(m - Mn) : 0.f;
-            const float r = M[k] == -INFINITY ? 0.f : exp2f(M[k] - Mn);
-            acc[k] *= r;
-            L[k] = L[k] * r + warp_sum(l * f[k]);
-            M[k] = Mn;
-            const float MSn = fmaxf(MS[k], warp_max(e1 > 0.f ? ms : -INFINITY));
-            const float fe = e1 > 0.f ? exp2f(ms - MSn) : 0.f;
-            const float re = MS[k] == -INFINITY ? 0.f : exp2f(MS[k] - MSn);
-            E1[k] = E1[k] * re + warp_sum(e1 * fe);
-            E2[k] = E2[k] * re * re + warp_sum(e2 * fe * fe);
-            MS[k] = MSn;
+            const int i = tid + k * NT;
+            if (i < g * D) {
+                const int hh = i / D, col = hh * PSTR + 8 + (i - hh * D);
+                float v = acc[k] * s_r[hh];
+                for (int s = 0; s < n; ++s) v = fmaf(s_f[hh][s], stage[s * wstride + col], v);
+                acc[k] = v;
+            }
         }
-        for (int s = 0; s < n; ++s) {
-            const float *ps = stage + s * wstride;
-#pragma unroll
-            for (int k = 0; k < OPT; ++k)
-                acc[k] = fmaf(__shfl_sync(0xffffffffu, f[k], s), ps[col[k]], acc[k]);
-        }
-        __syncthreads();  // the next chunk overwrites the stage
+        __syncthreads();  // the next batch overwrites the stage and the factors
     }
-    const int b = bh / a.geo.num_kv_heads, kv = bh - b * a.geo.num_kv_heads;
+    float M[OPT], L[OPT], MS[OPT], E1[OPT], E2[OPT];
+#pragma unroll
+    for (int k = 0; k < OPT; ++k) {
+        const int hh = min(tid + k * NT, g * D - 1) / D;
+        M[k] = s_M[hh];
+        L[k] = s_L[hh];
+        MS[k] = s_MS[hh];
+        E1[k] = s_E1[hh];
+        E2[k] = s_E2[hh];
+    }
 #pragma unroll
     for (int k = 0; k < OPT; ++k) {
         const int i = tid + k * NT;
         if (i < g * D) {
-            const int hh = i / D, dd = i - hh * D;
-            const int64_t oh = (int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g + hh;
-            if (a.part_out) {  // sequence shard: the unnormalised partial
-                const int nr = a.p2p.peers ? a.p2p.n : 1;
-                for (int r = 0; r < nr; ++r) {  // every rank's buffer, or part_out
-                    float *po = (a.p2p.peers ? p2p_part_slot(a.p2p, a.p2p.peers[r], a.p2p.rank)
-                                             : a.part_out) + oh * PSTR;
-                    po[8 + dd] = acc[k];
-                    if (dd == 0) {
-                        po[0] = M[k];
-                        po[1] = L[k];
-                        po[2] = MS[k];
-                        po[3] = E1[k];
-                        po[4] = E2[k];
-                        po[5] = (float)a.ws.head_meta[((int64_t)bh * 8 + hh) * 2 + 1];
-                        po[6] = 0.f;
-                        po[7] = 0.f;
-                    }
-                }
-                continue;
-            }
-            a.out[oh * D + dd] = L[k] > 0.f ? acc[k] / L[k] : 0.f;
-            if (dd == 0) {
-                if (a.lse) a.lse[oh] = L[k] > 0.f ? (M[k] + log2f(L[k])) * kLn2 : -INFINITY;
-                if (a.ess) {
-                    const int ns = a.ws.head_meta[((int64_t)bh * 8 + hh) * 2 + 1];
-                    a.ess[oh] = (ns > 0 && E2[k] > 0.f) ? (E1[k] * E1[k] / E2[k]) / (float)ns : 0.f;
-                }
+            const int hh = i / D;
+            write_merged<D>(a, bh, hh, i - hh * D, acc[k], M[k], L[k], MS[k], E1[k], E2[k],
+                            i - hh * D == 0 ? a.ws.head_meta[((int64_t)bh * 8 + hh) * 2 + 1] : 0);
+        }
+    }
+}
+
+// All the segments a CTA completes, merged together: their partials staged
+// in one cp.async batch (segment i's `count[i]` partials from `first[i]`),
+// the factors of every (segment, head) computed in parallel (one thread
+// each, with the head's sample count), one FMA pass over every output
+// element.  The caller checks that every count is at most 32, that there are
+// at most kMergeSegs segments and that all partials fit the stage.
+constexpr int kMergeSegs = 4;
+template <int D>
+__device__ void merge_segments_to_output(const DecodeArgs &a, const int *seg, const int *first,
+                                         const int *count, int nseg, int wstride, float *stage) {
+    constexpr int NT = kGThreads;
+    __shared__ float s_f[kMergeSegs][SANTA_MAX_GROUP][32];
+    __shared__ float s_hdr[kMergeSegs][SANTA_MAX_GROUP][6];  // M L MS E1 E2 n_samples
+    __shared__ int s_off[kMergeSegs + 1];
+    const int g = a.geo.group, PSTR = partial_stride(D);
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        int o = 0;
+        for (int i = 0; i < nseg; ++i) {
+            s_off[i] = o;
+            o += count[i];
+        }
+        s_off[nseg] = o;
+    }
+    // stage every segment's partials (stage slot s_off[i] + j = partial j of segment i)
+    int off = 0;
+    for (int i = 0; i < nseg; ++i) {
+        const float *src = a.ws.partial + ((int64_t)first[i] + seg[i]) * wstride;
+        const int n16 = count[i] * wstride / 4;
+        for (int c = tid; c < n16; c += NT) cp_async16(stage + off * wstride + 4 * c, src + 4 * c);
+        off += count[i];
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    __syncthreads();
+    if (tid < nseg * g) {
+        const int si = tid / g, hh = tid - si * g, n = count[si];
+        const float *sb = stage + s_off[si] * wstride + hh * PSTR;
+        float Mn = -INFINITY, MSn = -INFINITY;
+        for (int s = 0; s < n; ++s) {
+            const float *hs = sb + s * wstride;
+            if (hs[1] > 0.f) Mn = fmaxf(Mn, hs[0]);
+            if (hs[3] > 0.f) MSn = fmaxf(MSn, hs[2]);
+        }
+        float L = 0.f, E1 = 0.f, E2 = 0.f;
+        for (int s = 0; s < n; ++s) {
+            const float *hs = sb + s * wstride;
+            const float f = hs[1] > 0.f ? exp2f(hs[0] - Mn) : 0.f;
+            s_f[si][hh][s] = f;
+            L = fmaf(hs[1], f, L);
+            if (hs[3] > 0.f) {
+                const float fe = exp2f(hs[2] - MSn);
+                E1 = fmaf(hs[3], fe, E1);
+                E2 = fmaf(hs[4], fe * fe, E2);
             }
         }
+        float *hd = s_hdr[si][hh];
+        hd[0] = Mn;
+        hd[1] = L;
+        hd[2] = MSn;
+        hd[3] = E1;
+        hd[4] = E2;
+        hd[5] = (float)a.ws.head_meta[((int64_t)seg[si] * 8 + hh) * 2 + 1];
+    }
+    __syncthreads();
+    for (int i = tid; i < nseg * g * D; i += NT) {
+        const int si = i / (g * D), r = i - si * g * D, hh = r / D, dd = r - hh * D;
+        const float *sb = stage + s_off[si] * wstride + hh * PSTR + 8 + dd;
+        float acc = 0.f;
+        for (int s = 0; s < count[si]; ++s) acc = fmaf(s_f[si][hh][s], sb[s * wstride], acc);
+        const float *hd = s_hdr[si][hh];
+        write_merged<D>(a, seg[si], hh, dd, acc, hd[0], hd[1], hd[2], hd[3], hd[4], (int)hd[5]);
     }
 }
 
@@ -343,8 +453,10 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
             // segment cost: kCostRow per union / recent row, kCostSample per
             // sampled row (scattered rows stream ~1.5x slower than contiguous
             // cluster rows)
-            int x = i < BH ? kCostRow * a.ws.meta[(int64_t)i * 8 + 4] +
-                                 (kCostSample - kCostRow) * a.ws.meta[(int64_t)i * 8 + 3]
+            const int rows = i < BH ? a.ws.meta[(int64_t)i * 8 + 4] : 0;
+            int x = i < BH ? kCostRow * rows +
+                                 (kCostSample - kCostRow) * a.ws.meta[(int64_t)i * 8 + 3] +
+                                 (rows > 0 ? kCostSegment : 0)
                            : 0;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
@@ -359,9 +471,10 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
     __syncthreads();  // the only block-wide barrier
 
     // every CTA takes an equal share [r0, r1) of the total cost; within a
-    // segment, row v starts at cost kCostRow * v (union and recent rows) or
-    // kCostRow * (U + R) + kCostSample * (v - U - R) (sampled rows), and
-    // belongs to the CTA whose share holds that start
+    // segment (after its kCostSegment start charge), row v starts at cost
+    // kCostRow * v (union and recent rows) or kCostRow * (U + R) +
+    // kCostSample * (v - U - R) (sampled rows), and belongs to the CTA whose
+    // share holds that start
     const int T_all = pre[BH];
     const int P = max(1, ceil_div(T_all, (int)gridDim.x));
     const int r0 = min(T_all, (int)blockIdx.x * P);
@@ -386,7 +499,8 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
         if (c0 >= c1) continue;
         const int32_t *meta = a.ws.meta + (int64_t)bh * 8;
         const int U = meta[1], R = meta[2];
-        const int s0 = row_at_cost(c0, U + R), s1 = row_at_cost(c1, U + R);
+        const int s0 = row_at_cost(max(0, c0 - kCostSegment), U + R);
+        const int s1 = row_at_cost(max(0, c1 - kCostSegment), U + R);
         const int nt = ceil_div(s1 - s0, kGRows);
         const int j0 = ((warp - k_base) % kGW + kGW) % kGW;  // my first tile in the segment
         const int n_my = nt > j0 ? ceil_div(nt - j0, kGW) : 0;
@@ -710,15 +824,42 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
             if (lane == 0) s_lastmask = m;
         }
         __syncthreads();
-        for (unsigned m = s_lastmask; m; m &= m - 1) {
-            const int bh = b0 + __ffs(m) - 1;
-            const int seg0 = pre[bh], total = pre[bh + 1] - seg0;
-            const int first = seg0 / P, last = (seg0 + total - 1) / P;
-            __threadfence();
-            if (tid == 0) a.ws.counters[bh] = 0;  // every CTA of the segment has arrived
-            merge_staged_to_output<D>(a, bh, a.ws.partial + ((int64_t)first + bh) * wstride,
-                                      last - first + 1, wstride, (float *)base,
-                                      kGW * GG::WARP / 4);
+        if (s_lastmask) {
+            // the segments this CTA completed, listed in shared memory
+            __shared__ int m_seg[kMergeSegs], m_first[kMergeSegs], m_cnt[kMergeSegs];
+            __shared__ int m_n, m_fast;
+            __threadfence();  // the completed segments' partials are visible
+            if (tid == 0) {
+                int nseg = 0, tot = 0;
+                bool fast = __popc(s_lastmask) <= kMergeSegs;
+                for (unsigned m = s_lastmask; m; m &= m - 1) {
+                    const int bh = b0 + __ffs(m) - 1;
+                    a.ws.counters[bh] = 0;  // every CTA of the segment has arrived
+                    if (!fast) continue;
+                    const int seg0 = pre[bh], total = pre[bh + 1] - seg0;
+                    m_seg[nseg] = bh;
+                    m_first[nseg] = seg0 / P;
+                    m_cnt[nseg] = (seg0 + total - 1) / P - seg0 / P + 1;
+                    fast = m_cnt[nseg] <= 32;
+                    tot += m_cnt[nseg++];
+                }
+                m_n = nseg;
+                m_fast = fast && (int64_t)tot * wstride <= (int64_t)kGW * GG::WARP / 4;
+            }
+            __syncthreads();
+            if (m_fast) {
+                merge_segments_to_output<D>(a, m_seg, m_first, m_cnt, m_n, wstride, (float *)base);
+            } else {
+                for (unsigned m = s_lastmask; m; m &= m - 1) {
+                    const int bh = b0 + __ffs(m) - 1;
+                    const int seg0 = pre[bh], total = pre[bh + 1] - seg0;
+                    const int f0 = seg0 / P, last = (seg0 + total - 1) / P;
+                    merge_staged_to_output<D>(a, bh, a.ws.partial + ((int64_t)f0 + bh) * wstride,
+                                              last - f0 + 1, wstride, (float *)base,
+                                              kGW * GG::WARP / 4);
+                    __syncthreads();  // the stage is reused by the next segment
+                }
+            }
         }
         __syncthreads();  // s_lastmask is rewritten by the next batch
     }
