@@ -199,7 +199,7 @@ inline size_t gather_smem_bytes(int BH) {
 template <int D>
 __device__ __forceinline__ void write_merged(const DecodeArgs &a, int bh, int hh, int dd, float acc,
                                              float M, float L, float MS, float E1, float E2,
-                                             int ns) {
+                                             int ns, float inv_l) {
     const int g = a.geo.group, PSTR = partial_stride(D);
     const int b = bh / a.geo.num_kv_heads, kv = bh - b * a.geo.num_kv_heads;
     const int64_t oh = (int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g + hh;
@@ -222,7 +222,7 @@ __device__ __forceinline__ void write_merged(const DecodeArgs &a, int bh, int hh
         }
         return;
     }
-    a.out[oh * D + dd] = L > 0.f ? acc / L : 0.f;
+    a.out[oh * D + dd] = acc * inv_l;
     if (dd == 0) {
         if (a.lse) a.lse[oh] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
         if (a.ess) a.ess[oh] = (ns > 0 && E2 > 0.f) ? (E1 * E1 / E2) / (float)ns : 0.f;
@@ -322,7 +322,8 @@ __device__ void merge_staged_to_output(const DecodeArgs &a, int bh, const float 
         if (i < g * D) {
             const int hh = i / D;
             write_merged<D>(a, bh, hh, i - hh * D, acc[k], M[k], L[k], MS[k], E1[k], E2[k],
-                            i - hh * D == 0 ? a.ws.head_meta[((int64_t)bh * 8 + hh) * 2 + 1] : 0);
+                            i - hh * D == 0 ? a.ws.head_meta[((int64_t)bh * 8 + hh) * 2 + 1] : 0,
+                            L[k] > 0.f ? 1.f / L[k] : 0.f);
         }
     }
 }
@@ -339,7 +340,7 @@ __device__ void merge_segments_to_output(const DecodeArgs &a, const int *seg, co
                                          const int *count, int nseg, int wstride, float *stage) {
     constexpr int NT = kGThreads;
     __shared__ float s_f[kMergeSegs][SANTA_MAX_GROUP][32];
-    __shared__ float s_hdr[kMergeSegs][SANTA_MAX_GROUP][6];  // M L MS E1 E2 n_samples
+    __shared__ float s_hdr[kMergeSegs][SANTA_MAX_GROUP][7];  // M L MS E1 E2 n_samples 1/L
     __shared__ int s_off[kMergeSegs + 1];
     const int g = a.geo.group, PSTR = partial_stride(D);
     const int tid = threadIdx.x;
@@ -351,6 +352,10 @@ __device__ void merge_segments_to_output(const DecodeArgs &a, const int *seg, co
         }
         s_off[nseg] = o;
     }
+    // the sample count of my (segment, head), requested before the staging
+    // round trip so the two overlap
+    int my_ns = 0;
+    if (tid < nseg * g) my_ns = a.ws.head_meta[((int64_t)seg[tid / g] * 8 + tid % g) * 2 + 1];
     // stage every segment's partials (stage slot s_off[i] + j = partial j of segment i)
     int off = 0;
     for (int i = 0; i < nseg; ++i) {
@@ -389,7 +394,8 @@ __device__ void merge_segments_to_output(const DecodeArgs &a, const int *seg, co
         hd[2] = MSn;
         hd[3] = E1;
         hd[4] = E2;
-        hd[5] = (float)a.ws.head_meta[((int64_t)seg[si] * 8 + hh) * 2 + 1];
+        hd[5] = (float)my_ns;
+        hd[6] = L > 0.f ? 1.f / L : 0.f;
     }
     __syncthreads();
     for (int i = tid; i < nseg * g * D; i += NT) {
@@ -398,7 +404,8 @@ __device__ void merge_segments_to_output(const DecodeArgs &a, const int *seg, co
         float acc = 0.f;
         for (int s = 0; s < count[si]; ++s) acc = fmaf(s_f[si][hh][s], sb[s * wstride], acc);
         const float *hd = s_hdr[si][hh];
-        write_merged<D>(a, seg[si], hh, dd, acc, hd[0], hd[1], hd[2], hd[3], hd[4], (int)hd[5]);
+        write_merged<D>(a, seg[si], hh, dd, acc, hd[0], hd[1], hd[2], hd[3], hd[4], (int)hd[5],
+                        hd[6]);
     }
 }
 

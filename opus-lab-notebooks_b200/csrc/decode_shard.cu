@@ -55,7 +55,8 @@ __global__ void __launch_bounds__(D) merge_shards_kernel(int rows, int num_shard
         }
         ns += p[5];
     }
-    out[(int64_t)row * D + d] = L > 0.f ? acc / L : 0.f;
+    // times 1/L, as the single-GPU merge does (one shard gives the same bits)
+    out[(int64_t)row * D + d] = acc * (L > 0.f ? 1.f / L : 0.f);
     if (d == 0) {
         if (lse) lse[row] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
         if (ess) ess[row] = (ns > 0.f && E2 > 0.f) ? (E1 * E1 / E2) / ns : 0.f;
