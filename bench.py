@@ -54,6 +54,9 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="skip the host-side extras (byte accounting, e2e, CPU baseline)")
+    ap.add_argument("--prefill-prompt", type=int, default=32768,
+                    help="prompt length of the prefill workload (the reported one is 32768; "
+                         "smaller values are for profiler captures)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="bound on the CPU-baseline sample")
     ap.add_argument("--transport", choices=["nccl", "p2p"], default="nccl",
@@ -423,8 +426,8 @@ def run_prefill(args):
     from santapp_b200.synthetic import scaled_shape
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    B, Hq, Hkv, T, D = 1, 28, 4, 32768, 128
-    shape = scaled_shape(QWEN7B_32K, batch=1, steps=1)
+    B, Hq, Hkv, T, D = 1, 28, 4, args.prefill_prompt, 128
+    shape = scaled_shape(QWEN7B_32K, batch=1, steps=1, context=T)
     w = make_decode_workload(shape, seed=args.seed, device=dev)
     g = torch.Generator(device=dev).manual_seed(args.seed + 1)
     q = torch.randn(B, Hq, T, D, device=dev, generator=g).to(torch.bfloat16)
@@ -465,7 +468,7 @@ def run_prefill(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) queries, Gaussian-mixture keys, N(0,1) values)",
-        "config": {"workload": "qwen2.5-7b-prefill-ctx32768", "query_heads": Hq,
+        "config": {"workload": f"qwen2.5-7b-prefill-ctx{T}", "query_heads": Hq,
                    "kv_heads": Hkv, "head_dim": D, "batch": B, "prompt": T, "causal": True,
                    "kmeans": {"k": 256, "batch_size": 4096, "max_iter": 20, "rows": shape.sample_end,
                               "features": D}},
