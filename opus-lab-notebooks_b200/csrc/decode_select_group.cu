@@ -180,10 +180,9 @@ __device__ __forceinline__ int2 grp_block_scan2(int a, int b, int2 *sw, int2 &to
 // One centroid row (cluster c, slice row i) against NH query heads part ..
 // part + NH - 1 (heads >= g are padding: q rows past the group, no key):
 // one fmaf chain per head in ascending d, the FMAs component-major across
-// the NH chains.  The row comes from shared memory (staged slice) or, with
-// GLOBAL, straight from global memory through L1.  The keys go to
-// keys[head * per + i].
-template <int NH, int D, int QP, bool GLOBAL>
+// the NH chains, the row read from the staged slice in shared memory.  The
+// keys go to keys[head * per + i].
+template <int NH, int D, int QP>
 __device__ __forceinline__ void grp_score_row(const float *row, const float *qs, int part, int g,
                                               float log_n, float scale, int c, int n_groups,
                                               int cbase, uint64_t *keys, int per, int i) {
@@ -192,7 +191,7 @@ __device__ __forceinline__ void grp_score_row(const float *row, const float *qs,
     for (int j = 0; j < NH; ++j) acc[j] = 0.f;
 #pragma unroll 4
     for (int d = 0; d < D; d += 4) {
-        const float4 x = GLOBAL ? __ldg((const float4 *)(row + d)) : *(const float4 *)(row + d);
+        const float4 x = *(const float4 *)(row + d);
         float4 u[NH];
 #pragma unroll
         for (int j = 0; j < NH; ++j) u[j] = *(const float4 *)(qs + (part + j) * QP + d);
@@ -216,11 +215,81 @@ __device__ __forceinline__ void grp_score_row(const float *row, const float *qs,
     }
 }
 
+// Unstaged slice: the warp scores the rows of its 32 lanes (lane row r, heads
+// part .. part + NH - 1), the rows streamed through the warp's 2 KB buffer
+// [32 rows][16 floats] one 16-dim piece at a time.  Each piece is one batch
+// of coalesced cp.async copies (four lanes per row, 8 rows per instruction),
+// 16-byte slot k of row j held at slot k ^ ((j >> 1) & 3), so a quarter
+// warp reading its eight rows hits eight distinct bank groups.  The chains
+// are those of grp_score_row: one fmaf chain per head in ascending d.
+constexpr int kGrpPiece = 16;  // floats of a row per piece
+template <int NH, int D, int QP>
+__device__ __forceinline__ void grp_score_pieces(const float *cent, float *buf, const float *qs,
+                                                 bool active, int r, int part, int g,
+                                                 float log_n, float scale, int c, int n_groups,
+                                                 int cbase, uint64_t *keys, int per) {
+    const int lane = threadIdx.x & 31;
+    // the copies of this lane: rows of lanes 8i + lane / 4, slot lane % 4
+    const float *src[4];
+    int dst[4];
+    bool cp[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int j = 8 * i + (lane >> 2), k = lane & 3;
+        const int rj = __shfl_sync(0xffffffffu, r, j);
+        cp[i] = __shfl_sync(0xffffffffu, active ? 1 : 0, j) != 0;
+        src[i] = cent + (int64_t)rj * D + 4 * k;
+        dst[i] = j * kGrpPiece + 4 * (k ^ ((j >> 1) & 3));
+    }
+    const int swz = (lane >> 1) & 3;
+    float acc[NH];
+#pragma unroll
+    for (int j = 0; j < NH; ++j) acc[j] = 0.f;
+#pragma unroll 1
+    for (int p = 0; p < D; p += kGrpPiece) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            if (cp[i]) cp_async16(buf + dst[i], src[i] + p);
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+        __syncwarp();
+        if (active) {
+#pragma unroll
+            for (int e = 0; e < kGrpPiece / 4; ++e) {
+                const float4 x = *(const float4 *)(buf + lane * kGrpPiece + 4 * (e ^ swz));
+                const int d = p + 4 * e;
+                float4 u[NH];
+#pragma unroll
+                for (int j = 0; j < NH; ++j) u[j] = *(const float4 *)(qs + (part + j) * QP + d);
+#pragma unroll
+                for (int j = 0; j < NH; ++j) acc[j] = fmaf(x.x, u[j].x, acc[j]);
+#pragma unroll
+                for (int j = 0; j < NH; ++j) acc[j] = fmaf(x.y, u[j].y, acc[j]);
+#pragma unroll
+                for (int j = 0; j < NH; ++j) acc[j] = fmaf(x.z, u[j].z, acc[j]);
+#pragma unroll
+                for (int j = 0; j < NH; ++j) acc[j] = fmaf(x.w, u[j].w, acc[j]);
+            }
+        }
+        __syncwarp();  // the buffer is refilled by the next piece
+    }
+    if (!active) return;
+    const uint64_t low = (uint64_t)(0xFFFFFFFFu - (uint32_t)(c + cbase));
+#pragma unroll
+    for (int j = 0; j < NH; ++j) {
+        if (part + j < g) {
+            const float gs = __fadd_rn(log_n, __fmul_rn(acc[j], scale));
+            keys[(part + j) * per + r] =
+                c < n_groups ? (((uint64_t)float_order_key(gs) << 32) | low) : 0ull;
+        }
+    }
+}
+
 // Dynamic shared memory of one CTA: keys [g][per] u64, starts / lengths /
 // union masks / log n [Gmax] 32-bit, then the CTA's slice of per =
 // ceil(Gmax / g) centroid rows ([per][D + 4] fp32) when it fits the budget
 // (four CTAs per SM); a larger slice is read from global memory instead,
-// after one bulk prefetch of it into L2.
+// after one bulk prefetch of it into L2, through a 2 KB piece buffer per warp.
 constexpr int kGrpDynBudget = 43 * 1024;
 struct GrpLayout {
     int per;
@@ -235,7 +304,7 @@ __host__ __device__ inline GrpLayout grp_layout(int Gmax, int g, int D) {
     L.stage = L.meta + ((size_t)4 * Gmax * 4 + 15) / 16 * 16;
     const size_t slice = (size_t)L.per * (D + kGrpQPitch) * 4;
     L.staged = L.stage + slice <= (size_t)kGrpDynBudget;
-    L.bytes = L.staged ? L.stage + slice : L.stage;
+    L.bytes = L.stage + (L.staged ? slice : (size_t)kGrpWarps * 32 * kGrpPiece * 4);
     return L;
 }
 
@@ -269,7 +338,7 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
     int *len_s = starts_s + Gmax;
     int *mask_s = len_s + Gmax;
     float *logn_s = (float *)(mask_s + Gmax);
-    float *stage = (float *)(grp_dyn + L.stage);       // [nst][rows][QP]
+    float *stage = (float *)(grp_dyn + L.stage);       // staged: [rows][QP]; else [warps][32][kGrpPiece]
     const int c0 = rank * per;
     const int nrows = max(0, min(per, Gmax - c0));
     const int S = a.p.samples;
@@ -310,34 +379,47 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
     __syncthreads();
 
     // ---- 1. guesses of this CTA's centroid rows for every head -------------
-    // thread t takes row t % nrows and head set t / nrows: all heads when
+    // work item t takes row t % nrows and head set t / nrows: all heads when
     // g <= 4, else two sets of 4 (the second padded to 4), so the chain count
-    // per thread is uniform and warps are full
+    // per item is uniform and warps are full
     {
         const int nsets = g <= 4 ? 1 : 2;
         const int nh = g <= 4 ? g : 4;
-        for (int t = tid; t < nrows * nsets; t += kGrpThreads) {
-            const int set = t / nrows, r = t - set * nrows;
-            const int c = c0 + r;
-#define GRP_SCORE(N, G)                                                                       \
-    grp_score_row<N, D, QP, G>(G ? cent + (int64_t)r * D : stage + r * QP, qs, set * 4, g,     \
-                               logn_s[c], a.p.scale, c, n_groups, cbase, keys_s, per, r)
-            if (L.staged) {
+        const int total = nrows * nsets;
+        if (L.staged) {
+            for (int t = tid; t < total; t += kGrpThreads) {
+                const int set = t / nrows, r = t - set * nrows;
+                const int c = c0 + r;
+#define GRP_SCORE(N)                                                                           \
+    grp_score_row<N, D, QP>(stage + r * QP, qs, set * 4, g, logn_s[c], a.p.scale, c, n_groups, \
+                            cbase, keys_s, per, r)
                 switch (nh) {
-                    case 1: GRP_SCORE(1, false); break;
-                    case 2: GRP_SCORE(2, false); break;
-                    case 3: GRP_SCORE(3, false); break;
-                    default: GRP_SCORE(4, false); break;
+                    case 1: GRP_SCORE(1); break;
+                    case 2: GRP_SCORE(2); break;
+                    case 3: GRP_SCORE(3); break;
+                    default: GRP_SCORE(4); break;
                 }
-            } else {
-                switch (nh) {
-                    case 1: GRP_SCORE(1, true); break;
-                    case 2: GRP_SCORE(2, true); break;
-                    case 3: GRP_SCORE(3, true); break;
-                    default: GRP_SCORE(4, true); break;
-                }
-            }
 #undef GRP_SCORE
+            }
+        } else {
+            float *buf = stage + warp * 32 * kGrpPiece;
+            for (int t0 = warp * 32; t0 < total; t0 += kGrpThreads) {  // warp-uniform
+                const int t = t0 + lane;
+                const bool active = t < total;
+                const int set = active ? t / nrows : 0, r = active ? t - set * nrows : 0;
+                const int c = c0 + r;
+                const float log_n = active ? logn_s[c] : 0.f;
+#define GRP_SCORE(N)                                                                           \
+    grp_score_pieces<N, D, QP>(cent, buf, qs, active, r, set * 4, g, log_n, a.p.scale, c,       \
+                               n_groups, cbase, keys_s, per)
+                switch (nh) {
+                    case 1: GRP_SCORE(1); break;
+                    case 2: GRP_SCORE(2); break;
+                    case 3: GRP_SCORE(3); break;
+                    default: GRP_SCORE(4); break;
+                }
+#undef GRP_SCORE
+            }
         }
     }
     cl_sync();  // every CTA's keys are in place (and its metadata landed)
