@@ -201,8 +201,7 @@ __device__ __forceinline__ void write_merged(const DecodeArgs &a, int bh, int hh
                                              float M, float L, float MS, float E1, float E2,
                                              int ns, float inv_l) {
     const int g = a.geo.group, PSTR = partial_stride(D);
-    const int b = bh / a.geo.num_kv_heads, kv = bh - b * a.geo.num_kv_heads;
-    const int64_t oh = (int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g + hh;
+    const int64_t oh = (int64_t)bh * g + hh;  // (b * Hkv + kv) * g + hh
     if (a.part_out) {  // sequence shard: the unnormalised partial
         const int nr = a.p2p.peers ? a.p2p.n : 1;
         for (int r = 0; r < nr; ++r) {  // every rank's buffer, or part_out
@@ -329,83 +328,207 @@ __device__ void merge_staged_to_output(const DecodeArgs &a, int bh, const float 
 }
 
 // All the segments a CTA completes, merged together: their partials staged
-// in one cp.async batch (segment i's `count[i]` partials from `first[i]`),
-// the factors of every (segment, head) computed in parallel (one thread
-// each, with the head's sample count), one FMA pass over every output
-// element.  The caller checks that every count is at most 32, that there are
+// in one cp.async batch (segment i's `count[i]` partials from `first[i]`);
+// the factors of each (segment, head) computed by one warp, a lane per
+// partial (maxima and sums by shuffles); then every thread forms its output
+// elements' sums (factor-weighted, ascending partial order) before any of its
+// stores.  The caller checks that every count is at most 32, that there are
 // at most kMergeSegs segments and that all partials fit the stage.
 constexpr int kMergeSegs = 4;
 template <int D>
 __device__ void merge_segments_to_output(const DecodeArgs &a, const int *seg, const int *first,
                                          const int *count, int nseg, int wstride, float *stage) {
     constexpr int NT = kGThreads;
+    constexpr int IPT = (SANTA_MAX_GROUP * D + NT - 1) / NT;  // output elements per thread
     __shared__ float s_f[kMergeSegs][SANTA_MAX_GROUP][32];
-    __shared__ float s_hdr[kMergeSegs][SANTA_MAX_GROUP][7];  // M L MS E1 E2 n_samples 1/L
-    __shared__ int s_off[kMergeSegs + 1];
+    __shared__ float s_hdr[kMergeSegs][SANTA_MAX_GROUP][8];  // M L MS E1 E2 n_samples 1/L
     const int g = a.geo.group, PSTR = partial_stride(D);
-    const int tid = threadIdx.x;
-    if (tid == 0) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int npairs = nseg * g;
+    auto off_of = [&](int si) {  // stage slot of segment si's first partial
         int o = 0;
-        for (int i = 0; i < nseg; ++i) {
-            s_off[i] = o;
-            o += count[i];
-        }
-        s_off[nseg] = o;
-    }
-    // the sample count of my (segment, head), requested before the staging
-    // round trip so the two overlap
+        for (int i = 0; i < si; ++i) o += count[i];
+        return o;
+    };
+    // the sample counts of this warp's (segment, head) pairs warp + 8k, lane
+    // k requesting pair k's before the staging round trip so the two overlap
     int my_ns = 0;
-    if (tid < nseg * g) my_ns = a.ws.head_meta[((int64_t)seg[tid / g] * 8 + tid % g) * 2 + 1];
-    // stage every segment's partials (stage slot s_off[i] + j = partial j of segment i)
-    int off = 0;
-    for (int i = 0; i < nseg; ++i) {
+    if (lane < 4 && warp + kGW * lane < npairs) {
+        const int p = warp + kGW * lane, si = p / g;
+        my_ns = a.ws.head_meta[((int64_t)seg[si] * 8 + (p - si * g)) * 2 + 1];
+    }
+    // stage every segment's partials (stage slot off[i] + j = partial j of segment i)
+    for (int i = 0, o = 0; i < nseg; o += count[i++]) {
         const float *src = a.ws.partial + ((int64_t)first[i] + seg[i]) * wstride;
         const int n16 = count[i] * wstride / 4;
-        for (int c = tid; c < n16; c += NT) cp_async16(stage + off * wstride + 4 * c, src + 4 * c);
-        off += count[i];
+        for (int c = tid; c < n16; c += NT) cp_async16(stage + o * wstride + 4 * c, src + 4 * c);
     }
     asm volatile("cp.async.commit_group;\n" ::: "memory");
     asm volatile("cp.async.wait_group 0;\n" ::: "memory");
     __syncthreads();
-    if (tid < nseg * g) {
-        const int si = tid / g, hh = tid - si * g, n = count[si];
-        const float *sb = stage + s_off[si] * wstride + hh * PSTR;
-        float Mn = -INFINITY, MSn = -INFINITY;
-        for (int s = 0; s < n; ++s) {
-            const float *hs = sb + s * wstride;
-            if (hs[1] > 0.f) Mn = fmaxf(Mn, hs[0]);
-            if (hs[3] > 0.f) MSn = fmaxf(MSn, hs[2]);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {  // npairs <= kMergeSegs * 8 = 4 * kGW
+        const int p = warp + kGW * k;
+        const int ns = __shfl_sync(0xffffffffu, my_ns, k);
+        if (p >= npairs) break;  // warp-uniform
+        const int si = p / g, hh = p - si * g, n = count[si];
+        float m = -INFINITY, l = 0.f, ms = -INFINITY, e1 = 0.f, e2 = 0.f;
+        if (lane < n) {
+            const float *hs = stage + (off_of(si) + lane) * wstride + hh * PSTR;
+            m = hs[0];
+            l = hs[1];
+            ms = hs[2];
+            e1 = hs[3];
+            e2 = hs[4];
         }
-        float L = 0.f, E1 = 0.f, E2 = 0.f;
-        for (int s = 0; s < n; ++s) {
-            const float *hs = sb + s * wstride;
-            const float f = hs[1] > 0.f ? exp2f(hs[0] - Mn) : 0.f;
-            s_f[si][hh][s] = f;
-            L = fmaf(hs[1], f, L);
-            if (hs[3] > 0.f) {
-                const float fe = exp2f(hs[2] - MSn);
-                E1 = fmaf(hs[3], fe, E1);
-                E2 = fmaf(hs[4], fe * fe, E2);
-            }
+        float M = l > 0.f ? m : -INFINITY, MS = e1 > 0.f ? ms : -INFINITY;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+            MS = fmaxf(MS, __shfl_xor_sync(0xffffffffu, MS, o));
         }
-        float *hd = s_hdr[si][hh];
-        hd[0] = Mn;
-        hd[1] = L;
-        hd[2] = MSn;
-        hd[3] = E1;
-        hd[4] = E2;
-        hd[5] = (float)my_ns;
-        hd[6] = L > 0.f ? 1.f / L : 0.f;
+        const float f = l > 0.f ? exp2f(m - M) : 0.f;
+        const float fe = e1 > 0.f ? exp2f(ms - MS) : 0.f;
+        float L = l * f, E1 = e1 * fe, E2 = e2 * fe * fe;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            L += __shfl_xor_sync(0xffffffffu, L, o);
+            E1 += __shfl_xor_sync(0xffffffffu, E1, o);
+            E2 += __shfl_xor_sync(0xffffffffu, E2, o);
+        }
+        s_f[si][hh][lane] = f;
+        if (lane == 0) {
+            float *hd = s_hdr[si][hh];
+            hd[0] = M;
+            hd[1] = L;
+            hd[2] = MS;
+            hd[3] = E1;
+            hd[4] = E2;
+            hd[5] = (float)ns;
+            hd[6] = L > 0.f ? 1.f / L : 0.f;
+        }
     }
     __syncthreads();
-    for (int i = tid; i < nseg * g * D; i += NT) {
-        const int si = i / (g * D), r = i - si * g * D, hh = r / D, dd = r - hh * D;
-        const float *sb = stage + s_off[si] * wstride + hh * PSTR + 8 + dd;
-        float acc = 0.f;
-        for (int s = 0; s < count[si]; ++s) acc = fmaf(s_f[si][hh][s], sb[s * wstride], acc);
-        const float *hd = s_hdr[si][hh];
-        write_merged<D>(a, seg[si], hh, dd, acc, hd[0], hd[1], hd[2], hd[3], hd[4], (int)hd[5],
-                        hd[6]);
+    for (int si = 0; si < nseg; ++si) {
+        const int n = count[si], bh = seg[si];
+        const float *sb = stage + off_of(si) * wstride + 8;
+        float acc[IPT];
+#pragma unroll
+        for (int k = 0; k < IPT; ++k) {
+            const int j = tid + k * NT;
+            acc[k] = 0.f;
+            if (j < g * D) {
+                const int hh = j / D, dd = j - hh * D;
+                const float *v = sb + hh * PSTR + dd;
+                const float *fs = s_f[si][hh];
+                float x = 0.f;
+                for (int s = 0; s < n; ++s) x = fmaf(fs[s], v[s * wstride], x);
+                acc[k] = x;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < IPT; ++k) {
+            const int j = tid + k * NT;
+            if (j < g * D) {
+                const int hh = j / D;
+                const float *hd = s_hdr[si][hh];
+                write_merged<D>(a, bh, hh, j - hh * D, acc[k], hd[0], hd[1], hd[2], hd[3], hd[4],
+                                (int)hd[5], hd[6]);
+            }
+        }
+    }
+}
+
+// The segments a CTA completes when each has at most kDirectMax partials:
+// one warp per (segment, head), a lane per VPL = D / 32 consecutive dims.
+// Two pairs at a time, every header and value the pair needs is loaded in
+// one batch straight from the partial slots (no staging, no barrier: the
+// whole merge is one L2 round trip), then the factors and sums are formed
+// in ascending partial order as in the staged merges (the maximum over the
+// non-empty partials, f_s = 2^(m_s - M), L = sum f_s l_s, acc = sum f_s v_s).
+constexpr int kDirectMax = 8;
+template <int D>
+__device__ void merge_pairs_direct(const DecodeArgs &a, const int *seg, const int *first,
+                                   const int *count, int nseg, int wstride) {
+    constexpr int VPL = D / 32;
+    const int g = a.geo.group, PSTR = partial_stride(D);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int npairs = nseg * g;
+    for (int p0 = warp; p0 < npairs; p0 += 2 * kGW) {
+        float mv[2][kDirectMax], lv[2][kDirectMax], vv[2][kDirectMax][VPL];
+        float xs[2][kDirectMax][3];  // ms e1 e2 (lane 0)
+        int ns[2], bhs[2], hhs[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int p = p0 + u * kGW;
+            const bool on = p < npairs;
+            const int si = on ? p / g : 0, hh = on ? p - si * g : 0;
+            const int n = on ? count[si] : 0, bh = seg[si];
+            bhs[u] = bh;
+            hhs[u] = hh;
+            ns[u] = (on && lane == 0) ? a.ws.head_meta[((int64_t)bh * 8 + hh) * 2 + 1] : 0;
+            const float *src = a.ws.partial + ((int64_t)first[si] + bh) * wstride + hh * PSTR;
+#pragma unroll
+            for (int s = 0; s < kDirectMax; ++s) {
+                mv[u][s] = -INFINITY;
+                lv[u][s] = 0.f;
+                xs[u][s][0] = -INFINITY;
+                xs[u][s][1] = xs[u][s][2] = 0.f;
+#pragma unroll
+                for (int e = 0; e < VPL; ++e) vv[u][s][e] = 0.f;
+                if (s < n) {
+                    const float *ps = src + (int64_t)s * wstride;
+                    mv[u][s] = ps[0];
+                    lv[u][s] = ps[1];
+                    if constexpr (VPL == 4) {
+                        const float4 x = *(const float4 *)(ps + 8 + 4 * lane);
+                        vv[u][s][0] = x.x;
+                        vv[u][s][1] = x.y;
+                        vv[u][s][2] = x.z;
+                        vv[u][s][3] = x.w;
+                    } else {
+                        const float2 x = *(const float2 *)(ps + 8 + 2 * lane);
+                        vv[u][s][0] = x.x;
+                        vv[u][s][1] = x.y;
+                    }
+                    if (lane == 0) {
+                        xs[u][s][0] = ps[2];
+                        xs[u][s][1] = ps[3];
+                        xs[u][s][2] = ps[4];
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            if (p0 + u * kGW >= npairs) break;  // warp-uniform
+            float M = -INFINITY, MS = -INFINITY;
+#pragma unroll
+            for (int s = 0; s < kDirectMax; ++s) {
+                if (lv[u][s] > 0.f) M = fmaxf(M, mv[u][s]);
+                if (xs[u][s][1] > 0.f) MS = fmaxf(MS, xs[u][s][0]);
+            }
+            float L = 0.f, E1 = 0.f, E2 = 0.f, acc[VPL];
+#pragma unroll
+            for (int e = 0; e < VPL; ++e) acc[e] = 0.f;
+#pragma unroll
+            for (int s = 0; s < kDirectMax; ++s) {
+                const float f = lv[u][s] > 0.f ? exp2f(mv[u][s] - M) : 0.f;
+                L = fmaf(lv[u][s], f, L);
+#pragma unroll
+                for (int e = 0; e < VPL; ++e) acc[e] = fmaf(f, vv[u][s][e], acc[e]);
+                if (xs[u][s][1] > 0.f) {
+                    const float fe = exp2f(xs[u][s][0] - MS);
+                    E1 = fmaf(xs[u][s][1], fe, E1);
+                    E2 = fmaf(xs[u][s][2], fe * fe, E2);
+                }
+            }
+            const float inv_l = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+            for (int e = 0; e < VPL; ++e)
+                write_merged<D>(a, bhs[u], hhs[u], VPL * lane + e, acc[e], M, L, MS, E1, E2, ns[u],
+                                inv_l);
+        }
     }
 }
 
@@ -452,6 +575,12 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
     unsigned char *wbase = base + warp * GG::WARP;     // this warp's ring
     int *pre = (int *)(base + kGW * GG::WARP);         // segment prefix [BH + 1]
     __shared__ float s_wfac[SANTA_MAX_GROUP][kGW];     // CTA fold: factor per head and warp
+    // The merge path reads the arguments from a shared-memory copy: after the
+    // row loops the constant cache no longer holds the fields only it uses
+    // (outputs, counters, partial slots), and each first touch of one costs a
+    // round trip on the tail's critical path.
+    __shared__ __align__(16) DecodeArgs s_args;
+    if (tid == kGThreads - 1) s_args = a;
 
     if (warp == 0) {
         int carry = 0;
@@ -809,10 +938,16 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
 
     // ---- LSE merge.  Every warp reaches this barrier (the loops above have
     // no early exit and no waits that can time out), so the stage rings are
-    // free and every CTA partial of this CTA is written ----
-    __threadfence();
+    // free and every CTA partial of this CTA is written.  The arrivals are
+    // acq_rel atomics at GPU scope, one lane per segment: the release covers
+    // this CTA's partials (ordered before it by the barrier), the acquire of
+    // the last arrival covers every other CTA's, and the barrier after the
+    // arrivals passes that on to the whole CTA ----
     __syncthreads();
+    const DecodeArgs &ma = s_args;
     __shared__ unsigned s_lastmask;
+    __shared__ int m_seg[kMergeSegs], m_first[kMergeSegs], m_cnt[kMergeSegs];
+    __shared__ int m_n, m_mode;  // merge form: 2 direct, 1 staged together, 0 one by one
     const int wstride = g * PSTR;  // floats between partial slots
     // arrivals at up to 32 segments at once (one atomic round trip), then
     // the merges of the segments this CTA completed
@@ -820,78 +955,88 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
         if (warp == 0) {
             const int bh = b0 + lane;
             bool done = false;
+            int first = 0, cnt = 0;
             if (bh < BH && pre[bh] < r1) {
                 const int seg0 = pre[bh], total = pre[bh + 1] - seg0;
                 if (max(r0, seg0) < min(r1, seg0 + total)) {
-                    const int first = seg0 / P, last = (seg0 + total - 1) / P;
-                    done = atomicAdd(&a.ws.counters[bh], 1) == last - first;
+                    first = seg0 / P;
+                    cnt = (seg0 + total - 1) / P - first + 1;
+                    unsigned old;
+                    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;\n"
+                                 : "=r"(old)
+                                 : "l"(ma.ws.counters + bh)
+                                 : "memory");
+                    done = (int)old == cnt - 1;
                 }
             }
             const unsigned m = __ballot_sync(0xffffffffu, done);
-            if (lane == 0) s_lastmask = m;
+            // the completed segments, listed in lane order
+            const int rank = __popc(m & ((1u << lane) - 1u));
+            const bool fit = !done || (rank < kMergeSegs && cnt <= 32);
+            const bool small = !done || (rank < kMergeSegs && cnt <= kDirectMax);
+            int tot = done ? cnt : 0;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+            const bool all_fit = __all_sync(0xffffffffu, fit);
+            const bool all_small = __all_sync(0xffffffffu, small);
+            if (done) {
+                ma.ws.counters[bh] = 0;  // every CTA of the segment has arrived
+                if (rank < kMergeSegs) {
+                    m_seg[rank] = bh;
+                    m_first[rank] = first;
+                    m_cnt[rank] = cnt;
+                }
+            }
+            if (lane == 0) {
+                s_lastmask = m;
+                m_n = __popc(m);
+                m_mode = all_small ? 2
+                         : (all_fit && (int64_t)tot * wstride <= (int64_t)kGW * GG::WARP / 4) ? 1
+                                                                                               : 0;
+            }
         }
         __syncthreads();
         if (s_lastmask) {
-            // the segments this CTA completed, listed in shared memory
-            __shared__ int m_seg[kMergeSegs], m_first[kMergeSegs], m_cnt[kMergeSegs];
-            __shared__ int m_n, m_fast;
-            __threadfence();  // the completed segments' partials are visible
-            if (tid == 0) {
-                int nseg = 0, tot = 0;
-                bool fast = __popc(s_lastmask) <= kMergeSegs;
-                for (unsigned m = s_lastmask; m; m &= m - 1) {
-                    const int bh = b0 + __ffs(m) - 1;
-                    a.ws.counters[bh] = 0;  // every CTA of the segment has arrived
-                    if (!fast) continue;
-                    const int seg0 = pre[bh], total = pre[bh + 1] - seg0;
-                    m_seg[nseg] = bh;
-                    m_first[nseg] = seg0 / P;
-                    m_cnt[nseg] = (seg0 + total - 1) / P - seg0 / P + 1;
-                    fast = m_cnt[nseg] <= 32;
-                    tot += m_cnt[nseg++];
-                }
-                m_n = nseg;
-                m_fast = fast && (int64_t)tot * wstride <= (int64_t)kGW * GG::WARP / 4;
-            }
-            __syncthreads();
-            if (m_fast) {
-                merge_segments_to_output<D>(a, m_seg, m_first, m_cnt, m_n, wstride, (float *)base);
+            if (m_mode == 2) {
+                merge_pairs_direct<D>(ma, m_seg, m_first, m_cnt, m_n, wstride);
+            } else if (m_mode == 1) {
+                merge_segments_to_output<D>(ma, m_seg, m_first, m_cnt, m_n, wstride, (float *)base);
             } else {
                 for (unsigned m = s_lastmask; m; m &= m - 1) {
                     const int bh = b0 + __ffs(m) - 1;
                     const int seg0 = pre[bh], total = pre[bh + 1] - seg0;
                     const int f0 = seg0 / P, last = (seg0 + total - 1) / P;
-                    merge_staged_to_output<D>(a, bh, a.ws.partial + ((int64_t)f0 + bh) * wstride,
+                    merge_staged_to_output<D>(ma, bh, ma.ws.partial + ((int64_t)f0 + bh) * wstride,
                                               last - f0 + 1, wstride, (float *)base,
                                               kGW * GG::WARP / 4);
                     __syncthreads();  // the stage is reused by the next segment
                 }
             }
         }
-        __syncthreads();  // s_lastmask is rewritten by the next batch
+        __syncthreads();  // s_lastmask and the merge list are rewritten by the next batch
     }
     // segments with no rows at all (every head empty) still get an output
     if (blockIdx.x == 0) {
         for (int bh = 0; bh < BH; ++bh) {
             if (pre[bh + 1] != pre[bh]) continue;
-            const int b = bh / a.geo.num_kv_heads, kv = bh - b * a.geo.num_kv_heads;
+            const int b = bh / ma.geo.num_kv_heads, kv = bh - b * ma.geo.num_kv_heads;
             for (int i = tid; i < g * D; i += kGThreads) {
                 const int h = i / D, d = i - h * D;
-                const int64_t oh = (int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g + h;
-                if (a.part_out) {
-                    const int nr = a.p2p.peers ? a.p2p.n : 1;
+                const int64_t oh = (int64_t)b * ma.geo.num_kv_heads * g + (int64_t)kv * g + h;
+                if (ma.part_out) {
+                    const int nr = ma.p2p.peers ? ma.p2p.n : 1;
                     for (int r = 0; r < nr; ++r) {
-                        float *po = (a.p2p.peers ? p2p_part_slot(a.p2p, a.p2p.peers[r], a.p2p.rank)
-                                                 : a.part_out) + oh * PSTR;
+                        float *po = (ma.p2p.peers ? p2p_part_slot(ma.p2p, ma.p2p.peers[r], ma.p2p.rank)
+                                                 : ma.part_out) + oh * PSTR;
                         po[8 + d] = 0.f;
                         if (d < 8) po[d] = (d == 0 || d == 2) ? -INFINITY : 0.f;
                     }
                     continue;
                 }
-                a.out[oh * D + d] = 0.f;
+                ma.out[oh * D + d] = 0.f;
                 if (d == 0) {
-                    if (a.lse) a.lse[oh] = -INFINITY;
-                    if (a.ess) a.ess[oh] = 0.f;
+                    if (ma.lse) ma.lse[oh] = -INFINITY;
+                    if (ma.ess) ma.ess[oh] = 0.f;
                 }
             }
         }

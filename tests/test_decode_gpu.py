@@ -445,6 +445,10 @@ def test_many_clusters_selection_bit_exact(mode):
                     true_clusters=64, n_clusters=64, topk_clusters=8, samples=64)),
     ("g8-k1", dict(num_query_heads=16, num_kv_heads=2, batch=2, context=4096, true_clusters=40,
                    n_clusters=40, topk_clusters=1, samples=32)),
+    # 32 (sequence, KV head) segments over 148 CTAs: a handful of CTA partials
+    # per segment, merged without staging (head_dim 64: two dims per lane)
+    ("g2-d64-b8", dict(num_query_heads=8, num_kv_heads=4, head_dim=64, batch=8, context=4096,
+                       true_clusters=48, n_clusters=48, topk_clusters=6, samples=64)),
 ])
 def test_hybrid_selection_shapes_bit_exact(name, changes):
     """The hybrid selection (one CTA per query head, a cluster per KV head)
