@@ -624,6 +624,12 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
 
     const float qscale = a.p.scale * kLog2e;
     const int PSTR = partial_stride(D);
+    // K / V rows are read once per step: their copies carry an L2 evict-first
+    // policy, so the streaming does not push the CTA partials (written as
+    // segments end, read by the merging CTA up to a whole loop later) and the
+    // row tables out of L2
+    uint64_t kv_policy;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(kv_policy));
     const char *sk_all = (const char *)a.sum.sorted_key;
     const char *sv_all = (const char *)a.sum.sorted_value;
     int k_base = 0;  // CTA tiles before the current segment
@@ -713,11 +719,11 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
                                            : (int64_t)((uintptr_t)cv - (uintptr_t)ck);
                 const int ok = rc == INT_MIN ? 0 : 16;
                 const uint32_t kd = kd0 + it * GG::RPI * GG::PITCH;
-                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(kd),
-                             "l"(ks + c * 16), "r"(ok)
+                asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;\n" ::"r"(kd),
+                             "l"(ks + c * 16), "r"(ok), "l"(kv_policy)
                              : "memory");
-                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(kd + GG::TILE),
-                             "l"(ks + dv + c * 16), "r"(ok)
+                asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;\n" ::"r"(kd + GG::TILE),
+                             "l"(ks + dv + c * 16), "r"(ok), "l"(kv_policy)
                              : "memory");
             }
             (void)i;
