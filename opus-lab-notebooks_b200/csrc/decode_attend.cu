@@ -524,10 +524,22 @@ __device__ void merge_pairs_direct(const DecodeArgs &a, const int *seg, const in
                 }
             }
             const float inv_l = L > 0.f ? 1.f / L : 0.f;
+            if (!a.part_out && ((uintptr_t)a.out & 15) == 0) {
+                // one vector store per lane: the warp writes the head's row whole
+                float *o = a.out + ((int64_t)bhs[u] * g + hhs[u]) * D + VPL * lane;
+                if constexpr (VPL == 4)
+                    *(float4 *)o = make_float4(acc[0] * inv_l, acc[1] * inv_l, acc[2] * inv_l,
+                                               acc[3] * inv_l);
+                else
+                    *(float2 *)o = make_float2(acc[0] * inv_l, acc[1] * inv_l);
+                if (lane == 0)  // lse / ess (and the dim-0 value again, identical)
+                    write_merged<D>(a, bhs[u], hhs[u], 0, acc[0], M, L, MS, E1, E2, ns[u], inv_l);
+            } else {
 #pragma unroll
-            for (int e = 0; e < VPL; ++e)
-                write_merged<D>(a, bhs[u], hhs[u], VPL * lane + e, acc[e], M, L, MS, E1, E2, ns[u],
-                                inv_l);
+                for (int e = 0; e < VPL; ++e)
+                    write_merged<D>(a, bhs[u], hhs[u], VPL * lane + e, acc[e], M, L, MS, E1, E2,
+                                    ns[u], inv_l);
+            }
         }
     }
 }
