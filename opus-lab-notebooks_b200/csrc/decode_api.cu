@@ -38,8 +38,9 @@ static int check_decode(const SantaGeometry *geo, const SantaDecodeParams *p, in
         // the attention kernel balances rows on a 32-bit cost scale
         // (at most 3 per row: union + recent + sampled rows of every segment)
         const int64_t rows = (int64_t)geo->n_total + (int64_t)geo->group * p->samples;
-        // (3 per row at most, plus a start charge of 256 per segment)
-        if ((int64_t)geo->batch * geo->num_kv_heads * (rows * 3 + 256) >= ((int64_t)1 << 31))
+        // (kCostSample per row at most, plus the start charge per segment)
+        if ((int64_t)geo->batch * geo->num_kv_heads * (rows * kCostSample + kCostSegment) >=
+            ((int64_t)1 << 31))
             return SANTA_ERR_UNSUPPORTED;
     }
     if (!(p->scale > 0.f)) return SANTA_ERR_INVALID_ARGUMENT;

@@ -169,12 +169,7 @@ constexpr int kGW = 8;        // warps per CTA
 constexpr int kGRows = 16;    // rows per warp tile (the mma N/K granule)
 constexpr int kGStages = 3;   // cp.async ring depth per warp
 constexpr int kGThreads = 32 * kGW;
-constexpr int kCostRow = 2;     // balancing cost of a union or recent-window row
-constexpr int kCostSample = 3;  // balancing cost of a sampled (scattered) row
-// balancing cost of starting a segment (ring drain, CTA fold, pipeline refill:
-// ~2 us, about 128 streamed rows); charged before the segment's first row, so
-// the CTA whose share covers a segment boundary takes fewer rows
-constexpr int kCostSegment = 256;
+// balancing costs kCostRow / kCostSample / kCostSegment: decode_common.cuh
 
 template <int D>
 struct GatherGeom {

@@ -456,6 +456,18 @@ bool select_group_supported(const DecodeArgs &a);
 int launch_select_group(DecodeArgs &a, cudaStream_t stream);
 int num_sms();
 int attend_partial_slots(const SantaGeometry *geo, int nsplit);
+
+// Row costs on which the gather attention kernel splits the step's rows into
+// equal CTA shares (a 32-bit scale: the API rejects geometries whose total
+// could overflow it).
+constexpr int kCostRow = 2;     // balancing cost of a union or recent-window row
+constexpr int kCostSample = 3;  // balancing cost of a sampled (scattered) row
+// balancing cost of starting a segment (ring drain, CTA fold, the next
+// segment's q fragments, row entries and first copies: ~4 us, about 768
+// streamed rows, measured with per-CTA timers; 768 / 1536 / 2048 / 3072 swept
+// on both decode workloads, 1536 best); charged before the segment's first
+// row, so the CTA whose share covers a segment boundary takes fewer rows
+constexpr int kCostSegment = 1536;
 int launch_merge_shards(int rows, int head_dim, int num_shards, const float *partials,
                         const P2PArgs &c, float *out, float *lse, float *ess,
                         cudaStream_t stream);

@@ -66,6 +66,10 @@ def test_workspace_queries_validate_arguments():
     bad = _lib.SantaGeometry(8, 4, 7, 128, 32768, 32768, 40000, _lib.DTYPE_BF16)
     assert lib.santa_decode_workspace_bytes(ctypes.byref(bad), ctypes.byref(p), 256,
                                             ctypes.byref(n)) == _lib.SANTA_ERR_INVALID_ARGUMENT
+    # 512 segments of 2M rows: the attention kernel's 32-bit row-cost scale would overflow
+    big = _lib.SantaGeometry(64, 8, 4, 128, 1 << 21, 1 << 21, (1 << 21) - 64, _lib.DTYPE_BF16)
+    assert lib.santa_decode_workspace_bytes(ctypes.byref(big), ctypes.byref(p), 256,
+                                            ctypes.byref(n)) == _lib.SANTA_ERR_UNSUPPORTED
     p_bad = _lib.SantaDecodeParams(_lib.MODE_HYBRID, 16, 0, 5000, 0.088, 0, 0, 0, 0)
     assert lib.santa_decode_workspace_bytes(ctypes.byref(geo), ctypes.byref(p_bad), 256,
                                             ctypes.byref(n)) == _lib.SANTA_ERR_INVALID_ARGUMENT
