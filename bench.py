@@ -37,6 +37,7 @@ WORKLOADS = {"qwen7b-32k": QWEN7B_32K, "qwen3-8b-128k": QWEN3_8B_128K,
 PREFILL_METRIC = "causal prefill attention TFLOP/s (tcgen05) and MiniBatchKMeans seconds per fit"
 METRIC = "SANTA++ decode attn tokens/s @32K-128K ctx; achieved HBM GB/s vs 8 TB/s peak"
 L2_FLUSH_BYTES = 256 << 20
+HEAD_START_S = 0.05  # device spin before eager multi-GPU timed steps
 
 
 def parse_args():
@@ -57,6 +58,9 @@ def parse_args():
     ap.add_argument("--prefill-prompt", type=int, default=32768,
                     help="prompt length of the prefill workload (the reported one is 32768; "
                          "smaller values are for profiler captures)")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="sequences per GPU instead of the workload's own (small profiler "
+                         "captures; the reported runs use the workload's batch)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="bound on the CPU-baseline sample")
     ap.add_argument("--transport", choices=["nccl", "p2p"], default="nccl",
@@ -186,13 +190,16 @@ def cluster_of_row(summ, shape):
 
 def run_ours(args, rank, world):
     from santapp_b200.attention import santapp as S
+    from santapp_b200.synthetic import scaled_shape
     shape = WORKLOADS[args.workload]
     if world > 1:
         raise SystemExit("multi-GPU decode is run by bench_multi (sequence shards)")
+    if args.batch is not None:
+        shape = scaled_shape(shape, batch=args.batch,
+                             name=shape.name.rsplit("-b", 1)[0] + f"-b{args.batch}")
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     n_q = max(shape.steps, args.steps + args.warmup)
-    from santapp_b200.synthetic import scaled_shape
     w = make_decode_workload(scaled_shape(shape, steps=n_q), seed=args.seed, device=dev)
     labels = w.labels[:, :, :shape.sample_end].contiguous()
     summ = S.build_summary(w.keys, w.values, labels, shape.n_clusters,
@@ -564,12 +571,19 @@ def run_sharded(args, rank, world):
         dist.barrier()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
+        # Eager steps are enqueued by Python (ctypes calls, NCCL calls, event
+        # records); a device-side spin ahead of the first step, outside every
+        # event, lets the host queue steps ahead of the GPU so that the per-step
+        # events time the kernels and collectives rather than host launch gaps
+        # (the single-GPU run gets the same from its CUDA graph).
+        torch.cuda._sleep(int(HEAD_START_S * 1.965e9))
         for i in range(args.steps):
             flush()
             if graphs:
                 graphs[i].replay()
             else:
                 one_step(i, ev[i])
+        enqueued = time.perf_counter() - t0
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
         clk = clocks.stop()
@@ -638,8 +652,11 @@ def run_sharded(args, rank, world):
             "phase_ms": phase,
             "timing": ("CUDA events around each step on every rank, max over ranks of the sum; "
                        + ("one CUDA graph per step (this library's four kernels)"
-                          if runner.p2p is not None else "eager launches")),
+                          if runner.p2p is not None else "eager launches")
+                       + f"; a {HEAD_START_S * 1e3:.0f} ms device spin before the first step "
+                         "lets the host queue steps ahead of the GPU"),
             "wall_s": wall,
+            "host_enqueue_s": enqueued,
             "clocks": clk,
             "gpu_launches": runner.kernels_per_call * args.steps,
             "e2e": e2e,
