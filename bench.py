@@ -37,7 +37,7 @@ WORKLOADS = {"qwen7b-32k": QWEN7B_32K, "qwen3-8b-128k": QWEN3_8B_128K,
 PREFILL_METRIC = "causal prefill attention TFLOP/s (tcgen05) and MiniBatchKMeans seconds per fit"
 METRIC = "SANTA++ decode attn tokens/s @32K-128K ctx; achieved HBM GB/s vs 8 TB/s peak"
 L2_FLUSH_BYTES = 256 << 20
-HEAD_START_S = 0.05  # device spin before eager multi-GPU timed steps
+HEAD_START_S = 0.05  # device spin before the eager multi-GPU timed steps
 
 
 def parse_args():
@@ -572,11 +572,14 @@ def run_sharded(args, rank, world):
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         # Eager steps are enqueued by Python (ctypes calls, NCCL calls, event
-        # records); a device-side spin ahead of the first step, outside every
-        # event, lets the host queue steps ahead of the GPU so that the per-step
-        # events time the kernels and collectives rather than host launch gaps
-        # (the single-GPU run gets the same from its CUDA graph).
-        torch.cuda._sleep(int(HEAD_START_S * 1.965e9))
+        # records).  A device-side spin ahead of the first step, outside every
+        # event, lets the host fill the launch queue before the GPU starts, so
+        # that the per-step events time the kernels and collectives rather than
+        # the gaps of a GPU waiting for its next launch (the single-GPU run gets
+        # the same from its CUDA graph).  ``host_enqueue_s`` ~ the spin + the
+        # drain: the host blocks on the full queue while the GPU spins.
+        head_start = HEAD_START_S
+        torch.cuda._sleep(int(head_start * 1.965e9))
         for i in range(args.steps):
             flush()
             if graphs:
@@ -653,7 +656,7 @@ def run_sharded(args, rank, world):
             "timing": ("CUDA events around each step on every rank, max over ranks of the sum; "
                        + ("one CUDA graph per step (this library's four kernels)"
                           if runner.p2p is not None else "eager launches")
-                       + f"; a {HEAD_START_S * 1e3:.0f} ms device spin before the first step "
+                       + f"; a {head_start * 1e3:.0f} ms device spin before the first step "
                          "lets the host queue steps ahead of the GPU"),
             "wall_s": wall,
             "host_enqueue_s": enqueued,

@@ -107,6 +107,7 @@ static int prepare_decode(const SantaGeometry *geo, const SantaDecodeParams *p, 
     a->nsplit = nsplit;
     a->cluster_base = 0;
     a->num_shards = 1;
+    a->shard_index = 0;
     a->cand_out = nullptr;
     a->shard_cands = nullptr;
     a->part_out = nullptr;
@@ -259,6 +260,7 @@ static int prepare_shard(const SantaGeometry *geo, const SantaDecodeParams *p, c
         return SANTA_ERR_INVALID_ARGUMENT;
     a->cluster_base = shard->cluster_base;
     a->num_shards = shard->num_shards;
+    a->shard_index = shard->shard_index;
     a->shard_cands = need_candidates ? shard->candidates : nullptr;
     st = bind_p2p(geo, p, shard, a);
     if (st) return st;

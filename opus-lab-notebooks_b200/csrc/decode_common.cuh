@@ -146,6 +146,7 @@ struct DecodeArgs {
     // sequence shards (HYBRID): global cluster id = cluster_base + cluster row
     int cluster_base;
     int num_shards;
+    int shard_index;              // this rank's shard (threshold selection reads its own keys)
     uint64_t *cand_out;           // select: write the local top-k keys and stop
     const uint64_t *shard_cands;  // select: [num_shards][B*Hq][k] keys -> global top-k
     float *part_out;              // attend: unnormalised partial per (b, query head)

@@ -345,6 +345,12 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
     const int sample_end = a.geo.sample_end;
     const int cbase = a.cluster_base;
     const int kk = a.p.topk_clusters;
+    // Sharded threshold form: the clusters of this shard that reach the global
+    // k-th key are all among this shard's own top-k keys (the candidates pass
+    // over the same q wrote them, sorted, into the gathered key list: a key at
+    // or above the global k-th has fewer than k larger keys anywhere), so the
+    // centroids are not scored again.
+    const bool thr_mode = a.shard_cands != nullptr;
 
     // ---- loads: q rows, cluster metadata and (staged layout) the slice -------
     // 16-byte cp.async copies by every thread; centroid rows and q rows land
@@ -352,7 +358,7 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
     // quarter warp sit on distinct bank groups)
     const float *qb = a.q + ((int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g) * D;
     const float *cent = a.sum.centroids + (int64_t)(bh * Gmax + c0) * D;  // the slice
-    if (!L.staged && nrows > 0 && tid == kGrpThreads - 32)
+    if (!thr_mode && !L.staged && nrows > 0 && tid == kGrpThreads - 32)
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(cent),
                      "r"((uint32_t)nrows * D * 4)
                      : "memory");
@@ -365,7 +371,7 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
         cp_async16(len_s + 4 * i, a.sum.lengths + (int64_t)bh * Gmax + 4 * i);
         cp_async16(logn_s + 4 * i, a.sum.log_n + (int64_t)bh * Gmax + 4 * i);
     }
-    if (L.staged) {
+    if (L.staged && !thr_mode) {
         for (int i = tid; i < nrows * (D / 4); i += kGrpThreads) {
             const int r = i / (D / 4), d = 4 * (i - r * (D / 4));
             cp_async16(stage + r * QP + d, cent + (int64_t)r * D + d);
@@ -382,7 +388,7 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
     // work item t takes row t % nrows and head set t / nrows: all heads when
     // g <= 4, else two sets of 4 (the second padded to 4), so the chain count
     // per item is uniform and warps are full
-    {
+    if (!thr_mode) {
         const int nsets = g <= 4 ? 1 : 2;
         const int nh = g <= 4 ? g : 4;
         const int total = nrows * nsets;
@@ -449,8 +455,12 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
             if (lists[j] != 0ull) last = j;
         thr = last >= 0 ? lists[last] : 1ull;
         __syncthreads();  // lists is reused below
-    }
-    {
+        // this shard's own top-k keys, descending and zero-padded
+        const uint64_t *own = a.shard_cands + (int64_t)a.shard_index * rows * kk +
+                              ((int64_t)bh * g + h) * kk;
+        if (tid < 32) lists[tid] = tid < kk ? own[tid] : 0ull;
+        __syncthreads();
+    } else {
         const uint32_t kbase = smem_u32(keys_s) + (uint32_t)(h * per) * 8u;
         block_top32(
             n_groups,
