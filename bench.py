@@ -609,15 +609,15 @@ def run_sharded(args, rank, world):
             q_dev = torch.empty_like(queries[0])
             dist.barrier()
             torch.cuda.synchronize()
-            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s0.record()
+            # as the single-GPU e2e: every step's output is read back into
+            # pinned memory and waited for before the next step is issued
+            t0 = time.perf_counter()
             for i in range(args.steps):
                 q_dev.copy_(q_host[i], non_blocking=True)
                 out = runner(q_dev, step=i)
                 out_host.copy_(out, non_blocking=True)
-            s1.record()
-            torch.cuda.synchronize()
-            t = torch.tensor([s0.elapsed_time(s1)], dtype=torch.float64, device=dev)
+                torch.cuda.current_stream().synchronize()
+            t = torch.tensor([(time.perf_counter() - t0) * 1e3], dtype=torch.float64, device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e = {"value": shape.batch * args.steps / (float(t.item()) / 1e3),
                    "unit": "tokens/s", "h2d_bytes_per_step": int(q_host[0].numel() * 4),
