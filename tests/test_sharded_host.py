@@ -161,3 +161,38 @@ def test_sharded_oracle_with_one_shard_is_the_hybrid_oracle():
     b = O.decode_hybrid(qv, K, V, summ, p.sample_end, SMALL.topk_clusters, ranks, SMALL.scale)
     assert np.allclose(a.out, b.out, atol=1e-12) and math.isclose(a.lse, b.lse, abs_tol=1e-12)
     assert math.isclose(a.ess, b.ess, rel_tol=1e-12)
+
+
+def test_threshold_selection_lies_in_the_shards_own_candidates():
+    """The threshold selection takes a shard's clusters from its own top-k
+    candidate keys in the gathered list instead of scoring every centroid
+    again.  The invariant behind it: a local cluster whose key reaches the
+    global k-th key has fewer than k larger keys anywhere, so it is among the
+    shard's own top-k.  Checked on random shards, with tied guesses (clusters
+    that copy their neighbour's rows) broken by the lowest global id."""
+    rng = np.random.default_rng(7)
+    D, scale = 16, 0.25
+    for _ in range(40):
+        n, k = int(rng.integers(2, 6)), int(rng.integers(1, 9))
+        summaries, bases, base = [], [], 0
+        for _r in range(n):
+            G = int(rng.integers(1, 14))
+            rows = [rng.standard_normal((int(c), D)).astype(np.float32)
+                    for c in rng.integers(1, 6, size=G)]
+            for j in range(1, G):
+                if rng.random() < 0.3:
+                    rows[j] = rows[j - 1].copy()
+            labels = np.repeat(np.arange(G), [len(x) for x in rows])
+            summaries.append(O.build_summary(np.concatenate(rows), labels, G))
+            bases.append(base)
+            base += G
+        q = rng.standard_normal(D).astype(np.float32)
+        cands = [O.shard_candidate_keys(s, q, scale, k, b) for s, b in zip(summaries, bases)]
+        thr = O.keys_threshold(np.stack(cands), k)
+        want = O.shard_topk(summaries, q, scale, k, bases)
+        for r, (s, b) in enumerate(zip(summaries, bases)):
+            full = O.selected_by_threshold(s, q, scale, thr, b)
+            own = sorted(0xFFFFFFFF - (int(x) & 0xFFFFFFFF) - b
+                         for x in cands[r] if int(x) and int(x) >= thr)
+            assert np.array_equal(full, want[r])
+            assert own == full.tolist()
