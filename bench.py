@@ -673,6 +673,20 @@ def run_sharded(args, rank, world):
             bad = torch.tensor([int(runner.p2p_error.item())], device=dev)
             dist.all_reduce(bad, op=dist.ReduceOp.MAX)
             line["p2p_wait_timeouts"] = int(bad.item())
+            # the same step through the NCCL exchanges: same kernels, same merge
+            # order, so the outputs must agree bit for bit
+            ref = ShardedDecodeStep(p.keys, p.values, summ,
+                                    num_query_heads=shape.num_query_heads, n_total=p.n_total,
+                                    topk_clusters=shape.topk_clusters, samples=p.samples,
+                                    shard_index=rank, num_shards=world,
+                                    cluster_base=p.cluster_base, seed=args.seed)
+            st = args.warmup
+            a = runner(queries[st], step=st).clone()
+            b = ref(queries[st], step=st)
+            torch.cuda.synchronize()
+            diff = torch.tensor([float((a - b).abs().max())], dtype=torch.float64, device=dev)
+            dist.all_reduce(diff, op=dist.ReduceOp.MAX)
+            line["p2p_vs_nccl_max_abs_diff"] = float(diff.item())
         return line if rank == 0 else None
     finally:
         dist.barrier()

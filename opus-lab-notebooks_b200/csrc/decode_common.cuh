@@ -190,10 +190,13 @@ __device__ inline bool p2p_wait(const P2PArgs &c, int ex) {
     }
     return true;
 }
-// one thread, at the start of the kernel that consumes exchange ex: this
-// rank's contribution was stored by the previous kernel on the stream, which
-// has completed, so the flag can go up now (every consuming CTA raises it;
-// the stores are idempotent, and no CTA depends on another being resident)
+// one thread of the first CTA, at the start of the kernel that consumes
+// exchange ex: this rank's contribution was stored by the previous kernel on
+// the stream, which has completed, so the flag can go up now.  One release
+// store per peer and rank: when every consuming CTA raised it, the hundreds
+// of system-scope releases delayed the flags the peers wait for.  The other
+// CTAs wait for the flags with a bounded wait, so a first CTA that could
+// not be scheduled would end in the error flag, not a hang.
 __device__ inline void p2p_publish(const P2PArgs &c, int ex) {
     for (int r = 0; r < c.n; ++r)
         p2p_st_release((unsigned long long *)((unsigned char *)c.peers[r] + kP2PFlags) +

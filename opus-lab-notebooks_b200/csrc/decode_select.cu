@@ -300,7 +300,7 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
     if (a.shard_cands) {
         if (a.p2p.peers) {  // the peers' keys arrive through peer memory
             if (tid == 0) {
-                p2p_publish(a.p2p, 0);
+                if (blockIdx.x == 0) p2p_publish(a.p2p, 0);
                 p2p_wait(a.p2p, 0);
             }
             __syncthreads();

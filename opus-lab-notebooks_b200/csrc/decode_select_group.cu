@@ -435,7 +435,7 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
     if (a.shard_cands) {
         if (a.p2p.peers) {  // the peers' keys arrive through peer memory
             if (tid == 0) {
-                p2p_publish(a.p2p, 0);
+                if (blockIdx.x == 0 && blockIdx.y == 0) p2p_publish(a.p2p, 0);
                 p2p_wait(a.p2p, 0);
             }
             __syncthreads();

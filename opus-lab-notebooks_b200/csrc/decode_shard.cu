@@ -28,7 +28,7 @@ __global__ void __launch_bounds__(D) merge_shards_kernel(int rows, int num_shard
     const int row = blockIdx.x, d = threadIdx.x;
     if (c.peers) {  // the partials arrive through peer memory
         if (d == 0) {
-            p2p_publish(c, 1);
+            if (row == 0) p2p_publish(c, 1);
             p2p_wait(c, 1);
         }
         __syncthreads();
