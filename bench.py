@@ -4,15 +4,18 @@
 One step = one decode step of SANTA++ attention for every (sequence, query
 head) of the batch: cluster selection (q . centroid scoring, top-k) plus the
 gather attention over the selected clusters, the uniformly sampled remainder
-and the exact recent window.  Default workload: Qwen2.5-7B attention shape
-(28 query heads, 4 KV heads, head_dim 128), bf16 K/V, batch 8 at 32K context,
-256 centroids per KV head, top-16 clusters + 256 samples per head, 128 steps
-with fresh queries.  Data: seeded synthetic Gaussian-mixture keys.
+and the exact recent window.  Default workload: the Qwen3-8B attention shape
+(32 query heads, 8 KV heads, head_dim 128), bf16 K/V, batch 16 at 128K
+context, 1024 centroids per KV head, top-32 clusters + 512 samples per head.
+On N GPUs (torchrun) the same job is split into N sequence shards (strong
+scaling).  The single-GPU line also carries the Qwen2.5-7B batch-8 32K decode
+and the Qwen2.5-7B 32K prefill (against torch SDPA in the same run).  Data:
+seeded synthetic Gaussian-mixture keys.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Prints one JSON line (rank 0).  ``--impl reference`` times the CPU
-restatement of the reference algorithm on the host cores instead.
+Prints one JSON line (rank 0).  ``--impl reference`` times the torch-CPU
+restatement of the reference's per-head decode on the host cores instead.
 """
 
 from __future__ import annotations
@@ -46,7 +49,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="qwen7b-32k",
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="qwen3-8b-128k",
                     help="qwen7b-prefill-32k: prompt prefill + clustering of the Qwen2.5-7B "
                          "shape (one GPU), not a decode step")
     ap.add_argument("--mode", default="hybrid")
@@ -63,8 +66,10 @@ def parse_args():
                          "captures; the reported runs use the workload's batch)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="bound on the CPU-baseline sample")
-    ap.add_argument("--transport", choices=["nccl", "p2p"], default="nccl",
-                    help="N > 1: NCCL all-gathers, or the kernels' own peer-memory exchange")
+    ap.add_argument("--transport", choices=["nccl", "p2p"], default="p2p",
+                    help="N > 1: the kernels' own peer-memory exchange, or NCCL all-gathers")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="single GPU: skip the 32K decode and prefill blocks")
     return ap.parse_args()
 
 
@@ -188,23 +193,20 @@ def cluster_of_row(summ, shape):
     return (torch.cumsum(marks[:, :N], dim=1) - 1).clamp_min_(0)
 
 
-def run_ours(args, rank, world):
+def measure_decode(args, shape, steps, warmup, dev, keep=False):
+    """The K timed decode steps of one workload on one GPU: device time per
+    step, the select / attend split, and the attend kernel's roofline from
+    the algorithmic bytes of every timed step.  keep: also return the
+    workload, summary and step object (for the e2e run)."""
     from santapp_b200.attention import santapp as S
     from santapp_b200.synthetic import scaled_shape
-    shape = WORKLOADS[args.workload]
-    if world > 1:
-        raise SystemExit("multi-GPU decode is run by bench_multi (sequence shards)")
-    if args.batch is not None:
-        shape = scaled_shape(shape, batch=args.batch,
-                             name=shape.name.rsplit("-b", 1)[0] + f"-b{args.batch}")
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    n_q = max(shape.steps, args.steps + args.warmup)
+    n_q = max(shape.steps, steps + warmup)
     w = make_decode_workload(scaled_shape(shape, steps=n_q), seed=args.seed, device=dev)
     labels = w.labels[:, :, :shape.sample_end].contiguous()
     summ = S.build_summary(w.keys, w.values, labels, shape.n_clusters,
                            sample_end=shape.sample_end, n_total=shape.context)
     del labels
+    w.labels = None
     runner = S.DecodeStep(w.keys, w.values, summ, num_query_heads=shape.num_query_heads,
                           mode=args.mode, n_total=shape.context,
                           topk_clusters=shape.topk_clusters, samples=shape.samples,
@@ -217,8 +219,8 @@ def run_ours(args, rank, world):
     attend_bytes, select_bytes, rows_touched = [], [], []
     if not args.profile:
         cid = cluster_of_row(summ, shape)
-        for i in range(args.steps):
-            step = args.warmup + i
+        for i in range(steps):
+            step = warmup + i
             a_b, s_b, r_t = algorithmic_bytes(runner, queries[step], step, shape, summ, cid)
             attend_bytes.append(a_b)
             select_bytes.append(s_b)
@@ -226,7 +228,7 @@ def run_ours(args, rank, world):
         del cid
     torch.cuda.synchronize()
 
-    for i in range(args.warmup):
+    for i in range(warmup):
         flush()
         runner(queries[i], step=i)
     torch.cuda.synchronize()
@@ -237,13 +239,13 @@ def run_ours(args, rank, world):
     # captured around its two kernels (the flush lies outside them); the
     # middle event splits the phases.
     inner = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)]
-             for _ in range(args.steps)]
+             for _ in range(steps)]
     cap = torch.cuda.Stream()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.stream(cap):
         with torch.cuda.graph(graph, stream=cap):
-            for i in range(args.steps):
-                step = args.warmup + i
+            for i in range(steps):
+                step = warmup + i
                 flush()
                 inner[i][0].record(cap)
                 runner.plan(queries[step], step=step)
@@ -260,46 +262,17 @@ def run_ours(args, rank, world):
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
     clk = clocks.stop()
+    del graph
     step_ms = np.array([e[0].elapsed_time(e[2]) for e in inner])
     plan_ms = np.array([e[0].elapsed_time(e[1]) for e in inner])
     att_ms = np.array([e[1].elapsed_time(e[2]) for e in inner])
-    total_s = step_ms.sum() / 1e3
-    value = shape.batch * args.steps / total_s
     peak, peak_kind = peaks()
-    if attend_bytes:
-        achieved = float(np.sum(attend_bytes) / (att_ms.sum() / 1e3) / 1e9)
-    else:
-        achieved = float("nan")
-    traffic = load_traffic(shape)
-    del graph
-
-    e2e = None if (args.no_e2e or args.profile) else run_e2e(args, shape, w, summ, runner)
-    cpu = (None if (args.no_cpu_baseline or args.profile)
-           else cpu_baseline_sample(args, shape, w, summ))
-    line = {
-        "metric": METRIC,
-        "value": value,
-        "unit": "tokens/s",
-        "n_gpus": 1,
-        "steps": args.steps,
-        "warmup": args.warmup,
+    achieved = (float(np.sum(attend_bytes) / (att_ms.sum() / 1e3) / 1e9) if attend_bytes
+                else float("nan"))
+    step_bytes = (np.array(attend_bytes) + np.array(select_bytes)) if attend_bytes else None
+    res = {
+        "value": shape.batch * steps / (step_ms.sum() / 1e3),
         "ms_per_step": float(step_ms.mean()),
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "bf16" if shape.kv_dtype == torch.bfloat16 else "f32",
-        "data": "synthetic (seeded Gaussian-mixture keys, N(0,1) values and queries)",
-        "config": {
-            "workload": shape.name,
-            "query_heads": shape.num_query_heads, "kv_heads": shape.num_kv_heads,
-            "head_dim": shape.head_dim, "batch": shape.batch, "context": shape.context,
-            "clusters": shape.n_clusters, "topk_clusters": shape.topk_clusters,
-            "samples": shape.samples, "recent_window": shape.recent_window, "mode": args.mode,
-            "parallelism": "single GPU",
-            "l2": (f"flushed before every step, outside the events: {L2_FLUSH_BYTES >> 20} MiB "
-                   f"write, then a {L2_FLUSH_BYTES >> 20} MiB read of another buffer so that "
-                   "no dirty flush line is written back inside the step"),
-        },
         "phase_ms": {"select": float(plan_ms.mean()), "attend": float(att_ms.mean())},
         "roofline": {
             "kernel": "decode_attend_gather_kernel",
@@ -309,7 +282,7 @@ def run_ours(args, rank, world):
             "peak_kind": peak_kind,
             "unit": "GB/s",
             "frac": achieved / peak,
-            "traffic": traffic,
+            "traffic": load_traffic(shape),
             "algorithmic_bytes_per_launch": float(np.mean(attend_bytes)) if attend_bytes else None,
             "rows_touched_per_step": float(np.mean(rows_touched)) if rows_touched else None,
             "dense_kv_bytes_per_step": float(shape.batch * shape.num_kv_heads * shape.context
@@ -320,15 +293,107 @@ def run_ours(args, rank, world):
                          if select_bytes else None),
             "unit": "GB/s",
         },
+        "step_roofline": {
+            "note": "both kernels: attend + select algorithmic bytes over the whole step time",
+            "achieved": (float(step_bytes.sum() / (step_ms.sum() / 1e3) / 1e9)
+                         if step_bytes is not None else None),
+            "frac": (float(step_bytes.sum() / (step_ms.sum() / 1e3) / 1e9) / peak
+                     if step_bytes is not None else None),
+            "unit": "GB/s",
+        },
+        "wall_s": wall,
+        "clocks": clk,
+        "gpu_launches": runner.kernels_per_call * steps,
+    }
+    if keep:
+        return res, (w, summ, runner)
+    del runner, summ, w
+    torch.cuda.empty_cache()
+    return res
+
+
+def decode_config(shape, mode, world, p=None, p2p=True):
+    """The config block of a decode line (our arm and the reference arm
+    print the same one for the same run)."""
+    cfg = {
+        "workload": shape.name,
+        "query_heads": shape.num_query_heads, "kv_heads": shape.num_kv_heads,
+        "head_dim": shape.head_dim, "batch": shape.batch, "context": shape.context,
+        "clusters": shape.n_clusters, "topk_clusters": shape.topk_clusters,
+        "samples": shape.samples, "recent_window": shape.recent_window, "mode": mode,
+    }
+    if world == 1:
+        cfg["parallelism"] = "single GPU"
+        cfg["l2"] = (f"flushed before every step, outside the events: {L2_FLUSH_BYTES >> 20} MiB "
+                     f"write, then a {L2_FLUSH_BYTES >> 20} MiB read of another buffer so that "
+                     "no dirty flush line is written back inside the step")
+    else:
+        cfg["parallelism"] = (f"sequence shards x{world}: the job's cache, clusters and sample "
+                              "budget split over the ranks; "
+                              + ("top-k keys and (m, l, o) partials stored by the kernels into "
+                                 "every rank's buffer over NVLink (2 launches per step)"
+                                 if p2p else "NCCL all-gathers of the top-k keys and of the "
+                                             "(m, l, o) partials"))
+        cfg["l2"] = ("flushed before every step outside the events (256 MiB write + 256 MiB "
+                     "read of another buffer)")
+    return cfg
+
+
+def run_ours(args, rank, world):
+    from santapp_b200.synthetic import scaled_shape
+    shape = WORKLOADS[args.workload]
+    if world > 1:
+        raise SystemExit("multi-GPU decode runs in run_sharded (sequence shards)")
+    if args.batch is not None:
+        shape = scaled_shape(shape, batch=args.batch,
+                             name=shape.name.rsplit("-b", 1)[0] + f"-b{args.batch}")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    res, (w, summ, runner) = measure_decode(args, shape, args.steps, args.warmup, dev, keep=True)
+    e2e = None if (args.no_e2e or args.profile) else run_e2e(args, shape, w, summ, runner)
+    del runner, summ, w
+    torch.cuda.empty_cache()
+    line = {
+        "metric": METRIC,
+        "value": res["value"],
+        "unit": "tokens/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": res["ms_per_step"],
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16" if shape.kv_dtype == torch.bfloat16 else "f32",
+        "data": "synthetic (seeded Gaussian-mixture keys, N(0,1) values and queries)",
+        "config": decode_config(shape, args.mode, 1),
+        "phase_ms": res["phase_ms"],
+        "roofline": res["roofline"],
+        "select_roofline": res["select_roofline"],
+        "step_roofline": res["step_roofline"],
         "timing": ("one CUDA graph holding the K timed steps (per step: L2 flush, selection, "
                    "attention); each step timed by event-record nodes around its two kernels, "
                    "the phase split and roofline by the middle one"),
-        "wall_s": wall,
-        "clocks": clk,
-        "gpu_launches": runner.kernels_per_call * args.steps,
+        "wall_s": res["wall_s"],
+        "clocks": res["clocks"],
+        "gpu_launches": res["gpu_launches"],
         "e2e": e2e,
-        "cpu_baseline": cpu,
+        "cpu_baseline": None,
     }
+    if not args.no_extras and not args.profile and args.workload == "qwen3-8b-128k":
+        # the other decode context of the metric (Qwen2.5-7B batch 8 at 32K),
+        # and the prefill of that layer, next to torch SDPA in the same run
+        steps32 = min(args.steps, 64)
+        r32 = measure_decode(args, QWEN7B_32K, steps32, args.warmup, dev)
+        line["ctx32768"] = {
+            "workload": QWEN7B_32K.name, "steps": steps32, "value": r32["value"],
+            "unit": "tokens/s", "ms_per_step": r32["ms_per_step"], "phase_ms": r32["phase_ms"],
+            "roofline": r32["roofline"], "select_roofline": r32["select_roofline"],
+            "step_roofline": r32["step_roofline"], "clocks": r32["clocks"],
+            "gpu_launches": r32["gpu_launches"], "config": decode_config(QWEN7B_32K, args.mode, 1)}
+        line["prefill"] = prefill_block(args, dev, 32768, steps=min(args.steps, 10))
+    if not (args.no_cpu_baseline or args.profile):
+        line["cpu_baseline"] = cpu_baseline_sample(args, shape)
     return line
 
 
@@ -377,63 +442,76 @@ def run_e2e(args, shape, w, summ, runner):
                    "santa_decode_execute C ABI)"}
 
 
-def _oracle_inputs(shape, w, summ, pairs):
-    from oracle import santa_oracle as O
-    data = {}
-    for b, kv in pairs:
-        K = w.keys[b, kv].float().cpu().numpy()
-        V = w.values[b, kv].float().cpu().numpy()
-        lab = w.labels[b, kv, :shape.sample_end].cpu().numpy()
-        data[(b, kv)] = (K, V, O.build_summary(K[:shape.sample_end], lab, shape.n_clusters))
-    return data
+def _port_sample(shape, seed, n_seq=1):
+    """A bounded CPU sample of the workload for the torch-CPU restatement:
+    the first n_seq sequences' caches (drawn on the host with the workload's
+    generator and shape) and their cluster summaries."""
+    from oracle import santa_torch_port as P
+    from santapp_b200.synthetic import scaled_shape
+    sh = scaled_shape(shape, batch=n_seq, steps=max(shape.steps, 64))
+    w = make_decode_workload(sh, seed=seed, device="cpu")
+    summ = {}
+    for b in range(n_seq):
+        for kv in range(shape.num_kv_heads):
+            summ[(b, kv)] = P.build_summary(w.keys[b, kv, :shape.sample_end].float(),
+                                            w.labels[b, kv, :shape.sample_end], shape.n_clusters)
+    return w, summ
 
 
-def _cpu_head_call(shape, data, q, b, h, step, seed):
-    from oracle import santa_oracle as O
-    kv = h // shape.group
-    K, V, o = data[(b, kv)]
-    g = O.centroid_guess(o, q, shape.scale)
-    chosen = O.select_topk(g, shape.topk_clusters)
-    n_rest = shape.sample_end - int(o.lengths[chosen].sum())
-    ranks = O.philox_ranks(seed, step, b, h, shape.samples, n_rest)
-    return O.decode_hybrid(q, K, V, o, shape.sample_end, shape.topk_clusters, ranks, shape.scale)
+def _port_step(shape, w, summ, step, gen, n_seq=1):
+    """One decode step of the sample's sequences, one call per (sequence,
+    query head) as the reference's engine makes them."""
+    from oracle import santa_torch_port as P
+    for b in range(n_seq):
+        for h in range(shape.num_query_heads):
+            kv = h // shape.group
+            P.approximate_attention_hybrid(w.queries[step, b, h], w.keys[b, kv], w.values[b, kv],
+                                           summ[(b, kv)], shape.sample_end,
+                                           shape.topk_clusters, shape.samples, generator=gen)
 
 
-def cpu_baseline_sample(args, shape, w, summ):
-    """The CPU restatement timed on one host core over a bounded sample of
-    head calls of one step; reported as tokens/s (Hq head calls = 1 token)."""
-    pairs = [(0, kv) for kv in range(shape.num_kv_heads)]
-    data = _oracle_inputs(shape, w, summ, pairs)
-    q = w.queries[args.warmup].cpu().numpy()
-    calls = 0
+def cpu_baseline_sample(args, shape):
+    """The torch-CPU restatement of the reference's per-head decode, timed on
+    all host cores (torch intra-op threads, as the reference runs) over a
+    bounded sample: decode steps of sequence 0 until ~args.cpu_seconds have
+    passed; tokens/s = sequences decoded per second."""
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    w, summ = _port_sample(shape, args.seed)
+    gen = torch.Generator().manual_seed(args.seed)
+    _port_step(shape, w, summ, 0, gen)  # warm-up
+    steps = 0
     t0 = time.perf_counter()
-    while time.perf_counter() - t0 < args.cpu_seconds and calls < 4 * shape.num_query_heads:
-        h = calls % shape.num_query_heads
-        _cpu_head_call(shape, data, q[0, h], 0, h, args.warmup, args.seed)
-        calls += 1
+    while time.perf_counter() - t0 < args.cpu_seconds and steps < 63:
+        _port_step(shape, w, summ, 1 + steps, gen)
+        steps += 1
     dt = time.perf_counter() - t0
-    return {"value": calls / shape.num_query_heads / dt, "unit": "tokens/s", "cores": 1,
-            "kind": "port",
-            "sample": f"{calls} query-head calls of sequence 0 at step {args.warmup} "
-                      f"({calls / shape.num_query_heads:.1f} tokens), numpy/C oracle, 1 thread"}
+    return {"value": steps / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{steps} decode steps of sequence 0 ({steps * shape.num_query_heads} "
+                      f"query-head calls over {shape.num_kv_heads} KV heads x {shape.context} "
+                      "tokens), torch-CPU restatement of the reference's per-head "
+                      "_approximate_attention (oracle/santa_torch_port.py), "
+                      f"torch.set_num_threads({cores})"}
 
 
 # ---------------------------------------------------------------------------
 # prefill + clustering of one layer (Qwen2.5-7B shape, 32K prompt)
 # ---------------------------------------------------------------------------
 
-def run_prefill(args):
-    """Causal prefill attention of one layer, [1, 28, 32768, 128] bf16 with 4
-    KV heads, through santa_prefill (tcgen05), then MiniBatchKMeans of each KV
-    head's 32704 prefix keys (k=256, minibatch 4096, 20 iterations, seed 0)
-    through SklearnLikeTorchMiniBatchKMeans.  Seeded N(0,1) Q/K/V; the keys are
-    the 256-component Gaussian mixture of the decode workloads."""
+def prefill_block(args, dev, T, steps, kv_heads_fit=1):
+    """Causal prefill attention of one Qwen2.5-7B layer, [1, 28, T, 128] bf16
+    with 4 KV heads: santa_prefill (tcgen05) and torch SDPA (the library
+    path the reference's prefill calls, santapp.py:320-346; flash / cuDNN
+    as the wheel picks) timed the same way in the same run, the outputs
+    compared; then MiniBatchKMeans of KV heads' 32K-token prefixes (k=256,
+    minibatch 4096, 20 iterations, seed 0) through
+    SklearnLikeTorchMiniBatchKMeans.  Seeded N(0,1) queries and values, the
+    Gaussian-mixture keys of the decode workloads."""
+    import torch.nn.functional as F
     from santapp_b200.attention.kmeans import SklearnLikeTorchMiniBatchKMeans
     from santapp_b200.attention.prefill import santa_prefill
     from santapp_b200.synthetic import scaled_shape
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    B, Hq, Hkv, T, D = 1, 28, 4, args.prefill_prompt, 128
+    B, Hq, Hkv, D = 1, 28, 4, 128
     shape = scaled_shape(QWEN7B_32K, batch=1, steps=1, context=T)
     w = make_decode_workload(shape, seed=args.seed, device=dev)
     g = torch.Generator(device=dev).manual_seed(args.seed + 1)
@@ -442,27 +520,41 @@ def run_prefill(args):
     flops = 4.0 * Hq * D * T * (T + 1) / 2
     out = santa_prefill(q, k, v)
     flush = L2Flush(dev)
+
+    def timed(fn):
+        ts = []
+        for i in range(args.warmup + steps):
+            flush()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                ts.append(e0.elapsed_time(e1))
+        return float(np.mean(ts))
+
     torch.cuda.synchronize()
-    ts = []
-    for i in range(args.warmup + args.steps):
-        flush()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        santa_prefill(q, k, v, out=out)
-        e1.record()
-        torch.cuda.synchronize()
-        if i >= args.warmup:
-            ts.append(e0.elapsed_time(e1))
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    ms = timed(lambda: santa_prefill(q, k, v, out=out))
+    clk = clocks.stop()
     err = int(out._santa_error_flag.item())
-    ms = float(np.mean(ts))
+    sdpa_out = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+    ms_sdpa = timed(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True,
+                                                           enable_gqa=True))
+    diff = (out.float() - sdpa_out.float()).abs()
+    cmp = {"max_abs": float(diff.max()), "mean_abs": float(diff.mean())}
+    del sdpa_out, diff
     peaks_d = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json"))) \
         if os.path.exists(os.path.join(REPO, "MEASURED_PEAKS.json")) else {}
     peak = float(peaks_d.get("bf16_tflops", 1590.0))
     tflops = flops / (ms / 1e3) / 1e12
     # clustering: one fit per KV head, each timed with a host clock around the
-    # call (the fit synchronises every mini-batch, as the reference does)
+    # call (the fit reads back one value per mini-batch, as the reference's
+    # control flow needs)
     fits = []
-    for kv in range(Hkv):
+    for kv in range(kv_heads_fit):
         x = k[0, kv, :shape.sample_end].float()
         est = SklearnLikeTorchMiniBatchKMeans(256, batch_size=4096, max_iter=20, random_state=0)
         torch.cuda.synchronize()
@@ -471,22 +563,40 @@ def run_prefill(args):
         torch.cuda.synchronize()
         fits.append((time.perf_counter() - t0, est.n_steps_))
     return {
-        "metric": PREFILL_METRIC, "value": tflops, "unit": "TFLOP/s", "n_gpus": 1,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded N(0,1) queries, Gaussian-mixture keys, N(0,1) values)",
-        "config": {"workload": f"qwen2.5-7b-prefill-ctx{T}", "query_heads": Hq,
-                   "kv_heads": Hkv, "head_dim": D, "batch": B, "prompt": T, "causal": True,
-                   "kmeans": {"k": 256, "batch_size": 4096, "max_iter": 20, "rows": shape.sample_end,
-                              "features": D}},
+        "workload": f"qwen2.5-7b-prefill-ctx{T}", "query_heads": Hq, "kv_heads": Hkv,
+        "head_dim": D, "batch": B, "prompt": T, "causal": True, "steps": steps,
+        "ms": ms, "tflops": tflops,
         "roofline": {"kernel": "prefill_fwd_kernel", "bound": "tensor", "achieved": tflops,
-                     "peak": peak, "peak_kind": "measured" if peaks_d else "fallback",
-                     "unit": "TFLOP/s", "frac": tflops / peak,
-                     "algorithmic_flops": flops},
-        "kmeans_seconds_per_fit": [round(f[0], 4) for f in fits],
-        "kmeans_steps_per_fit": [int(f[1]) for f in fits],
+                     "peak": peak, "peak_kind": "measured (burst)" if peaks_d else "fallback",
+                     "unit": "TFLOP/s", "frac": tflops / peak, "algorithmic_flops": flops},
+        "torch_sdpa_ms": ms_sdpa, "torch_sdpa_tflops": flops / (ms_sdpa / 1e3) / 1e12,
+        "vs_torch_sdpa": ms_sdpa / ms,
+        "vs_torch_sdpa_outputs": cmp,
         "error_flag": err,
-        "gpu_launches": 2 * args.steps,
+        "clocks": clk,
+        "kmeans": {"k": 256, "batch_size": 4096, "max_iter": 20, "rows": shape.sample_end,
+                   "features": D, "seconds_per_fit": [round(f[0], 4) for f in fits],
+                   "steps_per_fit": [int(f[1]) for f in fits]},
+    }
+
+
+def run_prefill(args):
+    """--workload qwen7b-prefill-32k: the prefill block as its own line."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    blk = prefill_block(args, dev, args.prefill_prompt, args.steps, kv_heads_fit=4)
+    return {
+        "metric": PREFILL_METRIC, "value": blk["tflops"], "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": blk["ms"],
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) queries, Gaussian-mixture keys, N(0,1) values)",
+        "config": {"workload": blk["workload"], "query_heads": blk["query_heads"],
+                   "kv_heads": blk["kv_heads"], "head_dim": blk["head_dim"], "batch": 1,
+                   "prompt": blk["prompt"], "causal": True, "kmeans": blk["kmeans"]},
+        "roofline": blk["roofline"], "torch_sdpa_ms": blk["torch_sdpa_ms"],
+        "vs_torch_sdpa": blk["vs_torch_sdpa"], "vs_torch_sdpa_outputs": blk["vs_torch_sdpa_outputs"],
+        "error_flag": blk["error_flag"], "clocks": blk["clocks"],
+        "gpu_launches": 2 * (args.steps + args.warmup),
     }
 
 
@@ -495,12 +605,16 @@ def run_prefill(args):
 # ---------------------------------------------------------------------------
 
 def run_sharded(args, rank, world):
-    """Weak scaling over sequence shards: the job decodes ``batch * N``
-    sequences of the workload's context; every sequence's clustered prefix
-    is split into N contiguous shards, one per rank, so each GPU holds as
-    many cache tokens as the single-GPU run.  One step = candidates ->
-    NCCL all-gather of the top-k keys -> select -> attend -> NCCL all-gather
-    of the partials -> merge.  Time = max over ranks of the device time."""
+    """Strong scaling over sequence shards: the workload's whole job (the
+    Qwen3-8B batch-16 128K decode by default) is split over the N ranks,
+    every sequence's clustered prefix into N contiguous shards, the
+    mixture's clusters and the sample budget likewise.  Peer-memory exchange
+    (default): one step = the selection launch (local candidates, key
+    exchange, global top-k threshold, draws) and the attention launch
+    (gather attention, partial exchange, merge), the K timed steps captured
+    in one CUDA graph with event nodes.  NCCL exchange: candidates -> NCCL
+    all-gather -> select -> attend -> NCCL all-gather -> merge, eager.  Time
+    = max over ranks of the summed per-step device time."""
     import datetime
     import torch.distributed as dist
     from santapp_b200.attention import santapp as S
@@ -512,8 +626,9 @@ def run_sharded(args, rank, world):
     dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     try:
         base = WORKLOADS[args.workload]
-        shape = scaled_shape(base, batch=base.batch * world,
-                             steps=max(base.steps, args.steps + args.warmup))
+        shape = scaled_shape(base, steps=max(base.steps, args.steps + args.warmup))
+        if args.batch is not None:
+            shape = scaled_shape(shape, batch=args.batch)
         p = make_shard_workload(shape, rank, world, seed=args.seed, device=dev)
         summ = S.build_summary(p.keys, p.values, p.labels, p.n_clusters,
                                sample_end=p.sample_end, n_total=p.n_total)
@@ -522,6 +637,7 @@ def run_sharded(args, rank, world):
                                    samples=p.samples, shard_index=rank, num_shards=world,
                                    cluster_base=p.cluster_base, seed=args.seed,
                                    transport=args.transport)
+        p2p = runner.p2p is not None
         queries = p.queries
         flush = L2Flush(dev)
         torch.cuda.synchronize()
@@ -530,18 +646,26 @@ def run_sharded(args, rank, world):
             flush()
             runner(queries[i], step=i)
         torch.cuda.synchronize()
+        if p2p:
+            runner.check_p2p()
 
-        # per step: events around the step, and on every rank the phase
-        # split (keys | exchange 1 | select | attend | exchange 2 | merge).
-        # NCCL transport: eager launches.  Peer-memory transport: the step is
-        # four kernels of this library and no library collective, captured in
-        # one CUDA graph per step (epoch baked in) with event-record nodes.
-        use_graphs = runner.p2p is not None
-        ev = [[torch.cuda.Event(enable_timing=True, external=use_graphs) for _ in range(7)]
+        # peer memory: per step events around (select | attend); NCCL: around
+        # (keys | exchange 1 | select | attend | exchange 2 | merge)
+        names = (["select", "attend"] if p2p else
+                 ["keys", "exchange_keys", "select", "attend", "exchange_partials", "merge"])
+        ev = [[torch.cuda.Event(enable_timing=True, external=p2p) for _ in range(len(names) + 1)]
               for _ in range(args.steps)]
 
         def one_step(i, e, stream=None):
             st = args.warmup + i
+            if p2p:
+                runner.begin(queries[st], st)
+                e[0].record(stream)
+                runner.plan(stream=stream)
+                e[1].record(stream)
+                runner.execute(stream=stream)
+                e[2].record(stream)
+                return
             e[0].record(stream)
             runner.candidates(queries[st], st, stream=stream)
             e[1].record(stream)
@@ -556,49 +680,55 @@ def run_sharded(args, rank, world):
             runner.merge(stream=stream)
             e[6].record(stream)
 
-        graphs = []
-        if use_graphs:
+        graph = None
+        if p2p:
+            # the K timed steps (each behind its L2 flush) as one CUDA graph,
+            # as the single-GPU run; every captured launch carries its step's
+            # epoch, and every rank captures the same sequence
             cap = torch.cuda.Stream()
+            graph = torch.cuda.CUDAGraph()
             with torch.cuda.stream(cap):
-                for i in range(args.steps):
-                    gph = torch.cuda.CUDAGraph()
-                    with torch.cuda.graph(gph, stream=cap):
+                with torch.cuda.graph(graph, stream=cap):
+                    for i in range(args.steps):
+                        flush()
                         one_step(i, ev[i], cap)
-                    graphs.append(gph)
             torch.cuda.synchronize()
         clocks = ClockSampler(local)
         clocks.start()
         dist.barrier()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        # Eager steps are enqueued by Python (ctypes calls, NCCL calls, event
-        # records).  A device-side spin ahead of the first step, outside every
-        # event, lets the host fill the launch queue before the GPU starts, so
-        # that the per-step events time the kernels and collectives rather than
-        # the gaps of a GPU waiting for its next launch (the single-GPU run gets
-        # the same from its CUDA graph).  ``host_enqueue_s`` ~ the spin + the
-        # drain: the host blocks on the full queue while the GPU spins.
-        head_start = HEAD_START_S
-        torch.cuda._sleep(int(head_start * 1.965e9))
-        for i in range(args.steps):
-            flush()
-            if graphs:
-                graphs[i].replay()
-            else:
+        head_start = 0.0
+        if graph is not None:
+            graph.replay()
+        else:
+            # Eager steps are enqueued by Python (ctypes calls, NCCL calls,
+            # event records).  A device-side spin ahead of the first step,
+            # outside every event, lets the host fill the launch queue before
+            # the GPU starts, so that the per-step events time the kernels
+            # and collectives rather than a GPU waiting for its next launch.
+            head_start = HEAD_START_S
+            torch.cuda._sleep(int(head_start * 1.965e9))
+            for i in range(args.steps):
+                flush()
                 one_step(i, ev[i])
         enqueued = time.perf_counter() - t0
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
         clk = clocks.stop()
-        del graphs
-        ph = np.array([[e[j].elapsed_time(e[j + 1]) for j in range(6)] for e in ev])
+        del graph
+        if p2p:
+            runner.check_p2p()
+        ph = np.array([[e[j].elapsed_time(e[j + 1]) for j in range(len(names))] for e in ev])
         mine = torch.tensor([ph.sum()], dtype=torch.float64, device=dev)
         dist.all_reduce(mine, op=dist.ReduceOp.MAX)
         total_ms = float(mine.item())
         value = shape.batch * args.steps / (total_ms / 1e3)
-        phase = {k: float(v) for k, v in zip(
-            ["keys", "exchange_keys", "select", "attend", "exchange_partials", "merge"],
-            ph.mean(axis=0))}
+        phase = {k: float(v) for k, v in zip(names, ph.mean(axis=0))}
+        # per-rank step times: the limiter is the slowest rank
+        per_rank = [torch.zeros(1, dtype=torch.float64, device=dev) for _ in range(world)]
+        dist.all_gather(per_rank, torch.tensor([ph.sum() / args.steps], dtype=torch.float64,
+                                               device=dev))
 
         # end to end through the public call: pinned q in, merged out back
         e2e = None
@@ -614,7 +744,7 @@ def run_sharded(args, rank, world):
             t0 = time.perf_counter()
             for i in range(args.steps):
                 q_dev.copy_(q_host[i], non_blocking=True)
-                out = runner(q_dev, step=i)
+                out = runner(q_dev, step=args.warmup + args.steps + i)
                 out_host.copy_(out, non_blocking=True)
                 torch.cuda.current_stream().synchronize()
             t = torch.tensor([(time.perf_counter() - t0) * 1e3], dtype=torch.float64, device=dev)
@@ -622,8 +752,9 @@ def run_sharded(args, rank, world):
             e2e = {"value": shape.batch * args.steps / (float(t.item()) / 1e3),
                    "unit": "tokens/s", "h2d_bytes_per_step": int(q_host[0].numel() * 4),
                    "d2h_bytes_per_step": int(out_host.numel() * 4),
-                   "api": "santapp_b200.attention.ShardedDecodeStep (ctypes -> santa_shard_* "
-                          "C ABI, NCCL all-gathers)"}
+                   "api": "santapp_b200.attention.ShardedDecodeStep (ctypes -> "
+                          + ("santa_shard_plan / santa_shard_attend C ABI, peer-memory exchange)"
+                             if p2p else "santa_shard_* C ABI, NCCL all-gathers)")}
         peak, peak_kind = peaks()
         line = {
             "metric": METRIC,
@@ -634,30 +765,20 @@ def run_sharded(args, rank, world):
             "warmup": args.warmup,
             "ms_per_step": total_ms / args.steps,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong",
             "vs_baseline": None,
             "dtype": "bf16" if shape.kv_dtype == torch.bfloat16 else "f32",
             "data": "synthetic (seeded Gaussian-mixture keys per shard, N(0,1) values and "
                     "queries)",
-            "config": {
-                "workload": f"{base.name}-per-gpu-seqshard{world}",
-                "query_heads": shape.num_query_heads, "kv_heads": shape.num_kv_heads,
-                "head_dim": shape.head_dim, "batch": shape.batch, "context": shape.context,
-                "clusters": shape.n_clusters, "topk_clusters": shape.topk_clusters,
-                "samples": shape.samples, "recent_window": shape.recent_window, "mode": "hybrid",
-                "parallelism": (f"sequence shards x{world} (NCCL all-gather of top-k keys and "
-                                f"of (m, l, o) partials)" if args.transport == "nccl" else
-                                f"sequence shards x{world} (top-k keys and (m, l, o) partials "
-                                f"stored by the kernels into every rank's buffer over NVLink)"),
-                "l2": "flushed before every step outside the events (256 MiB write + 256 MiB "
-                      "read of another buffer)",
-            },
+            "config": decode_config(shape, "hybrid", world, p2p=p2p),
+            "shard": {"tokens": p.n_total, "clusters": p.n_clusters, "samples": p.samples},
             "phase_ms": phase,
-            "timing": ("CUDA events around each step on every rank, max over ranks of the sum; "
-                       + ("one CUDA graph per step (this library's four kernels)"
-                          if runner.p2p is not None else "eager launches")
-                       + f"; a {head_start * 1e3:.0f} ms device spin before the first step "
-                         "lets the host queue steps ahead of the GPU"),
+            "rank_ms_per_step": [round(float(x.item()), 5) for x in per_rank],
+            "timing": ("CUDA events around each step's launches on every rank, max over ranks "
+                       "of the sum; "
+                       + ("the K timed steps as one CUDA graph (flush, select, attend per step)"
+                          if p2p else f"eager launches behind a {head_start * 1e3:.0f} ms "
+                                      "device spin that lets the host queue steps ahead")),
             "wall_s": wall,
             "host_enqueue_s": enqueued,
             "clocks": clk,
@@ -669,12 +790,12 @@ def run_sharded(args, rank, world):
                          "frac": None, "traffic": None,
                          "note": "per-kernel roofline is reported by the single-GPU run"},
         }
-        if runner.p2p is not None:
+        if p2p:
             bad = torch.tensor([int(runner.p2p_error.item())], device=dev)
             dist.all_reduce(bad, op=dist.ReduceOp.MAX)
             line["p2p_wait_timeouts"] = int(bad.item())
-            # the same step through the NCCL exchanges: same kernels, same merge
-            # order, so the outputs must agree bit for bit
+            # the same step through the NCCL exchanges: same kernels, same
+            # merge arithmetic, so the outputs must agree bit for bit
             ref = ShardedDecodeStep(p.keys, p.values, summ,
                                     num_query_heads=shape.num_query_heads, n_total=p.n_total,
                                     topk_clusters=shape.topk_clusters, samples=p.samples,
@@ -687,6 +808,9 @@ def run_sharded(args, rank, world):
             diff = torch.tensor([float((a - b).abs().max())], dtype=torch.float64, device=dev)
             dist.all_reduce(diff, op=dist.ReduceOp.MAX)
             line["p2p_vs_nccl_max_abs_diff"] = float(diff.item())
+        if rank == 0 and not args.no_cpu_baseline and not args.profile:
+            line["cpu_baseline"] = cpu_baseline_sample(args, shape)
+        dist.barrier()
         return line if rank == 0 else None
     finally:
         dist.barrier()
@@ -701,58 +825,48 @@ def run_sharded(args, rank, world):
 # reference arm: the CPU restatement on all host cores
 # ---------------------------------------------------------------------------
 
-_REF = {}
-
-
-def _ref_worker(task):
-    b, h, step = task
-    shape, data, queries, seed = _REF["shape"], _REF["data"], _REF["queries"], _REF["seed"]
-    _cpu_head_call(shape, data, queries[step][b, h], b, h, step, seed)
-    return 1
-
-
 def run_reference(args, rank, world):
-    import multiprocessing as mp
+    """The reference's decode path on the host cores: the torch-CPU
+    restatement of SantaPlusEngine._approximate_attention for the hybrid
+    estimator (one call per (sequence, query head), torch intra-op threads
+    on every core), on the same workload and config as our arm.  Each step
+    decodes a bounded sample of that workload (one sequence's query heads
+    over its full cache), reported as tokens/s.  Under torchrun only rank 0
+    runs."""
     if rank != 0:
         return None
     shape = WORKLOADS[args.workload]
     if shape is None:
         raise SystemExit("the reference arm times the decode workloads")
-    from santapp_b200.synthetic import scaled_shape
-    # one sequence's cache (its 4 KV heads) is enough to time per-token cost;
-    # each step decodes that sequence's Hq heads across all host cores
-    sh1 = scaled_shape(shape, batch=1, steps=args.steps + args.warmup)
-    w = make_decode_workload(sh1, seed=args.seed, device="cpu")
-    pairs = [(0, kv) for kv in range(shape.num_kv_heads)]
-    data = _oracle_inputs(sh1, w, None, pairs)
-    _REF.update(shape=sh1, data=data, queries=w.queries.numpy(), seed=args.seed)
     cores = os.cpu_count() or 1
-    ctx = mp.get_context("fork")  # no CUDA in this process: fork shares the cache arrays
-    with ctx.Pool(cores) as pool:
-        for i in range(args.warmup):
-            pool.map(_ref_worker, [(0, h, i) for h in range(shape.num_query_heads)])
-        t0 = time.perf_counter()
-        for i in range(args.steps):
-            step = args.warmup + i
-            pool.map(_ref_worker, [(0, h, step) for h in range(shape.num_query_heads)])
-        dt = time.perf_counter() - t0
+    torch.set_num_threads(cores)
+    w, summ = _port_sample(shape, args.seed)
+    gen = torch.Generator().manual_seed(args.seed)
+    n_q = w.queries.shape[0]
+    for i in range(args.warmup):
+        _port_step(shape, w, summ, i % n_q, gen)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        _port_step(shape, w, summ, (args.warmup + i) % n_q, gen)
+    dt = time.perf_counter() - t0
     value = args.steps / dt
-    sample = (f"sequence 0 of the batch ({shape.num_query_heads} query-head calls per step, "
-              f"{shape.num_kv_heads} KV heads x {shape.context} tokens), numpy/C oracle")
+    sample = (f"{args.steps} decode steps of sequence 0 of the batch ({shape.num_query_heads} "
+              f"query-head calls per step over {shape.num_kv_heads} KV heads x {shape.context} "
+              "tokens), torch-CPU restatement of the reference's per-head "
+              "_approximate_attention (oracle/santa_torch_port.py)")
     return {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32",
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded Gaussian-mixture keys, N(0,1) values and queries)",
-        "config": {"workload": shape.name, "mode": args.mode, "batch": shape.batch,
-                   "context": shape.context, "timed_batch": 1},
+        "config": decode_config(shape, args.mode, world, p2p=args.transport == "p2p"),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-        "note": "the reference is pure Python/PyTorch and is not present at run time; its "
-                "CPU algorithm is timed through the oracle restatement",
+        "note": "the reference is Python over torch and is not present at run time; its "
+                "per-head CPU path is timed through a torch restatement with the same ops",
     }
 
 

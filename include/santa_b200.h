@@ -385,28 +385,39 @@ int santa_kmeans_plusplus(const float *x, const int64_t *rows, const float *xx, 
 /* Peer-memory exchange (optional): every rank allocates one exchange buffer
  * (santa_p2p_alloc, santa_p2p_buffer_bytes), shares its IPC handle, maps the
  * others' (santa_p2p_ipc_open) and passes the table of all ranks' buffers as
- * mapped in this process.  The kernels then write candidate keys and partials
- * straight into every rank's buffer and signal a per-rank flag; the consuming
- * kernels wait for the flags (bounded: error_flag is set to 1 if a peer never
- * signals within ~2 s) instead of the caller running two all-gathers.  epoch =
- * the step number + 1, increasing per step; the same epoch for the
- * candidates, plan, execute and merge calls of one step. */
+ * mapped in this process.  A step is then two launches and no collective:
+ *   santa_shard_plan   scores this shard's clusters, stores its top-k keys
+ *                      straight into every rank's buffer, waits for every
+ *                      rank's keys of the same (sequence, query head), and
+ *                      selects and draws as with gathered keys;
+ *   santa_shard_attend the gather attention, then stores this shard's
+ *                      partials into every rank's buffer, waits for every
+ *                      rank's and merges them into out / lse / ess.
+ * Every 8-byte word a kernel stores into a peer's buffer carries the step's
+ * epoch beside its data (no flags, no fences).  Waits are bounded by
+ * wait_limit_us (0: 2 s); a wait that runs out sets *error_flag to 1, and the
+ * outputs of that step (and of later steps until the flag is cleared) are
+ * NaN.  epoch = the step number + 1, increasing by one per step, the same
+ * for the plan and attend calls of one step on every rank; all ranks make the
+ * same calls in the same order.  The plan launch needs all of its thread-block
+ * clusters resident at once (SANTA_ERR_UNSUPPORTED otherwise) and k <= 32;
+ * global cluster ids must stay below 2^24 - 1. */
 typedef struct SantaP2P {
     void *const *peer_buffers;   /* device array [num_shards] of buffers (own at shard_index) */
-    void *local_buffer;          /* this rank's buffer */
+    void *local_buffer;          /* this rank's buffer (256-byte aligned) */
     uint64_t epoch;
     int32_t *error_flag;         /* device int32 */
     int32_t rows;                /* B * Hq */
     int32_t keys_per_row;        /* topk_clusters */
     int32_t partial_floats;      /* SANTA_PARTIAL_FLOATS(head_dim) */
-    int32_t reserved;
+    int32_t wait_limit_us;       /* bound of every wait; 0 = 2 s */
 } SantaP2P;
 
 #define SANTA_IPC_HANDLE_BYTES 64
 
 int santa_p2p_buffer_bytes(int32_t num_shards, int32_t rows, int32_t keys_per_row,
                            int32_t head_dim, size_t *bytes);
-/* cudaMalloc'd exchange buffer, zeroed (flags start at epoch 0). */
+/* cudaMalloc'd exchange buffer, zeroed (no word carries an epoch tag). */
 int santa_p2p_alloc(size_t bytes, void **buffer);
 int santa_p2p_free(void *buffer);
 int santa_p2p_ipc_handle(void *buffer, void *handle);
@@ -422,7 +433,7 @@ typedef struct SantaShard {
     int32_t cluster_base;        /* global id of row 0 of this shard's summary */
     int32_t reserved;
     const uint64_t *candidates;  /* plan: [num_shards][B*Hq][topk_clusters] gathered keys
-                                    (ignored with p2p: they are in the exchange buffer) */
+                                    (ignored with p2p: the plan launch exchanges them) */
     const SantaP2P *p2p;         /* NULL: the caller exchanges keys and partials */
 } SantaShard;
 
@@ -450,7 +461,8 @@ int santa_shard_execute(const SantaGeometry *geo, const SantaDecodeParams *p, co
                         const SantaSummary *summary, const SantaShard *shard, float *partial,
                         void *workspace, size_t workspace_bytes, cudaStream_t stream);
 
-/* Selection readout of santa_shard_plan (arguments of santa_decode_select). */
+/* Selection readout of santa_shard_plan (arguments of santa_decode_select);
+ * with shard->p2p it takes part in the key exchange like santa_shard_plan. */
 int santa_shard_select(const SantaGeometry *geo, const SantaDecodeParams *p, const float *q,
                        const void *key_cache, const void *value_cache,
                        const SantaSummary *summary, const SantaShard *shard,
@@ -458,13 +470,21 @@ int santa_shard_select(const SantaGeometry *geo, const SantaDecodeParams *p, con
                        int32_t *n_exact, void *workspace, size_t workspace_bytes,
                        cudaStream_t stream);
 
-/* partials: [num_shards][rows][SANTA_PARTIAL_FLOATS(head_dim)]; rows = B*Hq
- * (with p2p: NULL, read from the exchange buffer after the peers' flags).
+/* Peer-memory form of santa_shard_execute + exchange 2 + santa_merge_shards
+ * in one launch (shard->p2p required): out [B*Hq][head_dim] (16-byte aligned
+ * for head_dim 128, 8-byte for 64), lse and ess as santa_decode writes them,
+ * identical on every rank and bit-identical to the NCCL-exchange path. */
+int santa_shard_attend(const SantaGeometry *geo, const SantaDecodeParams *p, const float *q,
+                       const void *key_cache, const void *value_cache,
+                       const SantaSummary *summary, const SantaShard *shard, float *out,
+                       float *lse, float *ess, void *workspace, size_t workspace_bytes,
+                       cudaStream_t stream);
+
+/* partials: [num_shards][rows][SANTA_PARTIAL_FLOATS(head_dim)]; rows = B*Hq.
  * out [rows][head_dim], lse [rows] (natural log) and ess [rows] (may be
  * NULL) as santa_decode writes them. */
 int santa_merge_shards(int32_t rows, int32_t head_dim, int32_t num_shards, const float *partials,
-                       const SantaP2P *p2p, int32_t shard_index, float *out, float *lse,
-                       float *ess, cudaStream_t stream);
+                       float *out, float *lse, float *ess, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -87,3 +87,15 @@ __device__ __forceinline__ int warp_sum_int(int v) {
     } while (0)
 
 void santa_set_cuda_error(cudaError_t e);
+
+namespace santa {
+// Per-device launch set-up, safe from several host threads and for one
+// process that drives several GPUs (santa_lib.cu).
+// Raises fn's dynamic shared memory limit on the current device to at least
+// `bytes` (cudaFuncSetAttribute is a per-device setting).
+int ensure_dyn_smem(const void *fn, size_t bytes);
+// Multiprocessor count of the current device.
+int num_sms();
+// A device attribute of the current device (0 if it cannot be read).
+int device_attr(cudaDeviceAttr attr);
+}  // namespace santa

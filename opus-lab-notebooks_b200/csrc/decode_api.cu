@@ -214,14 +214,17 @@ static int bind_p2p(const SantaGeometry *geo, const SantaDecodeParams *p,
     memset(&a->p2p, 0, sizeof(a->p2p));
     const SantaP2P *c = shard->p2p;
     if (!c) return SANTA_OK;
-    if (!c->peer_buffers || !c->local_buffer || !c->error_flag || c->epoch == 0)
+    if (!c->peer_buffers || !c->local_buffer || !c->error_flag || c->epoch == 0 ||
+        c->wait_limit_us < 0)
         return SANTA_ERR_INVALID_ARGUMENT;
     if (c->rows != geo->batch * geo->num_kv_heads * geo->group ||
         c->keys_per_row != p->topk_clusters || c->partial_floats != geo->head_dim + 8)
         return SANTA_ERR_INVALID_ARGUMENT;
+    if (((uintptr_t)c->local_buffer & 255) != 0) return SANTA_ERR_INVALID_ARGUMENT;
     a->p2p.peers = c->peer_buffers;
     a->p2p.local = (unsigned char *)c->local_buffer;
     a->p2p.epoch = c->epoch;
+    a->p2p.wait_ns = (unsigned long long)(c->wait_limit_us > 0 ? c->wait_limit_us : 2000000) * 1000ull;
     a->p2p.err = c->error_flag;
     a->p2p.rank = shard->shard_index;
     a->p2p.n = shard->num_shards;
@@ -262,12 +265,16 @@ static int prepare_shard(const SantaGeometry *geo, const SantaDecodeParams *p, c
     a->num_shards = shard->num_shards;
     a->shard_index = shard->shard_index;
     a->shard_cands = need_candidates ? shard->candidates : nullptr;
-    st = bind_p2p(geo, p, shard, a);
-    if (st) return st;
-    if (need_candidates && a->p2p.peers) {  // the gathered keys live in the exchange buffer
-        const size_t per = (size_t)a->p2p.rows * a->p2p.kk;
-        a->shard_cands = (const uint64_t *)(a->p2p.local + kP2PKeys) +
-                         (size_t)(a->p2p.epoch & 1) * a->p2p.n * per;
+    if (need_candidates && shard->p2p) {
+        // the selection launch runs the candidates pass and the key exchange
+        // itself (peer memory, low-latency words whose keys carry 24-bit ids)
+        st = bind_p2p(geo, p, shard, a);
+        if (st) return st;
+        if ((int64_t)shard->cluster_base + summary->max_groups >= 0xFFFFFFll)
+            return SANTA_ERR_UNSUPPORTED;
+        if (shard->p2p->partial_floats != geo->head_dim + 8) return SANTA_ERR_INVALID_ARGUMENT;
+        a->shard_cands = nullptr;
+        if (!select_group_supported(*a)) return SANTA_ERR_UNSUPPORTED;
     }
     return SANTA_OK;
 }
@@ -308,12 +315,34 @@ extern "C" int santa_shard_execute(const SantaGeometry *geo, const SantaDecodePa
     int st = check_shard(geo, p, shard, false);
     if (st) return st;
     DecodeArgs a;
+    if (shard->p2p) return SANTA_ERR_INVALID_ARGUMENT;  // santa_shard_attend merges in place
+    st = prepare_decode(geo, p, q, key_cache, value_cache, summary, nullptr, nullptr, false,
+                        workspace, workspace_bytes, &a);
+    if (st) return st;
+    a.part_out = partial;
+    return launch_execute(a, stream);
+}
+
+extern "C" int santa_shard_attend(const SantaGeometry *geo, const SantaDecodeParams *p,
+                                  const float *q, const void *key_cache, const void *value_cache,
+                                  const SantaSummary *summary, const SantaShard *shard, float *out,
+                                  float *lse, float *ess, void *workspace, size_t workspace_bytes,
+                                  cudaStream_t stream) {
+    if (!out || !shard || !shard->p2p) return SANTA_ERR_INVALID_ARGUMENT;
+    int st = check_shard(geo, p, shard, false);
+    if (st) return st;
+    // the merged rows are written with one vector store per lane
+    if (((uintptr_t)out & (geo->head_dim == 128 ? 15 : 7)) != 0) return SANTA_ERR_INVALID_ARGUMENT;
+    DecodeArgs a;
     st = prepare_decode(geo, p, q, key_cache, value_cache, summary, nullptr, nullptr, false,
                         workspace, workspace_bytes, &a);
     if (st) return st;
     st = bind_p2p(geo, p, shard, &a);
     if (st) return st;
-    a.part_out = partial;
+    a.out = out;
+    a.lse = lse;
+    a.ess = ess;
+    a.part_out = (float *)(a.p2p.local + p2p_stage_offset(a.p2p.n, a.p2p.rows, a.p2p.kk, a.p2p.pf));
     return launch_execute(a, stream);
 }
 
@@ -334,28 +363,10 @@ extern "C" int santa_shard_select(const SantaGeometry *geo, const SantaDecodePar
 }
 
 extern "C" int santa_merge_shards(int32_t rows, int32_t head_dim, int32_t num_shards,
-                                  const float *partials, const SantaP2P *p2p,
-                                  int32_t shard_index, float *out, float *lse, float *ess,
+                                  const float *partials, float *out, float *lse, float *ess,
                                   cudaStream_t stream) {
     if (rows <= 0 || num_shards < 1 || num_shards > SANTA_MAX_SHARDS) return SANTA_ERR_INVALID_ARGUMENT;
     if (head_dim != 64 && head_dim != 128) return SANTA_ERR_UNSUPPORTED;
-    if ((!partials && !p2p) || !out) return SANTA_ERR_INVALID_ARGUMENT;
-    P2PArgs c;
-    memset(&c, 0, sizeof(c));
-    if (p2p) {
-        if (!p2p->peer_buffers || !p2p->local_buffer || !p2p->error_flag || p2p->epoch == 0 ||
-            p2p->rows != rows || p2p->partial_floats != head_dim + 8 || shard_index < 0 ||
-            shard_index >= num_shards)
-            return SANTA_ERR_INVALID_ARGUMENT;
-        c.peers = p2p->peer_buffers;
-        c.local = (unsigned char *)p2p->local_buffer;
-        c.epoch = p2p->epoch;
-        c.err = p2p->error_flag;
-        c.rank = shard_index;
-        c.n = num_shards;
-        c.rows = rows;
-        c.kk = p2p->keys_per_row;
-        c.pf = p2p->partial_floats;
-    }
-    return launch_merge_shards(rows, head_dim, num_shards, partials, c, out, lse, ess, stream);
+    if (!partials || !out) return SANTA_ERR_INVALID_ARGUMENT;
+    return launch_merge_shards(rows, head_dim, num_shards, partials, out, lse, ess, stream);
 }

@@ -185,7 +185,9 @@ struct GatherGeom {
 
 template <int D>
 inline size_t gather_smem_bytes(int BH) {
-    return 128 + (size_t)kGW * GatherGeom<D>::WARP + ((size_t)BH + 1) * 4;
+    // rings, segment prefix [BH + 1], completed-segment bitmap [ceil(BH / 32)]
+    return 128 + (size_t)kGW * GatherGeom<D>::WARP + ((size_t)BH + 1) * 4 +
+           (size_t)((BH + 31) / 32) * 4;
 }
 
 // One merged output element (head hh, dim dd) of segment bh: out / lse / ess,
@@ -198,21 +200,17 @@ __device__ __forceinline__ void write_merged(const DecodeArgs &a, int bh, int hh
     const int g = a.geo.group, PSTR = partial_stride(D);
     const int64_t oh = (int64_t)bh * g + hh;  // (b * Hkv + kv) * g + hh
     if (a.part_out) {  // sequence shard: the unnormalised partial
-        const int nr = a.p2p.peers ? a.p2p.n : 1;
-        for (int r = 0; r < nr; ++r) {  // every rank's buffer, or part_out
-            float *po = (a.p2p.peers ? p2p_part_slot(a.p2p, a.p2p.peers[r], a.p2p.rank)
-                                     : a.part_out) + oh * PSTR;
-            po[8 + dd] = acc;
-            if (dd == 0) {
-                po[0] = M;
-                po[1] = L;
-                po[2] = MS;
-                po[3] = E1;
-                po[4] = E2;
-                po[5] = (float)ns;
-                po[6] = 0.f;
-                po[7] = 0.f;
-            }
+        float *po = a.part_out + oh * PSTR;
+        po[8 + dd] = acc;
+        if (dd == 0) {
+            po[0] = M;
+            po[1] = L;
+            po[2] = MS;
+            po[3] = E1;
+            po[4] = E2;
+            po[5] = (float)ns;
+            po[6] = 0.f;
+            po[7] = 0.f;
         }
         return;
     }
@@ -539,6 +537,125 @@ __device__ void merge_pairs_direct(const DecodeArgs &a, const int *seg, const in
     }
 }
 
+// Peer-memory exchange of the shard partials, fused into the attention
+// kernel (the segments `done` marks, which this CTA merged into this rank's
+// partial rows in the stage area).  Every CTA first sends all of its rows to
+// every rank (16-byte lines, each 8-byte word tagged with the epoch), and
+// only then waits for the other ranks' rows of the same segments: no CTA
+// waits before it has sent, so every wait ends once the peers' kernels reach
+// their own tails (all CTAs of this kernel are resident: one per SM).  Then
+// one warp per (segment, query head) merges the ranks' partials in ascending
+// rank order (the merge kernel's arithmetic, so both exchange paths give the
+// same bits) into out / lse / ess.  A wait that runs out of time sets the
+// error flag and the rows it could not complete, and every row after it in
+// this CTA, come out NaN.
+template <int D>
+__device__ void fused_shard_exchange(const DecodeArgs &a, const unsigned *done, int BH,
+                                     float *hdr_smem) {
+    constexpr int VPL = D / 32, LPL = VPL / 2;
+    const int g = a.geo.group, pf = partial_stride(D), pl = pf / 2;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n = a.p2p.n;
+    const uint32_t tag = (uint32_t)a.p2p.epoch;
+    const uint64_t tg = (uint64_t)tag << 32;
+    const float *stage = a.part_out;
+    // 1. send: lines of each completed segment's g rows, to every rank
+    for (int w = 0; w < (BH + 31) / 32; ++w) {
+        for (unsigned m = done[w]; m; m &= m - 1) {
+            const int bh = 32 * w + __ffs(m) - 1;
+            const int nl = g * pl;  // lines of the segment (rows bh*g .. bh*g+g-1 are contiguous)
+            const float2 *src = (const float2 *)(stage + (int64_t)bh * g * pf);
+            for (int i = tid; i < n * nl; i += kGThreads) {
+                const int r = i / nl, j = i - r * nl;
+                const float2 v = src[j];
+                st_relaxed_sys_v2(p2p_part_slot(a.p2p, a.p2p.peers[r], a.p2p.rank) +
+                                      (int64_t)bh * g * pl + j,
+                                  tg | __float_as_uint(v.x), tg | __float_as_uint(v.y));
+            }
+        }
+    }
+    // 2. wait and merge: one warp per (segment, head)
+    volatile int32_t *errp = a.p2p.err;
+    bool ok = *errp == 0;  // a wait of the selection already gave up: NaN rows
+    const uint64_t t0 = p2p_now_ns();
+    float *sh = hdr_smem + warp * (SANTA_MAX_SHARDS * 8);  // [rank][8] headers
+    int k = 0;
+    for (int w = 0; w < (BH + 31) / 32; ++w) {
+        for (unsigned m = done[w]; m; m &= m - 1) {
+            const int bh = 32 * w + __ffs(m) - 1;
+            for (int hh = 0; hh < g; ++hh, ++k) {
+                if ((k % kGW) != warp) continue;
+                const int64_t oh = (int64_t)bh * g + hh;
+                // headers: lane -> rank r0 + lane / 4, line lane % 4 (lines 0-2
+                // hold m l ms e1 e2 samples)
+                for (int r0 = 0; r0 < n; r0 += 8) {
+                    const int r = r0 + (lane >> 2), j = lane & 3;
+                    if (r < n && j < 3) {
+                        const float2 v = ll_part_wait(
+                            a.p2p, p2p_part_slot(a.p2p, a.p2p.local, r) + oh * pl + j, tag, t0, ok);
+                        sh[r * 8 + 2 * j] = v.x;
+                        sh[r * 8 + 2 * j + 1] = v.y;
+                    }
+                }
+                __syncwarp();
+                const ShardMerged s =
+                    shard_merge_header(n, [&](int r, int j) { return sh[r * 8 + j]; });
+                float acc[VPL];
+#pragma unroll
+                for (int e = 0; e < VPL; ++e) acc[e] = 0.f;
+                for (int r0 = 0; r0 < n; r0 += 8) {
+                    ulonglong2 v[8][LPL];
+#pragma unroll
+                    for (int rr = 0; rr < 8; ++rr) {  // one batch of loads
+                        if (r0 + rr < n) {
+                            const ulonglong2 *p = p2p_part_slot(a.p2p, a.p2p.local, r0 + rr) +
+                                                  oh * pl + 4 + LPL * lane;
+#pragma unroll
+                            for (int e = 0; e < LPL; ++e) v[rr][e] = ld_relaxed_sys_v2(p + e);
+                        }
+                    }
+#pragma unroll
+                    for (int rr = 0; rr < 8; ++rr) {
+                        const int r = r0 + rr;
+                        if (r >= n || !(sh[r * 8 + 1] > 0.f)) continue;
+                        const float f = exp2f(sh[r * 8] - s.M);
+                        const ulonglong2 *p =
+                            p2p_part_slot(a.p2p, a.p2p.local, r) + oh * pl + 4 + LPL * lane;
+#pragma unroll
+                        for (int e = 0; e < LPL; ++e) {
+                            float2 x;
+                            if ((uint32_t)(v[rr][e].x >> 32) == tag &&
+                                (uint32_t)(v[rr][e].y >> 32) == tag)
+                                x = make_float2(__uint_as_float((uint32_t)v[rr][e].x),
+                                                __uint_as_float((uint32_t)v[rr][e].y));
+                            else
+                                x = ll_part_wait(a.p2p, p + e, tag, t0, ok);
+                            acc[2 * e] = fmaf(x.x, f, acc[2 * e]);
+                            acc[2 * e + 1] = fmaf(x.y, f, acc[2 * e + 1]);
+                        }
+                    }
+                }
+                ok = __all_sync(0xffffffffu, ok);
+                const float sc = shard_out_scale(s);
+                const float nan = __int_as_float(0x7FC00000);
+                float *o = a.out + oh * D + VPL * lane;
+                if constexpr (VPL == 4)
+                    *(float4 *)o = ok ? make_float4(acc[0] * sc, acc[1] * sc, acc[2] * sc,
+                                                    acc[3] * sc)
+                                      : make_float4(nan, nan, nan, nan);
+                else
+                    *(float2 *)o = ok ? make_float2(acc[0] * sc, acc[1] * sc)
+                                      : make_float2(nan, nan);
+                if (lane == 0) {
+                    if (a.lse) a.lse[oh] = ok ? shard_lse(s) : nan;
+                    if (a.ess) a.ess[oh] = ok ? shard_ess(s) : nan;
+                }
+                __syncwarp();  // sh is rewritten by the warp's next row
+            }
+        }
+    }
+}
+
 // A row entry prefetched ahead of its copy.
 struct RowEntry {
     int kind;   // 0 none, 1 union row, 2 recent row, 3 sampled row
@@ -581,6 +698,8 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
     unsigned char *base = (unsigned char *)(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
     unsigned char *wbase = base + warp * GG::WARP;     // this warp's ring
     int *pre = (int *)(base + kGW * GG::WARP);         // segment prefix [BH + 1]
+    unsigned *done_bits = (unsigned *)(pre + BH + 1);  // segments this CTA merged (p2p)
+    const bool fused = a.p2p.peers != nullptr;
     __shared__ float s_wfac[SANTA_MAX_GROUP][kGW];     // CTA fold: factor per head and warp
     // The merge path reads the arguments from a shared-memory copy: after the
     // row loops the constant cache no longer holds the fields only it uses
@@ -610,6 +729,8 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
             carry += __shfl_sync(0xffffffffu, x, 31);
         }
         if (lane == 0) pre[0] = 0;
+    } else if (fused) {
+        for (int i = tid - 32; i < (BH + 31) / 32; i += kGThreads - 32) done_bits[i] = 0u;
     }
     __syncthreads();  // the only block-wide barrier
 
@@ -994,6 +1115,7 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
             const bool all_small = __all_sync(0xffffffffu, small);
             if (done) {
                 ma.ws.counters[bh] = 0;  // every CTA of the segment has arrived
+                if (fused) atomicOr(done_bits + (bh >> 5), 1u << (bh & 31));
                 if (rank < kMergeSegs) {
                     m_seg[rank] = bh;
                     m_first[rank] = first;
@@ -1033,17 +1155,14 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
         for (int bh = 0; bh < BH; ++bh) {
             if (pre[bh + 1] != pre[bh]) continue;
             const int b = bh / ma.geo.num_kv_heads, kv = bh - b * ma.geo.num_kv_heads;
+            if (fused && tid == 0) atomicOr(done_bits + (bh >> 5), 1u << (bh & 31));
             for (int i = tid; i < g * D; i += kGThreads) {
                 const int h = i / D, d = i - h * D;
                 const int64_t oh = (int64_t)b * ma.geo.num_kv_heads * g + (int64_t)kv * g + h;
                 if (ma.part_out) {
-                    const int nr = ma.p2p.peers ? ma.p2p.n : 1;
-                    for (int r = 0; r < nr; ++r) {
-                        float *po = (ma.p2p.peers ? p2p_part_slot(ma.p2p, ma.p2p.peers[r], ma.p2p.rank)
-                                                 : ma.part_out) + oh * PSTR;
-                        po[8 + d] = 0.f;
-                        if (d < 8) po[d] = (d == 0 || d == 2) ? -INFINITY : 0.f;
-                    }
+                    float *po = ma.part_out + oh * PSTR;
+                    po[8 + d] = 0.f;
+                    if (d < 8) po[d] = (d == 0 || d == 2) ? -INFINITY : 0.f;
                     continue;
                 }
                 ma.out[oh * D + d] = 0.f;
@@ -1053,6 +1172,10 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
                 }
             }
         }
+    }
+    if (fused) {
+        __syncthreads();  // this CTA's partial rows and done bits are in place
+        fused_shard_exchange<D>(ma, done_bits, BH, (float *)base);
     }
 }
 
@@ -1079,25 +1202,14 @@ static int launch_execute_d(DecodeArgs &a, cudaStream_t stream) {
     // the segment counters are zeroed by the selection kernel and put back
     // to zero by each segment's merging CTA
     if (a.geo.kv_dtype == SANTA_DTYPE_BF16) {
-        static size_t done = 0;
         const size_t sm = gather_smem_bytes<D>(BH);
         if (sm > 227 * 1024) return SANTA_ERR_UNSUPPORTED;
-        if (done < sm) {
-            SANTA_CUDA_CHECK(cudaFuncSetAttribute(decode_attend_gather_kernel<D>,
-                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                  (int)sm));
-            done = sm;
-        }
+        if (int st = ensure_dyn_smem((const void *)decode_attend_gather_kernel<D>, sm)) return st;
         decode_attend_gather_kernel<D><<<num_sms(), kGThreads, sm, stream>>>(a);
     } else {
-        static size_t done = 0;
         const size_t sm = simt_smem_bytes<D>(Gmax);
-        if (done < sm) {
-            SANTA_CUDA_CHECK(cudaFuncSetAttribute(decode_attend_simt_kernel<D, float>,
-                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                  (int)sm));
-            done = sm;
-        }
+        if (int st = ensure_dyn_smem((const void *)decode_attend_simt_kernel<D, float>, sm))
+            return st;
         dim3 grid(a.nsplit, BH);
         decode_attend_simt_kernel<D, float><<<grid, kSimtThreads, sm, stream>>>(a);
     }

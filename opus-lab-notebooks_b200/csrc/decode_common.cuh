@@ -101,33 +101,43 @@ inline size_t decode_ws_layout(int BH, int G, int g, int S, int n_slots, int D, 
 
 // ---------------------------------------------------------------------------
 // peer-memory exchange between sequence shards (one buffer per rank, mapped
-// into every other rank's address space):
-//   [0, 512)      flags  u64 [2 exchanges][32 ranks]: last epoch rank r signalled
-//   [512, 1024)   unused (set-up marker at 768)
-//   [1024, ...)   keys   u64 [2 parities][n ranks][rows * kk]
-//   parts         f32    [2 parities][n ranks][rows][pf]
-// Epoch e (the step number + 1, increasing) uses parity e & 1, so a rank one
-// step ahead never overwrites what a slower peer still reads (a rank cannot
-// get two steps ahead: its next use of a parity waits for the peers' flags of
-// the step in between).  The producing kernels (candidates, attention) only
-// store; the consuming kernels (threshold selection, shard merge) raise this
-// rank's flag for the epoch and wait for every rank's.
+// into every other rank's address space through CUDA IPC).  Low-latency
+// protocol: every 8-byte word a producer stores into a peer's buffer carries
+// the step's epoch tag next to its data, so a consumer polls its own (local)
+// buffer until each word it needs shows the current tag.  No flags and no
+// memory fences: an aligned 8-byte store is single-copy atomic, so a word
+// with the right tag also holds the right data.
+//   [0, 1024)     set-up marker (at 768)
+//   keys   u64   [2 parities][n ranks][rows][kk]  candidate keys, tag in
+//                bits 24-31 (see ll_key_encode)
+//   parts  u64x2 [2 parities][n ranks][rows][pf / 2] partials: one 16-byte
+//                line holds two floats, each word = tag << 32 | float bits
+//   stage  f32   [rows][pf]  this rank's partials before they are sent
+//                (local use only)
+// Epoch e (> 0, increasing by one per step) uses parity e & 1: a rank cannot
+// run two steps ahead of a peer, because each step's selection waits for
+// every peer's keys of that step, which a peer only sends after it finished
+// reading the previous step's partials (the kernels of one rank run in
+// stream order).
 // ---------------------------------------------------------------------------
 struct P2PArgs {
     void *const *peers;      // device array [n]: every rank's buffer as mapped here
     unsigned char *local;    // this rank's buffer
     unsigned long long epoch;
+    unsigned long long wait_ns;  // bound of every wait (globaltimer ns)
     int32_t *err;            // set to 1 when a wait for a peer gave up
     int rank, n, rows, kk, pf;
 };
-constexpr size_t kP2PFlags = 0, kP2PKeys = 1024;
+constexpr size_t kP2PKeys = 1024;
 __host__ __device__ inline size_t p2p_parts_offset(int n, int rows, int kk) {
     return (kP2PKeys + (size_t)2 * n * rows * kk * 8 + 255) / 256 * 256;
 }
-__host__ __device__ inline size_t p2p_buffer_bytes(int n, int rows, int kk, int pf) {
-    return p2p_parts_offset(n, rows, kk) + (size_t)2 * n * rows * pf * 4;
+__host__ __device__ inline size_t p2p_stage_offset(int n, int rows, int kk, int pf) {
+    return p2p_parts_offset(n, rows, kk) + (size_t)2 * n * rows * pf * 8;
 }
-
+__host__ __device__ inline size_t p2p_buffer_bytes(int n, int rows, int kk, int pf) {
+    return p2p_stage_offset(n, rows, kk, pf) + (size_t)rows * pf * 4;
+}
 struct DecodeArgs {
     SantaGeometry geo;
     SantaDecodeParams p;
@@ -153,55 +163,135 @@ struct DecodeArgs {
     P2PArgs p2p;                  // peers == nullptr: the caller exchanges
 };
 
+// rank r's key list region (this step's parity) in the buffer at base
 __device__ __forceinline__ uint64_t *p2p_key_slot(const P2PArgs &c, void *base, int r) {
     return (uint64_t *)((unsigned char *)base + kP2PKeys) +
            ((size_t)((c.epoch & 1) * c.n + r) * c.rows * c.kk);
 }
-__device__ __forceinline__ float *p2p_part_slot(const P2PArgs &c, void *base, int r) {
-    return (float *)((unsigned char *)base + p2p_parts_offset(c.n, c.rows, c.kk)) +
-           ((size_t)((c.epoch & 1) * c.n + r) * c.rows * c.pf);
+// rank r's partial lines (this step's parity) in the buffer at base
+__device__ __forceinline__ ulonglong2 *p2p_part_slot(const P2PArgs &c, void *base, int r) {
+    return (ulonglong2 *)((unsigned char *)base + p2p_parts_offset(c.n, c.rows, c.kk)) +
+           ((size_t)((c.epoch & 1) * c.n + r) * c.rows * (c.pf / 2));
 }
-__device__ __forceinline__ unsigned long long p2p_ld_acquire(const unsigned long long *p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
+__device__ __forceinline__ float *p2p_stage(const P2PArgs &c) {
+    return (float *)(c.local + p2p_stage_offset(c.n, c.rows, c.kk, c.pf));
+}
+
+// tags: 8 bits (never 0) inside a key, 32 bits (never 0 in practice) beside
+// a float; a zeroed buffer and the previous use of a parity (epoch - 2) never
+// match the current epoch
+__device__ __forceinline__ uint32_t ll_key_tag(unsigned long long epoch) {
+    return (uint32_t)(epoch % 255ull) + 1u;
+}
+// key = order bits << 32 | (0xFFFFFFFF - global id) with global id < 2^24 - 1
+// (the top byte of the low word is 0xFF and carries the tag instead); key 0
+// (no key) is sent as the tag alone
+__device__ __forceinline__ uint64_t ll_key_encode(uint64_t key, uint32_t tag) {
+    return (key & 0xFFFFFFFF00FFFFFFull) | ((uint64_t)tag << 24);
+}
+__device__ __forceinline__ uint64_t ll_key_decode(uint64_t w) {
+    const uint64_t lo = w & 0xFFFFFFull;
+    return ((w >> 32) == 0ull && lo == 0ull) ? 0ull : ((w & 0xFFFFFFFF00000000ull) | 0xFF000000ull | lo);
+}
+__device__ __forceinline__ void st_relaxed_sys(uint64_t *p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys(const uint64_t *p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ void p2p_st_release(unsigned long long *p, unsigned long long v) {
-    asm volatile("st.release.sys.global.u64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys_v2(ulonglong2 *p, uint64_t x, uint64_t y) {
+    asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};\n" ::"l"(p), "l"(x), "l"(y)
+                 : "memory");
 }
-// one thread: wait (at most ~2 s) until every rank signalled exchange ex for
-// this epoch; false (and the error flag set) if one never did
-__device__ inline bool p2p_wait(const P2PArgs &c, int ex) {
-    const unsigned long long *fl = (const unsigned long long *)(c.local + kP2PFlags) + ex * 32;
-    uint64_t t0 = 0;
-    asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t0));
-    for (int r = 0; r < c.n; ++r) {
-        for (uint32_t i = 0;; ++i) {
-            if (p2p_ld_acquire(fl + r) >= c.epoch) break;
-            if ((i & 63u) == 63u) {
-                uint64_t t;
-                asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
-                if (t - t0 > 2000000000ull) {
-                    atomicExch(c.err, 1);
-                    return false;
-                }
-            }
+__device__ __forceinline__ ulonglong2 ld_relaxed_sys_v2(const ulonglong2 *p) {
+    ulonglong2 v;
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];\n"
+                 : "=l"(v.x), "=l"(v.y)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ uint64_t p2p_now_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+    return t;
+}
+// Poll one key word of the local buffer until it carries `tag` (bounded by
+// c.wait_ns from t0; on time-out the error flag is set and the word is
+// returned as "no key").  ok is cleared on time-out and skips later waits.
+__device__ __forceinline__ uint64_t ll_key_wait(const P2PArgs &c, const uint64_t *p, uint32_t tag,
+                                                uint64_t t0, bool &ok) {
+    for (uint32_t i = 0;; ++i) {
+        const uint64_t w = ld_relaxed_sys(p);
+        if ((uint32_t)((w >> 24) & 0xFFu) == tag) return ll_key_decode(w);
+        if (!ok) return 0ull;
+        if ((i & 31u) == 31u && p2p_now_ns() - t0 > c.wait_ns) {
+            atomicExch(c.err, 1);
+            ok = false;
+            return 0ull;
         }
     }
-    return true;
 }
-// one thread of the first CTA, at the start of the kernel that consumes
-// exchange ex: this rank's contribution was stored by the previous kernel on
-// the stream, which has completed, so the flag can go up now.  One release
-// store per peer and rank: when every consuming CTA raised it, the hundreds
-// of system-scope releases delayed the flags the peers wait for.  The other
-// CTAs wait for the flags with a bounded wait, so a first CTA that could
-// not be scheduled would end in the error flag, not a hang.
-__device__ inline void p2p_publish(const P2PArgs &c, int ex) {
-    for (int r = 0; r < c.n; ++r)
-        p2p_st_release((unsigned long long *)((unsigned char *)c.peers[r] + kP2PFlags) +
-                           ex * 32 + c.rank,
-                       c.epoch);
+// Poll one partial line of the local buffer until both words carry `tag`;
+// the two floats, or NaN on time-out (error flag set, ok cleared).
+__device__ __forceinline__ float2 ll_part_wait(const P2PArgs &c, const ulonglong2 *p,
+                                               uint32_t tag, uint64_t t0, bool &ok) {
+    for (uint32_t i = 0;; ++i) {
+        const ulonglong2 v = ld_relaxed_sys_v2(p);
+        if ((uint32_t)(v.x >> 32) == tag && (uint32_t)(v.y >> 32) == tag)
+            return make_float2(__uint_as_float((uint32_t)v.x), __uint_as_float((uint32_t)v.y));
+        if (!ok) return make_float2(__int_as_float(0x7FC00000), __int_as_float(0x7FC00000));
+        if ((i & 31u) == 31u && p2p_now_ns() - t0 > c.wait_ns) {
+            atomicExch(c.err, 1);
+            ok = false;
+            return make_float2(__int_as_float(0x7FC00000), __int_as_float(0x7FC00000));
+        }
+    }
+}
+
+// LSE merge of one (sequence, query head) row over the shards' partials
+// (header m, l, ms, e1, e2, samples; values o[d]) in ascending shard order;
+// part(r, j) returns float j of shard r's partial.  The single-launch merge
+// kernel and the attention kernel's fused merge both use it, so the two
+// exchange paths give the same bits.  One shard gives acc = o, L = l.
+struct ShardMerged {
+    float M, L, MS, E1, E2, ns;
+};
+template <typename Part>
+__device__ __forceinline__ ShardMerged shard_merge_header(int num_shards, Part part) {
+    ShardMerged s;
+    s.M = -INFINITY;
+    s.MS = -INFINITY;
+    for (int r = 0; r < num_shards; ++r) {
+        if (part(r, 1) > 0.f) s.M = fmaxf(s.M, part(r, 0));
+        if (part(r, 3) > 0.f) s.MS = fmaxf(s.MS, part(r, 2));
+    }
+    s.L = 0.f;
+    s.E1 = 0.f;
+    s.E2 = 0.f;
+    s.ns = 0.f;
+    for (int r = 0; r < num_shards; ++r) {
+        if (part(r, 1) > 0.f) s.L = fmaf(part(r, 1), exp2f(part(r, 0) - s.M), s.L);
+        if (part(r, 3) > 0.f) {
+            const float fe = exp2f(part(r, 2) - s.MS);
+            s.E1 = fmaf(part(r, 3), fe, s.E1);
+            s.E2 = fmaf(part(r, 4), fe * fe, s.E2);
+        }
+        s.ns += part(r, 5);
+    }
+    return s;
+}
+// (times 1/L, as the single-GPU merge does: one shard gives the same bits)
+__device__ __forceinline__ float shard_out_scale(const ShardMerged &s) {
+    return s.L > 0.f ? 1.f / s.L : 0.f;
+}
+__device__ __forceinline__ float shard_lse(const ShardMerged &s) {
+    return s.L > 0.f ? (s.M + log2f(s.L)) * kLn2 : -INFINITY;
+}
+__device__ __forceinline__ float shard_ess(const ShardMerged &s) {
+    return (s.ns > 0.f && s.E2 > 0.f) ? (s.E1 * s.E1 / s.E2) / s.ns : 0.f;
 }
 
 // ---------------------------------------------------------------------------
@@ -426,14 +516,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
         if ((i & 255u) == 0u && global_timer_ns() - t0 > 2000000000ull) return false;
     }
 }
-__device__ __forceinline__ void bulk_g2s(void *dst_smem, const void *src, uint32_t bytes,
-                                         uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
-            smem_u32(dst_smem)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
-}
 __device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
 }
@@ -473,7 +555,6 @@ constexpr int kCostSample = 3;  // balancing cost of a sampled (scattered) row
 // row, so the CTA whose share covers a segment boundary takes fewer rows
 constexpr int kCostSegment = 1536;
 int launch_merge_shards(int rows, int head_dim, int num_shards, const float *partials,
-                        const P2PArgs &c, float *out, float *lse, float *ess,
-                        cudaStream_t stream);
+                        float *out, float *lse, float *ess, cudaStream_t stream);
 
 }  // namespace santa

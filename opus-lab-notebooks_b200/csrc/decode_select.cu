@@ -126,13 +126,9 @@ __device__ __forceinline__ void warp_top16(const uint64_t (&k8)[8], uint64_t (&t
     }
 }
 
-// a candidate key: into every rank's buffer (peer exchange) or cand_out
+// a candidate key (the peer-memory exchange runs on the cluster kernel only)
 __device__ __forceinline__ void store_key(const DecodeArgs &a, int64_t idx, uint64_t key) {
-    if (a.p2p.peers) {
-        for (int r = 0; r < a.p2p.n; ++r) p2p_key_slot(a.p2p, a.p2p.peers[r], a.p2p.rank)[idx] = key;
-    } else {
-        a.cand_out[idx] = key;
-    }
+    a.cand_out[idx] = key;
 }
 
 // KPL: keys per lane in the top-k extraction (clusters lane, lane+32, ...).
@@ -298,13 +294,6 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
     const int kk = a.p.topk_clusters;  // HYBRID: candidate keys per (b, query head)
     uint64_t *cand_s = (uint64_t *)ct;  // sharded plan: [g][num_shards][kk], in the free tile area
     if (a.shard_cands) {
-        if (a.p2p.peers) {  // the peers' keys arrive through peer memory
-            if (tid == 0) {
-                if (blockIdx.x == 0) p2p_publish(a.p2p, 0);
-                p2p_wait(a.p2p, 0);
-            }
-            __syncthreads();
-        }
         const int NS = a.num_shards, per = NS * kk;
         const int64_t rows = (int64_t)a.geo.batch * a.geo.num_kv_heads * g;
         for (int i = tid; i < g * per; i += kSelThreads) {
@@ -816,15 +805,9 @@ template <int D, int KPL>
 static int launch_select(DecodeArgs &a, cudaStream_t stream) {
     const int BH = a.geo.batch * a.geo.num_kv_heads;
     const int kcap = (a.p.mode == SANTA_MODE_HYBRID) ? (a.p.topk_clusters > 0 ? a.p.topk_clusters : 1) : 1;
-    static size_t done = 0;
     const size_t smem = select_smem_bytes<D, KPL>(a.sum.max_groups, kcap);
     if (smem > 227 * 1024) return SANTA_ERR_UNSUPPORTED;
-    if (done < smem) {
-        SANTA_CUDA_CHECK(cudaFuncSetAttribute(decode_select_kernel<D, KPL>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              (int)smem));
-        done = smem;
-    }
+    if (int st = ensure_dyn_smem((const void *)decode_select_kernel<D, KPL>, smem)) return st;
     decode_select_kernel<D, KPL><<<BH, kSelThreads, smem, stream>>>(a);
     SANTA_LAUNCH_CHECK();
     return SANTA_OK;
@@ -853,21 +836,6 @@ int launch_expand(DecodeArgs &a, uint8_t *selected, int32_t *sample_rows, cudaSt
                                                                              sample_rows);
     SANTA_LAUNCH_CHECK();
     return SANTA_OK;
-}
-
-static int g_num_sms = 0;
-
-int num_sms() {
-    if (!g_num_sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-            g_num_sms <= 0) {
-            cudaGetLastError();
-            g_num_sms = 148;
-        }
-    }
-    return g_num_sms;
 }
 
 }  // namespace santa

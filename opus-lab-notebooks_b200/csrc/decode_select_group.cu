@@ -323,6 +323,7 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
     __shared__ int sid[kGrpMaxK], gap[kGrpMaxK], cum[kGrpMaxK + 1];
     __shared__ int2 sw[kGrpWarps];
     __shared__ int s_nunion, s_U;
+    __shared__ uint64_t own_s[kGrpMaxK];        // peer exchange: this shard's own top-k
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = a.geo.group;
@@ -351,6 +352,12 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
     // or above the global k-th has fewer than k larger keys anywhere), so the
     // centroids are not scored again.
     const bool thr_mode = a.shard_cands != nullptr;
+    // Peer-memory exchange: this launch also scores and ranks the shard's own
+    // clusters (as the candidates form), sends its top-k keys straight into
+    // every rank's exchange buffer and reads every rank's keys of the same
+    // (sequence, query head) from its own buffer as they arrive, so that one
+    // launch replaces candidates -> all-gather -> threshold selection.
+    const bool fused = a.p2p.peers != nullptr;
 
     // ---- loads: q rows, cluster metadata and (staged layout) the slice -------
     // 16-byte cp.async copies by every thread; centroid rows and q rows land
@@ -433,13 +440,6 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
     // ---- 2. ranking of head h ---------------------------------------------------
     uint64_t thr = 1ull;  // threshold mode: the global k-th key
     if (a.shard_cands) {
-        if (a.p2p.peers) {  // the peers' keys arrive through peer memory
-            if (tid == 0) {
-                if (blockIdx.x == 0 && blockIdx.y == 0) p2p_publish(a.p2p, 0);
-                p2p_wait(a.p2p, 0);
-            }
-            __syncthreads();
-        }
         const int64_t rows = (int64_t)a.geo.batch * a.geo.num_kv_heads * g;
         const uint64_t *cand = a.shard_cands + ((int64_t)bh * g + h) * kk;
         block_top32(
@@ -474,10 +474,44 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
             },
             lists, warp, lane);
     }
+    if (fused) {
+        // send this shard's top-k keys (zero-padded, as the candidates form
+        // writes them) to every rank, each word tagged with the epoch
+        const int64_t row0 = ((int64_t)bh * g + h) * kk;
+        const uint32_t tag = ll_key_tag(a.p2p.epoch);
+        if (warp == 0) {
+            const uint64_t key = lane < kk ? lists[lane] : 0ull;
+            own_s[lane] = key;
+            if (lane < kk) {
+                const uint64_t w = ll_key_encode(key, tag);
+                for (int r = 0; r < a.p2p.n; ++r)
+                    st_relaxed_sys(p2p_key_slot(a.p2p, a.p2p.peers[r], a.p2p.rank) + row0 + lane, w);
+            }
+        }
+        __syncthreads();  // lists is reused
+        // every rank's keys of this row, polled in this rank's buffer
+        const uint64_t t0 = p2p_now_ns();
+        bool ok = true;
+        block_top32(
+            a.p2p.n * kk,
+            [&](int i) {
+                const int r = i / kk, j = i - r * kk;
+                return ll_key_wait(a.p2p, p2p_key_slot(a.p2p, a.p2p.local, r) + row0 + j, tag,
+                                   t0, ok);
+            },
+            lists, warp, lane);
+        int last = -1;
+        for (int j = 0; j < kk; ++j)
+            if (lists[j] != 0ull) last = j;
+        thr = last >= 0 ? lists[last] : 1ull;
+        __syncthreads();
+        if (tid < 32) lists[tid] = own_s[tid];
+        __syncthreads();
+    }
     if (warp == 0) {
         const uint64_t key = lists[lane];
         const int kmax = min(kk, n_groups);
-        const bool on = key != 0ull && (a.shard_cands ? key >= thr : lane < kmax);
+        const bool on = key != 0ull && ((a.shard_cands || fused) ? key >= thr : lane < kmax);
         const int c = on ? (int)(0xFFFFFFFFu - (uint32_t)key) - cbase : 0;
         const unsigned bal = __ballot_sync(0xffffffffu, on);
         const int nsel = __popc(bal);  // a prefix of the sorted list
@@ -486,13 +520,7 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
         if (a.cand_out) {  // shard candidates: the local top-k keys, zero-padded
             if (lane < kk) {
                 const int64_t idx = ((int64_t)bh * g + h) * kk + lane;
-                const uint64_t v = on ? key : 0ull;
-                if (a.p2p.peers) {
-                    for (int r = 0; r < a.p2p.n; ++r)
-                        p2p_key_slot(a.p2p, a.p2p.peers[r], a.p2p.rank)[idx] = v;
-                } else {
-                    a.cand_out[idx] = v;
-                }
+                a.cand_out[idx] = on ? key : 0ull;
             }
         }
         if (lane == 0) {
@@ -675,21 +703,18 @@ static int launch_select_group_d(DecodeArgs &a, cudaStream_t stream) {
     const GrpLayout L = grp_layout(a.sum.max_groups, a.geo.group, D);
     // at most ceil(CTAs / SMs) CTAs per SM: extra dynamic shared memory keeps
     // the cluster scheduler from packing CTAs onto a few SMs
-    static int smem_sm = 0, smem_reserved = 0, static_smem = -1;
-    if (static_smem < 0) {
-        int dev = 0;
-        cudaGetDevice(&dev);
+    // (the kernel's static shared memory is a property of the code, the same
+    // on every device; a thread-safe one-time initialisation)
+    static const int static_smem = [] {
         cudaFuncAttributes fa;
-        SANTA_CUDA_CHECK(cudaFuncGetAttributes(&fa, decode_select_group_kernel<D>));
-        static_smem = (int)fa.sharedSizeBytes;
-        if (cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) !=
-                cudaSuccess ||
-            cudaDeviceGetAttribute(&smem_reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) !=
-                cudaSuccess) {
+        if (cudaFuncGetAttributes(&fa, decode_select_group_kernel<D>) != cudaSuccess) {
             cudaGetLastError();
-            smem_sm = 0;
+            return -1;
         }
-    }
+        return (int)fa.sharedSizeBytes;
+    }();
+    const int smem_sm = static_smem < 0 ? 0 : device_attr(cudaDevAttrMaxSharedMemoryPerMultiprocessor);
+    const int smem_reserved = device_attr(cudaDevAttrReservedSharedMemoryPerBlock);
     size_t dyn = L.bytes;
     const int ctas = a.geo.group * BH;
     const int per_sm = (ctas + num_sms() - 1) / num_sms();
@@ -698,13 +723,7 @@ static int launch_select_group_d(DecodeArgs &a, cudaStream_t stream) {
         const long lim = 227L * 1024 - static_smem;
         if (cap > (long)dyn) dyn = (size_t)(cap < lim ? cap : lim);
     }
-    static size_t attr_done = 0;
-    if (dyn > attr_done) {
-        SANTA_CUDA_CHECK(cudaFuncSetAttribute(decode_select_group_kernel<D>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              (int)dyn));
-        attr_done = dyn;
-    }
+    if (int st = ensure_dyn_smem((const void *)decode_select_group_kernel<D>, dyn)) return st;
     cfg.dynamicSmemBytes = dyn;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -714,6 +733,16 @@ static int launch_select_group_d(DecodeArgs &a, cudaStream_t stream) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    if (a.p2p.peers) {
+        // The peer-memory form waits inside the kernel for the peers' keys of
+        // each (sequence, query head): every cluster must be resident at once,
+        // or a waiting cluster could hold the SMs that a cluster the peers
+        // wait for needs.
+        int max_clusters = 0;
+        SANTA_CUDA_CHECK(
+            cudaOccupancyMaxActiveClusters(&max_clusters, decode_select_group_kernel<D>, &cfg));
+        if (max_clusters < BH) return SANTA_ERR_UNSUPPORTED;
+    }
     SANTA_CUDA_CHECK(cudaLaunchKernelEx(&cfg, decode_select_group_kernel<D>, a));
     return SANTA_OK;
 }

@@ -9,8 +9,7 @@
 //   out = sum_r 2^(m_r - M) o_r / sum_r 2^(m_r - M) l_r,   M = max_r m_r,
 // the same self-normalised combine as santapp.py:472-506 over the union of
 // the shards' rows.  The ESS sums (santapp.py:481-485) merge the same way.
-// With the peer-memory exchange the kernel first waits (bounded) for every
-// rank's flag and reads the partials from this rank's exchange buffer.
+// (The peer-memory exchange merges inside the attention kernel instead.)
 //
 // Also the exchange buffer's host side: allocation, IPC handles, mapping.
 #include "decode_common.cuh"
@@ -22,56 +21,29 @@ namespace santa {
 
 template <int D>
 __global__ void __launch_bounds__(D) merge_shards_kernel(int rows, int num_shards,
-                                                         const float *partials, P2PArgs c,
-                                                         float *out, float *lse, float *ess) {
+                                                         const float *partials, float *out,
+                                                         float *lse, float *ess) {
     constexpr int PS = D + 8;
     const int row = blockIdx.x, d = threadIdx.x;
-    if (c.peers) {  // the partials arrive through peer memory
-        if (d == 0) {
-            if (row == 0) p2p_publish(c, 1);
-            p2p_wait(c, 1);
-        }
-        __syncthreads();
-        partials = p2p_part_slot(c, c.local, 0);
-    }
-    float M = -INFINITY, MS = -INFINITY;
-    for (int r = 0; r < num_shards; ++r) {
-        const float *p = partials + ((int64_t)r * rows + row) * PS;
-        if (p[1] > 0.f) M = fmaxf(M, p[0]);
-        if (p[3] > 0.f) MS = fmaxf(MS, p[2]);
-    }
-    float L = 0.f, acc = 0.f, E1 = 0.f, E2 = 0.f, ns = 0.f;
-    for (int r = 0; r < num_shards; ++r) {
-        const float *p = partials + ((int64_t)r * rows + row) * PS;
-        if (p[1] > 0.f) {
-            const float f = exp2f(p[0] - M);
-            L = fmaf(p[1], f, L);
-            acc = fmaf(p[8 + d], f, acc);
-        }
-        if (p[3] > 0.f) {
-            const float fe = exp2f(p[2] - MS);
-            E1 = fmaf(p[3], fe, E1);
-            E2 = fmaf(p[4], fe * fe, E2);
-        }
-        ns += p[5];
-    }
-    // times 1/L, as the single-GPU merge does (one shard gives the same bits)
-    out[(int64_t)row * D + d] = acc * (L > 0.f ? 1.f / L : 0.f);
+    auto part = [&](int r, int j) { return partials[((int64_t)r * rows + row) * PS + j]; };
+    const ShardMerged s = shard_merge_header(num_shards, part);
+    float acc = 0.f;
+    for (int r = 0; r < num_shards; ++r)
+        if (part(r, 1) > 0.f) acc = fmaf(part(r, 8 + d), exp2f(part(r, 0) - s.M), acc);
+    out[(int64_t)row * D + d] = acc * shard_out_scale(s);
     if (d == 0) {
-        if (lse) lse[row] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
-        if (ess) ess[row] = (ns > 0.f && E2 > 0.f) ? (E1 * E1 / E2) / ns : 0.f;
+        if (lse) lse[row] = shard_lse(s);
+        if (ess) ess[row] = shard_ess(s);
     }
 }
 
 int launch_merge_shards(int rows, int head_dim, int num_shards, const float *partials,
-                        const P2PArgs &c, float *out, float *lse, float *ess,
-                        cudaStream_t stream) {
+                        float *out, float *lse, float *ess, cudaStream_t stream) {
     if (head_dim == 64)
-        merge_shards_kernel<64>
-            <<<rows, 64, 0, stream>>>(rows, num_shards, partials, c, out, lse, ess);
+        merge_shards_kernel<64><<<rows, 64, 0, stream>>>(rows, num_shards, partials, out, lse, ess);
     else
         merge_shards_kernel<128>
-            <<<rows, 128, 0, stream>>>(rows, num_shards, partials, c, out, lse, ess);
+            <<<rows, 128, 0, stream>>>(rows, num_shards, partials, out, lse, ess);
     SANTA_LAUNCH_CHECK();
     return SANTA_OK;
 }

@@ -573,10 +573,7 @@ __global__ void __launch_bounds__(kKppThreads) kpp_candidates_kernel(
 // host launchers
 // ---------------------------------------------------------------------------
 static int km_set_smem(const void *fn, size_t bytes) {
-    if (bytes > 48 * 1024)
-        SANTA_CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              (int)bytes));
-    return SANTA_OK;
+    return bytes > 48 * 1024 ? ensure_dyn_smem(fn, bytes) : SANTA_OK;
 }
 
 }  // namespace santa

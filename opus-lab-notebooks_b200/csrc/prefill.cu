@@ -518,13 +518,7 @@ extern "C" int santa_prefill(const SantaPrefillShape *shape, const void *q, cons
     a.scale_log2 = shape->scale * 1.4426950408889634f;
     a.causal = shape->causal ? 1 : 0;
     const size_t smem = 6 * (size_t)kPfTile + 1024;
-    static bool attr = false;
-    if (!attr) {
-        SANTA_CUDA_CHECK(cudaFuncSetAttribute(prefill_fwd_kernel,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              (int)smem));
-        attr = true;
-    }
+    if (int st = ensure_dyn_smem((const void *)prefill_fwd_kernel, smem)) return st;
     const unsigned grid = (unsigned)a.n_pairs * a.B * a.Hq;
     prefill_fwd_kernel<<<grid, kPfThreads, smem, stream>>>(a);
     SANTA_LAUNCH_CHECK();

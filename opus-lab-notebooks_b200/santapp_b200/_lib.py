@@ -57,7 +57,7 @@ class SantaDecodeParams(ctypes.Structure):
 class SantaP2P(ctypes.Structure):
     _fields_ = [("peer_buffers", _vp), ("local_buffer", _vp), ("epoch", ctypes.c_uint64),
                 ("error_flag", _vp), ("rows", _i32), ("keys_per_row", _i32),
-                ("partial_floats", _i32), ("reserved", _i32)]
+                ("partial_floats", _i32), ("wait_limit_us", _i32)]
 
 
 IPC_HANDLE_BYTES = 64
@@ -123,8 +123,10 @@ SIGNATURES = {
     "santa_shard_select": (ctypes.c_int, [_P(SantaGeometry), _P(SantaDecodeParams), _vp, _vp,
                                           _vp, _P(SantaSummary), _P(SantaShard), _vp, _vp, _vp,
                                           _vp, _vp, ctypes.c_size_t, _vp]),
-    "santa_merge_shards": (ctypes.c_int, [_i32, _i32, _i32, _vp, _vp, _i32, _vp, _vp, _vp,
-                                          _vp]),
+    "santa_shard_attend": (ctypes.c_int, [_P(SantaGeometry), _P(SantaDecodeParams), _vp, _vp,
+                                          _vp, _P(SantaSummary), _P(SantaShard), _vp, _vp, _vp,
+                                          _vp, ctypes.c_size_t, _vp]),
+    "santa_merge_shards": (ctypes.c_int, [_i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
     "santa_p2p_buffer_bytes": (ctypes.c_int, [_i32, _i32, _i32, _i32, _P(ctypes.c_size_t)]),
     "santa_p2p_alloc": (ctypes.c_int, [ctypes.c_size_t, _P(_vp)]),
     "santa_p2p_free": (ctypes.c_int, [_vp]),

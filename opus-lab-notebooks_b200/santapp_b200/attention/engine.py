@@ -20,7 +20,14 @@ reference supports batch 1, :293-294):
   (``SklearnLikeTorchMiniBatchKMeans``) and the cluster summary
   (``build_summary``, batched over the layer);
 * ``generate`` (:794-908): prefill + clustering, trim the cache by one token,
-  re-feed the last prompt token, greedy decoding.
+  re-feed the last prompt token, greedy decoding;
+* ``_approximate_attention`` (:365-506): the reference's per-head call
+  (one query head of sequence 0), kept for callers that drive the engine
+  head by head; it routes to ``santa_decode`` on that head's summary.
+
+The engine takes the reference's own ``SantaPlusConfig`` (config.py:68-78,
+a slotted dataclass) or ``SantaB200Config``: fields the reference's config
+lacks (``topk_clusters``, ``n_clusters``) fall back to their defaults.
 
 Probe queries are captured inside the patched forward at the probe positions
 only (the reference keeps every layer's full q_proj output).
@@ -95,8 +102,16 @@ class LayerCache:
 
 @dataclass(frozen=True)
 class SantaGeneration:
-    token_ids: list[list[int]]
+    """Result of ``generate``: ``token_ids`` is ``list[int]`` for a batch of
+    one sequence (the reference's SantaGeneration, santapp.py:145-148, which
+    SantaPlusBackend.generate decodes directly) and one ``list[int]`` per
+    sequence for larger batches."""
+    token_ids: list[int] | list[list[int]]
     metrics: dict[str, Any]
+
+
+# fields of SantaB200Config that the reference's SantaPlusConfig does not have
+_EXTRA_DEFAULTS = {"topk_clusters": 16, "n_clusters": None}
 
 
 def _patched_forward(attention, hidden_states, position_embeddings=None, attention_mask=None,
@@ -138,8 +153,15 @@ class SantaB200Engine:
         self._probe_q: dict[int, torch.Tensor] = {}
         self._decode_step = 0
         self._n_groups_host: dict[int, np.ndarray] = {}
-        self.track_traffic = True  # draw accounting needs a device->host read per layer call
+        self.track_traffic = True  # draw accounting, read back once per generate
+        self._traffic_pending: list = []
+        self._head_calls = 0
         self._lib = _lib.load()
+
+    def _cfg(self, name: str):
+        """A config field; SantaPlusConfig lacks the hybrid estimator's
+        fields, which then take SantaB200Config's defaults."""
+        return getattr(self.config, name, _EXTRA_DEFAULTS.get(name))
 
     # ---- patch ---------------------------------------------------------------
     @contextlib.contextmanager
@@ -168,6 +190,7 @@ class SantaB200Engine:
         self.summaries.clear()
         self._probe_q.clear()
         self._n_groups_host.clear()
+        self._traffic_pending = []
         self.traffic = DecodeTrafficTracker()
 
     def _trim_cache(self, length: int) -> None:
@@ -218,18 +241,17 @@ class SantaB200Engine:
             res = santa_decode(q_f32[:, :, 0].contiguous(), cached.key, cached.value,
                                self.summaries[layer_id], mode=self.config.mode,
                                n_total=cached.length, sample_end=self.sample_end,
-                               topk_clusters=self.config.topk_clusters,
+                               topk_clusters=self._cfg("topk_clusters"),
                                token_budget=self.config.samples_per_head,
                                samples=self.config.samples_per_head,
                                scale=float(attention.scaling), seed=self.config.sample_seed,
                                step=self._decode_step, with_stats=self.track_traffic)
             if self.track_traffic:
+                # kept on the device; read back once when generate finishes
                 if layer_id not in self._n_groups_host:
-                    self._n_groups_host[layer_id] = self.summaries[layer_id].n_groups.cpu().numpy()
-                self.traffic.record_step(
-                    mode=self.config.mode, n_total=cached.length, sample_end=self.sample_end,
-                    n_exact=res.n_exact.cpu().numpy(), samples=self.config.samples_per_head,
-                    n_groups=self._n_groups_host[layer_id], ess=res.ess.cpu().numpy())
+                    self._n_groups_host[layer_id] = self.summaries[layer_id].n_groups
+                self._traffic_pending.append((cached.length, layer_id, res.n_exact.clone(),
+                                              res.ess.clone()))
             out = res.out.to(torch.bfloat16).view(B, 1, Hq * D)
         elif start == 0:
             # prompt: causal attention of every position over the prompt
@@ -274,7 +296,7 @@ class SantaB200Engine:
             self._probe_idx = None
         torch.cuda.synchronize()
         prefill_s = time.perf_counter() - t0
-        n_clusters = self.config.n_clusters or cluster_count(sample_end, self.config.group_size)
+        n_clusters = self._cfg("n_clusters") or cluster_count(sample_end, self.config.group_size)
         km = self.config.kmeans
         P = len(probes)
         t1 = time.perf_counter()
@@ -341,6 +363,7 @@ class SantaB200Engine:
                         break
             torch.cuda.synchronize()
             decode_s = time.perf_counter() - t2
+            self._flush_traffic()
         metrics = {
             "backend": "santapp_b200", "mode": self.config.mode, "batch": B,
             "prompt_tokens": T, "generated_tokens": len(generated[0]),
@@ -350,4 +373,53 @@ class SantaB200Engine:
             **self.traffic.as_dict(),
         }
         self.clear()
-        return SantaGeneration(token_ids=generated, metrics=metrics)
+        return SantaGeneration(token_ids=generated[0] if B == 1 else generated, metrics=metrics)
+
+    def _flush_traffic(self) -> None:
+        """Feed the decode calls' draw counts to the traffic tracker (one
+        device->host read for the whole generation)."""
+        if not self._traffic_pending:
+            return
+        n_exact = torch.stack([t[2] for t in self._traffic_pending]).cpu().numpy()
+        ess = torch.stack([t[3] for t in self._traffic_pending]).cpu().numpy()
+        groups = {k: v.cpu().numpy() for k, v in self._n_groups_host.items()}
+        for i, (n_total, layer_id, _, _) in enumerate(self._traffic_pending):
+            self.traffic.record_step(
+                mode=self.config.mode, n_total=n_total, sample_end=self.sample_end,
+                n_exact=n_exact[i], samples=self.config.samples_per_head,
+                n_groups=groups[layer_id], ess=ess[i])
+        self._traffic_pending = []
+
+    # ---- the reference's per-head call ----------------------------------------
+    def _approximate_attention(self, query: torch.Tensor, full_key: torch.Tensor,
+                               full_value: torch.Tensor, layer_id: int,
+                               kv_head: int) -> torch.Tensor:
+        """santapp.py:365-506 for one query head of sequence 0: query [D],
+        full_key / full_value [n_total, D] (the layer's cache of that KV
+        head), in ``self.mode``.  Returns the fp32 attention output [D] and
+        records the call's draw counts.  Each call draws from its own Philox
+        stream (seed, layer, KV head and a per-engine call counter), as the
+        reference's per-head torch draws are independent."""
+        n_total = int(full_key.shape[0])
+        if not 0 < self.sample_end <= n_total:
+            raise RuntimeError(
+                f"Invalid sampled-prefix boundary {self.sample_end} for cache length {n_total}.")
+        D = self.head_dim
+        q = query.detach().float().reshape(1, 1, D).contiguous()
+        kc = full_key.contiguous().view(1, 1, n_total, D)
+        vc = full_value.contiguous().view(1, 1, n_total, D)
+        summary = self.summaries[layer_id].segment(0, kv_head)
+        mode = self.mode if self.mode != "dense" else self.config.mode
+        seed = (int(self.config.sample_seed) + 0x9E3779B97F4A7C15 * (layer_id * 4096 + kv_head + 1)
+                ) & 0xFFFFFFFFFFFFFFFF
+        res = santa_decode(q, kc, vc, summary, mode=mode, n_total=n_total,
+                           sample_end=self.sample_end, topk_clusters=self._cfg("topk_clusters"),
+                           token_budget=self.config.samples_per_head,
+                           samples=self.config.samples_per_head, scale=1.0 / math.sqrt(D),
+                           seed=seed, step=self._head_calls, with_stats=True)
+        self._head_calls += 1
+        self.traffic.record_step(
+            mode=mode, n_total=n_total, sample_end=self.sample_end,
+            n_exact=res.n_exact.cpu().numpy(), samples=self.config.samples_per_head,
+            n_groups=summary.n_groups.cpu().numpy(), ess=res.ess.cpu().numpy())
+        return res.out.view(D)

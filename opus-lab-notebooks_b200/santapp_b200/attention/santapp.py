@@ -116,6 +116,17 @@ class ClusterSummary:
             "key_centroids": self.key_centroids[b, kv, :n],
         }
 
+    def segment(self, b: int, kv: int) -> "ClusterSummary":
+        """The summary of one (batch, KV head) as a one-segment summary
+        (views, no copy), for a decode call on that head alone."""
+        sl = (slice(b, b + 1), slice(kv, kv + 1))
+        return ClusterSummary(
+            members=self.members[sl], positions=self.positions[sl], starts=self.starts[sl],
+            lengths_long=self.lengths_long[sl], log_n=self.log_n[sl],
+            key_centroids=self.key_centroids[sl], n_groups=self.n_groups[sl],
+            sorted_key=self.sorted_key[sl], sorted_value=self.sorted_value[sl],
+            max_groups=self.max_groups, sample_end=self.sample_end)
+
     def nbytes(self) -> int:
         return sum(t.numel() * t.element_size() for t in (
             self.members, self.positions, self.starts, self.lengths_long, self.log_n,

@@ -22,14 +22,20 @@ held by the last shard.  A decode step is
 6. ``santa_merge_shards``: the LSE merge, identical on every rank.
 
 Both exchanges move a few hundred KB.  With ``transport="nccl"`` they are
-NCCL all-gathers on the ranks' own buffers; with ``transport="p2p"`` the
-producing kernels store keys and partials straight into every rank's
-exchange buffer (mapped through CUDA IPC) and raise a per-rank flag that the
-consuming kernels wait for (bounded; ``p2p_error`` is set if a peer never
-signals).  Either way remote data lands in local memory before a kernel
-reads it; no TMA or multicast is involved.  ``ShardExchange`` holds the host logic (shard bounds,
-sample split, Philox seeds, exchange buffers and order) apart from the
-kernel calls, so that it can be checked on CPU ranks.
+NCCL all-gathers on the ranks' own buffers (six steps, four launches).  With
+``transport="p2p"`` a step is two launches and no collective: the selection
+launch scores the shard's clusters, stores its top-k keys straight into every
+rank's exchange buffer (mapped through CUDA IPC) and reads every rank's keys
+from its own buffer as they arrive (steps 1-3); the attention launch stores
+the shard's partials the same way and merges every rank's in its tail (steps
+4-6).  Each 8-byte word stored into a peer's buffer carries the step's epoch
+beside its data, so the consumer polls its own memory and needs no flag or
+fence; every wait is bounded, and a wait that runs out sets ``p2p_error``
+and turns the step's outputs into NaN (``ShardedDecodeStep`` raises on the
+next call).  Either way remote data lands in local memory before a kernel
+reads it; no TMA or multicast is involved.  ``ShardExchange`` holds the host
+logic (shard bounds, sample split, Philox seeds, exchange buffers and order)
+apart from the kernel calls, so that it can be checked on CPU ranks.
 """
 
 from __future__ import annotations
@@ -42,7 +48,8 @@ import torch
 from .. import _lib
 from .santapp import ClusterSummary, _geometry, _require_cuda, decode_params
 
-__all__ = ["shard_bounds", "split_counts", "shard_seed", "ShardExchange", "ShardedDecodeStep"]
+__all__ = ["shard_bounds", "split_counts", "shard_seed", "exchange_layout", "key_words",
+           "partial_words", "ShardExchange", "ShardedDecodeStep"]
 
 _GOLDEN = 0x9E3779B97F4A7C15
 
@@ -80,6 +87,38 @@ def split_counts(total: int, weights) -> list[int]:
 def shard_seed(seed: int, shard: int) -> int:
     """Philox key of shard ``shard``: independent draw streams per shard."""
     return (int(seed) + int(shard) * _GOLDEN) & 0xFFFFFFFFFFFFFFFF
+
+
+def exchange_layout(num_shards: int, rows: int, topk: int, head_dim: int) -> dict:
+    """Byte offsets of the regions of a peer-memory exchange buffer (the
+    layout the kernels use): ``keys`` u64 [2 parities][num_shards][rows][topk],
+    ``parts`` u64 [2][num_shards][rows][head_dim + 8] (one word per partial
+    float), ``stage`` f32 [rows][head_dim + 8], ``bytes`` in all."""
+    pf = _lib.partial_floats(head_dim)
+    keys = 1024
+    parts = (keys + 2 * num_shards * rows * topk * 8 + 255) // 256 * 256
+    stage = parts + 2 * num_shards * rows * pf * 8
+    return {"keys": keys, "parts": parts, "stage": stage, "bytes": stage + rows * pf * 4}
+
+
+def key_words(keys: torch.Tensor, epoch: int) -> torch.Tensor:
+    """Candidate keys (int64, as santa_shard_candidates writes them) as the
+    words the peer-memory exchange stores for step ``epoch``: the tag
+    ``epoch % 255 + 1`` in bits 24-31 of each key."""
+    tag = epoch % 255 + 1
+    # -0xFF000001 is the 64-bit mask 0xFFFFFFFF00FFFFFF as a signed integer
+    return (keys & -0xFF000001) | (tag << 24)
+
+
+def partial_words(partial: torch.Tensor, epoch: int) -> torch.Tensor:
+    """Partials (fp32, as santa_shard_execute writes them) as the words the
+    peer-memory exchange stores for step ``epoch``: ``epoch`` (32 bits) in
+    the high half of each word, the float's bits in the low half."""
+    bits = partial.contiguous().view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    tag = epoch & 0xFFFFFFFF
+    if tag >= 1 << 31:
+        tag -= 1 << 32
+    return bits | (tag << 32)
 
 
 class ShardExchange:
@@ -137,7 +176,7 @@ class ShardedDecodeStep(ShardExchange):
                  summary: ClusterSummary, *, num_query_heads: int, n_total: int,
                  topk_clusters: int, samples: int, shard_index: int, num_shards: int,
                  cluster_base: int, group=None, scale: float | None = None, seed: int = 0,
-                 injected: bool = False, transport: str = "nccl"):
+                 injected: bool = False, transport: str = "nccl", wait_limit_us: int = 0):
         _require_cuda("key_cache", key_cache)
         _require_cuda("value_cache", value_cache)
         if key_cache.dtype != torch.bfloat16:
@@ -159,8 +198,11 @@ class ShardedDecodeStep(ShardExchange):
         if transport not in ("nccl", "p2p"):
             raise ValueError(f"unknown transport {transport!r}")
         self.transport = transport
+        self.wait_limit_us = int(wait_limit_us)
         self.epoch = 0
         self.p2p = None
+        self._err_host = None
+        self._err_event = None
         self._p2p_buffers: list[int] = []  # every rank's buffer as mapped here
         self._p2p_owned = False
         nbytes = ctypes.c_size_t()
@@ -186,19 +228,51 @@ class ShardedDecodeStep(ShardExchange):
             self.num_shards, self.rows, self.topk, self.head_dim, ctypes.byref(n)))
         return n.value
 
-    def bind_p2p(self, buffers: list[int], *, owned: bool = False) -> None:
+    def bind_p2p(self, buffers: list[int], *, owned: bool = False,
+                 epoch_base: int | None = None) -> None:
         """Use the exchange buffers ``buffers`` (device addresses of every
-        rank's buffer as mapped in this process, own one at shard_index)."""
+        rank's buffer as mapped in this process, own one at shard_index).
+
+        Every rank must bind at the same point, with the same
+        ``epoch_base``: the first step then uses epoch ``epoch_base + 1``.
+        Buffers fresh from ``santa_p2p_alloc`` (zeroed) work with any base;
+        buffers that an earlier binding used need a base at or above that
+        binding's last epoch (its ``epoch``), or a stale word of that run
+        could pass for a new one."""
         dev = self.out.device
         self._p2p_buffers = list(buffers)
         self._p2p_owned = owned
+        if epoch_base is not None:
+            self.epoch = int(epoch_base)
         self._peer_table = torch.tensor(buffers, dtype=torch.int64, device=dev)
         self.p2p_error = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._err_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self._err_event = torch.cuda.Event()
+        self._err_step = None
         self.p2p = _lib.SantaP2P(self._peer_table.data_ptr(), buffers[self.shard_index], 0,
                                  self.p2p_error.data_ptr(), self.rows, self.topk,
-                                 _lib.partial_floats(self.head_dim), 0)
+                                 _lib.partial_floats(self.head_dim), self.wait_limit_us)
         self.shard.p2p = ctypes.addressof(self.p2p)
         self.transport = "p2p"
+
+    def check_p2p(self) -> None:
+        """Raise if a peer-memory wait ran out (waits for the device)."""
+        if self.p2p is not None and int(self.p2p_error.item()) != 0:
+            raise RuntimeError("sequence-shard exchange: a wait for a peer rank ran out of time; "
+                               "the outputs of that step and of later steps are NaN")
+
+    def _poll_p2p_error(self, step: int, stream=None) -> None:
+        """Cheap asynchronous check: the previous step's error flag, copied
+        to pinned memory behind it, raises once it has landed; then this
+        step's flag is queued the same way."""
+        if self._err_step is not None and self._err_event.query() and int(self._err_host[0]):
+            raise RuntimeError(f"sequence-shard exchange: a wait for a peer rank ran out of "
+                               f"time at or before step {self._err_step}; its outputs are NaN")
+        s = stream if stream is not None else torch.cuda.current_stream()
+        with torch.cuda.stream(s):
+            self._err_host.copy_(self.p2p_error, non_blocking=True)
+            self._err_event.record(s)
+        self._err_step = step
 
     def _p2p_setup(self, group) -> None:
         """Allocate this rank's exchange buffer, share its IPC handle through
@@ -250,12 +324,20 @@ class ShardedDecodeStep(ShardExchange):
         self._p2p_owned = False
 
     # ---- the kernel calls -------------------------------------------------
-    def candidates(self, q: torch.Tensor, step: int = 0, stream=None) -> torch.Tensor:
+    def begin(self, q: torch.Tensor, step: int = 0) -> None:
+        """Start step ``step`` with queries ``q``: the Philox step counter and
+        the exchange epoch (one per step, the same sequence on every rank)."""
         self.p.step = int(step) & 0xFFFFFFFFFFFFFFFF
         self._q = q
         self.epoch += 1
         if self.p2p is not None:
             self.p2p.epoch = self.epoch
+
+    def candidates(self, q: torch.Tensor, step: int = 0, stream=None) -> torch.Tensor:
+        """NCCL transport, step 1: this shard's top-k keys into ``keys``."""
+        self.begin(q, step)
+        if self.p2p is not None:
+            raise RuntimeError("with the peer-memory exchange, plan() runs the candidates pass")
         g, p, c, s = self._refs
         _lib.check("santa_shard_candidates", self.lib.santa_shard_candidates(
             g, p, q.data_ptr(), self.key_cache.data_ptr(), self.value_cache.data_ptr(), c, s,
@@ -265,6 +347,8 @@ class ShardedDecodeStep(ShardExchange):
 
     def plan(self, sample_a: torch.Tensor | None = None, n_exact: torch.Tensor | None = None,
              stream=None) -> None:
+        """Step 3 (NCCL: after exchange 1); with the peer-memory exchange
+        steps 1-3 in one launch."""
         g, p, c, s = self._refs
         _lib.check("santa_shard_plan", self.lib.santa_shard_plan(
             g, p, self._q.data_ptr(), self.key_cache.data_ptr(), self.value_cache.data_ptr(),
@@ -272,7 +356,16 @@ class ShardedDecodeStep(ShardExchange):
             _lib.stream_handle(stream)))
 
     def execute(self, stream=None) -> torch.Tensor:
+        """Step 4 (NCCL: the partial, returned); with the peer-memory
+        exchange steps 4-6 in one launch (the merged output, returned)."""
         g, p, c, s = self._refs
+        if self.p2p is not None:
+            _lib.check("santa_shard_attend", self.lib.santa_shard_attend(
+                g, p, self._q.data_ptr(), self.key_cache.data_ptr(),
+                self.value_cache.data_ptr(), c, s, self.out.data_ptr(), self.lse.data_ptr(),
+                self.ess.data_ptr(), self.ws.data_ptr(), self.ws_bytes,
+                _lib.stream_handle(stream)))
+            return self.out
         _lib.check("santa_shard_execute", self.lib.santa_shard_execute(
             g, p, self._q.data_ptr(), self.key_cache.data_ptr(), self.value_cache.data_ptr(),
             c, s, self.partial.data_ptr(), self.ws.data_ptr(), self.ws_bytes,
@@ -280,10 +373,11 @@ class ShardedDecodeStep(ShardExchange):
         return self.partial
 
     def merge(self, stream=None) -> torch.Tensor:
-        p2p = ctypes.byref(self.p2p) if self.p2p is not None else None
+        """Step 6 (NCCL transport; the peer-memory attention launch merged)."""
+        if self.p2p is not None:
+            return self.out
         _lib.check("santa_merge_shards", self.lib.santa_merge_shards(
-            self.rows, self.head_dim, self.num_shards,
-            None if p2p is not None else self.all_partials.data_ptr(), p2p, self.shard_index,
+            self.rows, self.head_dim, self.num_shards, self.all_partials.data_ptr(),
             self.out.data_ptr(), self.lse.data_ptr(), self.ess.data_ptr(),
             _lib.stream_handle(stream)))
         return self.out
@@ -317,6 +411,12 @@ class ShardedDecodeStep(ShardExchange):
     def __call__(self, q: torch.Tensor, step: int = 0, sample_a: torch.Tensor | None = None):
         """The whole step on the current stream; returns ``out [B, Hq, D]``
         (identical on every rank)."""
+        if self.p2p is not None:
+            self.begin(q, step)
+            self.plan(sample_a)
+            out = self.execute()
+            self._poll_p2p_error(step)
+            return out
         self.candidates(q, step)
         self.exchange_keys()
         self.plan(sample_a)
@@ -324,4 +424,7 @@ class ShardedDecodeStep(ShardExchange):
         self.exchange_partials()
         return self.merge()
 
-    kernels_per_call = 4  # candidates, select, attend, merge
+    @property
+    def kernels_per_call(self) -> int:
+        # peer memory: select, attend; NCCL: candidates, select, attend, merge
+        return 2 if self.p2p is not None else 4

@@ -1,9 +1,10 @@
 """Generate the golden vectors under tests/golden/ by running the reference.
 
 Run in a container where the reference source tree is mounted (read-only is
-fine):
+fine), naming its ``src`` directory:
 
-    python tests/golden/make_golden.py [--reference-src PATH]
+    python tests/golden/make_golden.py --reference-src PATH
+    SANTA_REFERENCE_SRC=PATH python tests/golden/make_golden.py
 
 It imports santapp_ruler from the reference's ``src`` directory and drives
 its hot-path functions headlessly on seeded synthetic inputs:
@@ -11,7 +12,10 @@ its hot-path functions headlessly on seeded synthetic inputs:
 * ``SklearnLikeTorchMiniBatchKMeans.fit_predict``  (minibatch_kmeans.py:128-334)
 * ``SantaPlusEngine._build_summary``                (santapp.py:508-540)
 * ``SantaPlusEngine._approximate_attention``        (santapp.py:365-506)
-  in the topk, guided, uniform and santa modes.
+  in the topk, guided, uniform and santa modes, with the engine's
+  ``DecodeTrafficTracker`` (santapp.py:80-142) accumulating over every head
+  call of a mode: its ``as_dict()`` and each call's exact-token count and ESS
+  ratio are kept.
 
 Shims (documented in the fixture's ``notes`` field):
 
@@ -32,6 +36,7 @@ Inputs are not stored: they are regenerated from the seed by
 from __future__ import annotations
 
 import argparse
+import json
 import math
 import os
 import sys
@@ -124,16 +129,24 @@ def run_decode_case(shape, labels_by_bkv, santapp_mod, config_mod, prefix, out,
     for mode, samples in modes_budget:
         res = np.zeros((B, Hq, D), np.float32)
         draws_g, draws_w, draws_i = [], [], []
+        tracker = santapp_mod.DecodeTrafficTracker()
+        n_draw = np.zeros((B, Hq), np.int64)
+        ess = np.full((B, Hq), np.nan, np.float64)
         for b in range(B):
             for h in range(Hq):
                 kv = h // g
                 eng = _engine(santapp_mod, config_mod, D, mode, samples, se,
                               {(0, kv): summaries[(b, kv)]})
+                eng.traffic = tracker
+                drawn0, n_ess0 = tracker.sampled_token_draws, len(tracker.ess_ratios)
                 q = w.queries[0, b, h].float()
                 torch.manual_seed(1000 * b + h)
                 with _Recorder() as rec:
                     o = eng._approximate_attention(q, w.keys[b, kv], w.values[b, kv], 0, kv)
                 res[b, h] = o.numpy()
+                n_draw[b, h] = tracker.sampled_token_draws - drawn0
+                if len(tracker.ess_ratios) > n_ess0:
+                    ess[b, h] = tracker.ess_ratios[-1]
                 d = dict((n, t) for n, t in rec.draws)
                 if mode == "guided":
                     lengths = summaries[(b, kv)].lengths_long
@@ -148,6 +161,9 @@ def run_decode_case(shape, labels_by_bkv, santapp_mod, config_mod, prefix, out,
                     draws_i.append(d["multinomial"].numpy().astype(np.int64))
         out[f"{prefix}{mode}_out"] = res
         out[f"{prefix}{mode}_samples"] = np.array(samples)
+        out[f"{prefix}{mode}_traffic"] = np.array(json.dumps(tracker.as_dict()))
+        out[f"{prefix}{mode}_draws_per_call"] = n_draw
+        out[f"{prefix}{mode}_ess"] = ess
         if draws_g:
             out[f"{prefix}{mode}_groups"] = np.stack(draws_g).reshape(B, Hq, -1)
             out[f"{prefix}{mode}_within"] = np.stack(draws_w).reshape(B, Hq, -1)
@@ -157,9 +173,12 @@ def run_decode_case(shape, labels_by_bkv, santapp_mod, config_mod, prefix, out,
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference-src",
-                    default="/root/reference/santapp-ruler-bench/src")
+    ap.add_argument("--reference-src", default=os.environ.get("SANTA_REFERENCE_SRC"),
+                    help="the reference's santapp-ruler-bench/src directory "
+                         "(or the SANTA_REFERENCE_SRC environment variable)")
     args = ap.parse_args()
+    if not args.reference_src:
+        ap.error("name the reference source tree: --reference-src PATH or SANTA_REFERENCE_SRC")
     sys.path.insert(0, args.reference_src)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     from santapp_ruler import config as config_mod

@@ -92,7 +92,8 @@ def test_generate_runs_and_accounts_draws(model):
                           probe_queries=16, n_clusters=16, topk_clusters=3,
                           kmeans=KMeansConfig(batch_size=256, max_iter=5))
     gen = SantaB200Engine(model, cfg).generate(ids, max_new_tokens=5)
-    assert len(gen.token_ids) == 1 and len(gen.token_ids[0]) == 5
+    # batch 1: list[int], as the reference's SantaGeneration
+    assert len(gen.token_ids) == 5 and all(isinstance(t, int) for t in gen.token_ids)
     m = gen.metrics
     assert m["prompt_tokens"] == 600 and m["generated_tokens"] == 5
     assert m["sampled_prefix_tokens"] == 600 - 1 - 64
@@ -104,7 +105,7 @@ def test_batch_decodes_like_single_sequences(model):
                           probe_queries=16, n_clusters=16, topk_clusters=4,
                           kmeans=KMeansConfig(batch_size=256, max_iter=5))
     both = SantaB200Engine(model, cfg).generate(ids, max_new_tokens=4).token_ids
-    one = [SantaB200Engine(model, cfg).generate(ids[b:b + 1], max_new_tokens=4).token_ids[0]
+    one = [SantaB200Engine(model, cfg).generate(ids[b:b + 1], max_new_tokens=4).token_ids
            for b in range(2)]
     # the sampler draws from (seed, step, batch, head): batch row b of the
     # pair and the single run (batch 0) use different streams, so compare the
@@ -147,3 +148,91 @@ def test_planted_keys_land_in_selected_clusters():
         assert len(active) == rows
         chosen = set(active[np.nonzero(sel[0, h, :rows].cpu().numpy())[0]])
         assert all(lab[0, kv, p] in chosen for p in planted[kv])
+
+
+# A mirror of the reference's configuration classes (santapp_ruler/config.py:
+# 57-78): slotted dataclasses with exactly the reference's fields, so an
+# attribute the reference lacks raises AttributeError as it would there.
+from dataclasses import dataclass, field  # noqa: E402
+
+
+@dataclass(slots=True)
+class RefMiniBatchKMeansConfig:
+    batch_size: int = 4096
+    n_init: int = 1
+    max_iter: int = 100
+    tol: float = 0.0
+    max_no_improvement: int | None = 10
+    init_size: int | None = None
+    reassignment_ratio: float = 0.01
+    random_state: int = 0
+
+
+@dataclass(slots=True)
+class RefSantaPlusConfig:
+    mode: str = "guided"
+    group_size: int = 16
+    samples_per_head: int = 128
+    probe_queries: int = 64
+    recent_window: int = 64
+    probe_region_start_fraction: float = 0.75
+    probe_strategy: str = "end_quarter"
+    sample_seed: int = 0
+    kmeans: RefMiniBatchKMeansConfig = field(default_factory=RefMiniBatchKMeansConfig)
+
+
+def test_reference_config_drives_generate_like_the_backend(model):
+    """SantaPlusBackend.generate (backends.py:220-236) hands the engine the
+    reference's slotted SantaPlusConfig and decodes result.token_ids directly
+    with the tokenizer: both must work unchanged, for each reference mode."""
+    ids = _prompt(1, 600, seed=6)
+
+    def decode(token_ids):  # a tokenizer's decode takes a flat list of ints
+        assert isinstance(token_ids, list) and all(isinstance(t, int) for t in token_ids)
+        return " ".join(f"<{t}>" for t in token_ids)
+
+    for mode in ("guided", "topk", "uniform", "santa"):
+        cfg = RefSantaPlusConfig(mode=mode, samples_per_head=32, probe_queries=16,
+                                 kmeans=RefMiniBatchKMeansConfig(batch_size=256, max_iter=5))
+        with pytest.raises(AttributeError):
+            cfg.topk_clusters  # noqa: B018  (the reference's config has no such field)
+        eng = SantaB200Engine(model, cfg)
+        result = eng.generate(ids, max_new_tokens=3, eos_token_ids={0}, stop_on_eos=False,
+                              random_seed=0)
+        text = decode(result.token_ids)
+        assert len(result.token_ids) == 3 and text.count("<") == 3
+        assert result.metrics["mode"] == mode
+        assert result.metrics["sampled_prefix_tokens"] == 600 - 1 - 64
+
+
+def test_per_head_approximate_attention_matches_batched_decode(model):
+    """The reference's per-head call (santapp.py:365-506) on the engine's
+    cache and summaries gives the batched decode's output for that head
+    (topk mode: no random draws, the same selected rows)."""
+    from santapp_b200.attention import santapp as S
+    ids = _prompt(1, 700, seed=8)
+    cfg = SantaB200Config(mode="topk", samples_per_head=96, recent_window=64, probe_queries=16,
+                          n_clusters=24, kmeans=KMeansConfig(batch_size=256, max_iter=5))
+    eng = SantaB200Engine(model, cfg)
+    T = ids.shape[1]
+    eng.cache_capacity = T + 8
+    with torch.inference_mode(), eng.patched():
+        eng._dense_prefill_and_cluster(ids, probe_seed=0)
+        eng.mode = "topk"
+        layer = 1
+        c = eng.cache[layer]
+        n = c.length
+        g = torch.Generator(device="cuda").manual_seed(3)
+        q = torch.randn(1, eng.num_query_heads, eng.head_dim, device="cuda", generator=g)
+        batched = S.santa_decode(q, c.key, c.value, eng.summaries[layer], mode="topk",
+                                 n_total=n, sample_end=eng.sample_end,
+                                 token_budget=cfg.samples_per_head,
+                                 scale=1.0 / math.sqrt(eng.head_dim)).out
+        for h in range(eng.num_query_heads):
+            kv = h // eng.group
+            got = eng._approximate_attention(q[0, h], c.key[0, kv, :n], c.value[0, kv, :n],
+                                             layer, kv)
+            assert got.shape == (eng.head_dim,) and got.dtype == torch.float32
+            torch.testing.assert_close(got, batched[0, h], rtol=1e-5, atol=1e-5)
+        assert eng.traffic.as_dict()["decode_attention_head_calls"] == eng.num_query_heads
+    eng.clear()

@@ -179,3 +179,36 @@ def test_fixed_point_sum_is_order_independent():
 def test_log_count_is_correctly_rounded_double_log():
     n = np.arange(1, 1 << 17)
     assert np.array_equal(O.log_count(n), np.array([math.log(i) for i in n], np.float64).astype(np.float32))
+
+
+@pytest.mark.parametrize("prefix,shape", [("qwen05b_", QWEN05B_4K), ("qwen7b_", QWEN7B_SMALL)])
+@pytest.mark.parametrize("mode", ["topk", "guided", "uniform", "santa"])
+def test_traffic_tracker_matches_reference(golden_decode, prefix, shape, mode):
+    """DecodeTrafficTracker.record_step (one batched call per (sequence, KV
+    head) segment) accumulates the counters the reference's per-head
+    record() calls produced (santapp.py:419-426, 498-505) over the same head
+    calls: same exact-token counts (topk), sample counts, recent window,
+    cluster metadata reads and ESS ratios."""
+    import json
+    from santapp_b200.attention.santapp import DecodeTrafficTracker
+    want = json.loads(str(golden_decode[f"{prefix}{mode}_traffic"]))
+    draws = golden_decode[f"{prefix}{mode}_draws_per_call"]
+    ess = golden_decode[f"{prefix}{mode}_ess"]
+    samples = int(golden_decode[f"{prefix}{mode}_samples"])
+    g = shape.group
+    t = DecodeTrafficTracker()
+    for b in range(shape.batch):
+        for kv in range(shape.num_kv_heads):
+            n_groups = golden_decode[f"{prefix}summary_{b}_{kv}_lengths"].size
+            heads = slice(kv * g, (kv + 1) * g)
+            t.record_step(mode=mode, n_total=shape.context, sample_end=shape.sample_end,
+                          n_exact=draws[b, heads] if mode == "topk" else np.zeros(g, np.int64),
+                          samples=samples, n_groups=np.array([n_groups]),
+                          ess=None if mode == "topk" else ess[b, heads])
+    got = t.as_dict()
+    assert set(got) == set(want)
+    for k, v in want.items():
+        if v is None or isinstance(v, int):
+            assert got[k] == v, k
+        else:
+            assert got[k] == pytest.approx(v, rel=1e-9, abs=1e-12), k

@@ -25,8 +25,8 @@ SH = scaled_shape(QWEN7B_32K, name="shard-gpu", batch=2, context=3000, true_clus
 
 
 class Shards:
-    def __init__(self, shape, n, injected, seed=0, p2p=False):
-        self.shape, self.n = shape, n
+    def __init__(self, shape, n, injected, seed=0):
+        self.shape, self.n, self.seed = shape, n, seed
         self.parts = [make_shard_workload(shape, r, n, seed=seed) for r in range(n)]
         self.steps = []
         for r, p in enumerate(self.parts):
@@ -37,19 +37,6 @@ class Shards:
                 kc, vc, summ, num_query_heads=shape.num_query_heads, n_total=p.n_total,
                 topk_clusters=shape.topk_clusters, samples=p.samples, shard_index=r,
                 num_shards=n, cluster_base=p.cluster_base, seed=seed, injected=injected))
-        self.p2p = p2p
-        self.buffers = []
-        if p2p:  # one exchange buffer per shard, all on this device
-            import ctypes
-            from santapp_b200 import _lib
-            lib = _lib.load()
-            nbytes = self.steps[0].p2p_buffer_bytes()
-            for _ in range(n):
-                ptr = ctypes.c_void_p()
-                _lib.check("alloc", lib.santa_p2p_alloc(nbytes, ctypes.byref(ptr)))
-                self.buffers.append(ptr.value)
-            for st in self.steps:
-                st.bind_p2p(self.buffers)
         self.osum = {}
         for r, p in enumerate(self.parts):
             for b in range(shape.batch):
@@ -58,42 +45,15 @@ class Shards:
                     self.osum[(r, b, kv)] = O.build_summary(K[:p.sample_end],
                                                             p.labels[b, kv].numpy(), p.n_clusters)
 
-    def _raise_flags(self, ex):
-        """Emulated ranks share one stream, so no kernel may wait for another:
-        after the producing kernels finished, the host raises every shard's
-        flag in every buffer; the consuming kernels then find them up."""
-        import ctypes
-        from santapp_b200 import _lib
-        torch.cuda.synchronize()
-        lib = _lib.load()
-        epoch = self.steps[0].epoch
-        for buf in self.buffers:
-            for r in range(self.n):
-                _lib.check("poke", lib.santa_p2p_poke(ctypes.c_void_p(buf + (ex * 32 + r) * 8),
-                                                      epoch))
-
     def exchange_keys(self):
-        if self.p2p:  # the kernels wrote every shard's keys into every buffer
-            self._raise_flags(0)
-            return
         for st in self.steps:
             for r, src in enumerate(self.steps):
                 st.all_keys[r].copy_(src.keys)
 
     def exchange_partials(self):
-        if self.p2p:
-            self._raise_flags(1)
-            return
         for st in self.steps:
             for r, src in enumerate(self.steps):
                 st.all_partials[r].copy_(src.partial)
-
-    def close(self):
-        import ctypes
-        from santapp_b200 import _lib
-        for ptr in self.buffers:
-            _lib.load().santa_p2p_free(ctypes.c_void_p(ptr))
-        self.buffers = []
 
     def run(self, step, ranks=None):
         q = self.parts[0].queries[step].cuda().contiguous()
@@ -240,25 +200,110 @@ def test_shard_api_rejects_unsupported():
                           num_shards=2, cluster_base=0)
 
 
-@pytest.mark.parametrize("n", [2, 3])
-def test_sharded_peer_memory_exchange_matches_oracle(n):
-    """The kernels' own exchange (keys and partials stored into every
-    shard's buffer, flags awaited) gives the same result as the host-side
-    exchange.  The emulated shards run on one stream, so the host raises the
-    flags between the producing and the consuming kernels and no wait is
-    ever outstanding."""
+class PeerShards:
+    """The peer-memory form of the same shards on one GPU.  Emulated ranks
+    share one device, so no kernel may wait for another one's stores: before
+    rank r's launches, the other ranks' words of the step (their keys and
+    partials, from the NCCL-form run of the same step, tagged with the
+    epoch) are written into rank r's buffer, so its waits find them at once.
+    The exchange buffers are torch allocations (zeroed) on this device."""
+
+    def __init__(self, base: Shards, wait_limit_us=0):
+        from santapp_b200.attention.sharded import exchange_layout
+        sh = base.shape
+        self.base, self.n = base, base.n
+        self.steps = []
+        for r, p in enumerate(base.parts):
+            st0 = base.steps[r]
+            self.steps.append(ShardedDecodeStep(
+                st0.key_cache, st0.value_cache, st0.summary,
+                num_query_heads=sh.num_query_heads, n_total=p.n_total,
+                topk_clusters=sh.topk_clusters, samples=p.samples, shard_index=r,
+                num_shards=self.n, cluster_base=p.cluster_base, seed=base.seed,
+                wait_limit_us=wait_limit_us))
+        st = self.steps[0]
+        self.lay = exchange_layout(self.n, st.rows, st.topk, st.head_dim)
+        self.bufs = [torch.zeros(self.lay["bytes"], dtype=torch.uint8, device="cuda")
+                     for _ in range(self.n)]
+        for s_ in self.steps:
+            s_.bind_p2p([b.data_ptr() for b in self.bufs])
+
+    def _words(self, r, region, epoch, rank):
+        """The int64 words of `rank`'s slot of `region` in buffer r."""
+        st = self.steps[0]
+        per = st.rows * (st.topk if region == "keys" else st.partial.shape[1])
+        off = self.lay[region] // 8 + ((epoch & 1) * self.n + rank) * per
+        return self.bufs[r].view(torch.int64)[off: off + per]
+
+    def run(self, step, ref_keys, ref_partials):
+        """Step `step` on every emulated rank; ref_keys / ref_partials: every
+        rank's candidate keys and partials of this step (NCCL form)."""
+        from santapp_b200.attention.sharded import key_words, partial_words
+        q = self.base.parts[0].queries[step].cuda().contiguous()
+        outs, sels = [], []
+        for r, st in enumerate(self.steps):
+            st.begin(q, step)
+            for o in range(self.n):
+                if o != r:
+                    self._words(r, "keys", st.epoch, o).copy_(key_words(ref_keys[o],
+                                                                              st.epoch))
+            st.plan()
+            sels.append(st.select())
+            for o in range(self.n):
+                if o != r:
+                    self._words(r, "parts", st.epoch, o).copy_(
+                        partial_words(ref_partials[o].reshape(-1), st.epoch))
+            outs.append(st.execute().clone())
+        torch.cuda.synchronize()
+        return q, sels, outs
+
+
+@pytest.mark.parametrize("n", [1, 2, 3])
+def test_sharded_peer_memory_exchange_matches_nccl_form(n):
+    """The kernels' own exchange (selection launch: candidates + key exchange
+    + threshold selection; attention launch: partial exchange + merge) gives
+    the same bits as the NCCL form with its four launches and host-side
+    exchanges, over both parities of the exchange buffers, and the result
+    matches the oracle's sharded estimator."""
     sh = scaled_shape(SH, steps=3)
-    obj = Shards(sh, n, injected=False, seed=5, p2p=True)
     ref = Shards(sh, n, injected=False, seed=5)
-    for step in range(3):  # both parities of the exchange buffers
-        q, sels, outs = obj.run(step)
-        _, _, outs_ref = ref.run(step)
-        for out in outs:
-            assert torch.equal(out, outs_ref[0])
+    obj = PeerShards(ref)
+    for step in range(3):
+        q, sels_ref, outs_ref = ref.run(step)
+        keys = [st.keys.clone() for st in ref.steps]
+        parts = [st.partial.clone() for st in ref.steps]
+        _, sels, outs = obj.run(step, keys, parts)
+        for r in range(n):
+            assert torch.equal(sels[r][0], sels_ref[r][0]), (step, r)
+            assert torch.equal(sels[r][1], sels_ref[r][1]), (step, r)
+            assert torch.equal(outs[r], outs_ref[0]), (step, r)
+            assert torch.equal(obj.steps[r].lse, ref.steps[0].lse)
+            assert torch.equal(obj.steps[r].ess, ref.steps[0].ess)
         assert all(int(st.p2p_error.item()) == 0 for st in obj.steps)
 
     def ranks_of(b, h, osel, osums):
-        return _oracle_ranks(sh, obj.parts, osums, osel, b, h, seed=5, step=2)
+        return _oracle_ranks(sh, ref.parts, osums, osel, b, h, seed=5, step=2)
 
-    _check(obj, q, sels, outs, ranks_of)
-    obj.close()
+    _check(ref, q, sels_ref, outs_ref, ranks_of)
+
+
+def test_peer_memory_wait_runs_out():
+    """A peer that never sends: rank 0 of two emulated shards runs alone with
+    a 2 ms wait limit.  Its selection launch gives up waiting for rank 1's
+    keys and sets the error flag; the attention launch sees the flag, does
+    not wait at all and writes NaN outputs; both launches return; the Python
+    step raises on its next call and in check_p2p()."""
+    sh = scaled_shape(SH, steps=2)
+    ref = Shards(sh, 2, injected=False, seed=9)
+    obj = PeerShards(ref, wait_limit_us=2000)
+    st = obj.steps[0]
+    q = ref.parts[0].queries[0].cuda().contiguous()
+    out = st(q, 0)
+    torch.cuda.synchronize()
+    assert int(st.p2p_error.item()) == 1
+    assert torch.isnan(out).all()
+    assert torch.isnan(st.lse).all()
+    with pytest.raises(RuntimeError, match="ran out of time"):
+        st.check_p2p()
+    with pytest.raises(RuntimeError, match="ran out of time"):
+        st(q, 1)
