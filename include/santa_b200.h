@@ -190,8 +190,11 @@ int santa_decode_execute(const SantaGeometry *geo, const SantaDecodeParams *p, c
  *   - Geometries whose santa_decode_workspace_bytes exceeds the array are
  *     refused with SANTA_ERR_WORKSPACE.
  *   - The first call on a device looks up the array's device address (once
- *     per device, with that device current); make that first call before any
- *     stream capture.
+ *     per device, with that device current) and keeps it for the life of the
+ *     process; make that first call before any stream capture.  The address
+ *     belongs to the device's primary context: a process that destroys that
+ *     context (cudaDeviceReset) must not call this entry point on that device
+ *     again, since the kept address would be stale.
  *   - All calls on a device share the one array and it keeps the previous
  *     call's contents; each call clears what must start at zero, but calls
  *     whose work overlaps on the GPU (other streams, other host threads) race

@@ -707,6 +707,11 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
     // round trip on the tail's critical path.
     __shared__ __align__(16) DecodeArgs s_args;
     if (tid == kGThreads - 1) s_args = a;
+    // Launched as a programmatic dependent of the selection kernel: this
+    // CTA may start while the selection's last CTAs still run; everything
+    // below reads what the selection wrote, so wait for it to complete
+    // (a no-op when the launch had no such dependency).
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
 
     if (warp == 0) {
         int carry = 0;
@@ -1205,7 +1210,19 @@ static int launch_execute_d(DecodeArgs &a, cudaStream_t stream) {
         const size_t sm = gather_smem_bytes<D>(BH);
         if (sm > 227 * 1024) return SANTA_ERR_UNSUPPORTED;
         if (int st = ensure_dyn_smem((const void *)decode_attend_gather_kernel<D>, sm)) return st;
-        decode_attend_gather_kernel<D><<<num_sms(), kGThreads, sm, stream>>>(a);
+        // programmatic dependent launch: the grid is set up while the
+        // selection kernel (which triggers it at its start) finishes
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)num_sms(), 1, 1);
+        cfg.blockDim = dim3(kGThreads, 1, 1);
+        cfg.dynamicSmemBytes = sm;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        SANTA_CUDA_CHECK(cudaLaunchKernelEx(&cfg, decode_attend_gather_kernel<D>, a));
     } else {
         const size_t sm = simt_smem_bytes<D>(Gmax);
         if (int st = ensure_dyn_smem((const void *)decode_attend_simt_kernel<D, float>, sm))

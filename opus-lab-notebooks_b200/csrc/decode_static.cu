@@ -25,7 +25,10 @@ void *g_scratch_ptr[kMaxDevices] = {};  // device address of g_decode_scratch pe
 // Device address of the scratch array on the current device.  Host code must
 // not use the name g_decode_scratch as a pointer: on the host it is only a
 // stand-in, so its address is looked up once per device, with that device
-// current, and cached.
+// current, and cached for the life of the process.  The address belongs to
+// the device's primary context; after cudaDeviceReset destroys that context
+// the cached address is stale, so a process that resets a device must not
+// call this entry point on it again (the header says so).
 static int scratch_address(void **out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);

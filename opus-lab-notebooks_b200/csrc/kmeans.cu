@@ -26,9 +26,12 @@
 //   kmeans_partition_kernel     stable counting sort of the batch labels
 //   kmeans_update_kernel        one CTA per cluster, one thread per feature
 //   kmeans_reassign_kernel      centre <- batch row, count <- given value
-//   kpp_*                       greedy k-means++ (:73-126): one fixed-point
-//                               scan + search launch and one candidate
-//                               launch per new centre, no host round trip
+//   kpp_persistent_kernel       greedy k-means++ (:73-126) in one cooperative
+//                               launch: per new centre a one-CTA fixed-point
+//                               scan + search phase and an all-CTA candidate
+//                               phase between bounded grid barriers (the
+//                               kpp_first / scan / candidates kernels are the
+//                               same phases as separate launches)
 #include "common.cuh"
 
 #include <math.h>
@@ -376,6 +379,8 @@ __global__ void kmeans_reassign_kernel(const float *x, const int64_t *rows, cons
 // greedy k-means++ (minibatch_kmeans.py:73-126)
 // ---------------------------------------------------------------------------
 struct KppWs {
+    int32_t *err;                 // set to 1 if a grid barrier of the seeding gave up
+    unsigned *bar;                // grid barrier counter of the persistent seeding kernel
     float *closest;               // [n]
     float *cum;                   // [n]
     float *cand;                  // [trials][n]
@@ -390,10 +395,13 @@ static size_t kpp_layout(int64_t n, int trials, char *base, KppWs *ws) {
         off = (off + b + 255) & ~(size_t)255;
         return o;
     };
+    const size_t o_er = take(16);  // first: err, bar
     const size_t o_cl = take((size_t)n * 4), o_cu = take((size_t)n * 4);
     const size_t o_ca = take((size_t)trials * n * 4);
     const size_t o_pf = take((size_t)(trials + 1) * 16), o_ci = take((size_t)trials * 8);
     if (base && ws) {
+        ws->err = (int32_t *)(base + o_er);
+        ws->bar = (unsigned *)(base + o_er + 4);
         ws->closest = (float *)(base + o_cl);
         ws->cum = (float *)(base + o_cu);
         ws->cand = (float *)(base + o_ca);
@@ -405,7 +413,30 @@ static size_t kpp_layout(int64_t n, int trials, char *base, KppWs *ws) {
 
 constexpr int kKppThreads = 256;
 
-// centre 0 = init row first_id; closest distance of every init row to it
+// centre 0 = init row first_id; closest distance of every init row to it.
+// Rows i = blk * NT + tid, blk + nblk, ... (a grid-stride loop); c0s is the
+// first centre staged in shared memory by the caller.
+template <int NT>
+__device__ __forceinline__ void kpp_first_rows(const float *x, const int64_t *rows,
+                                               const float *xx, int64_t n, int d, int trials,
+                                               int64_t first_id, const float *c0s, int blk,
+                                               int nblk, KppWs &ws, u128 *sw) {
+    const float c0 = xx[row_of(rows, first_id)];
+    for (int64_t i0 = (int64_t)blk * NT; i0 < n; i0 += (int64_t)nblk * NT) {
+        const int64_t i = i0 + threadIdx.x;
+        u128 fx = 0;
+        if (i < n) {
+            const float *xi = x + row_of(rows, i) * d;
+            float acc = 0.0f;
+            for (int t = 0; t < d; ++t) acc = fmaf(xi[t], c0s[t], acc);
+            const float v = dist2_def(xx[row_of(rows, i)], c0, acc);
+            ws.closest[i] = v;
+            fx = fx_of(v);
+        }
+        block_add_u128<NT>(fx, ws.pot_fx + 2 * trials, sw);
+    }
+}
+
 __global__ void __launch_bounds__(kKppThreads) kpp_first_kernel(
     const float *x, const int64_t *rows, const float *xx, int64_t n, int d, int trials,
     int64_t first_id, float *centers, int64_t *chosen, KppWs ws) {
@@ -418,32 +449,24 @@ __global__ void __launch_bounds__(kKppThreads) kpp_first_kernel(
     }
     if (blockIdx.x == 0 && threadIdx.x == 0 && chosen) chosen[0] = first_id;
     __syncthreads();
-    const float c0 = xx[fr];
-    const int64_t i = (int64_t)blockIdx.x * kKppThreads + threadIdx.x;
-    u128 fx = 0;
-    if (i < n) {
-        const float *xi = x + row_of(rows, i) * d;
-        float acc = 0.0f;
-        for (int t = 0; t < d; ++t) acc = fmaf(xi[t], kpp_smem[t], acc);
-        const float v = dist2_def(xx[row_of(rows, i)], c0, acc);
-        ws.closest[i] = v;
-        fx = fx_of(v);
-    }
-    block_add_u128<kKppThreads>(fx, ws.pot_fx + 2 * trials, sw);
+    kpp_first_rows<kKppThreads>(x, rows, xx, n, d, trials, first_id, kpp_smem, blockIdx.x,
+                                gridDim.x, ws, sw);
 }
 
 constexpr int kScanThreads = 1024;
 
-// One CTA.  ci >= 2: pick the best candidate of centre ci-1 (lowest
-// potential, first on ties), make it centre ci-1 and its distances the new
-// closest distances.  ci <= k-1: fixed-point prefix sums of closest,
-// then the searchsorted of the trials' uniform draws for centre ci.
-__global__ void __launch_bounds__(kScanThreads) kpp_scan_kernel(
-    const float *x, const int64_t *rows, int64_t n, int d, int k, int trials, int ci,
-    const double *uniforms, float *centers, int64_t *chosen, KppWs ws) {
-    __shared__ u128 sw[kScanThreads / 32 + 1];
-    __shared__ float s_pot;
-    __shared__ int s_best;
+// One CTA of NT threads.  ci >= 2: pick the best candidate of centre ci-1
+// (lowest potential, first on ties), make it centre ci-1 and its distances
+// the new closest distances.  ci <= k-1: fixed-point prefix sums of closest,
+// then the searchsorted of the trials' uniform draws for centre ci.  The
+// prefix sums are exact integers, so any split of the rows over threads
+// gives the same values.
+template <int NT>
+__device__ __forceinline__ void kpp_scan_cta(const float *x, const int64_t *rows, int64_t n,
+                                             int d, int k, int trials, int ci,
+                                             const double *uniforms, float *centers,
+                                             int64_t *chosen, KppWs &ws, u128 *sw, float &s_pot,
+                                             int &s_best) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) {
         if (ci >= 2) {
@@ -470,16 +493,15 @@ __global__ void __launch_bounds__(kScanThreads) kpp_scan_kernel(
     const int best = s_best;
     if (best >= 0) {
         const int64_t src = row_of(rows, ws.cid[best]);
-        for (int j = tid; j < d; j += kScanThreads)
-            centers[(int64_t)(ci - 1) * d + j] = x[src * d + j];
+        for (int j = tid; j < d; j += NT) centers[(int64_t)(ci - 1) * d + j] = x[src * d + j];
         const float *cb = ws.cand + (int64_t)best * n;
-        for (int64_t i = tid; i < n; i += kScanThreads) ws.closest[i] = cb[i];
+        for (int64_t i = tid; i < n; i += NT) ws.closest[i] = cb[i];
     }
     __syncthreads();
     if (ci >= k) return;  // the last centre is placed: no further draw
     if (tid < 2 * trials) ws.pot_fx[tid] = 0ull;  // candidate sums of centre ci
     // inclusive prefix sums: thread chunks, block scan of the chunk totals
-    const int64_t per = (n + kScanThreads - 1) / kScanThreads;
+    const int64_t per = (n + NT - 1) / NT;
     const int64_t i0 = (int64_t)tid * per, i1 = min(n, i0 + per);
     u128 local = 0;
     for (int64_t i = i0; i < i1; ++i) local += fx_of(ws.closest[i]);
@@ -493,7 +515,7 @@ __global__ void __launch_bounds__(kScanThreads) kpp_scan_kernel(
     if (lane == 31) sw[warp] = v;
     __syncthreads();
     if (warp == 0) {
-        const u128 w = sw[lane];
+        const u128 w = lane < NT / 32 ? sw[lane] : (u128)0;
         u128 s = w;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -502,7 +524,7 @@ __global__ void __launch_bounds__(kScanThreads) kpp_scan_kernel(
                 __shfl_up_sync(0xffffffffu, (unsigned long long)(s >> 64), o);
             if (lane >= o) s += ((u128)hi << 64) | lo;
         }
-        sw[lane] = s - w;
+        if (lane < NT / 32) sw[lane] = s - w;
     }
     __syncthreads();
     u128 run = sw[warp] + v - local;
@@ -524,48 +546,150 @@ __global__ void __launch_bounds__(kScanThreads) kpp_scan_kernel(
     }
 }
 
+__global__ void __launch_bounds__(kScanThreads) kpp_scan_kernel(
+    const float *x, const int64_t *rows, int64_t n, int d, int k, int trials, int ci,
+    const double *uniforms, float *centers, int64_t *chosen, KppWs ws) {
+    __shared__ u128 sw[kScanThreads / 32 + 1];
+    __shared__ float s_pot;
+    __shared__ int s_best;
+    kpp_scan_cta<kScanThreads>(x, rows, n, d, k, trials, ci, uniforms, centers, chosen, ws, sw,
+                               s_pot, s_best);
+}
+
+// The trials' candidate rows staged into shared memory ([trials][d]) and
+// their squared norms.
+__device__ __forceinline__ void kpp_stage_candidates(const float *x, const int64_t *rows,
+                                                     const float *xx, int d, int trials,
+                                                     const KppWs &ws, float *cs, float *s_cc,
+                                                     int nt) {
+    for (int i = threadIdx.x; i < trials * d; i += nt) {
+        const int t = i / d, j = i - t * d;
+        cs[i] = x[row_of(rows, ws.cid[t]) * d + j];
+    }
+    if (threadIdx.x < trials) s_cc[threadIdx.x] = xx[row_of(rows, ws.cid[threadIdx.x])];
+}
+
 // distance of every init row to each candidate (capped by the closest
-// distance so far) and the candidates' potentials
+// distance so far) and the candidates' potentials; rows as kpp_first_rows
+template <int NT>
+__device__ __forceinline__ void kpp_candidate_rows(const float *x, const int64_t *rows,
+                                                   const float *xx, int64_t n, int d, int trials,
+                                                   const float *cs, const float *s_cc, int blk,
+                                                   int nblk, KppWs &ws, u128 *sw) {
+    for (int64_t r0 = (int64_t)blk * NT; r0 < n; r0 += (int64_t)nblk * NT) {
+        const int64_t i = r0 + threadIdx.x;
+        float acc[kKmMaxTrials];
+#pragma unroll
+        for (int t = 0; t < kKmMaxTrials; ++t) acc[t] = 0.f;
+        float xxi = 0.f, cl = 0.f;
+        if (i < n) {
+            const float *xi = x + row_of(rows, i) * d;
+            for (int tt = 0; tt < d; ++tt) {
+                const float a = xi[tt];
+#pragma unroll
+                for (int t = 0; t < kKmMaxTrials; ++t)
+                    if (t < trials) acc[t] = fmaf(cs[t * d + tt], a, acc[t]);
+            }
+            xxi = xx[row_of(rows, i)];
+            cl = ws.closest[i];
+        }
+#pragma unroll
+        for (int t = 0; t < kKmMaxTrials; ++t) {
+            if (t < trials) {  // block-uniform
+                u128 fx = 0;
+                if (i < n) {
+                    float v = dist2_def(s_cc[t], xxi, acc[t]);
+                    if (cl < v) v = cl;
+                    ws.cand[(int64_t)t * n + i] = v;
+                    fx = fx_of(v);
+                }
+                block_add_u128<NT>(fx, ws.pot_fx + 2 * t, sw);
+            }
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kKppThreads) kpp_candidates_kernel(
     const float *x, const int64_t *rows, const float *xx, int64_t n, int d, int trials,
     KppWs ws) {
     extern __shared__ __align__(16) float kpp_smem[];  // [trials][d]
     __shared__ u128 sw[kKppThreads / 32];
     __shared__ float s_cc[kKmMaxTrials];
-    for (int i = threadIdx.x; i < trials * d; i += kKppThreads) {
-        const int t = i / d, j = i - t * d;
-        kpp_smem[i] = x[row_of(rows, ws.cid[t]) * d + j];
-    }
-    if (threadIdx.x < trials) s_cc[threadIdx.x] = xx[row_of(rows, ws.cid[threadIdx.x])];
+    kpp_stage_candidates(x, rows, xx, d, trials, ws, kpp_smem, s_cc, kKppThreads);
     __syncthreads();
-    const int64_t i = (int64_t)blockIdx.x * kKppThreads + threadIdx.x;
-    float acc[kKmMaxTrials];
-#pragma unroll
-    for (int t = 0; t < kKmMaxTrials; ++t) acc[t] = 0.f;
-    float xxi = 0.f, cl = 0.f;
-    if (i < n) {
-        const float *xi = x + row_of(rows, i) * d;
-        for (int tt = 0; tt < d; ++tt) {
-            const float a = xi[tt];
-#pragma unroll
-            for (int t = 0; t < kKmMaxTrials; ++t)
-                if (t < trials) acc[t] = fmaf(kpp_smem[t * d + tt], a, acc[t]);
-        }
-        xxi = xx[row_of(rows, i)];
-        cl = ws.closest[i];
-    }
-#pragma unroll
-    for (int t = 0; t < kKmMaxTrials; ++t) {
-        if (t < trials) {  // block-uniform
-            u128 fx = 0;
-            if (i < n) {
-                float v = dist2_def(s_cc[t], xxi, acc[t]);
-                if (cl < v) v = cl;
-                ws.cand[(int64_t)t * n + i] = v;
-                fx = fx_of(v);
+    kpp_candidate_rows<kKppThreads>(x, rows, xx, n, d, trials, kpp_smem, s_cc, blockIdx.x,
+                                    gridDim.x, ws, sw);
+}
+
+// Grid-wide barrier of the persistent seeding kernel (all CTAs resident: a
+// cooperative launch).  Instance `phase` completes when the counter reaches
+// phase * gridDim.x.  The wait is bounded (~2 s): a CTA that gives up sets
+// the error flag and every later barrier of that CTA fails at once.
+__device__ __forceinline__ bool kpp_grid_sync(KppWs &ws, unsigned phase, int *s_fail) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (!*s_fail) {
+            __threadfence();  // this CTA's global writes before its arrival
+            atomicAdd(ws.bar, 1u);
+            const unsigned target = phase * gridDim.x;
+            uint64_t t0, t;
+            asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t0));
+            for (uint32_t it = 0;; ++it) {
+                unsigned v;
+                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(ws.bar)
+                             : "memory");
+                if (v >= target) break;
+                if ((it & 63u) == 63u) {
+                    asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+                    if (t - t0 > 2000000000ull) {
+                        atomicExch(ws.err, 1);
+                        *s_fail = 1;
+                        break;
+                    }
+                }
             }
-            block_add_u128<kKppThreads>(fx, ws.pot_fx + 2 * t, sw);
         }
+    }
+    __syncthreads();
+    return !*s_fail;
+}
+
+// The whole greedy k-means++ seeding in one cooperative launch: the first
+// centre's distances, then per centre ci the scan phase (CTA 0: pick the
+// previous centre's best candidate, prefix sums, searchsorted) and the
+// candidate phase (every CTA), with a grid barrier after each.  The same
+// arithmetic as the three-kernel form above, so the same centres.
+__global__ void __launch_bounds__(kKppThreads) kpp_persistent_kernel(
+    const float *x, const int64_t *rows, const float *xx, int64_t n, int d, int k, int trials,
+    int64_t first_id, const double *uniforms, float *centers, int64_t *chosen, KppWs ws) {
+    extern __shared__ __align__(16) float kpp_smem[];  // [max(d, trials * d)]
+    __shared__ u128 sw[kKppThreads / 32];
+    __shared__ float s_cc[kKmMaxTrials];
+    __shared__ float s_pot;
+    __shared__ int s_best, s_fail;
+    if (threadIdx.x == 0) s_fail = 0;
+    const int64_t fr = row_of(rows, first_id);
+    for (int j = threadIdx.x; j < d; j += kKppThreads) {
+        kpp_smem[j] = x[fr * d + j];
+        if (blockIdx.x == 0) centers[j] = kpp_smem[j];
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0 && chosen) chosen[0] = first_id;
+    __syncthreads();
+    kpp_first_rows<kKppThreads>(x, rows, xx, n, d, trials, first_id, kpp_smem, blockIdx.x,
+                                gridDim.x, ws, sw);
+    unsigned phase = 0;
+    if (!kpp_grid_sync(ws, ++phase, &s_fail)) return;
+    for (int ci = 1; ci <= k; ++ci) {
+        if (blockIdx.x == 0)
+            kpp_scan_cta<kKppThreads>(x, rows, n, d, k, trials, ci, uniforms, centers, chosen, ws,
+                                      sw, s_pot, s_best);
+        if (ci == k || k < 2) break;
+        if (!kpp_grid_sync(ws, ++phase, &s_fail)) return;
+        kpp_stage_candidates(x, rows, xx, d, trials, ws, kpp_smem, s_cc, kKppThreads);
+        __syncthreads();
+        kpp_candidate_rows<kKppThreads>(x, rows, xx, n, d, trials, kpp_smem, s_cc, blockIdx.x,
+                                        gridDim.x, ws, sw);
+        if (!kpp_grid_sync(ws, ++phase, &s_fail)) return;
     }
 }
 
@@ -670,7 +794,35 @@ extern "C" int santa_kmeans_plusplus(const float *x, const int64_t *rows, const 
     if (!workspace || workspace_bytes < need) return SANTA_ERR_WORKSPACE;
     KppWs ws;
     kpp_layout(n, trials, (char *)workspace, &ws);
+    // the error word, the barrier counter and the potential sums start at zero
+    SANTA_CUDA_CHECK(cudaMemsetAsync(ws.err, 0, 16, stream));
     SANTA_CUDA_CHECK(cudaMemsetAsync(ws.pot_fx, 0, (size_t)(trials + 1) * 16, stream));
+    const size_t psm = (size_t)(trials > 1 ? trials : 1) * d * 4;
+    {
+        // one cooperative launch: every CTA resident (the grid barriers need it)
+        int st = km_set_smem((const void *)kpp_persistent_kernel, psm);
+        if (st) return st;
+        int per_sm = 0;
+        SANTA_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &per_sm, kpp_persistent_kernel, kKppThreads, psm));
+        const int64_t want = ceil_div64(n, kKppThreads);
+        const int64_t cap = (int64_t)per_sm * num_sms();
+        if (cap > 0) {
+            int grid = (int)(want < cap ? want : cap);
+            int64_t n64 = n;
+            int d32 = d, k32 = k, t32 = trials;
+            int64_t f64 = first_id;
+            void *args[] = {(void *)&x,        (void *)&rows,     (void *)&xx,
+                            (void *)&n64,      (void *)&d32,      (void *)&k32,
+                            (void *)&t32,      (void *)&f64,      (void *)&uniforms,
+                            (void *)&centers,  (void *)&chosen_ids, (void *)&ws};
+            SANTA_CUDA_CHECK(cudaLaunchCooperativeKernel((const void *)kpp_persistent_kernel,
+                                                         dim3(grid), dim3(kKppThreads), args,
+                                                         psm, stream));
+            return SANTA_OK;
+        }
+    }
+    // (no occupancy: the launch-per-phase form)
     const unsigned grid = (unsigned)ceil_div64(n, kKppThreads);
     kpp_first_kernel<<<grid, kKppThreads, (size_t)d * 4, stream>>>(x, rows, xx, n, d, trials,
                                                                    first_id, centers, chosen_ids,

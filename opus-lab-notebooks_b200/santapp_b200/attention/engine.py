@@ -156,6 +156,8 @@ class SantaB200Engine:
         self.track_traffic = True  # draw accounting, read back once per generate
         self._traffic_pending: list = []
         self._head_calls = 0
+        self._capture_q: dict[int, torch.Tensor] | None = None
+        self._planted: dict | None = None
         self._lib = _lib.load()
 
     def _cfg(self, name: str):
@@ -191,6 +193,7 @@ class SantaB200Engine:
         self._probe_q.clear()
         self._n_groups_host.clear()
         self._traffic_pending = []
+        self._planted = None
         self.traffic = DecodeTrafficTracker()
 
     def _trim_cache(self, length: int) -> None:
@@ -252,6 +255,9 @@ class SantaB200Engine:
                     self._n_groups_host[layer_id] = self.summaries[layer_id].n_groups
                 self._traffic_pending.append((cached.length, layer_id, res.n_exact.clone(),
                                               res.ess.clone()))
+            if self._planted is not None and self._decode_step == 0:
+                self._check_planted(layer_id, q_f32[:, :, 0].contiguous(), cached,
+                                    float(attention.scaling))
             out = res.out.to(torch.bfloat16).view(B, 1, Hq * D)
         elif start == 0:
             # prompt: causal attention of every position over the prompt
@@ -262,6 +268,8 @@ class SantaB200Engine:
             out = out.transpose(1, 2).reshape(B, Tn, Hq * D)
         else:
             # dense decode / continued prompt over the cache (fidelity path)
+            if self._capture_q is not None and Tn == 1:
+                self._capture_q[layer_id] = q_bf[:, :, 0].float()
             kf, vf = cached.view()
             kf = kf.repeat_interleave(self.group, dim=1)
             vf = vf.repeat_interleave(self.group, dim=1)
@@ -277,6 +285,14 @@ class SantaB200Engine:
     # ---- prefill and clustering ---------------------------------------------
     @torch.inference_mode()
     def _dense_prefill_and_cluster(self, input_ids: torch.Tensor, *, probe_seed: int):
+        prefill_s, sample_end = self._prefill(input_ids, probe_seed=probe_seed)
+        cluster_s, n_clusters = self._cluster()
+        return prefill_s, cluster_s, sample_end, n_clusters
+
+    @torch.inference_mode()
+    def _prefill(self, input_ids: torch.Tensor, *, probe_seed: int):
+        """Dense prefill of the prompt into the caches, keeping every layer's
+        queries at the probe positions (santapp.py:542-597)."""
         B, T = input_ids.shape
         sample_end = T - 1 - self.config.recent_window
         if sample_end < 2:
@@ -295,16 +311,22 @@ class SantaB200Engine:
         finally:
             self._probe_idx = None
         torch.cuda.synchronize()
-        prefill_s = time.perf_counter() - t0
+        return time.perf_counter() - t0, sample_end
+
+    @torch.inference_mode()
+    def _cluster(self):
+        """Fingerprints, MiniBatchKMeans and the cluster summary of every
+        (layer, KV head, sequence) over the old prefix (santapp.py:598-722)."""
+        sample_end = self.sample_end
         n_clusters = self._cfg("n_clusters") or cluster_count(sample_end, self.config.group_size)
         km = self.config.kmeans
-        P = len(probes)
         t1 = time.perf_counter()
         for layer_id in range(self.num_layers):
             qp = self._probe_q.pop(layer_id)  # [B, Hq, P, D] fp32
             cached = self.cache[layer_id]
+            B, P = qp.shape[0], qp.shape[2]
             labels = torch.empty(B, self.num_kv_heads, sample_end, dtype=torch.int32,
-                                 device=input_ids.device)
+                                 device=qp.device)
             for b in range(B):
                 for kv in range(self.num_kv_heads):
                     fp = build_fingerprints(cached.key[b, kv, :sample_end], qp[b].contiguous(),
@@ -320,13 +342,84 @@ class SantaB200Engine:
                                                      n_clusters, sample_end=sample_end,
                                                      n_total=cached.length)
         torch.cuda.synchronize()
-        return prefill_s, time.perf_counter() - t1, sample_end, n_clusters
+        return time.perf_counter() - t1, n_clusters
+
+    # ---- planted-key retrieval check ------------------------------------------
+    @torch.inference_mode()
+    def _plant_keys(self, last_token: torch.Tensor, position: int, *, n_planted: int,
+                    scale: float, seed: int) -> dict:
+        """Synthetic retrieval check: for every (layer, sequence, KV head),
+        ``n_planted`` old-prefix keys at seeded random positions are replaced
+        by ``scale`` x the mean key norm along the direction of the first
+        query head of the group at the first decode step.  That direction
+        comes from a dense dry run of that step (the decode query of a layer
+        depends on the earlier layers' attention outputs, which the planted
+        keys barely move).  Call after the prefill, before clustering."""
+        B = last_token.shape[0]
+        self._capture_q = {}
+        try:
+            self.model(last_token, position_ids=torch.full((B, 1), position, dtype=torch.long,
+                                                           device=last_token.device),
+                       use_cache=False, logits_to_keep=1)
+            queries = self._capture_q
+        finally:
+            self._capture_q = None
+        self._trim_cache(position)
+        rs = np.random.RandomState(seed)
+        planted = {}
+        for layer_id in range(self.num_layers):
+            c = self.cache[layer_id]
+            pos = np.stack([[np.sort(rs.choice(self.sample_end, n_planted, replace=False))
+                             for _ in range(self.num_kv_heads)] for _ in range(B)])
+            for b in range(B):
+                for kv in range(self.num_kv_heads):
+                    qd = queries[layer_id][b, kv * self.group]
+                    qhat = qd / qd.norm()
+                    norm = c.key[b, kv, :self.sample_end].float().norm(dim=-1).mean()
+                    idx = torch.from_numpy(pos[b, kv]).to(c.key.device)
+                    c.key[b, kv, idx] = (scale * norm * qhat).to(c.key.dtype)[None]
+            planted[layer_id] = pos
+        return planted
+
+    def _check_planted(self, layer_id: int, q: torch.Tensor, cached, scale: float) -> None:
+        """At the first sparse decode step: the selection of the first query
+        head of every group, read out, must cover every planted position."""
+        from .santapp import santa_decode_select
+        summ = self.summaries[layer_id]
+        sel, _, _ = santa_decode_select(q, cached.key, cached.value, summ,
+                                        mode=self.config.mode, n_total=cached.length,
+                                        sample_end=self.sample_end,
+                                        topk_clusters=self._cfg("topk_clusters"),
+                                        token_budget=self.config.samples_per_head,
+                                        samples=self.config.samples_per_head, scale=scale,
+                                        seed=self.config.sample_seed, step=0)
+        pos = self._planted["positions"][layer_id]                  # [B, Hkv, n]
+        B, Hkv, n = pos.shape
+        positions = summ.positions.long()                           # [B, Hkv, N]
+        p = torch.from_numpy(pos).to(positions.device)
+        member_pos = torch.gather(positions, 2, p)                  # position in members
+        # cluster row of a member position: the last start at or before it
+        starts = summ.starts.long()
+        G = starts.shape[2]
+        valid = torch.arange(G, device=starts.device)[None, None] < summ.n_groups.long()[..., None]
+        big = torch.where(valid, starts, torch.full_like(starts, 1 << 40))
+        row = torch.searchsorted(big.contiguous(), member_pos.contiguous(), right=True) - 1
+        heads = torch.arange(Hkv, device=sel.device) * self.group   # first head of each group
+        sel_g = sel[:, heads]                                        # [B, Hkv, G]
+        landed = torch.gather(sel_g.long(), 2, row)                  # [B, Hkv, n]
+        self._planted["landed"] += int(landed.sum())
+        self._planted["total"] += B * Hkv * n
 
     # ---- generation ------------------------------------------------------------
     @torch.inference_mode()
     def generate(self, input_ids: torch.Tensor, *, max_new_tokens: int,
                  eos_token_ids: set[int] | None = None, stop_on_eos: bool = False,
-                 random_seed: int = 0) -> SantaGeneration:
+                 random_seed: int = 0, planted_keys: int = 0, plant_scale: float = 4.0,
+                 plant_seed: int = 0) -> SantaGeneration:
+        """santapp.py:794-908: prefill, clustering, then greedy decoding of
+        ``max_new_tokens`` tokens.  ``planted_keys`` > 0 adds the synthetic
+        retrieval check (``_plant_keys``): the metrics then report how many
+        planted positions the first decode step's selections covered."""
         if input_ids.ndim != 2:
             raise ValueError("input_ids must be [batch, T]")
         B, T = input_ids.shape
@@ -336,9 +429,17 @@ class SantaB200Engine:
         self.cache_capacity = T + max_new_tokens
         t0 = time.perf_counter()
         with self.patched():
-            prefill_s, cluster_s, sample_end, n_clusters = self._dense_prefill_and_cluster(
-                input_ids, probe_seed=random_seed)
+            prefill_s, sample_end = self._prefill(input_ids, probe_seed=random_seed)
             self._trim_cache(T - 1)
+            plant_s = 0.0
+            if planted_keys > 0:
+                tp = time.perf_counter()
+                pos = self._plant_keys(input_ids[:, -1:], T - 1, n_planted=planted_keys,
+                                       scale=plant_scale, seed=plant_seed)
+                self._planted = {"positions": pos, "landed": 0, "total": 0}
+                torch.cuda.synchronize()
+                plant_s = time.perf_counter() - tp
+            cluster_s, n_clusters = self._cluster()
             self.mode = self.config.mode
             self.traffic = DecodeTrafficTracker()
             generated = [[] for _ in range(B)]
@@ -370,6 +471,11 @@ class SantaB200Engine:
             "prefill_seconds": prefill_s, "clustering_seconds": cluster_s,
             "decode_seconds": decode_s, "total_seconds": time.perf_counter() - t0,
             "sampled_prefix_tokens": sample_end, "nominal_clusters_per_kv_head": n_clusters,
+            "planted_check": (None if self._planted is None else {
+                "planted_per_layer_sequence_kv_head": planted_keys,
+                "landed": self._planted["landed"], "total": self._planted["total"],
+                "all_landed": self._planted["landed"] == self._planted["total"],
+                "scale": plant_scale, "dry_run_seconds": plant_s}),
             **self.traffic.as_dict(),
         }
         self.clear()

@@ -11,8 +11,11 @@ centre update, the low-count reassignment — runs in the CUDA kernels
 and centres are reproducible bit for bit.
 
 Per mini-batch step the host uploads the step's batch ids and reads back the
-counts and the batch inertia (the early-stopping rule and the reassignment
-rule of minibatch_kmeans.py:241-315 need them), as the reference does.
+counts and the batch inertia into pinned memory, waiting on an event behind
+the copies (the early-stopping rule and the reassignment rule of
+minibatch_kmeans.py:241-315 need them before the next step's draws), as the
+reference's control flow requires.  The greedy k-means++ seeding is one
+cooperative kernel launch.
 """
 
 from __future__ import annotations
@@ -91,6 +94,7 @@ class SklearnLikeTorchMiniBatchKMeans:
             u_dev.data_ptr(), centers.data_ptr(), chosen.data_ptr(), ws.data_ptr(),
             nbytes.value, _lib.stream_handle()))
         self.init_ids_ = chosen
+        self._kpp_err = ws[:4].view(torch.int32)  # set if the seeding's grid barrier gave up
         return centers
 
     # ---- fit ---------------------------------------------------------------
@@ -159,6 +163,7 @@ class SklearnLikeTorchMiniBatchKMeans:
         ids_dev = torch.empty(batch_size, dtype=torch.int64, device=dev)
         labels_b = torch.empty(batch_size, dtype=torch.int32, device=dev)
         back = torch.empty(k + 4, dtype=torch.float32).pin_memory()
+        landed = torch.cuda.Event()  # the step's read-back is in pinned memory
         stream = _lib.stream_handle()
 
         n_steps = (self.max_iter * n) // batch_size
@@ -181,7 +186,8 @@ class SklearnLikeTorchMiniBatchKMeans:
                 uws.data_ptr(), ub.value, stream))
             back[:k].copy_(counts, non_blocking=True)
             back[k:].copy_(self._fx.view(torch.float32), non_blocking=True)
-            torch.cuda.current_stream().synchronize()
+            landed.record()
+            landed.synchronize()
             counts_host = back[:k].numpy().copy()
             batch_inertia = _fx_value(back[k:].numpy().view(np.uint64))
             if random_reassign and self.reassignment_ratio > 0.0:
@@ -231,6 +237,8 @@ class SklearnLikeTorchMiniBatchKMeans:
         labels = self._assign(x, None, xx_all, n, centers)
         self.labels_ = labels.long()
         self.inertia_ = _fx_value(self._fx.cpu().numpy().view(np.uint64))
+        if int(self._kpp_err.item()):
+            raise RuntimeError("k-means++ seeding: a grid barrier wait ran out of time")
         if self.verbose:
             print(f"GPU MiniBatchKMeans: {self.n_steps_} mini-batches, "
                   f"{self.n_iter_} effective epochs")

@@ -33,8 +33,17 @@ def model():
     with torch.device("cuda"):
         m = Qwen2ForCausalLM(cfg)
     m = m.to(torch.bfloat16).eval()
-    for p in m.parameters():  # N(0, 0.02) weights, as the random-init model of the spec
-        torch.nn.init.normal_(p, 0.0, 0.02)
+    # random init as the model's own initialiser does it: weight matrices and
+    # embeddings N(0, 0.02), biases 0, RMSNorm gains 1
+    g = torch.Generator(device="cuda").manual_seed(0)
+    with torch.no_grad():
+        for mod in m.modules():
+            if isinstance(mod, (torch.nn.Linear, torch.nn.Embedding)):
+                mod.weight.normal_(0.0, 0.02, generator=g)
+                if getattr(mod, "bias", None) is not None:
+                    mod.bias.zero_()
+            elif hasattr(mod, "variance_epsilon"):  # Qwen2RMSNorm
+                mod.weight.fill_(1.0)
     return m
 
 
@@ -236,3 +245,18 @@ def test_per_head_approximate_attention_matches_batched_decode(model):
             torch.testing.assert_close(got, batched[0, h], rtol=1e-5, atol=1e-5)
         assert eng.traffic.as_dict()["decode_attention_head_calls"] == eng.num_query_heads
     eng.clear()
+
+
+def test_planted_keys_through_the_engine(model):
+    """The model-level retrieval check: keys planted along each layer's first
+    decode query direction (before clustering) all land in the clusters the
+    first sparse decode step selects, in every layer, sequence and KV head."""
+    ids = _prompt(2, 900, seed=12)
+    cfg = SantaB200Config(mode="hybrid", samples_per_head=32, recent_window=64,
+                          probe_queries=16, n_clusters=24, topk_clusters=4,
+                          kmeans=KMeansConfig(batch_size=256, max_iter=10))
+    gen = SantaB200Engine(model, cfg).generate(ids, max_new_tokens=3, planted_keys=16)
+    chk = gen.metrics["planted_check"]
+    assert chk["total"] == 2 * 2 * 2 * 16  # layers x sequences x KV heads x planted
+    assert chk["all_landed"], chk
+    assert len(gen.token_ids) == 2 and all(len(t) == 3 for t in gen.token_ids)
