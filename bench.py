@@ -652,23 +652,36 @@ def run_model(args):
     query direction and the check reports how many land in the selections.
     Decode tokens/s = batch x steps / decode seconds (host clock around the
     synchronised loop)."""
+    import faulthandler
     from santapp_b200.attention.engine import KMeansConfig, SantaB200Config, SantaB200Engine
+    # a stuck phase shows up as periodic stack dumps on stderr
+    faulthandler.dump_traceback_later(300, repeat=True, file=sys.stderr)
+    t_start = time.perf_counter()
+
+    def log(msg):
+        print(f"[model {time.perf_counter() - t_start:8.1f} s] {msg}", file=sys.stderr, flush=True)
+
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     B, T = 4, args.model_context
+    log("building the random-init model")
     model = qwen7b_model(args.model_layers, dev, seed=args.seed)
+    log(f"model ready ({sum(p.numel() for p in model.parameters()) / 1e9:.2f} B parameters)")
     g = torch.Generator(device="cpu").manual_seed(args.seed)
     ids = torch.randint(0, 152064, (B, T), generator=g).to(dev)
     cfg = SantaB200Config(mode="hybrid", samples_per_head=256, topk_clusters=16, n_clusters=512,
                           recent_window=64, probe_queries=64, sample_seed=args.seed,
                           kmeans=KMeansConfig())
     eng = SantaB200Engine(model, cfg)
+    eng.log = log
     torch.cuda.synchronize()
     clocks = ClockSampler(torch.cuda.current_device())
     clocks.start()
     gen = eng.generate(ids, max_new_tokens=args.steps, planted_keys=16, plant_scale=4.0,
                        plant_seed=args.seed)
     clk = clocks.stop()
+    faulthandler.cancel_dump_traceback_later()
+    log("done")
     m = gen.metrics
     value = B * m["generated_tokens"] / m["decode_seconds"]
     return {

@@ -26,12 +26,13 @@
 //   kmeans_partition_kernel     stable counting sort of the batch labels
 //   kmeans_update_kernel        one CTA per cluster, one thread per feature
 //   kmeans_reassign_kernel      centre <- batch row, count <- given value
-//   kpp_persistent_kernel       greedy k-means++ (:73-126) in one cooperative
-//                               launch: per new centre a one-CTA fixed-point
-//                               scan + search phase and an all-CTA candidate
-//                               phase between bounded grid barriers (the
-//                               kpp_first / scan / candidates kernels are the
-//                               same phases as separate launches)
+//   kpp_*                       greedy k-means++ (:73-126): one fixed-point
+//                               scan + search launch (one CTA of 1024
+//                               threads) and one candidate launch per new
+//                               centre, no host round trip.  (One cooperative
+//                               launch with grid barriers between the phases
+//                               measured slower: its one-CTA scan phase ran
+//                               on the persistent grid's 256-thread CTA.)
 #include "common.cuh"
 
 #include <math.h>
@@ -379,8 +380,6 @@ __global__ void kmeans_reassign_kernel(const float *x, const int64_t *rows, cons
 // greedy k-means++ (minibatch_kmeans.py:73-126)
 // ---------------------------------------------------------------------------
 struct KppWs {
-    int32_t *err;                 // set to 1 if a grid barrier of the seeding gave up
-    unsigned *bar;                // grid barrier counter of the persistent seeding kernel
     float *closest;               // [n]
     float *cum;                   // [n]
     float *cand;                  // [trials][n]
@@ -395,13 +394,10 @@ static size_t kpp_layout(int64_t n, int trials, char *base, KppWs *ws) {
         off = (off + b + 255) & ~(size_t)255;
         return o;
     };
-    const size_t o_er = take(16);  // first: err, bar
     const size_t o_cl = take((size_t)n * 4), o_cu = take((size_t)n * 4);
     const size_t o_ca = take((size_t)trials * n * 4);
     const size_t o_pf = take((size_t)(trials + 1) * 16), o_ci = take((size_t)trials * 8);
     if (base && ws) {
-        ws->err = (int32_t *)(base + o_er);
-        ws->bar = (unsigned *)(base + o_er + 4);
         ws->closest = (float *)(base + o_cl);
         ws->cum = (float *)(base + o_cu);
         ws->cand = (float *)(base + o_ca);
@@ -621,78 +617,6 @@ __global__ void __launch_bounds__(kKppThreads) kpp_candidates_kernel(
                                     gridDim.x, ws, sw);
 }
 
-// Grid-wide barrier of the persistent seeding kernel (all CTAs resident: a
-// cooperative launch).  Instance `phase` completes when the counter reaches
-// phase * gridDim.x.  The wait is bounded (~2 s): a CTA that gives up sets
-// the error flag and every later barrier of that CTA fails at once.
-__device__ __forceinline__ bool kpp_grid_sync(KppWs &ws, unsigned phase, int *s_fail) {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        if (!*s_fail) {
-            __threadfence();  // this CTA's global writes before its arrival
-            atomicAdd(ws.bar, 1u);
-            const unsigned target = phase * gridDim.x;
-            uint64_t t0, t;
-            asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t0));
-            for (uint32_t it = 0;; ++it) {
-                unsigned v;
-                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(ws.bar)
-                             : "memory");
-                if (v >= target) break;
-                if ((it & 63u) == 63u) {
-                    asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
-                    if (t - t0 > 2000000000ull) {
-                        atomicExch(ws.err, 1);
-                        *s_fail = 1;
-                        break;
-                    }
-                }
-            }
-        }
-    }
-    __syncthreads();
-    return !*s_fail;
-}
-
-// The whole greedy k-means++ seeding in one cooperative launch: the first
-// centre's distances, then per centre ci the scan phase (CTA 0: pick the
-// previous centre's best candidate, prefix sums, searchsorted) and the
-// candidate phase (every CTA), with a grid barrier after each.  The same
-// arithmetic as the three-kernel form above, so the same centres.
-__global__ void __launch_bounds__(kKppThreads) kpp_persistent_kernel(
-    const float *x, const int64_t *rows, const float *xx, int64_t n, int d, int k, int trials,
-    int64_t first_id, const double *uniforms, float *centers, int64_t *chosen, KppWs ws) {
-    extern __shared__ __align__(16) float kpp_smem[];  // [max(d, trials * d)]
-    __shared__ u128 sw[kKppThreads / 32];
-    __shared__ float s_cc[kKmMaxTrials];
-    __shared__ float s_pot;
-    __shared__ int s_best, s_fail;
-    if (threadIdx.x == 0) s_fail = 0;
-    const int64_t fr = row_of(rows, first_id);
-    for (int j = threadIdx.x; j < d; j += kKppThreads) {
-        kpp_smem[j] = x[fr * d + j];
-        if (blockIdx.x == 0) centers[j] = kpp_smem[j];
-    }
-    if (blockIdx.x == 0 && threadIdx.x == 0 && chosen) chosen[0] = first_id;
-    __syncthreads();
-    kpp_first_rows<kKppThreads>(x, rows, xx, n, d, trials, first_id, kpp_smem, blockIdx.x,
-                                gridDim.x, ws, sw);
-    unsigned phase = 0;
-    if (!kpp_grid_sync(ws, ++phase, &s_fail)) return;
-    for (int ci = 1; ci <= k; ++ci) {
-        if (blockIdx.x == 0)
-            kpp_scan_cta<kKppThreads>(x, rows, n, d, k, trials, ci, uniforms, centers, chosen, ws,
-                                      sw, s_pot, s_best);
-        if (ci == k || k < 2) break;
-        if (!kpp_grid_sync(ws, ++phase, &s_fail)) return;
-        kpp_stage_candidates(x, rows, xx, d, trials, ws, kpp_smem, s_cc, kKppThreads);
-        __syncthreads();
-        kpp_candidate_rows<kKppThreads>(x, rows, xx, n, d, trials, kpp_smem, s_cc, blockIdx.x,
-                                        gridDim.x, ws, sw);
-        if (!kpp_grid_sync(ws, ++phase, &s_fail)) return;
-    }
-}
-
 // ---------------------------------------------------------------------------
 // host launchers
 // ---------------------------------------------------------------------------
@@ -794,35 +718,7 @@ extern "C" int santa_kmeans_plusplus(const float *x, const int64_t *rows, const 
     if (!workspace || workspace_bytes < need) return SANTA_ERR_WORKSPACE;
     KppWs ws;
     kpp_layout(n, trials, (char *)workspace, &ws);
-    // the error word, the barrier counter and the potential sums start at zero
-    SANTA_CUDA_CHECK(cudaMemsetAsync(ws.err, 0, 16, stream));
     SANTA_CUDA_CHECK(cudaMemsetAsync(ws.pot_fx, 0, (size_t)(trials + 1) * 16, stream));
-    const size_t psm = (size_t)(trials > 1 ? trials : 1) * d * 4;
-    {
-        // one cooperative launch: every CTA resident (the grid barriers need it)
-        int st = km_set_smem((const void *)kpp_persistent_kernel, psm);
-        if (st) return st;
-        int per_sm = 0;
-        SANTA_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-            &per_sm, kpp_persistent_kernel, kKppThreads, psm));
-        const int64_t want = ceil_div64(n, kKppThreads);
-        const int64_t cap = (int64_t)per_sm * num_sms();
-        if (cap > 0) {
-            int grid = (int)(want < cap ? want : cap);
-            int64_t n64 = n;
-            int d32 = d, k32 = k, t32 = trials;
-            int64_t f64 = first_id;
-            void *args[] = {(void *)&x,        (void *)&rows,     (void *)&xx,
-                            (void *)&n64,      (void *)&d32,      (void *)&k32,
-                            (void *)&t32,      (void *)&f64,      (void *)&uniforms,
-                            (void *)&centers,  (void *)&chosen_ids, (void *)&ws};
-            SANTA_CUDA_CHECK(cudaLaunchCooperativeKernel((const void *)kpp_persistent_kernel,
-                                                         dim3(grid), dim3(kKppThreads), args,
-                                                         psm, stream));
-            return SANTA_OK;
-        }
-    }
-    // (no occupancy: the launch-per-phase form)
     const unsigned grid = (unsigned)ceil_div64(n, kKppThreads);
     kpp_first_kernel<<<grid, kKppThreads, (size_t)d * 4, stream>>>(x, rows, xx, n, d, trials,
                                                                    first_id, centers, chosen_ids,

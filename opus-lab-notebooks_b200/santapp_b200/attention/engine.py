@@ -158,7 +158,12 @@ class SantaB200Engine:
         self._head_calls = 0
         self._capture_q: dict[int, torch.Tensor] | None = None
         self._planted: dict | None = None
+        self.log = None  # optional progress callback: log(message)
         self._lib = _lib.load()
+
+    def _log(self, msg: str) -> None:
+        if self.log is not None:
+            self.log(msg)
 
     def _cfg(self, name: str):
         """A config field; SantaPlusConfig lacks the hybrid estimator's
@@ -314,32 +319,69 @@ class SantaB200Engine:
         return time.perf_counter() - t0, sample_end
 
     @torch.inference_mode()
-    def _cluster(self):
+    def _cluster(self, workers: int | None = None):
         """Fingerprints, MiniBatchKMeans and the cluster summary of every
-        (layer, KV head, sequence) over the old prefix (santapp.py:598-722)."""
+        (layer, KV head, sequence) over the old prefix (santapp.py:598-722).
+
+        The fits are independent and each one is a chain of small launches
+        with a host read-back per mini-batch (the reference's control flow),
+        so they run concurrently: a pool of host threads, each fit on its own
+        CUDA stream (the ctypes calls and torch's copies release the GIL)."""
+        import concurrent.futures as cf
         sample_end = self.sample_end
         n_clusters = self._cfg("n_clusters") or cluster_count(sample_end, self.config.group_size)
         km = self.config.kmeans
         t1 = time.perf_counter()
-        for layer_id in range(self.num_layers):
-            qp = self._probe_q.pop(layer_id)  # [B, Hq, P, D] fp32
+        layers = list(range(self.num_layers))
+        probes = {layer_id: self._probe_q.pop(layer_id) for layer_id in layers}
+        B = probes[0].shape[0]
+        dev = probes[0].device
+        labels = {layer_id: torch.empty(B, self.num_kv_heads, sample_end, dtype=torch.int32,
+                                        device=dev) for layer_id in layers}
+        jobs = [(layer_id, b, kv) for layer_id in layers for b in range(B)
+                for kv in range(self.num_kv_heads)]
+        n_workers = workers or min(16, len(jobs))
+        streams = [torch.cuda.Stream(device=dev) for _ in range(n_workers)]
+        main = torch.cuda.current_stream(dev)
+        ready = torch.cuda.Event()
+        ready.record(main)  # the caches and probe queries are complete
+
+        def fit(i, job):
+            layer_id, b, kv = job
+            st = streams[i % n_workers]
+            with torch.cuda.device(dev), torch.cuda.stream(st):
+                st.wait_event(ready)
+                qp = probes[layer_id]
+                P = qp.shape[2]
+                fp = build_fingerprints(self.cache[layer_id].key[b, kv, :sample_end],
+                                        qp[b].contiguous(), kv, self.group, np.arange(P))
+                est = SklearnLikeTorchMiniBatchKMeans(
+                    n_clusters, batch_size=km.batch_size, n_init=km.n_init,
+                    max_iter=km.max_iter, tol=km.tol,
+                    max_no_improvement=km.max_no_improvement, init_size=km.init_size,
+                    reassignment_ratio=km.reassignment_ratio, random_state=km.random_state)
+                labels[layer_id][b, kv].copy_(est.fit_predict(fp).to(torch.int32))
+                if i % 64 == 63:
+                    self._log(f"k-means fit {i + 1} of {len(jobs)}")
+                done = torch.cuda.Event()
+                done.record(st)
+                return done
+
+        if n_workers == 1:
+            events = [fit(i, j) for i, j in enumerate(jobs)]
+        else:
+            # worker w runs jobs w, w + n, ... in order on stream w
+            def run_lane(w):
+                return [fit(i, jobs[i]) for i in range(w, len(jobs), n_workers)]
+            with cf.ThreadPoolExecutor(n_workers) as pool:
+                events = [e for lane in pool.map(run_lane, range(n_workers)) for e in lane]
+        for e in events:
+            main.wait_event(e)
+        for layer_id in layers:
             cached = self.cache[layer_id]
-            B, P = qp.shape[0], qp.shape[2]
-            labels = torch.empty(B, self.num_kv_heads, sample_end, dtype=torch.int32,
-                                 device=qp.device)
-            for b in range(B):
-                for kv in range(self.num_kv_heads):
-                    fp = build_fingerprints(cached.key[b, kv, :sample_end], qp[b].contiguous(),
-                                            kv, self.group, np.arange(P))
-                    est = SklearnLikeTorchMiniBatchKMeans(
-                        n_clusters, batch_size=km.batch_size, n_init=km.n_init,
-                        max_iter=km.max_iter, tol=km.tol,
-                        max_no_improvement=km.max_no_improvement, init_size=km.init_size,
-                        reassignment_ratio=km.reassignment_ratio,
-                        random_state=km.random_state)
-                    labels[b, kv] = est.fit_predict(fp).to(torch.int32)
-            self.summaries[layer_id] = build_summary(cached.key, cached.value, labels,
-                                                     n_clusters, sample_end=sample_end,
+            self.summaries[layer_id] = build_summary(cached.key, cached.value,
+                                                     labels[layer_id], n_clusters,
+                                                     sample_end=sample_end,
                                                      n_total=cached.length)
         torch.cuda.synchronize()
         return time.perf_counter() - t1, n_clusters
@@ -429,7 +471,9 @@ class SantaB200Engine:
         self.cache_capacity = T + max_new_tokens
         t0 = time.perf_counter()
         with self.patched():
+            self._log(f"prefill of {B} x {T} tokens")
             prefill_s, sample_end = self._prefill(input_ids, probe_seed=random_seed)
+            self._log(f"prefill done in {prefill_s:.2f} s")
             self._trim_cache(T - 1)
             plant_s = 0.0
             if planted_keys > 0:
@@ -439,7 +483,9 @@ class SantaB200Engine:
                 self._planted = {"positions": pos, "landed": 0, "total": 0}
                 torch.cuda.synchronize()
                 plant_s = time.perf_counter() - tp
+            self._log("clustering")
             cluster_s, n_clusters = self._cluster()
+            self._log(f"clustering done in {cluster_s:.2f} s")
             self.mode = self.config.mode
             self.traffic = DecodeTrafficTracker()
             generated = [[] for _ in range(B)]
@@ -449,6 +495,8 @@ class SantaB200Engine:
             torch.cuda.synchronize()
             t2 = time.perf_counter()
             for step in range(max_new_tokens):
+                if step % 64 == 0:
+                    self._log(f"decode step {step}")
                 self._decode_step = step
                 out = self.model(current, position_ids=torch.full(
                     (B, 1), position, dtype=torch.long, device=input_ids.device),

@@ -14,8 +14,8 @@ Per mini-batch step the host uploads the step's batch ids and reads back the
 counts and the batch inertia into pinned memory, waiting on an event behind
 the copies (the early-stopping rule and the reassignment rule of
 minibatch_kmeans.py:241-315 need them before the next step's draws), as the
-reference's control flow requires.  The greedy k-means++ seeding is one
-cooperative kernel launch.
+reference's control flow requires.  The greedy k-means++ seeding runs on
+the device with no host round trip (two launches per centre).
 """
 
 from __future__ import annotations
@@ -94,7 +94,6 @@ class SklearnLikeTorchMiniBatchKMeans:
             u_dev.data_ptr(), centers.data_ptr(), chosen.data_ptr(), ws.data_ptr(),
             nbytes.value, _lib.stream_handle()))
         self.init_ids_ = chosen
-        self._kpp_err = ws[:4].view(torch.int32)  # set if the seeding's grid barrier gave up
         return centers
 
     # ---- fit ---------------------------------------------------------------
@@ -237,8 +236,6 @@ class SklearnLikeTorchMiniBatchKMeans:
         labels = self._assign(x, None, xx_all, n, centers)
         self.labels_ = labels.long()
         self.inertia_ = _fx_value(self._fx.cpu().numpy().view(np.uint64))
-        if int(self._kpp_err.item()):
-            raise RuntimeError("k-means++ seeding: a grid barrier wait ran out of time")
         if self.verbose:
             print(f"GPU MiniBatchKMeans: {self.n_steps_} mini-batches, "
                   f"{self.n_iter_} effective epochs")
