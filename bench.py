@@ -242,25 +242,32 @@ def measure_decode(args, shape, steps, warmup, dev, keep=False):
 
     # The K timed steps as one CUDA graph, the way a decode loop is captured
     # for serving: per step the L2 flush, then the selection and attention
-    # kernels.  Each step is timed on the device by event-record nodes
-    # captured around its two kernels (the flush lies outside them); the
-    # middle event splits the phases.
-    inner = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)]
-             for _ in range(steps)]
-    cap = torch.cuda.Stream()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(cap):
-        with torch.cuda.graph(graph, stream=cap):
-            for i in range(steps):
-                step = warmup + i
-                flush()
-                inner[i][0].record(cap)
-                runner.plan(queries[step], step=step)
-                inner[i][1].record(cap)
-                runner.execute()
-                inner[i][2].record(cap)
-    torch.cuda.synchronize()
+    # kernels, timed on the device by event-record nodes around the two
+    # kernels (the flush lies outside them).  Nothing sits between the two
+    # kernels, so the attention kernel's programmatic launch overlaps the
+    # selection's tail as in a serving loop.  A second graph of the same
+    # steps records one more event between the kernels: the phase split and
+    # the attention kernel's roofline come from it.
+    def capture(split):
+        ev = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)]
+              for _ in range(steps)]
+        cap = torch.cuda.Stream()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(cap):
+            with torch.cuda.graph(graph, stream=cap):
+                for i in range(steps):
+                    step = warmup + i
+                    flush()
+                    ev[i][0].record(cap)
+                    runner.plan(queries[step], step=step)
+                    if split:
+                        ev[i][1].record(cap)
+                    runner.execute()
+                    ev[i][2].record(cap)
+        torch.cuda.synchronize()
+        return graph, ev
 
+    graph, inner = capture(False)
     clocks = ClockSampler(torch.cuda.current_device())
     clocks.start()
     torch.cuda.synchronize()
@@ -271,8 +278,13 @@ def measure_decode(args, shape, steps, warmup, dev, keep=False):
     clk = clocks.stop()
     del graph
     step_ms = np.array([e[0].elapsed_time(e[2]) for e in inner])
-    plan_ms = np.array([e[0].elapsed_time(e[1]) for e in inner])
-    att_ms = np.array([e[1].elapsed_time(e[2]) for e in inner])
+    graph, split = capture(True)
+    graph.replay()
+    torch.cuda.synchronize()
+    del graph
+    split_step_ms = np.array([e[0].elapsed_time(e[2]) for e in split])
+    plan_ms = np.array([e[0].elapsed_time(e[1]) for e in split])
+    att_ms = np.array([e[1].elapsed_time(e[2]) for e in split])
     peak, peak_kind = peaks()
     achieved = (float(np.sum(attend_bytes) / (att_ms.sum() / 1e3) / 1e9) if attend_bytes
                 else float("nan"))
@@ -280,7 +292,8 @@ def measure_decode(args, shape, steps, warmup, dev, keep=False):
     res = {
         "value": shape.batch * steps / (step_ms.sum() / 1e3),
         "ms_per_step": float(step_ms.mean()),
-        "phase_ms": {"select": float(plan_ms.mean()), "attend": float(att_ms.mean())},
+        "phase_ms": {"select": float(plan_ms.mean()), "attend": float(att_ms.mean()),
+                     "step_with_split_event": float(split_step_ms.mean())},
         "roofline": {
             "kernel": "decode_attend_gather_kernel",
             "bound": "hbm",
@@ -379,8 +392,9 @@ def run_ours(args, rank, world):
         "select_roofline": res["select_roofline"],
         "step_roofline": res["step_roofline"],
         "timing": ("one CUDA graph holding the K timed steps (per step: L2 flush, selection, "
-                   "attention); each step timed by event-record nodes around its two kernels, "
-                   "the phase split and roofline by the middle one"),
+                   "attention); each step timed by event-record nodes around its two kernels; "
+                   "the phase split and roofline from a second graph of the same steps with "
+                   "one more event between the kernels"),
         "wall_s": res["wall_s"],
         "clocks": res["clocks"],
         "gpu_launches": res["gpu_launches"],
@@ -760,13 +774,14 @@ def run_sharded(args, rank, world):
         ev = [[torch.cuda.Event(enable_timing=True, external=p2p) for _ in range(len(names) + 1)]
               for _ in range(args.steps)]
 
-        def one_step(i, e, stream=None):
+        def one_step(i, e, stream=None, split=True):
             st = args.warmup + i
             if p2p:
                 runner.begin(queries[st], st)
                 e[0].record(stream)
                 runner.plan(stream=stream)
-                e[1].record(stream)
+                if split:
+                    e[1].record(stream)
                 runner.execute(stream=stream)
                 e[2].record(stream)
                 return
@@ -785,18 +800,26 @@ def run_sharded(args, rank, world):
             e[6].record(stream)
 
         graph = None
-        if p2p:
+
+        def capture(events, split):
             # the K timed steps (each behind its L2 flush) as one CUDA graph,
             # as the single-GPU run; every captured launch carries its step's
             # epoch, and every rank captures the same sequence
             cap = torch.cuda.Stream()
-            graph = torch.cuda.CUDAGraph()
+            g = torch.cuda.CUDAGraph()
             with torch.cuda.stream(cap):
-                with torch.cuda.graph(graph, stream=cap):
+                with torch.cuda.graph(g, stream=cap):
                     for i in range(args.steps):
                         flush()
-                        one_step(i, ev[i], cap)
+                        one_step(i, events[i], cap, split)
             torch.cuda.synchronize()
+            return g
+
+        if p2p:
+            # timed without an event between the two launches (the attention
+            # launch overlaps the selection's tail, as in a serving loop); the
+            # phase split comes from a second graph of the same steps below
+            graph = capture(ev, False)
         clocks = ClockSampler(local)
         clocks.start()
         dist.barrier()
@@ -823,16 +846,29 @@ def run_sharded(args, rank, world):
         del graph
         if p2p:
             runner.check_p2p()
-        ph = np.array([[e[j].elapsed_time(e[j + 1]) for j in range(len(names))] for e in ev])
-        mine = torch.tensor([ph.sum()], dtype=torch.float64, device=dev)
+            steps_ms = np.array([e[0].elapsed_time(e[2]) for e in ev])
+            ev2 = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)]
+                   for _ in range(args.steps)]
+            dist.barrier()
+            g2 = capture(ev2, True)
+            dist.barrier()
+            g2.replay()
+            torch.cuda.synchronize()
+            del g2
+            runner.check_p2p()
+            ph = np.array([[e[j].elapsed_time(e[j + 1]) for j in range(len(names))] for e in ev2])
+        else:
+            ph = np.array([[e[j].elapsed_time(e[j + 1]) for j in range(len(names))] for e in ev])
+            steps_ms = ph.sum(axis=1)
+        mine = torch.tensor([steps_ms.sum()], dtype=torch.float64, device=dev)
         dist.all_reduce(mine, op=dist.ReduceOp.MAX)
         total_ms = float(mine.item())
         value = shape.batch * args.steps / (total_ms / 1e3)
         phase = {k: float(v) for k, v in zip(names, ph.mean(axis=0))}
         # per-rank step times: the limiter is the slowest rank
         per_rank = [torch.zeros(1, dtype=torch.float64, device=dev) for _ in range(world)]
-        dist.all_gather(per_rank, torch.tensor([ph.sum() / args.steps], dtype=torch.float64,
-                                               device=dev))
+        dist.all_gather(per_rank, torch.tensor([steps_ms.sum() / args.steps],
+                                               dtype=torch.float64, device=dev))
 
         # end to end through the public call: pinned q in, merged out back
         e2e = None
