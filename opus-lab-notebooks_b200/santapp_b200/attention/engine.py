@@ -159,6 +159,7 @@ class SantaB200Engine:
         self._capture_q: dict[int, torch.Tensor] | None = None
         self._planted: dict | None = None
         self.log = None  # optional progress callback: log(message)
+        self._prefill_flags: list[torch.Tensor] = []  # error words of the prefill launches
         self._lib = _lib.load()
 
     def _log(self, msg: str) -> None:
@@ -268,6 +269,11 @@ class SantaB200Engine:
             # prompt: causal attention of every position over the prompt
             out = santa_prefill(q_bf, cached.key, cached.value, causal=True,
                                 scale=float(attention.scaling))
+            self._prefill_flags.append(out._santa_error_flag)
+            if self.log is not None:  # progress (synchronises: diagnostics only)
+                torch.cuda.synchronize()
+                self._log(f"layer {layer_id} prefill attention done, error flag "
+                          f"{int(out._santa_error_flag.item())}")
             if self._probe_idx is not None:
                 self._probe_q[layer_id] = q_bf[:, :, self._probe_idx].float()
             out = out.transpose(1, 2).reshape(B, Tn, Hq * D)
@@ -311,11 +317,15 @@ class SantaB200Engine:
         self._probe_idx = torch.as_tensor(probes, dtype=torch.long, device=input_ids.device)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
+        self._prefill_flags = []
         try:
             self.model(input_ids, use_cache=False, logits_to_keep=1)
         finally:
             self._probe_idx = None
         torch.cuda.synchronize()
+        if self._prefill_flags and int(torch.stack(self._prefill_flags).max()):
+            raise RuntimeError("santa_prefill: a bounded wait of the prefill kernel gave up "
+                               "(its output is invalid)")
         return time.perf_counter() - t0, sample_end
 
     @torch.inference_mode()
@@ -349,7 +359,8 @@ class SantaB200Engine:
         def fit(i, job):
             layer_id, b, kv = job
             st = streams[i % n_workers]
-            with torch.cuda.device(dev), torch.cuda.stream(st):
+            # (inference mode is per thread: the worker enters it as well)
+            with torch.inference_mode(), torch.cuda.device(dev), torch.cuda.stream(st):
                 st.wait_event(ready)
                 qp = probes[layer_id]
                 P = qp.shape[2]
