@@ -200,6 +200,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
         if (t == 1) mbar_arrive(&bar_tok[0]);
         for (int j = 0; j < njt; ++j) {
             bool wok = !s_abort && mbar_wait(&bar_s[t], (uint32_t)(j & 1));
+            // the TMEM loads below are warp-collective: the warp goes on only
+            // if every lane's wait succeeded
+            wok = __all_sync(0xffffffffu, wok);
             tc_fence_after();
             // keys [0, lim) of this tile are visible to this row; only the
             // diagonal tile (causal) and the ragged last tile mask anything
@@ -242,14 +245,22 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
             const float mx =
                 fmaxf(s_red[j & 1][t][0][row], s_red[j & 1][t][1][row]) * a.scale_log2;
             const float m_new = fmaxf(m_used, mx);
+            // Lazy rescale: a row's O and l are rescaled only when its maximum
+            // grew by more than 8 (log2 units).  The decision is per row, but
+            // tcgen05.ld / st are warp-collective (.sync.aligned): a warp in
+            // which any row needs it rescales all 32 rows together, the others
+            // by 1 (exact).  PV(j-1) of this tile has finished (it was issued
+            // before S(j), whose commit this thread waited for).
+            const bool grow = m_used != -INFINITY && m_new > m_used + 8.0f;
+            float alpha = 1.f;
             if (m_used == -INFINITY) {
                 m_used = m_new;
-            } else if (m_new > m_used + 8.0f) {
-                // PV(j-1) of this tile has finished (it was issued before
-                // S(j), whose commit this thread waited for)
-                const float alpha = pf_exp2(m_used - m_new);
+            } else if (grow) {
+                alpha = pf_exp2(m_used - m_new);
                 m_used = m_new;
                 l *= alpha;
+            }
+            if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll
                 for (int c = 0; c < 2; ++c) {
                     uint32_t r[32];

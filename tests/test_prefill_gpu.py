@@ -109,3 +109,24 @@ def test_prefill_full_qwen7b_layer_32k_strided_rows():
     e = torch.cat(errs)
     assert torch.isfinite(e).all()
     assert e.max().item() < 2e-2 and e.mean().item() < 2e-3, (e.max().item(), e.mean().item())
+
+
+def test_prefill_rows_with_diverging_maxima():
+    """Rows of one warp whose running maxima grow at different key tiles: a
+    key planted 300 positions before every third query row (6x that row's
+    query) lifts only that row's maximum by far more than the lazy-rescale
+    threshold, at a later key tile than its neighbours' maxima settle.  The
+    rescale of O is warp-collective in the kernel; the result must match the
+    fp32 reference and the kernel's bounded waits must not give up."""
+    B, Hq, Hkv, T = 1, 7, 1, 1024
+    g = torch.Generator(device="cpu").manual_seed(21)
+    q = torch.randn(B, Hq, T, 128, generator=g)
+    k = 0.1 * torch.randn(B, Hkv, T, 128, generator=g)
+    v = torch.randn(B, Hkv, T, 128, generator=g)
+    for r in range(400, T, 3):
+        k[0, 0, r - 300] = 6.0 * q[0, 0, r] / q[0, 0, r].norm() * 4.0
+    q, k, v = (t.to(torch.bfloat16).cuda() for t in (q, k, v))
+    out = santa_prefill(q, k, v)
+    torch.cuda.synchronize()
+    assert int(out._santa_error_flag.item()) == 0
+    _check(out, _reference(q, k, v, True))
