@@ -157,6 +157,7 @@ class SantaB200Engine:
         self._traffic_pending: list = []
         self._head_calls = 0
         self._capture_q: dict[int, torch.Tensor] | None = None
+        self._plant_layer = None  # set during the planted-key dry run
         self._planted: dict | None = None
         self.log = None  # optional progress callback: log(message)
         self._prefill_flags: list[torch.Tensor] = []  # error words of the prefill launches
@@ -281,6 +282,8 @@ class SantaB200Engine:
             # dense decode / continued prompt over the cache (fidelity path)
             if self._capture_q is not None and Tn == 1:
                 self._capture_q[layer_id] = q_bf[:, :, 0].float()
+                if self._plant_layer is not None:
+                    self._plant_layer(layer_id, q_bf[:, :, 0].float(), cached)
             kf, vf = cached.view()
             kf = kf.repeat_interleave(self.group, dim=1)
             vf = vf.repeat_interleave(self.group, dim=1)
@@ -404,34 +407,38 @@ class SantaB200Engine:
         """Synthetic retrieval check: for every (layer, sequence, KV head),
         ``n_planted`` old-prefix keys at seeded random positions are replaced
         by ``scale`` x the mean key norm along the direction of the first
-        query head of the group at the first decode step.  That direction
-        comes from a dense dry run of that step (the decode query of a layer
-        depends on the earlier layers' attention outputs, which the planted
-        keys barely move).  Call after the prefill, before clustering."""
+        query head of the group at the first decode step.  The directions
+        come from a dense dry run of that step in which each layer plants its
+        keys just before its own attention, so a layer's query already
+        reflects the planted keys of the layers below it (they change those
+        layers' outputs, and so every later layer's queries).  Call after the
+        prefill, before clustering."""
         B = last_token.shape[0]
-        self._capture_q = {}
-        try:
-            self.model(last_token, position_ids=torch.full((B, 1), position, dtype=torch.long,
-                                                           device=last_token.device),
-                       use_cache=False, logits_to_keep=1)
-            queries = self._capture_q
-        finally:
-            self._capture_q = None
-        self._trim_cache(position)
         rs = np.random.RandomState(seed)
         planted = {}
-        for layer_id in range(self.num_layers):
-            c = self.cache[layer_id]
+
+        def plant(layer_id, q, c):
             pos = np.stack([[np.sort(rs.choice(self.sample_end, n_planted, replace=False))
                              for _ in range(self.num_kv_heads)] for _ in range(B)])
             for b in range(B):
                 for kv in range(self.num_kv_heads):
-                    qd = queries[layer_id][b, kv * self.group]
+                    qd = q[b, kv * self.group]
                     qhat = qd / qd.norm()
                     norm = c.key[b, kv, :self.sample_end].float().norm(dim=-1).mean()
                     idx = torch.from_numpy(pos[b, kv]).to(c.key.device)
                     c.key[b, kv, idx] = (scale * norm * qhat).to(c.key.dtype)[None]
             planted[layer_id] = pos
+
+        self._capture_q = {}
+        self._plant_layer = plant
+        try:
+            self.model(last_token, position_ids=torch.full((B, 1), position, dtype=torch.long,
+                                                           device=last_token.device),
+                       use_cache=False, logits_to_keep=1)
+        finally:
+            self._capture_q = None
+            self._plant_layer = None
+        self._trim_cache(position)
         return planted
 
     def _check_planted(self, layer_id: int, q: torch.Tensor, cached, scale: float) -> None:
