@@ -4,9 +4,11 @@ sequence-sharded decode (launched by torchrun, one process per GPU).
 Every rank decodes its shard of the same workload for three steps through
 both exchange paths (NCCL all-gathers, and the kernels' own peer-memory
 exchange); the outputs of the two must agree bit for bit and be identical on
-every rank.  Rank 0 then rebuilds every shard on the host and checks the
-selections of its own shard and the merged output against the oracle's
-sharded estimator (max-abs 2e-2 / mean-abs 2e-3).  Prints "RANK r OK".
+every rank.  Rank 0 then rebuilds every shard (with the ranks' own device
+generator) and checks the selections of its own shard and the merged output
+against the oracle's sharded estimator (max-abs 2e-2 / mean-abs 2e-3).
+Every rank takes the same collective steps on failure too; prints "RANK r OK"
+or one "RANK r FAIL ..." line per failure.
 """
 import datetime
 import os
@@ -43,6 +45,9 @@ def main():
               num_shards=world, cluster_base=p.cluster_base, seed=seed)
     nccl = ShardedDecodeStep(p.keys, p.values, summ, transport="nccl", **kw)
     peer = ShardedDecodeStep(p.keys, p.values, summ, transport="p2p", **kw)
+    # Every rank takes the same collective steps whatever fails: a failure is
+    # recorded, the steps go on, and the ranks agree on the outcome at the end.
+    failures = []
     try:
         for step in range(3):  # both parities of the exchange buffers
             q = p.queries[step].contiguous()
@@ -50,52 +55,74 @@ def main():
             sel = nccl.select()
             b = peer(q, step=step).clone()
             torch.cuda.synchronize()
-            peer.check_p2p()
-            assert torch.equal(a, b), f"rank {rank} step {step}: exchange paths differ"
-            assert torch.equal(nccl.lse, peer.lse) and torch.equal(nccl.ess, peer.ess)
+            try:
+                peer.check_p2p()
+            except RuntimeError as e:
+                failures.append(f"step {step}: {e}")
+            if not torch.equal(a, b):
+                failures.append(f"step {step}: exchange paths differ")
+            if not (torch.equal(nccl.lse, peer.lse) and torch.equal(nccl.ess, peer.ess)):
+                failures.append(f"step {step}: lse / ess differ between exchange paths")
             every = [torch.empty_like(a) for _ in range(world)]
             dist.all_gather(every, a)
-            for x in every:
-                assert torch.equal(x, a), "ranks hold different merged outputs"
-        # oracle check of the last step on rank 0 (every shard rebuilt on the host)
+            if not all(torch.equal(x, a) for x in every):
+                failures.append(f"step {step}: ranks hold different merged outputs")
         if rank == 0:
-            parts = [make_shard_workload(SH, r, world, seed=seed) for r in range(world)]
-            bases = [pp.cluster_base for pp in parts]
-            errs = []
-            qh = q.cpu().numpy()
-            for bb in range(SH.batch):
-                for h in range(SH.num_query_heads):
-                    kv = h // SH.group
-                    shards = []
-                    for pp in parts:
-                        K = pp.keys[bb, kv].float().numpy()
-                        osum = O.build_summary(K[:pp.sample_end], pp.labels[bb, kv].numpy(),
-                                               pp.n_clusters)
-                        shards.append((K, pp.values[bb, kv].float().numpy(), osum,
-                                       pp.sample_end, pp.n_total))
-                    osel = O.shard_topk([s_[2] for s_ in shards], qh[bb, h], SH.scale,
-                                        SH.topk_clusters, bases)
-                    got = np.nonzero(sel[0][bb, h].cpu().numpy())[0]
-                    assert np.array_equal(got, osel[0]), (bb, h)
-                    ranks = []
-                    for r, (pp, s_) in enumerate(zip(parts, shards)):
-                        n_rest = pp.sample_end - int(sum(s_[2].lengths[c] for c in osel[r]))
-                        ranks.append(O.philox_ranks(shard_seed(seed, r), 2, bb, h, pp.samples,
-                                                    n_rest) if n_rest > 0
-                                     else np.zeros(0, np.int64))
-                    ref = O.decode_hybrid_sharded(qh[bb, h], shards, SH.topk_clusters, ranks,
-                                                  SH.scale, bases)
-                    errs.append(np.abs(a[bb, h].cpu().numpy() - ref.out))
-            e = np.stack(errs)
-            assert e.max() < 2e-2 and e.mean() < 2e-3, (e.max(), e.mean())
-            print(f"oracle max-abs {e.max():.3g} mean-abs {e.mean():.3g}", flush=True)
-        dist.barrier()
-        print(f"RANK {rank} OK", flush=True)
+            try:
+                oracle_check(world, seed, dev, q, sel, a)
+            except AssertionError as e:
+                failures.append(f"oracle check: {e}")
     finally:
+        # every rank's kernels are done (its synchronize precedes its part of
+        # the reduction) before any rank unmaps the exchange buffers
         torch.cuda.synchronize()
+        flag = torch.tensor([len(failures)], dtype=torch.int32, device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+        any_failed = int(flag.item())
         peer.close()
-        dist.barrier()
         dist.destroy_process_group()
+    for f in failures:
+        print(f"RANK {rank} FAIL {f}", flush=True)
+    if failures or any_failed:
+        sys.exit(1)
+    print(f"RANK {rank} OK", flush=True)
+
+
+def oracle_check(world, seed, dev, q, sel, a):
+    """Rank 0: rebuild every shard (on the device, so that the generator is
+    the one the ranks used, then on the host) and check this shard's
+    selections and the merged output of the last step against the oracle's
+    sharded estimator."""
+    parts = [make_shard_workload(SH, r, world, seed=seed, device=dev) for r in range(world)]
+    bases = [pp.cluster_base for pp in parts]
+    errs = []
+    qh = q.cpu().numpy()
+    sel0 = sel[0].cpu().numpy()
+    host = [(pp.keys.float().cpu().numpy(), pp.values.float().cpu().numpy(),
+             pp.labels.cpu().numpy()) for pp in parts]
+    for bb in range(SH.batch):
+        for kv in range(SH.num_kv_heads):
+            shards = []
+            for pp, (K, V, L) in zip(parts, host):
+                osum = O.build_summary(K[bb, kv, :pp.sample_end], L[bb, kv], pp.n_clusters)
+                shards.append((K[bb, kv], V[bb, kv], osum, pp.sample_end, pp.n_total))
+            for h in range(kv * SH.group, (kv + 1) * SH.group):
+                osel = O.shard_topk([s_[2] for s_ in shards], qh[bb, h], SH.scale,
+                                    SH.topk_clusters, bases)
+                got = np.nonzero(sel0[bb, h])[0]
+                assert np.array_equal(got, osel[0]), f"selection of (b {bb}, head {h})"
+                ranks = []
+                for r, (pp, s_) in enumerate(zip(parts, shards)):
+                    n_rest = pp.sample_end - int(sum(s_[2].lengths[c] for c in osel[r]))
+                    ranks.append(O.philox_ranks(shard_seed(seed, r), 2, bb, h, pp.samples,
+                                                n_rest) if n_rest > 0
+                                 else np.zeros(0, np.int64))
+                ref = O.decode_hybrid_sharded(qh[bb, h], shards, SH.topk_clusters, ranks,
+                                              SH.scale, bases)
+                errs.append(np.abs(a[bb, h].cpu().numpy() - ref.out))
+    e = np.stack(errs)
+    assert e.max() < 2e-2 and e.mean() < 2e-3, f"max-abs {e.max():.3g} mean-abs {e.mean():.3g}"
+    print(f"oracle max-abs {e.max():.3g} mean-abs {e.mean():.3g}", flush=True)
 
 
 if __name__ == "__main__":

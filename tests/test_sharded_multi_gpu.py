@@ -26,6 +26,7 @@ def test_sharded_decode_on_real_gpus(world):
            "--master-port", str(29600 + world), os.path.join(HERE, "mgpu_sharded_worker.py")]
     res = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
     out = res.stdout + res.stderr
-    assert res.returncode == 0, out[-4000:]
+    fails = "\n".join(line for line in out.splitlines() if " FAIL " in line)
+    assert res.returncode == 0, (fails or out[-4000:])
     for r in range(world):
-        assert f"RANK {r} OK" in out, out[-4000:]
+        assert f"RANK {r} OK" in out, (fails or out[-4000:])
