@@ -17,6 +17,8 @@
  *   santa_prefill              santapp_ruler/attention/santapp.py:320-346
  *                              (prefill branch -> sdpa_attention_forward)
  *   santa_rope_append          santapp_ruler/attention/santapp.py:234-274, 308-313
+ *   santa_rope_append_paged    (_append_cache and the RoPE of _attention_forward;
+ *                              the paged form of the LayerCache of :66-77)
  *                              (_append_cache and the RoPE of _attention_forward)
  *   santa_fingerprints         santapp_ruler/attention/santapp.py:598-691
  *   santa_kmeans_*             santapp_ruler/attention/minibatch_kmeans.py:58-267
@@ -62,18 +64,34 @@ extern "C" {
 /* ---- shapes ---------------------------------------------------------- */
 
 /* Geometry of one attention layer's KV cache.
- * key/value caches are [batch, num_kv_heads, capacity, head_dim], row-major;
- * tokens [0, n_total) are valid; [0, sample_end) is the clustered old prefix
+ * Contiguous (block_table NULL): key/value caches are [batch, num_kv_heads,
+ * capacity, head_dim], row-major.
+ * Paged (block_table set, the LayerCache of santapp.py:66-77 split into
+ * fixed-size pages): key/value are page pools [num_pages, num_kv_heads,
+ * page_size, head_dim]; token p of sequence b lives in page
+ * block_table[b * max_pages + p / page_size], slot p % page_size (capacity =
+ * max_pages * page_size; page_size a power of two).  Page ids outside
+ * [0, num_pages) read page 0.  The summary build and every single-GPU decode
+ * entry point accept both layouts; the santa_shard_* entry points take
+ * contiguous caches only (SANTA_ERR_UNSUPPORTED).  Cache rows (batch x
+ * num_kv_heads x capacity, or num_pages x num_kv_heads x page_size) must be
+ * below 2^31 - 2 (SANTA_ERR_UNSUPPORTED).
+ * Tokens [0, n_total) are valid; [0, sample_end) is the clustered old prefix
  * (santapp.py:374-379), [sample_end, n_total) is attended exactly. */
 typedef struct SantaGeometry {
     int32_t batch;
     int32_t num_kv_heads;
     int32_t group;        /* query heads per KV head (GQA), <= 8 */
     int32_t head_dim;     /* 64 or 128 */
-    int32_t capacity;     /* row stride of the cache in tokens */
+    int32_t capacity;     /* tokens per sequence (contiguous: row stride of the cache) */
     int32_t n_total;      /* valid tokens */
     int32_t sample_end;   /* end of the clustered prefix, 0 < sample_end <= n_total */
     int32_t kv_dtype;     /* SANTA_DTYPE_F32 or SANTA_DTYPE_BF16 */
+    const int32_t *block_table; /* paged: device [batch][max_pages] page ids; NULL: contiguous */
+    int32_t page_size;    /* paged: tokens per page, a power of two */
+    int32_t max_pages;    /* paged: pages per sequence (block_table row length) */
+    int32_t num_pages;    /* paged: pages in each pool */
+    int32_t reserved;
 } SantaGeometry;
 
 /* Cluster summary of every (batch, KV head): the ClusterSummary fields of
@@ -245,6 +263,19 @@ int santa_rope_append(int32_t batch, int32_t tokens, int32_t num_query_heads,
                       const void *v, const void *cos, const void *sin, void *key_cache,
                       void *value_cache, int32_t capacity, int32_t start, void *q_rot_bf16,
                       float *q_rot_f32, cudaStream_t stream);
+
+/* The same into paged pools [num_pages, Hkv, page_size, head_dim] (the
+ * paged SantaGeometry layout): token start + t of sequence b goes to page
+ * block_table[b * max_pages + (start + t) / page_size], slot (start + t) %
+ * page_size.  page_size a power of two; start + tokens <= max_pages *
+ * page_size.  Tokens whose page id is outside [0, num_pages) are not written
+ * (the caller maps the pages before the append). */
+int santa_rope_append_paged(int32_t batch, int32_t tokens, int32_t num_query_heads,
+                            int32_t num_kv_heads, int32_t head_dim, const void *q, const void *k,
+                            const void *v, const void *cos, const void *sin, void *key_pool,
+                            void *value_pool, const int32_t *block_table, int32_t page_size,
+                            int32_t max_pages, int32_t num_pages, int32_t start,
+                            void *q_rot_bf16, float *q_rot_f32, cudaStream_t stream);
 
 /* ---- dense prefill (attention/santapp.py:320-346) ---------------------- */
 

@@ -65,6 +65,27 @@ __device__ __forceinline__ int warp_sum_int(int v) {
     return v;
 }
 
+// Row of token p of (batch, KV head) bh in the key / value cache, in rows of
+// head_dim elements from the cache base.  Contiguous caches [B, Hkv, cap, D]:
+// bh * capacity + p.  Paged pools [num_pages, Hkv, page_size, D] (page_size a
+// power of two, checked on the host): the page comes from the sequence's
+// block-table row; a page id outside [0, num_pages) reads page 0 so that a
+// corrupt table cannot address memory outside the pool.
+__device__ __forceinline__ int64_t cache_row(const SantaGeometry &g, int bh, int p) {
+    if (!g.block_table) return (int64_t)bh * g.capacity + p;
+    const int b = bh / g.num_kv_heads, kv = bh - b * g.num_kv_heads;
+    const int sh = __ffs(g.page_size) - 1;
+    int page = __ldg(g.block_table + (int64_t)b * g.max_pages + (p >> sh));
+    page = (unsigned)page < (unsigned)g.num_pages ? page : 0;
+    return (((int64_t)page * g.num_kv_heads + kv) << sh) + (p & (g.page_size - 1));
+}
+
+// Rows in the cache a geometry addresses (the bound of cache_row).
+__host__ __device__ inline int64_t cache_rows(const SantaGeometry &g) {
+    return g.block_table ? (int64_t)g.num_pages * g.num_kv_heads * g.page_size
+                         : (int64_t)g.batch * g.num_kv_heads * g.capacity;
+}
+
 }  // namespace santa
 
 // Status helpers for the C ABI.

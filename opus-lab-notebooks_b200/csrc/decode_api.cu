@@ -237,7 +237,8 @@ static int bind_p2p(const SantaGeometry *geo, const SantaDecodeParams *p,
 static int check_shard(const SantaGeometry *geo, const SantaDecodeParams *p,
                        const SantaShard *shard, bool need_candidates) {
     if (!geo || !p || !shard) return SANTA_ERR_INVALID_ARGUMENT;
-    if (p->mode != SANTA_MODE_HYBRID || geo->kv_dtype != SANTA_DTYPE_BF16)
+    // a shard owns a contiguous slice of every sequence: paged shards are not built
+    if (p->mode != SANTA_MODE_HYBRID || geo->kv_dtype != SANTA_DTYPE_BF16 || geo->block_table)
         return SANTA_ERR_UNSUPPORTED;
     if (shard->num_shards < 1 || shard->num_shards > SANTA_MAX_SHARDS) return SANTA_ERR_INVALID_ARGUMENT;
     if (shard->shard_index < 0 || shard->shard_index >= shard->num_shards)

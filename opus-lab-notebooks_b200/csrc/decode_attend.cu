@@ -659,7 +659,7 @@ __device__ void fused_shard_exchange(const DecodeArgs &a, const unsigned *done, 
 // A row entry prefetched ahead of its copy.
 struct RowEntry {
     int kind;   // 0 none, 1 union row, 2 recent row, 3 sampled row
-    int32_t e;  // union: row | mask << 24; recent: row offset; sampled: packed sample word
+    int32_t e;  // union: row | mask << 24; recent: cache row; sampled: packed sample word
     float off;
 };
 
@@ -675,7 +675,7 @@ __device__ __forceinline__ RowEntry load_entry(const DecodeArgs &a, int bh, int 
         r.e = a.ws.w_row[(int64_t)bh * a.geo.sample_end + v];
     } else if (v < U + R) {
         r.kind = 2;
-        r.e = v - U;
+        r.e = (int32_t)cache_row(a.geo, bh, a.geo.sample_end + (v - U));
     } else {
         const int64_t j = (int64_t)bh * a.geo.group * a.p.samples + (v - U - R);
         r.kind = 3;
@@ -783,8 +783,7 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
         const int b = bh / a.geo.num_kv_heads, kv = bh - b * a.geo.num_kv_heads;
         const char *sk = sk_all + (int64_t)bh * a.geo.sample_end * GG::ROWB;
         const char *sv = sv_all + (int64_t)bh * a.geo.sample_end * GG::ROWB;
-        const char *ck = a.key_cache + ((int64_t)bh * a.geo.capacity + a.geo.sample_end) * GG::ROWB;
-        const char *cv = a.value_cache + ((int64_t)bh * a.geo.capacity + a.geo.sample_end) * GG::ROWB;
+        const char *ck = a.key_cache, *cv = a.value_cache;  // recent rows: cache_row codes
 
         // q fragments of this (batch, KV head): rows = heads, split bf16 hi + lo
         const float *qb = a.q + ((int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g) * D;
@@ -818,7 +817,7 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
             int *mk = (int *)(stg + GG::STAGE);
             float *of = (float *)(mk + kGRows);
             // row code: >= 0 row of the cluster-sorted copy, -1 - x row x of
-            // the recent window in the cache, INT_MIN no row
+            // the cache (a recent-window token), INT_MIN no row
             int code = INT_MIN, mask = 0;
             if (en.kind == 1) {
                 code = en.e & (int)kPosMask;

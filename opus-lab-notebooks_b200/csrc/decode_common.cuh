@@ -334,7 +334,7 @@ __device__ __forceinline__ RowInfo resolve_row(const DecodeArgs &a, int bh, int 
         ri.off = 0.f;
         ri.mask = u_mask[lo];
     } else if (v < U + R) {
-        const int64_t row = (int64_t)bh * a.geo.capacity + sample_end + (v - U);
+        const int64_t row = cache_row(a.geo, bh, sample_end + (v - U));
         ri.k = a.key_cache + row * row_bytes;
         ri.v = a.value_cache + row * row_bytes;
         ri.off = 0.f;

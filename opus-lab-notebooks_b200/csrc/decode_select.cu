@@ -709,11 +709,11 @@ __global__ void __launch_bounds__(256) decode_old_lse_kernel(DecodeArgs a) {
         m[h] = -INFINITY;
         l[h] = 0.0f;
     }
-    const T *kb = (const T *)a.key_cache + (int64_t)bh * a.geo.capacity * D;
     for (int t = warp; t < a.geo.sample_end; t += 8) {
+        const T *kb = (const T *)a.key_cache + cache_row(a.geo, bh, t) * D;
         float kr[PER];
 #pragma unroll
-        for (int j = 0; j < PER; ++j) kr[j] = to_f32<T>(kb[(int64_t)t * D + lane + 32 * j]);
+        for (int j = 0; j < PER; ++j) kr[j] = to_f32<T>(kb[lane + 32 * j]);
 #pragma unroll
         for (int h = 0; h < SANTA_MAX_GROUP; ++h) {
             if (h < g) {

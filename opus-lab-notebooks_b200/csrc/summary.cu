@@ -169,7 +169,7 @@ template <int ROW_BYTES>
 __global__ void summary_scatter_kernel(const int32_t *__restrict__ labels,
                                        const char *__restrict__ key_cache,
                                        const char *__restrict__ value_cache,
-                                       int N, int G, int nchunks, int64_t cache_bh_stride_bytes,
+                                       int N, int G, int nchunks, SantaGeometry geo,
                                        SummaryWs ws, SantaSummary out) {
     extern __shared__ int32_t running_all[];  // [kWarpsPerCta][G]
     constexpr int CPR = ROW_BYTES / 16;        // 16-byte chunks per row
@@ -185,8 +185,6 @@ __global__ void summary_scatter_kernel(const int32_t *__restrict__ labels,
     const int32_t *lab = labels + (int64_t)bh * N;
     int32_t *members = out.members + (int64_t)bh * N;
     int32_t *positions = out.positions + (int64_t)bh * N;
-    const char *ksrc = key_cache + (int64_t)bh * cache_bh_stride_bytes;
-    const char *vsrc = value_cache + (int64_t)bh * cache_bh_stride_bytes;
     char *kdst = (char *)out.sorted_key + (int64_t)bh * N * ROW_BYTES;
     char *vdst = (char *)out.sorted_value + (int64_t)bh * N * ROW_BYTES;
 
@@ -212,14 +210,16 @@ __global__ void summary_scatter_kernel(const int32_t *__restrict__ labels,
             members[pos] = t;
             positions[t] = pos;
         }
+        // the cache row of this lane's token (contiguous or paged)
+        const long long src = valid ? (long long)cache_row(geo, bh, t) * ROW_BYTES : 0;
         // cooperative 16-byte row copies for the 32 tokens of this step
         for (int i = lane; i < 32 * CPR; i += 32) {
             const int r = i / CPR, c = i - r * CPR;
             const int pr = __shfl_sync(0xffffffffu, pos, r);
-            const int tr = base_t + r;
+            const long long sr = __shfl_sync(0xffffffffu, src, r);
             if (pr >= 0) {
-                const int4 kv = *(const int4 *)(ksrc + (int64_t)tr * ROW_BYTES + c * 16);
-                const int4 vv = *(const int4 *)(vsrc + (int64_t)tr * ROW_BYTES + c * 16);
+                const int4 kv = *(const int4 *)(key_cache + sr + c * 16);
+                const int4 vv = *(const int4 *)(value_cache + sr + c * 16);
                 *(int4 *)(kdst + (int64_t)pr * ROW_BYTES + c * 16) = kv;
                 *(int4 *)(vdst + (int64_t)pr * ROW_BYTES + c * 16) = vv;
             }
@@ -260,6 +260,15 @@ static int check_geo(const SantaGeometry *geo) {
         return SANTA_ERR_UNSUPPORTED;
     if (geo->n_total <= 0 || geo->capacity < geo->n_total) return SANTA_ERR_INVALID_ARGUMENT;
     if (geo->sample_end <= 0 || geo->sample_end > geo->n_total) return SANTA_ERR_INVALID_ARGUMENT;
+    if (geo->block_table) {
+        // paged: page_size a power of two, capacity = max_pages * page_size
+        if (geo->page_size <= 0 || (geo->page_size & (geo->page_size - 1)) ||
+            geo->max_pages <= 0 || geo->num_pages <= 0 ||
+            (int64_t)geo->max_pages * geo->page_size != geo->capacity)
+            return SANTA_ERR_INVALID_ARGUMENT;
+    }
+    // recent rows travel as negative 32-bit row codes in the gather kernel
+    if (cache_rows(*geo) >= (int64_t)INT32_MAX - 1) return SANTA_ERR_UNSUPPORTED;
     return SANTA_OK;
 }
 
@@ -301,7 +310,6 @@ extern "C" int santa_build_summary(const SantaGeometry *geo, const void *key_cac
 
     const int esize = geo->kv_dtype == SANTA_DTYPE_BF16 ? 2 : 4;
     const int row_bytes = D * esize;
-    const int64_t cache_stride = (int64_t)geo->capacity * row_bytes;
     dim3 grid_c(ceil_div(nchunks, kWarpsPerCta), BH);
     const size_t smem_c = (size_t)kWarpsPerCta * G * sizeof(int32_t);
     summary_count_kernel<<<grid_c, 32 * kWarpsPerCta, smem_c, stream>>>(labels, N, G, nchunks, ws);
@@ -312,17 +320,17 @@ extern "C" int santa_build_summary(const SantaGeometry *geo, const void *key_cac
         case 128:
             summary_scatter_kernel<128><<<grid_c, 32 * kWarpsPerCta, smem_c, stream>>>(
                 labels, (const char *)key_cache, (const char *)value_cache, N, G, nchunks,
-                cache_stride, ws, *out);
+                *geo, ws, *out);
             break;
         case 256:
             summary_scatter_kernel<256><<<grid_c, 32 * kWarpsPerCta, smem_c, stream>>>(
                 labels, (const char *)key_cache, (const char *)value_cache, N, G, nchunks,
-                cache_stride, ws, *out);
+                *geo, ws, *out);
             break;
         case 512:
             summary_scatter_kernel<512><<<grid_c, 32 * kWarpsPerCta, smem_c, stream>>>(
                 labels, (const char *)key_cache, (const char *)value_cache, N, G, nchunks,
-                cache_stride, ws, *out);
+                *geo, ws, *out);
             break;
         default:
             return SANTA_ERR_UNSUPPORTED;

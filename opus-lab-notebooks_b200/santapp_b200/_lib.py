@@ -39,7 +39,9 @@ _i32 = ctypes.c_int32
 
 class SantaGeometry(ctypes.Structure):
     _fields_ = [("batch", _i32), ("num_kv_heads", _i32), ("group", _i32), ("head_dim", _i32),
-                ("capacity", _i32), ("n_total", _i32), ("sample_end", _i32), ("kv_dtype", _i32)]
+                ("capacity", _i32), ("n_total", _i32), ("sample_end", _i32), ("kv_dtype", _i32),
+                ("block_table", _vp), ("page_size", _i32), ("max_pages", _i32),
+                ("num_pages", _i32), ("reserved", _i32)]
 
 
 class SantaSummary(ctypes.Structure):
@@ -137,6 +139,9 @@ SIGNATURES = {
     "santa_p2p_poke": (ctypes.c_int, [_vp, ctypes.c_uint64]),
     "santa_rope_append": (ctypes.c_int, [_i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp,
                                          _vp, _vp, _i32, _i32, _vp, _vp, _vp]),
+    "santa_rope_append_paged": (ctypes.c_int, [_i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp,
+                                               _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp,
+                                               _vp, _vp]),
     "santa_prefill_workspace_bytes": (ctypes.c_int, [_P(SantaPrefillShape),
                                                      _P(ctypes.c_size_t)]),
     "santa_prefill": (ctypes.c_int, [_P(SantaPrefillShape), _vp, _vp, _vp, _vp, _vp, _vp, _vp,

@@ -3,3 +3,4 @@
 from .santapp import (ClusterSummary, DecodeResult, DecodeTrafficTracker,  # noqa: F401
                       DecodeStep, DecodeWorkspace, allocate_summary, build_summary, santa_decode,
                       santa_decode_select)
+from .paged import PagedKVCache  # noqa: F401

@@ -28,6 +28,7 @@ import numpy as np
 import torch
 
 from .. import _lib
+from .paged import PagedKVCache
 
 __all__ = [
     "ClusterSummary", "build_summary", "santa_decode", "DecodeResult", "DecodeWorkspace",
@@ -52,9 +53,27 @@ def _kv_dtype(t: torch.Tensor) -> int:
     raise ValueError(f"KV cache dtype {t.dtype} unsupported (bf16 or fp32)")
 
 
-def _geometry(key_cache: torch.Tensor, num_query_heads: int, n_total: int,
+def _kv(key_cache, value_cache) -> tuple[torch.Tensor, torch.Tensor]:
+    """The K and V tensors handed to the C ABI: contiguous caches, or the page
+    pools of a PagedKVCache (passed as ``key_cache`` with ``value_cache``
+    None)."""
+    if isinstance(key_cache, PagedKVCache):
+        if value_cache is not None and value_cache is not key_cache:
+            raise ValueError("with a PagedKVCache, pass value_cache=None")
+        return key_cache.key_pool, key_cache.value_pool
+    _require_cuda("key_cache", key_cache)
+    _require_cuda("value_cache", value_cache)
+    if value_cache.shape != key_cache.shape or value_cache.dtype != key_cache.dtype:
+        raise ValueError("key and value caches must have the same shape and dtype")
+    return key_cache, value_cache
+
+
+def _geometry(key_cache, num_query_heads: int, n_total: int,
               sample_end: int) -> _lib.SantaGeometry:
-    if key_cache.dim() != 4:
+    """SantaGeometry of a contiguous ``[B, Hkv, capacity, D]`` cache or of a
+    PagedKVCache (the table pointer is set from the cache object)."""
+    paged = isinstance(key_cache, PagedKVCache)
+    if not paged and key_cache.dim() != 4:
         raise ValueError("key/value cache must be [batch, kv_heads, capacity, head_dim]")
     B, Hkv, cap, D = key_cache.shape
     if num_query_heads % Hkv:
@@ -64,8 +83,11 @@ def _geometry(key_cache: torch.Tensor, num_query_heads: int, n_total: int,
             f"Invalid sampled-prefix boundary {sample_end} for cache length {n_total}.")
     if n_total > cap:
         raise RuntimeError(f"cache length {n_total} exceeds capacity {cap}")
-    return _lib.SantaGeometry(B, Hkv, num_query_heads // Hkv, D, cap, n_total, sample_end,
-                              _kv_dtype(key_cache))
+    geo = _lib.SantaGeometry(B, Hkv, num_query_heads // Hkv, D, cap, n_total, sample_end,
+                             _kv_dtype(key_cache.key_pool if paged else key_cache))
+    if paged:
+        key_cache.fill_geometry(geo)
+    return geo
 
 
 # ---------------------------------------------------------------------------
@@ -157,31 +179,28 @@ def build_summary(key_cache: torch.Tensor, value_cache: torch.Tensor, labels: to
                   out: ClusterSummary | None = None, stream=None) -> ClusterSummary:
     """Cluster summary of the prefix ``[0, sample_end)`` from per-token labels.
 
-    key_cache / value_cache: ``[B, Hkv, capacity, D]`` (bf16 or fp32).
+    key_cache / value_cache: ``[B, Hkv, capacity, D]`` (bf16 or fp32), or a
+    PagedKVCache as ``key_cache`` with ``value_cache`` None.
     labels: ``[B, Hkv, sample_end]`` integer cluster ids in ``[0, n_clusters)``.
     """
-    _require_cuda("key_cache", key_cache)
-    _require_cuda("value_cache", value_cache)
-    if value_cache.shape != key_cache.shape or value_cache.dtype != key_cache.dtype:
-        raise ValueError("key and value caches must have the same shape and dtype")
+    kt, vt = _kv(key_cache, value_cache)
     B, Hkv, cap, D = key_cache.shape
     n_total = cap if n_total is None else n_total
     geo = _geometry(key_cache, Hkv, n_total, sample_end)
     if labels.shape != (B, Hkv, sample_end):
         raise ValueError(f"labels must be [{B}, {Hkv}, {sample_end}], got {tuple(labels.shape)}")
-    labels = labels.to(device=key_cache.device, dtype=torch.int32).contiguous()
+    labels = labels.to(device=kt.device, dtype=torch.int32).contiguous()
     if out is None:
-        out = allocate_summary(B, Hkv, sample_end, D, n_clusters, key_cache.dtype,
-                               key_cache.device)
+        out = allocate_summary(B, Hkv, sample_end, D, n_clusters, kt.dtype, kt.device)
     lib = _lib.load()
     nbytes = ctypes.c_size_t()
     _lib.check("santa_build_summary_workspace_bytes",
                lib.santa_build_summary_workspace_bytes(ctypes.byref(geo), n_clusters,
                                                        ctypes.byref(nbytes)))
-    ws = torch.empty(nbytes.value, dtype=torch.uint8, device=key_cache.device)
+    ws = torch.empty(nbytes.value, dtype=torch.uint8, device=kt.device)
     c = out.as_c()
     _lib.check("santa_build_summary", lib.santa_build_summary(
-        ctypes.byref(geo), key_cache.data_ptr(), value_cache.data_ptr(), labels.data_ptr(),
+        ctypes.byref(geo), kt.data_ptr(), vt.data_ptr(), labels.data_ptr(),
         n_clusters, ctypes.byref(c), ws.data_ptr(), nbytes.value, _lib.stream_handle(stream)))
     out._workspace = ws  # keeps the error flag readable; see summary_flag()
     return out
@@ -251,10 +270,10 @@ def santa_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Te
     ``uniform``, ``santa`` (``samples`` draws) or ``hybrid`` (exact
     ``topk_clusters`` clusters plus ``samples`` uniform draws of the rest).
     ``sample_a`` / ``sample_b`` inject the random draws instead of the
-    on-device Philox sampler (see include/santa_b200.h)."""
+    on-device Philox sampler (see include/santa_b200.h).  ``key_cache`` may
+    be a PagedKVCache (``value_cache`` None)."""
     _require_cuda("q", q)
-    _require_cuda("key_cache", key_cache)
-    _require_cuda("value_cache", value_cache)
+    kt, vt = _kv(key_cache, value_cache)
     if q.dtype != torch.float32 or q.dim() != 3:
         raise ValueError("q must be [batch, query_heads, head_dim] fp32")
     B, Hq, D = q.shape
@@ -288,8 +307,8 @@ def santa_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Te
     ess = torch.empty(B, Hq, dtype=torch.float32, device=q.device) if with_stats else None
     c = summary.as_c()
     _lib.check("santa_decode", lib.santa_decode(
-        ctypes.byref(geo), ctypes.byref(p), q.data_ptr(), key_cache.data_ptr(),
-        value_cache.data_ptr(), ctypes.byref(c), _lib.ptr(sample_a), _lib.ptr(sample_b),
+        ctypes.byref(geo), ctypes.byref(p), q.data_ptr(), kt.data_ptr(),
+        vt.data_ptr(), ctypes.byref(c), _lib.ptr(sample_a), _lib.ptr(sample_b),
         out.data_ptr(), lse.data_ptr(), _lib.ptr(n_exact), _lib.ptr(ess), ws.data_ptr(),
         nbytes.value, _lib.stream_handle(stream)))
     if injected:
@@ -309,9 +328,9 @@ class DecodeStep:
                  n_total: int, topk_clusters: int = 0, token_budget: int = 0, samples: int = 0,
                  scale: float | None = None, seed: int = 0, num_splits: int = 0,
                  injected: bool = False, with_stats: bool = False):
-        _require_cuda("key_cache", key_cache)
-        _require_cuda("value_cache", value_cache)
-        self.key_cache, self.value_cache, self.summary = key_cache, value_cache, summary
+        self.cache = key_cache   # holds a PagedKVCache's table alive
+        self.key_cache, self.value_cache = _kv(key_cache, value_cache)
+        self.summary = summary
         B, Hkv, _, D = key_cache.shape
         self.geo = _geometry(key_cache, num_query_heads, n_total, summary.sample_end)
         self.scale = 1.0 / math.sqrt(D) if scale is None else scale
@@ -326,7 +345,7 @@ class DecodeStep:
             ctypes.byref(self.geo), ctypes.byref(self.p), summary.max_groups,
             ctypes.byref(nbytes)))
         self.ws_bytes = nbytes.value
-        dev = key_cache.device
+        dev = self.key_cache.device
         self.ws = torch.empty(max(1, self.ws_bytes), dtype=torch.uint8, device=dev)
         self.out = torch.empty(B, num_query_heads, D, dtype=torch.float32, device=dev)
         self.lse = torch.empty(B, num_query_heads, dtype=torch.float32, device=dev)
@@ -379,6 +398,7 @@ def santa_decode_select(q: torch.Tensor, key_cache: torch.Tensor, value_cache: t
     Returns ``(selected [B, Hq, G] uint8, sample_rows [B, Hq, S] int32,
     n_exact [B, Hq] int32)``; ``sample_rows`` index the cluster-sorted copy."""
     _require_cuda("q", q)
+    kt, vt = _kv(key_cache, value_cache)
     B, Hq, D = q.shape
     sample_end = summary.sample_end if sample_end is None else sample_end
     geo = _geometry(key_cache, Hq, n_total, sample_end)
@@ -398,8 +418,8 @@ def santa_decode_select(q: torch.Tensor, key_cache: torch.Tensor, value_cache: t
     n_exact = torch.empty(B, Hq, dtype=torch.int32, device=q.device)
     c = summary.as_c()
     _lib.check("santa_decode_select", lib.santa_decode_select(
-        ctypes.byref(geo), ctypes.byref(p), q.data_ptr(), key_cache.data_ptr(),
-        value_cache.data_ptr(), ctypes.byref(c), _lib.ptr(sample_a), _lib.ptr(sample_b),
+        ctypes.byref(geo), ctypes.byref(p), q.data_ptr(), kt.data_ptr(),
+        vt.data_ptr(), ctypes.byref(c), _lib.ptr(sample_a), _lib.ptr(sample_b),
         selected.data_ptr(), rows.data_ptr(), n_exact.data_ptr(), ws.data_ptr(), nbytes.value,
         _lib.stream_handle(stream)))
     if sample_a is not None:

@@ -47,7 +47,10 @@ def test_struct_layout_matches_c():
     # SantaDecodeParams: 4 x int32, float, int32, 2 x uint64, int32 (+pad)
     assert ctypes.sizeof(_lib.SantaDecodeParams) == 48
     assert _lib.SantaDecodeParams.seed.offset == 24
-    assert ctypes.sizeof(_lib.SantaGeometry) == 32
+    # SantaGeometry: 8 x int32, pointer, 4 x int32
+    assert ctypes.sizeof(_lib.SantaGeometry) == 56
+    assert _lib.SantaGeometry.block_table.offset == 32
+    assert _lib.SantaGeometry.reserved.offset == 52
     assert _lib.SantaSummary.max_groups.offset == 72
 
 
@@ -89,3 +92,41 @@ def test_python_entry_points_refuse_cpu_tensors():
 
 def test_build_is_sm100a():
     assert "arch=compute_100a,code=sm_100a" in " ".join(_build.ARCH_FLAGS)
+
+
+def test_paged_geometry_is_validated():
+    """Paged caches: page_size a power of two, capacity = max_pages x
+    page_size, pool rows below 2^31 - 2 (the gather kernel's row codes).
+    Workspace queries only validate: the table pointer is never read."""
+    lib = _lib.load()
+    n = ctypes.c_size_t()
+    table = ctypes.c_void_p(4096)
+
+    def geo(page_size, max_pages, num_pages, capacity=32768):
+        return _lib.SantaGeometry(8, 4, 7, 128, capacity, 32768, 32704, _lib.DTYPE_BF16,
+                                  table, page_size, max_pages, num_pages, 0)
+
+    ok = geo(256, 128, 1024)
+    assert lib.santa_build_summary_workspace_bytes(ctypes.byref(ok), 256, ctypes.byref(n)) == 0
+    for bad in (geo(96, 342, 1024, capacity=96 * 342), geo(256, 64, 1024), geo(0, 128, 1024),
+                geo(256, 128, 0)):
+        assert lib.santa_build_summary_workspace_bytes(
+            ctypes.byref(bad), 256, ctypes.byref(n)) == _lib.SANTA_ERR_INVALID_ARGUMENT
+    huge = geo(1 << 16, 1, 1 << 13, capacity=1 << 16)   # 2^13 x 4 x 2^16 = 2^31 rows
+    huge.n_total, huge.sample_end = 1 << 15, (1 << 15) - 64
+    assert lib.santa_build_summary_workspace_bytes(
+        ctypes.byref(huge), 256, ctypes.byref(n)) == _lib.SANTA_ERR_UNSUPPORTED
+
+
+def test_paged_append_validates_arguments():
+    lib = _lib.load()
+    fake = ctypes.c_void_p(4096)
+    args = [1, 1, 28, 4, 128] + [fake] * 7
+    # page size not a power of two, then a missing table
+    assert lib.santa_rope_append_paged(*args, fake, 96, 4, 4, 0, None, None,
+                                       None) == _lib.SANTA_ERR_INVALID_ARGUMENT
+    assert lib.santa_rope_append_paged(*args, None, 64, 4, 4, 0, None, None,
+                                       None) == _lib.SANTA_ERR_INVALID_ARGUMENT
+    # past the last page of the table
+    assert lib.santa_rope_append_paged(*args, fake, 64, 4, 4, 256, None, None,
+                                       None) == _lib.SANTA_ERR_INVALID_ARGUMENT
