@@ -30,7 +30,7 @@ QWEN7B_SMALL = scaled_shape(QWEN7B_32K, name="qwen2.5-7b-attn-ctx2048-b3", batch
                             context=2048, true_clusters=32, n_clusters=32,
                             topk_clusters=4, samples=64, steps=1)
 SHAPES = {"fp32_d64": QWEN05B_4K, "bf16_d128": QWEN7B_SMALL}
-SUMMARY_FIELDS = ("members", "positions", "starts", "lengths", "log_n", "centroids",
+SUMMARY_FIELDS = ("members", "positions", "starts", "lengths_long", "log_n", "key_centroids",
                   "n_groups", "sorted_key", "sorted_value")
 
 
