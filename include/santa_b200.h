@@ -16,10 +16,10 @@
  *                              _attention_forward does per head at :347-358
  *   santa_prefill              santapp_ruler/attention/santapp.py:320-346
  *                              (prefill branch -> sdpa_attention_forward)
+ *   santa_prefill_paged        the same over the paged LayerCache
  *   santa_rope_append          santapp_ruler/attention/santapp.py:234-274, 308-313
- *   santa_rope_append_paged    (_append_cache and the RoPE of _attention_forward;
- *                              the paged form of the LayerCache of :66-77)
  *                              (_append_cache and the RoPE of _attention_forward)
+ *   santa_rope_append_paged    the same into the paged form of the LayerCache of :66-77
  *   santa_fingerprints         santapp_ruler/attention/santapp.py:598-691
  *   santa_kmeans_*             santapp_ruler/attention/minibatch_kmeans.py:58-267
  *                              (_squared_distances, _assign, _greedy_kmeans_plus_plus,
@@ -308,6 +308,16 @@ int santa_prefill_workspace_bytes(const SantaPrefillShape *shape, size_t *bytes)
 int santa_prefill(const SantaPrefillShape *shape, const void *q, const void *k, const void *v,
                   void *out, float *lse, int32_t *error_flag, void *workspace,
                   size_t workspace_bytes, cudaStream_t stream);
+
+/* The same with K and V in paged pools [num_pages, Hkv, page_size, D] (the
+ * paged SantaGeometry layout; tokens [0, seq_len) through block_table
+ * [batch][max_pages]; page ids outside [0, num_pages) read page 0).
+ * shape->kv_capacity is ignored; max_pages * page_size >= seq_len. */
+int santa_prefill_paged(const SantaPrefillShape *shape, const void *q, const void *key_pool,
+                        const void *value_pool, const int32_t *block_table, int32_t page_size,
+                        int32_t max_pages, int32_t num_pages, void *out, float *lse,
+                        int32_t *error_flag, void *workspace, size_t workspace_bytes,
+                        cudaStream_t stream);
 
 /* ---- key fingerprints (attention/santapp.py:598-690) -------------------- */
 

@@ -433,26 +433,26 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
     if (warp == kPfMmaWarp) tmem_dealloc(tmem, 512);
 }
 
-// K [B, Hkv, cap, D] and V (tokens [0, T)) -> the tile images of K and V^T
+// K and V (tokens [0, T) of a contiguous [B, Hkv, cap, D] cache or of paged
+// pools, rows through cache_row) -> the tile images of K and V^T
 // (pf_img_off layout, zeros past T).  One CTA per (128-key tile, b * kv head).
 __global__ void __launch_bounds__(256) prefill_image_kernel(const __nv_bfloat16 *k,
                                                             const __nv_bfloat16 *v,
                                                             unsigned char *kimg,
                                                             unsigned char *vimg, int T,
-                                                            int n_tiles, int64_t cap) {
+                                                            int n_tiles, SantaGeometry geo) {
     __shared__ __align__(16) __nv_bfloat16 vs[kPfRows][kPfD + 8];
     const int j = blockIdx.x, bh = blockIdx.y, tid = threadIdx.x;
-    const int64_t src0 = ((int64_t)bh * cap + (int64_t)j * kPfRows) * kPfD;
     unsigned char *ki = kimg + ((size_t)bh * n_tiles + j) * kPfTile;
     unsigned char *vi = vimg + ((size_t)bh * n_tiles + j) * kPfTile;
     for (int idx = tid; idx < kPfRows * 16; idx += 256) {
         const int r = idx >> 4, ch = idx & 15;
-        const bool ok = j * kPfRows + r < T;
-        const uint4 kv = ok ? *(const uint4 *)(k + src0 + (int64_t)r * kPfD + ch * 8)
-                            : make_uint4(0, 0, 0, 0);
+        const int t = j * kPfRows + r;
+        const bool ok = t < T;
+        const int64_t src = ok ? cache_row(geo, bh, t) * kPfD + ch * 8 : 0;
+        const uint4 kv = ok ? *(const uint4 *)(k + src) : make_uint4(0, 0, 0, 0);
         *(uint4 *)(ki + pf_img_off(r, ch)) = kv;
-        const uint4 vv = ok ? *(const uint4 *)(v + src0 + (int64_t)r * kPfD + ch * 8)
-                            : make_uint4(0, 0, 0, 0);
+        const uint4 vv = ok ? *(const uint4 *)(v + src) : make_uint4(0, 0, 0, 0);
         *(uint4 *)(&vs[r][ch * 8]) = vv;
     }
     __syncthreads();
@@ -493,11 +493,10 @@ extern "C" int santa_prefill_workspace_bytes(const SantaPrefillShape *shape, siz
     return SANTA_OK;
 }
 
-extern "C" int santa_prefill(const SantaPrefillShape *shape, const void *q, const void *k,
-                             const void *v, void *out, float *lse, int32_t *error_flag,
-                             void *workspace, size_t workspace_bytes, cudaStream_t stream) {
-    int st = check_prefill(shape);
-    if (st) return st;
+// Both entry points: geo describes where token t of (b, kv head) lives.
+static int prefill(const SantaPrefillShape *shape, const SantaGeometry &geo, const void *q,
+                   const void *k, const void *v, void *out, float *lse, int32_t *error_flag,
+                   void *workspace, size_t workspace_bytes, cudaStream_t stream) {
     if (!q || !k || !v || !out || !error_flag) return SANTA_ERR_INVALID_ARGUMENT;
     size_t need = 0;
     santa_prefill_workspace_bytes(shape, &need);
@@ -507,11 +506,10 @@ extern "C" int santa_prefill(const SantaPrefillShape *shape, const void *q, cons
     const int T = shape->seq_len;
     const int n_tiles = (T + kPfRows - 1) / kPfRows;
     const int BHkv = shape->batch * shape->num_kv_heads;
-    const int64_t cap = shape->kv_capacity ? shape->kv_capacity : T;
     unsigned char *kimg = (unsigned char *)workspace;
     unsigned char *vimg = kimg + (size_t)BHkv * n_tiles * kPfTile;
     prefill_image_kernel<<<dim3(n_tiles, BHkv), 256, 0, stream>>>(
-        (const __nv_bfloat16 *)k, (const __nv_bfloat16 *)v, kimg, vimg, T, n_tiles, cap);
+        (const __nv_bfloat16 *)k, (const __nv_bfloat16 *)v, kimg, vimg, T, n_tiles, geo);
     SANTA_LAUNCH_CHECK();
     PrefillArgs a;
     a.q = (const __nv_bfloat16 *)q;
@@ -534,4 +532,40 @@ extern "C" int santa_prefill(const SantaPrefillShape *shape, const void *q, cons
     prefill_fwd_kernel<<<grid, kPfThreads, smem, stream>>>(a);
     SANTA_LAUNCH_CHECK();
     return SANTA_OK;
+}
+
+extern "C" int santa_prefill(const SantaPrefillShape *shape, const void *q, const void *k,
+                             const void *v, void *out, float *lse, int32_t *error_flag,
+                             void *workspace, size_t workspace_bytes, cudaStream_t stream) {
+    int st = check_prefill(shape);
+    if (st) return st;
+    SantaGeometry geo = {};
+    geo.batch = shape->batch;
+    geo.num_kv_heads = shape->num_kv_heads;
+    geo.capacity = shape->kv_capacity ? shape->kv_capacity : shape->seq_len;
+    return prefill(shape, geo, q, k, v, out, lse, error_flag, workspace, workspace_bytes, stream);
+}
+
+extern "C" int santa_prefill_paged(const SantaPrefillShape *shape, const void *q,
+                                   const void *key_pool, const void *value_pool,
+                                   const int32_t *block_table, int32_t page_size,
+                                   int32_t max_pages, int32_t num_pages, void *out, float *lse,
+                                   int32_t *error_flag, void *workspace,
+                                   size_t workspace_bytes, cudaStream_t stream) {
+    int st = check_prefill(shape);
+    if (st) return st;
+    if (!block_table || page_size <= 0 || (page_size & (page_size - 1)) || max_pages <= 0 ||
+        num_pages <= 0 || (int64_t)max_pages * page_size < shape->seq_len ||
+        (int64_t)max_pages * page_size > INT32_MAX)
+        return SANTA_ERR_INVALID_ARGUMENT;
+    SantaGeometry geo = {};
+    geo.batch = shape->batch;
+    geo.num_kv_heads = shape->num_kv_heads;
+    geo.capacity = max_pages * page_size;
+    geo.block_table = block_table;
+    geo.page_size = page_size;
+    geo.max_pages = max_pages;
+    geo.num_pages = num_pages;
+    return prefill(shape, geo, q, key_pool, value_pool, out, lse, error_flag, workspace,
+                   workspace_bytes, stream);
 }

@@ -146,6 +146,9 @@ SIGNATURES = {
                                                      _P(ctypes.c_size_t)]),
     "santa_prefill": (ctypes.c_int, [_P(SantaPrefillShape), _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                      ctypes.c_size_t, _vp]),
+    "santa_prefill_paged": (ctypes.c_int, [_P(SantaPrefillShape), _vp, _vp, _vp, _vp, _i32,
+                                           _i32, _i32, _vp, _vp, _vp, _vp, ctypes.c_size_t,
+                                           _vp]),
     "santa_fingerprints_workspace_bytes": (ctypes.c_int, [_i32, _P(ctypes.c_size_t)]),
     "santa_fingerprints": (ctypes.c_int, [_vp, _i32, ctypes.c_int64, _i32, _vp, ctypes.c_int64,
                                           _i32, _vp, _i32, ctypes.c_float, _i32, _vp, _vp,

@@ -27,7 +27,12 @@ reference supports batch 1, :293-294):
 
 The engine takes the reference's own ``SantaPlusConfig`` (config.py:68-78,
 a slotted dataclass) or ``SantaB200Config``: fields the reference's config
-lacks (``topk_clusters``, ``n_clusters``) fall back to their defaults.
+lacks (``topk_clusters``, ``n_clusters``, ``kv_page_size``) fall back to
+their defaults.  With ``kv_page_size`` set, every layer's cache is a
+``PagedKVCache`` (page pools + block table, pages mapped as the sequences
+grow): the append, the prefill, the summary build and the sparse decode all
+read and write the pages directly; the dense fidelity path and the
+clustering inputs gather the tokens they need.
 
 Probe queries are captured inside the patched forward at the probe positions
 only (the reference keeps every layer's full q_proj output).
@@ -48,6 +53,7 @@ import torch
 from .. import _lib
 from .fingerprints import build_fingerprints, cluster_count, probe_positions
 from .kmeans import SklearnLikeTorchMiniBatchKMeans
+from .paged import PagedKVCache
 from .prefill import santa_prefill
 from .santapp import DecodeTrafficTracker, build_summary, santa_decode
 
@@ -84,19 +90,31 @@ class SantaB200Config:
     kmeans: KMeansConfig = field(default_factory=KMeansConfig)
     topk_clusters: int = 16
     n_clusters: int | None = None
+    kv_page_size: int | None = None   # paged KV cache (tokens per page, a power of two)
 
 
 @dataclass
 class LayerCache:
-    key: torch.Tensor     # [B, Hkv, capacity, D]
-    value: torch.Tensor
+    """One layer's K/V (LayerCache, santapp.py:66-77, batched): contiguous
+    ``[B, Hkv, capacity, D]`` tensors, or ``paged`` (key / value None)."""
+    key: torch.Tensor | None     # [B, Hkv, capacity, D]
+    value: torch.Tensor | None
     length: int
+    paged: PagedKVCache | None = None
 
     @property
     def capacity(self) -> int:
-        return int(self.key.shape[2])
+        return self.paged.capacity if self.paged is not None else int(self.key.shape[2])
+
+    def kv(self) -> tuple:
+        """The (key_cache, value_cache) arguments of the santa_* entry points."""
+        return (self.paged, None) if self.paged is not None else (self.key, self.value)
 
     def view(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """Tokens [0, length) as [B, Hkv, length, D] tensors (a gather copy
+        when paged)."""
+        if self.paged is not None:
+            return self.paged.to_contiguous(self.length)
         return self.key[:, :, : self.length], self.value[:, :, : self.length]
 
 
@@ -111,7 +129,7 @@ class SantaGeneration:
 
 
 # fields of SantaB200Config that the reference's SantaPlusConfig does not have
-_EXTRA_DEFAULTS = {"topk_clusters": 16, "n_clusters": None}
+_EXTRA_DEFAULTS = {"topk_clusters": 16, "n_clusters": None, "kv_page_size": None}
 
 
 def _patched_forward(attention, hidden_states, position_embeddings=None, attention_mask=None,
@@ -229,8 +247,13 @@ class SantaB200Engine:
         if cached is None:
             cap = max(self.cache_capacity, Tn)
             cap = (cap + 7) // 8 * 8
-            kb = torch.empty(B, Hkv, cap, D, dtype=torch.bfloat16, device=q.device)
-            cached = LayerCache(kb, torch.empty_like(kb), 0)
+            page_size = self._cfg("kv_page_size")
+            if page_size:
+                cached = LayerCache(None, None, 0, PagedKVCache.allocate(
+                    B, Hkv, D, max_tokens=cap, page_size=int(page_size), device=q.device))
+            else:
+                kb = torch.empty(B, Hkv, cap, D, dtype=torch.bfloat16, device=q.device)
+                cached = LayerCache(kb, torch.empty_like(kb), 0)
             self.cache[layer_id] = cached
         start = cached.length
         if start + Tn > cached.capacity:
@@ -241,14 +264,20 @@ class SantaB200Engine:
                                                       device=q.device)
         q_f32 = torch.empty(B, Hq, Tn, D, dtype=torch.float32, device=q.device) \
             if sparse_decode else None
-        _lib.check("santa_rope_append", self._lib.santa_rope_append(
-            B, Tn, Hq, Hkv, D, q.contiguous().data_ptr(), k.contiguous().data_ptr(),
-            v.contiguous().data_ptr(), cos.data_ptr(), sin.data_ptr(), cached.key.data_ptr(),
-            cached.value.data_ptr(), cached.capacity, start, _lib.ptr(q_bf), _lib.ptr(q_f32),
-            _lib.stream_handle()))
+        if cached.paged is not None:   # maps the pages the new tokens need
+            cached.paged.append(q.contiguous().view(B, Tn, Hq, D),
+                                k.contiguous().view(B, Tn, Hkv, D),
+                                v.contiguous().view(B, Tn, Hkv, D), cos, sin, start,
+                                q_rot_bf16=q_bf, q_rot_f32=q_f32)
+        else:
+            _lib.check("santa_rope_append", self._lib.santa_rope_append(
+                B, Tn, Hq, Hkv, D, q.contiguous().data_ptr(), k.contiguous().data_ptr(),
+                v.contiguous().data_ptr(), cos.data_ptr(), sin.data_ptr(),
+                cached.key.data_ptr(), cached.value.data_ptr(), cached.capacity, start,
+                _lib.ptr(q_bf), _lib.ptr(q_f32), _lib.stream_handle()))
         cached.length = start + Tn
         if sparse_decode:
-            res = santa_decode(q_f32[:, :, 0].contiguous(), cached.key, cached.value,
+            res = santa_decode(q_f32[:, :, 0].contiguous(), *cached.kv(),
                                self.summaries[layer_id], mode=self.config.mode,
                                n_total=cached.length, sample_end=self.sample_end,
                                topk_clusters=self._cfg("topk_clusters"),
@@ -268,7 +297,7 @@ class SantaB200Engine:
             out = res.out.to(torch.bfloat16).view(B, 1, Hq * D)
         elif start == 0:
             # prompt: causal attention of every position over the prompt
-            out = santa_prefill(q_bf, cached.key, cached.value, causal=True,
+            out = santa_prefill(q_bf, *cached.kv(), causal=True,
                                 scale=float(attention.scaling))
             self._prefill_flags.append(out._santa_error_flag)
             if self.log is not None:  # progress (synchronises: diagnostics only)
@@ -367,8 +396,11 @@ class SantaB200Engine:
                 st.wait_event(ready)
                 qp = probes[layer_id]
                 P = qp.shape[2]
-                fp = build_fingerprints(self.cache[layer_id].key[b, kv, :sample_end],
-                                        qp[b].contiguous(), kv, self.group, np.arange(P))
+                c = self.cache[layer_id]
+                keys = (c.paged.tokens(b, kv, sample_end) if c.paged is not None
+                        else c.key[b, kv, :sample_end])
+                fp = build_fingerprints(keys, qp[b].contiguous(), kv, self.group,
+                                        np.arange(P))
                 est = SklearnLikeTorchMiniBatchKMeans(
                     n_clusters, batch_size=km.batch_size, n_init=km.n_init,
                     max_iter=km.max_iter, tol=km.tol,
@@ -393,7 +425,7 @@ class SantaB200Engine:
             main.wait_event(e)
         for layer_id in layers:
             cached = self.cache[layer_id]
-            self.summaries[layer_id] = build_summary(cached.key, cached.value,
+            self.summaries[layer_id] = build_summary(*cached.kv(),
                                                      labels[layer_id], n_clusters,
                                                      sample_end=sample_end,
                                                      n_total=cached.length)
@@ -424,9 +456,16 @@ class SantaB200Engine:
                 for kv in range(self.num_kv_heads):
                     qd = q[b, kv * self.group]
                     qhat = qd / qd.norm()
-                    norm = c.key[b, kv, :self.sample_end].float().norm(dim=-1).mean()
-                    idx = torch.from_numpy(pos[b, kv]).to(c.key.device)
-                    c.key[b, kv, idx] = (scale * norm * qhat).to(c.key.dtype)[None]
+                    keys = (c.paged.tokens(b, kv, self.sample_end) if c.paged is not None
+                            else c.key[b, kv, :self.sample_end])
+                    norm = keys.float().norm(dim=-1).mean()
+                    new = (scale * norm * qhat).to(keys.dtype)[None]
+                    if c.paged is not None:
+                        pages, slots = c.paged.slots(b, pos[b, kv])
+                        c.paged.key_pool[pages, kv, slots] = new
+                    else:
+                        idx = torch.from_numpy(pos[b, kv]).to(keys.device)
+                        c.key[b, kv, idx] = new
             planted[layer_id] = pos
 
         self._capture_q = {}
@@ -446,7 +485,7 @@ class SantaB200Engine:
         head of every group, read out, must cover every planted position."""
         from .santapp import santa_decode_select
         summ = self.summaries[layer_id]
-        sel, _, _ = santa_decode_select(q, cached.key, cached.value, summ,
+        sel, _, _ = santa_decode_select(q, *cached.kv(), summ,
                                         mode=self.config.mode, n_total=cached.length,
                                         sample_end=self.sample_end,
                                         topk_clusters=self._cfg("topk_clusters"),

@@ -57,6 +57,7 @@ class PagedKVCache:
         self.key_pool, self.value_pool, self.block_table = key_pool, value_pool, block_table
         self._free: list[int] | None = None       # free page ids (allocate() only)
         self._host_table: torch.Tensor | None = None
+        self._mapped = 0                            # pages mapped in every sequence
 
     # ---- shape ------------------------------------------------------------
     @property
@@ -136,6 +137,8 @@ class PagedKVCache:
         if self._free is None:
             raise RuntimeError("reserve() needs a cache made by allocate()")
         need = -(-length // self.page_size)
+        if need <= self._mapped:      # every sequence holds these pages already
+            return
         if need > self.max_pages:
             raise ValueError(f"length {length} exceeds the capacity {self.capacity}")
         changed = False
@@ -146,6 +149,7 @@ class PagedKVCache:
                         raise RuntimeError("page pool exhausted")
                     self._host_table[b, i] = self._free.pop()
                     changed = True
+        self._mapped = need
         if changed:
             self.block_table.copy_(self._host_table, non_blocking=False)
 
@@ -158,6 +162,7 @@ class PagedKVCache:
             if page >= 0:
                 self._free.append(page)
                 self._host_table[b, i] = -1
+        self._mapped = 0
         self.block_table.copy_(self._host_table, non_blocking=False)
 
     @classmethod
@@ -195,6 +200,24 @@ class PagedKVCache:
                                                          n * self.page_size, self.head_dim)
             out.append(full[:, :, :length].contiguous())
         return out[0], out[1]
+
+    def slots(self, b: int, positions) -> tuple[torch.Tensor, torch.Tensor]:
+        """(page ids, slots) of sequence ``b``'s token positions, from the
+        host copy of the table: ``key_pool[pages, kv, slots]`` are the rows."""
+        if self._host_table is None:
+            raise RuntimeError("slots() needs a cache made by allocate()")
+        pos = torch.as_tensor(positions, dtype=torch.long)
+        pages = self._host_table[b].long()[pos // self.page_size]
+        if (pages < 0).any():
+            raise ValueError("position in an unmapped page")
+        return pages.to(self.device), (pos % self.page_size).to(self.device)
+
+    def tokens(self, b: int, kv: int, n: int, value: bool = False) -> torch.Tensor:
+        """Tokens ``[0, n)`` of sequence ``b``, KV head ``kv`` as a contiguous
+        ``[n, D]`` tensor (a gather over the sequence's pages, on the device)."""
+        pages = self.block_table[b, : -(-n // self.page_size)].long()
+        pool = self.value_pool if value else self.key_pool
+        return pool[pages, kv].reshape(-1, self.head_dim)[:n]
 
     # ---- the C view ----------------------------------------------------------
     def fill_geometry(self, geo: "_lib.SantaGeometry") -> None:

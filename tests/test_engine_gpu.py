@@ -260,3 +260,32 @@ def test_planted_keys_through_the_engine(model):
     assert chk["total"] == 2 * 2 * 2 * 16  # layers x sequences x KV heads x planted
     assert chk["all_landed"], chk
     assert len(gen.token_ids) == 2 and all(len(t) == 3 for t in gen.token_ids)
+
+
+def test_paged_cache_generates_like_the_contiguous_cache(model):
+    """kv_page_size: the engine keeps every layer's K/V in page pools (pages
+    mapped as the prompt and the generated tokens arrive); prefill, planted
+    keys, clustering, summaries and decode read the pages, and the run
+    reproduces the contiguous-cache run exactly."""
+    ids = _prompt(2, 900, seed=21)
+    kw = dict(mode="hybrid", samples_per_head=32, recent_window=64, probe_queries=16,
+              n_clusters=24, topk_clusters=4, kmeans=KMeansConfig(batch_size=256, max_iter=10))
+    runs = []
+    for page_size in (None, 64):
+        eng = SantaB200Engine(model, SantaB200Config(kv_page_size=page_size, **kw))
+        gen = eng.generate(ids, max_new_tokens=6, planted_keys=8)
+        runs.append((gen, eng))
+    (g0, e0), (g1, e1) = runs
+    assert g1.token_ids == g0.token_ids
+    assert g1.metrics["planted_check"] == g0.metrics["planted_check"]
+    for layer_id, s0 in e0.summaries.items():
+        s1 = e1.summaries[layer_id]
+        for f in ("members", "starts", "lengths_long", "key_centroids", "sorted_key"):
+            assert torch.equal(getattr(s0, f), getattr(s1, f)), (layer_id, f)
+    c = e1.cache[0]
+    assert c.paged is not None and c.key is None
+    k0, v0 = e0.cache[0].view()
+    k1, v1 = c.view()
+    assert torch.equal(k0, k1) and torch.equal(v0, v1)
+    # pages are mapped as needed: 900 + 6 - 1 tokens in 64-token pages
+    assert int((c.paged.block_table >= 0).sum(dim=1).max()) == -(-(900 + 5) // 64)

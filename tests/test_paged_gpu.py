@@ -174,3 +174,22 @@ def test_paged_rope_append_matches_contiguous():
     # the mapped slots past the last token were not written either
     last = cache.key_pool[t[:, (pos - 1) // page]][:, :, (pos % page):]
     assert torch.isnan(last.float()).all()
+
+
+def test_paged_prefill_bit_identical():
+    """santa_prefill over page pools (random page order, NaN spare pages)
+    equals the contiguous-cache prefill bit for bit, output and LSE."""
+    from santapp_b200.attention.prefill import santa_prefill
+    torch.manual_seed(3)
+    B, Hq, Hkv, D, T = 2, 8, 2, 128, 1000
+    dev = torch.device("cuda")
+    q = torch.randn(B, Hq, T, D, device=dev).to(torch.bfloat16)
+    kc = torch.randn(B, Hkv, T + 24, D, device=dev).to(torch.bfloat16)
+    vc = torch.randn_like(kc)
+    cache = _paged(kc, vc, T, 64, seed=9)
+    a, la = santa_prefill(q, kc, vc, causal=True, return_lse=True)
+    b, lb = santa_prefill(q, cache, None, causal=True, return_lse=True)
+    torch.cuda.synchronize()
+    assert int(a._santa_error_flag.item()) == 0 and int(b._santa_error_flag.item()) == 0
+    assert torch.isfinite(b.float()).all()
+    assert torch.equal(a, b) and torch.equal(la, lb)
