@@ -170,7 +170,7 @@ def algorithmic_bytes(runner, q, step, shape, summ, cid):
     metadata of every (sequence, KV head)."""
     from santapp_b200.attention import santapp as S
     sel, rows, _ = S.santa_decode_select(
-        q, runner.key_cache, runner.value_cache, summ, mode=runner.mode,
+        q, *runner.kv_args, summ, mode=runner.mode,
         n_total=shape.context, topk_clusters=shape.topk_clusters, samples=shape.samples,
         seed=runner.p.seed, step=step)
     B, Hq, G = sel.shape
@@ -200,21 +200,30 @@ def cluster_of_row(summ, shape):
     return (torch.cumsum(marks[:, :N], dim=1) - 1).clamp_min_(0)
 
 
-def measure_decode(args, shape, steps, warmup, dev, keep=False):
+def measure_decode(args, shape, steps, warmup, dev, keep=False, page_size=None):
     """The K timed decode steps of one workload on one GPU: device time per
     step, the select / attend split, and the attend kernel's roofline from
     the algorithmic bytes of every timed step.  keep: also return the
-    workload, summary and step object (for the e2e run)."""
+    workload, summary and step object (for the e2e run).  page_size: the
+    cache moved into page pools (pages in a seeded random order) first."""
     from santapp_b200.attention import santapp as S
+    from santapp_b200.attention.paged import PagedKVCache
     from santapp_b200.synthetic import scaled_shape
     n_q = max(shape.steps, steps + warmup)
     w = make_decode_workload(scaled_shape(shape, steps=n_q), seed=args.seed, device=dev)
+    kc, vc = w.keys, w.values
+    if page_size:
+        kc = PagedKVCache.from_contiguous(w.keys, w.values, length=shape.context,
+                                          page_size=page_size, page_order_seed=args.seed)
+        vc = None
+        w.keys = w.values = None
+        torch.cuda.empty_cache()
     labels = w.labels[:, :, :shape.sample_end].contiguous()
-    summ = S.build_summary(w.keys, w.values, labels, shape.n_clusters,
+    summ = S.build_summary(kc, vc, labels, shape.n_clusters,
                            sample_end=shape.sample_end, n_total=shape.context)
     del labels
     w.labels = None
-    runner = S.DecodeStep(w.keys, w.values, summ, num_query_heads=shape.num_query_heads,
+    runner = S.DecodeStep(kc, vc, summ, num_query_heads=shape.num_query_heads,
                           mode=args.mode, n_total=shape.context,
                           topk_clusters=shape.topk_clusters, samples=shape.samples,
                           seed=args.seed)
@@ -327,7 +336,7 @@ def measure_decode(args, shape, steps, warmup, dev, keep=False):
     }
     if keep:
         return res, (w, summ, runner)
-    del runner, summ, w
+    del runner, summ, w, kc, vc
     torch.cuda.empty_cache()
     return res
 
@@ -412,6 +421,15 @@ def run_ours(args, rank, world):
             "roofline": r32["roofline"], "select_roofline": r32["select_roofline"],
             "step_roofline": r32["step_roofline"], "clocks": r32["clocks"],
             "gpu_launches": r32["gpu_launches"], "config": decode_config(QWEN7B_32K, args.mode, 1)}
+        # the headline workload again with the cache in 256-token pages
+        # scattered over the pool (block-table reads in every kernel)
+        rp = measure_decode(args, shape, args.steps, args.warmup, dev, page_size=256)
+        line["paged"] = {
+            "workload": shape.name, "page_size": 256, "steps": args.steps,
+            "value": rp["value"], "unit": "tokens/s", "ms_per_step": rp["ms_per_step"],
+            "phase_ms": rp["phase_ms"], "roofline": rp["roofline"],
+            "step_roofline": rp["step_roofline"], "clocks": rp["clocks"],
+            "gpu_launches": rp["gpu_launches"]}
         line["prefill"] = prefill_block(args, dev, 32768, steps=min(args.steps, 10))
     if not (args.no_cpu_baseline or args.profile):
         line["cpu_baseline"] = cpu_baseline_sample(args, shape)

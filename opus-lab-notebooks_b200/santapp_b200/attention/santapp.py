@@ -328,7 +328,7 @@ class DecodeStep:
                  n_total: int, topk_clusters: int = 0, token_budget: int = 0, samples: int = 0,
                  scale: float | None = None, seed: int = 0, num_splits: int = 0,
                  injected: bool = False, with_stats: bool = False):
-        self.cache = key_cache   # holds a PagedKVCache's table alive
+        self.kv_args = (key_cache, value_cache)   # as given (a PagedKVCache stays alive)
         self.key_cache, self.value_cache = _kv(key_cache, value_cache)
         self.summary = summary
         B, Hkv, _, D = key_cache.shape
