@@ -273,19 +273,29 @@ def test_paged_cache_generates_like_the_contiguous_cache(model):
     runs = []
     for page_size in (None, 64):
         eng = SantaB200Engine(model, SantaB200Config(kv_page_size=page_size, **kw))
+        snap = {}
+        clear = eng.clear
+
+        def keep_then_clear(eng=eng, snap=snap, clear=clear):
+            # generate() frees the caches at the end: keep the last state
+            if eng.cache:
+                snap["cache"], snap["summaries"] = dict(eng.cache), dict(eng.summaries)
+            clear()
+        eng.clear = keep_then_clear
         gen = eng.generate(ids, max_new_tokens=6, planted_keys=8)
-        runs.append((gen, eng))
+        runs.append((gen, snap))
     (g0, e0), (g1, e1) = runs
     assert g1.token_ids == g0.token_ids
     p0, p1 = g0.metrics["planted_check"], g1.metrics["planted_check"]
     assert (p1["landed"], p1["total"]) == (p0["landed"], p0["total"])
-    for layer_id, s0 in e0.summaries.items():
-        s1 = e1.summaries[layer_id]
+    assert len(e0["summaries"]) == len(e1["summaries"]) == 2
+    for layer_id, s0 in e0["summaries"].items():
+        s1 = e1["summaries"][layer_id]
         for f in ("members", "starts", "lengths_long", "key_centroids", "sorted_key"):
             assert torch.equal(getattr(s0, f), getattr(s1, f)), (layer_id, f)
-    c = e1.cache[0]
+    c = e1["cache"][0]
     assert c.paged is not None and c.key is None
-    k0, v0 = e0.cache[0].view()
+    k0, v0 = e0["cache"][0].view()
     k1, v1 = c.view()
     assert torch.equal(k0, k1) and torch.equal(v0, v1)
     # pages are mapped as needed: 900 + 6 - 1 tokens in 64-token pages
