@@ -33,6 +33,15 @@
 
 namespace santa {
 
+// 1-D bulk copy (TMA engine, no multicast) of this GPU's global memory into
+// this CTA's shared memory: 16-byte aligned addresses, size a multiple of 16
+__device__ __forceinline__ void grp_bulk_g2s(void *dst, const void *src, uint32_t bytes,
+                                             uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
+        ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
 constexpr int kGrpThreads = 256;
 constexpr int kGrpWarps = kGrpThreads / 32;
 constexpr int kGrpMaxK = 32;
@@ -216,8 +225,8 @@ __device__ __forceinline__ void grp_score_row(const float *row, const float *qs,
 }
 
 // Unstaged slice: the warp scores the rows of its 32 lanes (lane row r, heads
-// part .. part + NH - 1), the rows streamed through the warp's 2 KB buffer
-// [32 rows][16 floats] one 16-dim piece at a time.  Each piece is one batch
+// part .. part + NH - 1), the rows streamed through the warp's two 2 KB
+// buffers [32 rows][16 floats] one 16-dim piece at a time.  Each piece is one batch
 // of coalesced cp.async copies (four lanes per row, 8 rows per instruction),
 // 16-byte slot k of row j held at slot k ^ ((j >> 1) & 3), so a quarter
 // warp reading its eight rows hits eight distinct bank groups.  The chains
@@ -242,22 +251,36 @@ __device__ __forceinline__ void grp_score_pieces(const float *cent, float *buf, 
         dst[i] = j * kGrpPiece + 4 * (k ^ ((j >> 1) & 3));
     }
     const int swz = (lane >> 1) & 3;
+    constexpr int NP = D / kGrpPiece;   // pieces per row
+    constexpr int PB = 32 * kGrpPiece;  // floats of one piece buffer
+    // piece p goes to buffer p & 1: the copies of piece p + 1 are in flight
+    // while piece p is scored
+    auto issue = [&](int p) {
+        float *bp = buf + (p & 1) * PB;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            if (cp[i]) cp_async16(bp + dst[i], src[i] + p * kGrpPiece);
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+    };
     float acc[NH];
 #pragma unroll
     for (int j = 0; j < NH; ++j) acc[j] = 0.f;
+    issue(0);
 #pragma unroll 1
-    for (int p = 0; p < D; p += kGrpPiece) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-            if (cp[i]) cp_async16(buf + dst[i], src[i] + p);
-        asm volatile("cp.async.commit_group;\n" ::: "memory");
-        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    for (int p = 0; p < NP; ++p) {
+        if (p + 1 < NP) {
+            issue(p + 1);
+            asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+        }
         __syncwarp();
         if (active) {
+            const float *bp = buf + (p & 1) * PB;
 #pragma unroll
             for (int e = 0; e < kGrpPiece / 4; ++e) {
-                const float4 x = *(const float4 *)(buf + lane * kGrpPiece + 4 * (e ^ swz));
-                const int d = p + 4 * e;
+                const float4 x = *(const float4 *)(bp + lane * kGrpPiece + 4 * (e ^ swz));
+                const int d = p * kGrpPiece + 4 * e;
                 float4 u[NH];
 #pragma unroll
                 for (int j = 0; j < NH; ++j) u[j] = *(const float4 *)(qs + (part + j) * QP + d);
@@ -271,7 +294,7 @@ __device__ __forceinline__ void grp_score_pieces(const float *cent, float *buf, 
                 for (int j = 0; j < NH; ++j) acc[j] = fmaf(x.w, u[j].w, acc[j]);
             }
         }
-        __syncwarp();  // the buffer is refilled by the next piece
+        __syncwarp();  // buffer p & 1 is refilled by piece p + 2
     }
     if (!active) return;
     const uint64_t low = (uint64_t)(0xFFFFFFFFu - (uint32_t)(c + cbase));
@@ -285,26 +308,45 @@ __device__ __forceinline__ void grp_score_pieces(const float *cent, float *buf, 
     }
 }
 
-// Dynamic shared memory of one CTA: keys [g][per] u64, starts / lengths /
-// union masks / log n [Gmax] 32-bit, then the CTA's slice of per =
-// ceil(Gmax / g) centroid rows ([per][D + 4] fp32) when it fits the budget
-// (four CTAs per SM); a larger slice is read from global memory instead,
-// after one bulk prefetch of it into L2, through a 2 KB piece buffer per warp.
-constexpr int kGrpDynBudget = 43 * 1024;
+// Dynamic shared memory of one CTA:
+//   keys  [g][per] u64       the guesses' keys of this CTA's rows (the
+//                            cluster's CTAs read them in the ranking)
+//   mask  [Gmax] int32       union masks
+//   qs    [nq][D + 4] fp32   the group's q rows (nq = g, or 8 when g > 4:
+//                            the second head set is padded to four)
+//   work  during the scoring: the CTA's slice of per = ceil(Gmax / g)
+//         centroid rows ([per][D + 4] fp32) when it fits the budget, else
+//         two 2 KB piece buffers per warp (the rows streamed from global
+//         memory, one piece in flight while the other is scored); after the
+//         scoring the same bytes hold starts / lengths [Gmax] int32 (one bulk
+//         copy each), the ranking lists [8][32] u64 and the union tables.
+// The budget keeps four CTAs on an SM (the static part is ~2 KB).
+constexpr int kGrpDynBudget = 53 * 1024;
+constexpr int kGrpUnion = SANTA_MAX_GROUP * kGrpMaxK;  // union entries at most
 struct GrpLayout {
-    int per;
+    int per, nq;
     bool staged;
-    size_t keys, meta, stage, bytes;
+    size_t keys, mask, qs, work, len, lists, ue, bytes;
 };
+__host__ __device__ inline size_t grp_al16(size_t v) { return (v + 15) / 16 * 16; }
 __host__ __device__ inline GrpLayout grp_layout(int Gmax, int g, int D) {
     GrpLayout L;
     L.per = (Gmax + g - 1) / g;
+    L.nq = g <= 4 ? g : 8;
     L.keys = 0;
-    L.meta = ((size_t)g * L.per * 8 + 15) / 16 * 16;
-    L.stage = L.meta + ((size_t)4 * Gmax * 4 + 15) / 16 * 16;
+    L.mask = grp_al16((size_t)g * L.per * 8);
+    L.qs = L.mask + grp_al16((size_t)Gmax * 4);
+    L.work = L.qs + grp_al16((size_t)L.nq * (D + kGrpQPitch) * 4);
+    // offsets inside work, after the scoring
+    L.len = grp_al16((size_t)Gmax * 4);
+    L.lists = 2 * L.len;
+    L.ue = L.lists + (size_t)kGrpWarps * 32 * 8;
+    const size_t post = L.ue + grp_al16((size_t)(4 * kGrpUnion + 1) * 4);
     const size_t slice = (size_t)L.per * (D + kGrpQPitch) * 4;
-    L.staged = L.stage + slice <= (size_t)kGrpDynBudget;
-    L.bytes = L.stage + (L.staged ? slice : (size_t)kGrpWarps * 32 * kGrpPiece * 4);
+    const size_t pieces = (size_t)2 * kGrpWarps * 32 * kGrpPiece * 4;
+    L.staged = L.work + (slice > post ? slice : post) <= (size_t)kGrpDynBudget;
+    const size_t scoring = L.staged ? slice : pieces;
+    L.bytes = L.work + (scoring > post ? scoring : post);
     return L;
 }
 
@@ -312,10 +354,6 @@ template <int D>
 __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(DecodeArgs a) {
     constexpr int QP = D + kGrpQPitch;
     extern __shared__ __align__(16) unsigned char grp_dyn[];
-    __shared__ __align__(16) float qs[SANTA_MAX_GROUP * QP];
-    __shared__ uint64_t lists[kGrpWarps * 32];
-    __shared__ int ue_start[SANTA_MAX_GROUP * kGrpMaxK], ue_mask[SANTA_MAX_GROUP * kGrpMaxK];
-    __shared__ int ue_cid[SANTA_MAX_GROUP * kGrpMaxK], ue_off[SANTA_MAX_GROUP * kGrpMaxK + 1];
     __shared__ int sel_s[kGrpMaxK];             // this head's clusters, descending key
     __shared__ int info_s[4];                   // this head: n_sel, n_exact, n_samples
     __shared__ int all_sel[SANTA_MAX_GROUP][kGrpMaxK];
@@ -324,6 +362,7 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
     __shared__ int2 sw[kGrpWarps];
     __shared__ int s_nunion, s_U;
     __shared__ uint64_t own_s[kGrpMaxK];        // peer exchange: this shard's own top-k
+    __shared__ uint64_t meta_bar;               // the starts / lengths bulk copies
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     // the attention kernel that follows may launch now (it waits for this
@@ -338,11 +377,12 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
     const GrpLayout L = grp_layout(Gmax, g, D);
     const int per = L.per;
     uint64_t *keys_s = (uint64_t *)(grp_dyn + L.keys);  // [g][per]
-    int *starts_s = (int *)(grp_dyn + L.meta);
-    int *len_s = starts_s + Gmax;
-    int *mask_s = len_s + Gmax;
-    float *logn_s = (float *)(mask_s + Gmax);
-    float *stage = (float *)(grp_dyn + L.stage);       // staged: [rows][QP]; else [warps][32][kGrpPiece]
+    int *mask_s = (int *)(grp_dyn + L.mask);
+    float *qs = (float *)(grp_dyn + L.qs);
+    unsigned char *work = grp_dyn + L.work;
+    float *stage = (float *)work;  // staged: [rows][QP]; else [warps][2][32][kGrpPiece]
+    // after the scoring (pointers formed where they are used)
+    int *starts_s = (int *)work;
     const int c0 = rank * per;
     const int nrows = max(0, min(per, Gmax - c0));
     const int S = a.p.samples;
@@ -362,24 +402,17 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
     // launch replaces candidates -> all-gather -> threshold selection.
     const bool fused = a.p2p.peers != nullptr;
 
-    // ---- loads: q rows, cluster metadata and (staged layout) the slice -------
+    // ---- loads: q rows and (staged layout) the slice ---------------------------
     // 16-byte cp.async copies by every thread; centroid rows and q rows land
     // in padded rows (pitch D + 4 floats: rows read at one offset by a
-    // quarter warp sit on distinct bank groups)
+    // quarter warp sit on distinct bank groups).  The starts and lengths are
+    // first read after the scoring: they come later, by bulk copy.
     const float *qb = a.q + ((int64_t)b * a.geo.num_kv_heads * g + (int64_t)kv * g) * D;
     const float *cent = a.sum.centroids + (int64_t)(bh * Gmax + c0) * D;  // the slice
-    if (!thr_mode && !L.staged && nrows > 0 && tid == kGrpThreads - 32)
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(cent),
-                     "r"((uint32_t)nrows * D * 4)
-                     : "memory");
+    const float *logn_g = a.sum.log_n + (int64_t)bh * Gmax;
     for (int i = tid; i < g * (D / 4); i += kGrpThreads) {
         const int hh = i / (D / 4), d = 4 * (i - hh * (D / 4));
         cp_async16(qs + hh * QP + d, qb + (int64_t)hh * D + d);
-    }
-    for (int i = tid; i < Gmax / 4; i += kGrpThreads) {
-        cp_async16(starts_s + 4 * i, a.sum.starts + (int64_t)bh * Gmax + 4 * i);
-        cp_async16(len_s + 4 * i, a.sum.lengths + (int64_t)bh * Gmax + 4 * i);
-        cp_async16(logn_s + 4 * i, a.sum.log_n + (int64_t)bh * Gmax + 4 * i);
     }
     if (L.staged && !thr_mode) {
         for (int i = tid; i < nrows * (D / 4); i += kGrpThreads) {
@@ -389,6 +422,10 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
     }
     asm volatile("cp.async.commit_group;\n" ::: "memory");
     for (int i = tid; i < Gmax; i += kGrpThreads) mask_s[i] = 0;
+    if (tid == 0) {
+        mbar_init(&meta_bar, 1);
+        mbar_fence_init();
+    }
     if (rank == 0 && tid == 0) a.ws.flag[bh] = 0;  // draws set it after two cluster barriers
     const int n_groups = a.sum.n_groups[bh];
     asm volatile("cp.async.wait_group 0;\n" ::: "memory");
@@ -407,8 +444,8 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
                 const int set = t / nrows, r = t - set * nrows;
                 const int c = c0 + r;
 #define GRP_SCORE(N)                                                                           \
-    grp_score_row<N, D, QP>(stage + r * QP, qs, set * 4, g, logn_s[c], a.p.scale, c, n_groups, \
-                            cbase, keys_s, per, r)
+    grp_score_row<N, D, QP>(stage + r * QP, qs, set * 4, g, __ldg(logn_g + c), a.p.scale, c,   \
+                            n_groups, cbase, keys_s, per, r)
                 switch (nh) {
                     case 1: GRP_SCORE(1); break;
                     case 2: GRP_SCORE(2); break;
@@ -418,13 +455,13 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
 #undef GRP_SCORE
             }
         } else {
-            float *buf = stage + warp * 32 * kGrpPiece;
+            float *buf = stage + warp * 2 * 32 * kGrpPiece;  // two pieces
             for (int t0 = warp * 32; t0 < total; t0 += kGrpThreads) {  // warp-uniform
                 const int t = t0 + lane;
                 const bool active = t < total;
                 const int set = active ? t / nrows : 0, r = active ? t - set * nrows : 0;
                 const int c = c0 + r;
-                const float log_n = active ? logn_s[c] : 0.f;
+                const float log_n = active ? __ldg(logn_g + c) : 0.f;
 #define GRP_SCORE(N)                                                                           \
     grp_score_pieces<N, D, QP>(cent, buf, qs, active, r, set * 4, g, log_n, a.p.scale, c,       \
                                n_groups, cbase, keys_s, per)
@@ -438,9 +475,20 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
             }
         }
     }
-    cl_sync();  // every CTA's keys are in place (and its metadata landed)
+    // starts and lengths into the work bytes, now free (the copies' async
+    // proxy writes follow this CTA's generic accesses of those bytes)
+    __syncthreads();
+    if (tid == 0) {
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&meta_bar, 2u * (uint32_t)Gmax * 4u);
+        grp_bulk_g2s(starts_s, a.sum.starts + (int64_t)bh * Gmax, (uint32_t)Gmax * 4u, &meta_bar);
+        grp_bulk_g2s(work + grp_al16((size_t)Gmax * 4), a.sum.lengths + (int64_t)bh * Gmax,
+                     (uint32_t)Gmax * 4u, &meta_bar);
+    }
+    cl_sync();  // every CTA's keys are in place
 
     // ---- 2. ranking of head h ---------------------------------------------------
+    uint64_t *lists = (uint64_t *)(work + 2 * grp_al16((size_t)Gmax * 4));
     uint64_t thr = 1ull;  // threshold mode: the global k-th key
     if (a.shard_cands) {
         const int64_t rows = (int64_t)a.geo.batch * a.geo.num_kv_heads * g;
@@ -511,6 +559,9 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
         if (tid < 32) lists[tid] = own_s[tid];
         __syncthreads();
     }
+    // the starts / lengths bulk copies (bounded wait; a local copy always lands)
+    if (!mbar_wait(&meta_bar, 0)) a.ws.flag[bh] = 2;
+    const int *len_s = (const int *)(work + grp_al16((size_t)Gmax * 4));
     if (warp == 0) {
         const uint64_t key = lists[lane];
         const int kmax = min(kk, n_groups);
@@ -539,6 +590,9 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
     cl_sync();  // every head's selection is in place
 
     // ---- 3. union of the group's selections ------------------------------------
+    int *ue_start = (int *)(work + 2 * grp_al16((size_t)Gmax * 4) + kGrpWarps * 32 * 8);
+    int *ue_mask = ue_start + kGrpUnion, *ue_cid = ue_mask + kGrpUnion;
+    int *ue_off = ue_cid + kGrpUnion;  // [kGrpUnion + 1]
     if (tid < g * 32) {
         const int hh = tid >> 5, j = tid & 31;
         all_sel[hh][j] = cl_ld_s32(cl_map(sel_s + j, (uint32_t)hh));

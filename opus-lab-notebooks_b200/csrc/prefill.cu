@@ -29,11 +29,14 @@
 //                          products while the other tile's softmax runs;
 //         warp 17          one thread streams K_j and V^T_j (two stages,
 //                          one 32 KB bulk copy each).
-//       The two softmax warpgroups take turns for their exp2 pass (an
-//       mbarrier token), so one tile's exponentials run beside the other
-//       tile's MMAs rather than beside its exponentials; exp2 is the MUFU
-//       ex2.approx instruction and row maxima and sums use eight independent
-//       partial accumulators (no serial fmax / fadd chains).
+//       The softmax is bound by its instruction issue, not by the MUFU:
+//       exp2 is the MUFU ex2.approx instruction, the scaling FMAs and the
+//       row-sum adds use the paired fp32 instructions (two lanes each), row
+//       maxima the three-input max, all over independent partial
+//       accumulators (no serial chains).  The two tiles' softmax passes run
+//       whenever their scores are ready (making them take turns for the
+//       MUFU, or moving part of the exponentials to an FMA-pipe polynomial,
+//       both measured slower).
 //       TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
 //       The running maximum is updated lazily: O and l are rescaled only
 //       when the maximum grows by more than 8 (log2 units), so p <= 2^8.
@@ -87,6 +90,32 @@ __device__ __forceinline__ float pf_exp2(float x) {
     return y;
 }
 
+// Paired fp32 arithmetic (the sm_100 two-lane FP32 instructions: each lane
+// rounds as the scalar instruction does) and the three-input maximum.
+__device__ __forceinline__ uint64_t pf_pack2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};\n" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void pf_unpack2(uint64_t v, float &lo, float &hi) {
+    asm("mov.b64 {%0, %1}, %2;\n" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t pf_fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;\n" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t pf_add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;\n" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float pf_max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;\n" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 // named barrier over n threads (whole warps) that also ORs a predicate
 __device__ __forceinline__ bool bar_red_or(int id, int n, bool v) {
     uint32_t r;
@@ -115,7 +144,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
     const uint32_t sK = sQ + 2 * kPfTile;            // K stage s at sK + s * kPfTile
     const uint32_t sV = sK + 2 * kPfTile;            // V^T stage s at sV + s * kPfTile
     __shared__ __align__(8) uint64_t bar_k[2], bar_v[2], bar_free[2], bar_s[2], bar_p[2];
-    __shared__ __align__(8) uint64_t bar_q, bar_o, bar_drain, bar_tok[2];
+    __shared__ __align__(8) uint64_t bar_q, bar_o, bar_drain;
     __shared__ uint32_t s_tmem;
     __shared__ volatile int s_abort;
 
@@ -140,8 +169,6 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
             mbar_init(&bar_p[s], 256);
         }
         mbar_init(&bar_q, 512);
-        mbar_init(&bar_tok[0], 256);
-        mbar_init(&bar_tok[1], 256);
         mbar_init(&bar_o, 1);
         mbar_init(&bar_drain, 1);
         s_abort = 0;
@@ -194,10 +221,6 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
         const int njt = t ? nj : nj0;
         float m_used = -INFINITY, l = 0.f;
         bool ok = true;
-        // the exp2 passes of the two tiles take turns (bar_tok[t] = tile t
-        // may start its pass 2), so one tile's exponentials overlap the other
-        // tile's MMAs instead of sharing the MUFU with its exponentials
-        if (t == 1) mbar_arrive(&bar_tok[0]);
         for (int j = 0; j < njt; ++j) {
             bool wok = !s_abort && mbar_wait(&bar_s[t], (uint32_t)(j & 1));
             // the TMEM loads below are warp-collective: the warp goes on only
@@ -223,21 +246,18 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
                     for (int i = 0; i < 32; ++i) {
                         const float v0 = i < lim ? __uint_as_float(r0[i]) : -INFINITY;
                         const float v1 = 32 + i < lim ? __uint_as_float(r1[i]) : -INFINITY;
-                        mp[i & 7] = fmaxf(mp[i & 7], fmaxf(v0, v1));
+                        mp[i & 7] = pf_max3(mp[i & 7], v0, v1);
                     }
                 } else {
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
-                        mp[i & 7] = fmaxf(mp[i & 7],
-                                          fmaxf(__uint_as_float(r0[i]), __uint_as_float(r1[i])));
+                        mp[i & 7] = pf_max3(mp[i & 7], __uint_as_float(r0[i]),
+                                            __uint_as_float(r1[i]));
                 }
             }
             s_red[j & 1][t][hf][row] = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
                                              fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
-            // my turn for the exp pass (tile 1's extra last iteration has no
-            // turn to wait for); its outcome joins the barrier's OR so both
-            // halves leave together
-            if (wok && j < nj0) wok = !s_abort && mbar_wait(&bar_tok[t], (uint32_t)(j & 1));
+            // a failed wait joins the barrier's OR so both halves leave together
             if (bar_red_or(bar_id, 256, !wok)) {
                 ok = false;
                 break;
@@ -276,9 +296,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
             // column) over my own first 32 score columns: the P columns of
             // chunk c, [16 c, 16 c + 16), lie below every column still to be read
             const float neg = m_used == -INFINITY ? 0.f : -m_used;
-            float lp[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) lp[e] = 0.f;
+            const uint64_t sc2 = pf_pack2(a.scale_log2, a.scale_log2), ng2 = pf_pack2(neg, neg);
+            uint64_t lp[2] = {0ull, 0ull};  // partial sums, two lanes each
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 uint32_t r[32], pk[16];
@@ -291,19 +310,21 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_fwd_kernel(PrefillArgs 
                 }
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const float p0 = pf_exp2(fmaf(__uint_as_float(r[2 * i]), a.scale_log2, neg));
-                    const float p1 =
-                        pf_exp2(fmaf(__uint_as_float(r[2 * i + 1]), a.scale_log2, neg));
-                    lp[i & 7] += p0 + p1;
+                    float x0, x1;
+                    pf_unpack2(pf_fma2(pf_pack2(__uint_as_float(r[2 * i]),
+                                                __uint_as_float(r[2 * i + 1])), sc2, ng2),
+                               x0, x1);
+                    const float p0 = pf_exp2(x0), p1 = pf_exp2(x1);
+                    lp[i & 1] = pf_add2(lp[i & 1], pf_pack2(p0, p1));
                     pk[i] = pack_bf16(p0, p1);
                 }
                 tmem_st_x16(tS + 16 * c, pk);
             }
-            l += ((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7]));
-            // the other tile's turn, while it has a turn left: nj0
-            // completions of each token, never two ahead of the waiter (a
-            // tile's next hand-over comes after it waited for the other's)
-            if (t == 0 || j + 1 < nj0) mbar_arrive(&bar_tok[1 - t]);
+            {
+                float s0, s1;
+                pf_unpack2(pf_add2(lp[0], lp[1]), s0, s1);
+                l += s0 + s1;
+            }
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(&bar_p[t]);
