@@ -450,35 +450,57 @@ def load_traffic(shape):
 
 def run_e2e(args, shape, w, summ, runner):
     """Through the public decode API with host buffers, the way a serving
-    loop calls it: a DecodeStep bound once to the cache and summary (what
-    the model-level engine uses), then per step the queries copied
-    host->device from pinned memory, santa_decode_plan + santa_decode_execute
-    (C ABI) and the output read back into pinned memory, synchronised."""
+    loop calls it, synchronised every step: the step's queries are copied on
+    the host into the pinned staging buffer, then one GraphedDecodeStep
+    launch (the DecodeStep bound once to the cache and summary, captured with
+    its transfers: queries and step counter host->device, selection,
+    attention, output device->pinned host), then the stream is synchronised
+    and the output is in host memory.  The per-call form (torch copies around
+    DecodeStep's santa_decode_plan + santa_decode_execute) is timed beside it."""
     from santapp_b200.attention import santapp as S
     steps = args.steps
-    q_host = w.queries[:steps].cpu().pin_memory()
+    q_all = w.queries[:steps].cpu()                     # the steps' queries on the host
+    q_host = torch.empty(tuple(q_all.shape[1:]), dtype=torch.float32).pin_memory()
     out_host = torch.empty(shape.batch, shape.num_query_heads, shape.head_dim).pin_memory()
-    q_dev = torch.empty_like(w.queries[0])
     step_api = S.DecodeStep(w.keys, w.values, summ, num_query_heads=shape.num_query_heads,
                             mode=args.mode, n_total=shape.context,
                             topk_clusters=shape.topk_clusters, samples=shape.samples,
                             seed=args.seed)
+    graphed = step_api.graphed(q_host, out_host)
+    stream = torch.cuda.current_stream()
     for i in range(2):
-        q_dev.copy_(q_host[i], non_blocking=True)
-        out_host.copy_(step_api(q_dev, step=i), non_blocking=True)
-        torch.cuda.current_stream().synchronize()
+        q_host.copy_(q_all[i])
+        graphed.run(i)
+        stream.synchronize()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for i in range(steps):
-        q_dev.copy_(q_host[i], non_blocking=True)
-        out_host.copy_(step_api(q_dev, step=i), non_blocking=True)
-        torch.cuda.current_stream().synchronize()
+        q_host.copy_(q_all[i])
+        graphed.run(i)
+        stream.synchronize()
     dt = time.perf_counter() - t0
+    # the per-call form: torch copies around two C ABI calls
+    q_pin = q_all.pin_memory()
+    q_dev = torch.empty_like(w.queries[0])
+    for i in range(2):
+        q_dev.copy_(q_pin[i], non_blocking=True)
+        out_host.copy_(step_api(q_dev, step=i), non_blocking=True)
+        stream.synchronize()
+    t1 = time.perf_counter()
+    for i in range(steps):
+        q_dev.copy_(q_pin[i], non_blocking=True)
+        out_host.copy_(step_api(q_dev, step=i), non_blocking=True)
+        stream.synchronize()
+    dt_calls = time.perf_counter() - t1
+    del graphed
     return {"value": shape.batch * steps / dt, "unit": "tokens/s",
-            "h2d_bytes_per_step": int(q_host[0].numel() * 4),
+            "h2d_bytes_per_step": int(q_host.numel() * 4) + 8,
             "d2h_bytes_per_step": int(out_host.numel() * 4),
-            "api": "santapp_b200.attention.DecodeStep (ctypes -> santa_decode_plan / "
-                   "santa_decode_execute C ABI)"}
+            "api": "santapp_b200.attention.GraphedDecodeStep.run (DecodeStep captured with "
+                   "its transfers; C ABI santa_decode_plan / santa_decode_execute)",
+            "per_call_api": {"value": shape.batch * steps / dt_calls, "unit": "tokens/s",
+                             "api": "torch copies + DecodeStep (santa_decode_plan + "
+                                    "santa_decode_execute per step)"}}
 
 
 def _port_sample(shape, seed, n_seq=1):

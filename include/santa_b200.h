@@ -122,6 +122,9 @@ typedef struct SantaDecodeParams {
     uint64_t seed;         /* Philox key for device sampling */
     uint64_t step;         /* Philox counter word (decode step) */
     int32_t num_splits;    /* CTAs per (batch, KV head); 0 = pick automatically */
+    const uint64_t *step_dev; /* optional device word read by the kernels in place of
+                                 step (a decode step captured once in a CUDA graph and
+                                 replayed with a new step each time); NULL: step */
 } SantaDecodeParams;
 
 /* ---- library --------------------------------------------------------- */

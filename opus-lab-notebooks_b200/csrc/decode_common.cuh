@@ -543,6 +543,13 @@ int launch_select_group(DecodeArgs &a, cudaStream_t stream);
 int num_sms();
 int attend_partial_slots(const SantaGeometry *geo, int nsplit);
 
+// The Philox counter word of this decode step: the device word when the
+// caller supplied one (a captured step replayed with a new counter), else
+// the parameter.
+__device__ __forceinline__ uint64_t decode_step_word(const SantaDecodeParams &p) {
+    return p.step_dev ? *p.step_dev : p.step;
+}
+
 // Row costs on which the gather attention kernel splits the step's rows into
 // equal CTA shares (a 32-bit scale: the API rejects geometries whose total
 // could overflow it).

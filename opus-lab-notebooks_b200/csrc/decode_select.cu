@@ -583,6 +583,7 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
         float *soff = a.ws.s_off + (int64_t)bh * g * S + sbase;
         const int64_t inj = ((int64_t)b * a.geo.num_kv_heads * g + gh) * S;
         const uint2 key = make_uint2((uint32_t)a.p.seed, (uint32_t)(a.p.seed >> 32));
+        const uint32_t stepw = (uint32_t)decode_step_word(a.p);
         const float logS = logf((float)ns);
         if (mode == SANTA_MODE_HYBRID) {
             const int *gap = gapcum + h * (2 * kcap + 1);
@@ -601,7 +602,7 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
                     r = (uint32_t)v;
                 } else {
                     const uint4 w = philox4x32_10(
-                        make_uint4((uint32_t)(i >> 2), (uint32_t)gh, (uint32_t)b, (uint32_t)a.p.step),
+                        make_uint4((uint32_t)(i >> 2), (uint32_t)gh, (uint32_t)b, stepw),
                         key);
                     r = (uint32_t)(((uint64_t)uint4_word(w, i & 3) * (uint64_t)n_rest) >> 32);
                 }
@@ -635,7 +636,7 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
                     }
                 } else {
                     const uint4 w = philox4x32_10(
-                        make_uint4((uint32_t)(i >> 1), (uint32_t)gh, (uint32_t)b, (uint32_t)a.p.step),
+                        make_uint4((uint32_t)(i >> 1), (uint32_t)gh, (uint32_t)b, stepw),
                         key);
                     const uint32_t w0 = (i & 1) ? w.z : w.x, w1 = (i & 1) ? w.w : w.y;
                     const float u = (float)(w0 >> 8) * (1.0f / 16777216.0f) * total;
@@ -669,7 +670,7 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
                     }
                 } else {
                     const uint4 w = philox4x32_10(
-                        make_uint4((uint32_t)(i >> 2), (uint32_t)gh, (uint32_t)b, (uint32_t)a.p.step),
+                        make_uint4((uint32_t)(i >> 2), (uint32_t)gh, (uint32_t)b, stepw),
                         key);
                     t = (int)(((uint64_t)uint4_word(w, i & 3) * (uint64_t)sample_end) >> 32);
                 }

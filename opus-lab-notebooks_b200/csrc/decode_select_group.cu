@@ -709,6 +709,7 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
         float *soff = a.ws.s_off + (int64_t)bh * g * S + sbase;
         const int64_t inj = ((int64_t)b * a.geo.num_kv_heads * g + gh) * S;
         const uint2 key = make_uint2((uint32_t)a.p.seed, (uint32_t)(a.p.seed >> 32));
+        const uint32_t stepw = (uint32_t)decode_step_word(a.p);
         const float logS = logf((float)ns);
         const int n_rest = sample_end - info_s[1];
         const float off = (logf((float)n_rest) - logS) * kLog2e;
@@ -723,7 +724,7 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
                 r = (uint32_t)v;
             } else {
                 const uint4 w = philox4x32_10(
-                    make_uint4((uint32_t)(i >> 2), (uint32_t)gh, (uint32_t)b, (uint32_t)a.p.step),
+                    make_uint4((uint32_t)(i >> 2), (uint32_t)gh, (uint32_t)b, stepw),
                     key);
                 r = (uint32_t)(((uint64_t)uint4_word(w, i & 3) * (uint64_t)n_rest) >> 32);
             }

@@ -53,7 +53,8 @@ class SantaSummary(ctypes.Structure):
 class SantaDecodeParams(ctypes.Structure):
     _fields_ = [("mode", _i32), ("topk_clusters", _i32), ("token_budget", _i32),
                 ("samples", _i32), ("scale", ctypes.c_float), ("sample_source", _i32),
-                ("seed", ctypes.c_uint64), ("step", ctypes.c_uint64), ("num_splits", _i32)]
+                ("seed", ctypes.c_uint64), ("step", ctypes.c_uint64), ("num_splits", _i32),
+                ("step_dev", _vp)]
 
 
 class SantaP2P(ctypes.Structure):

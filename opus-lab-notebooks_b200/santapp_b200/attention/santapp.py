@@ -33,6 +33,7 @@ from .paged import PagedKVCache
 __all__ = [
     "ClusterSummary", "build_summary", "santa_decode", "DecodeResult", "DecodeWorkspace",
     "DecodeTrafficTracker", "santa_decode_select", "allocate_summary", "DecodeStep",
+    "GraphedDecodeStep",
 ]
 
 
@@ -384,6 +385,77 @@ class DecodeStep:
         """Kernels of this library launched per step: select and attend, plus
         the old-prefix LSE pass in santa mode."""
         return 2 + (1 if self.mode == "santa" else 0)
+
+    def graphed(self, q_host: torch.Tensor, out_host: torch.Tensor) -> "GraphedDecodeStep":
+        """This step captured once in a CUDA graph together with its host
+        transfers (see ``GraphedDecodeStep``)."""
+        return GraphedDecodeStep(self, q_host, out_host)
+
+
+class GraphedDecodeStep:
+    """A ``DecodeStep`` and its host transfers as one CUDA graph.
+
+    Per ``run(step)`` the graph copies the queries in from the pinned host
+    buffer ``q_host`` ([B, Hq, D] fp32) together with the Philox step
+    counter (a device word the selection kernel reads in place of the
+    parameter, so each replay draws the samples of its own step), runs the
+    selection and the attention, and copies the output into the pinned
+    ``out_host``.  One graph launch per decode step instead of four API
+    calls; the output is in ``out_host`` once the stream is synchronised.
+    Write a step's queries into ``q_host`` only after the previous step's
+    output was read (the graph reads the buffer when it runs)."""
+
+    def __init__(self, step: DecodeStep, q_host: torch.Tensor, out_host: torch.Tensor):
+        for name, t in (("q_host", q_host), ("out_host", out_host)):
+            if t.device.type != "cpu" or not t.is_pinned() or t.dtype != torch.float32:
+                raise ValueError(f"{name} must be a pinned fp32 host tensor")
+            if tuple(t.shape) != tuple(step.out.shape):
+                raise ValueError(f"{name} must be {tuple(step.out.shape)}")
+        if step.p.sample_source != _lib.SAMPLES_DEVICE:
+            raise ValueError("a graphed step draws its samples on the device")
+        self.step, self.q_host, self.out_host = step, q_host, out_host
+        dev = step.out.device
+        self.q_dev = torch.empty(q_host.shape, dtype=torch.float32, device=dev)
+        self.step_host = torch.zeros(1, dtype=torch.int64).pin_memory()
+        self.step_dev = torch.zeros(1, dtype=torch.int64, device=dev)
+        # the step's parameters with the counter read from the device word
+        self.p = _lib.SantaDecodeParams.from_buffer_copy(step.p)
+        self.p.step_dev = self.step_dev.data_ptr()
+        self._refs = (ctypes.byref(step.geo), ctypes.byref(self.p), ctypes.byref(step.c))
+        stream = torch.cuda.Stream(device=dev)
+        stream.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(stream):
+            for _ in range(2):   # first launches (function attributes) outside the capture
+                self._body()
+        stream.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=stream):
+            self._body()
+        torch.cuda.synchronize(dev)
+
+    def _body(self) -> None:
+        st = self.step
+        g, p, c = self._refs
+        self.q_dev.copy_(self.q_host, non_blocking=True)
+        self.step_dev.copy_(self.step_host, non_blocking=True)
+        _lib.check("santa_decode_plan", st.lib.santa_decode_plan(
+            g, p, self.q_dev.data_ptr(), st.key_cache.data_ptr(), st.value_cache.data_ptr(), c,
+            None, None, _lib.ptr(st.n_exact), st.ws.data_ptr(), st.ws_bytes,
+            _lib.stream_handle()))
+        _lib.check("santa_decode_execute", st.lib.santa_decode_execute(
+            g, p, self.q_dev.data_ptr(), st.key_cache.data_ptr(), st.value_cache.data_ptr(), c,
+            st.out.data_ptr(), st.lse.data_ptr(), _lib.ptr(st.ess), st.ws.data_ptr(),
+            st.ws_bytes, _lib.stream_handle()))
+        self.out_host.copy_(st.out, non_blocking=True)
+
+    def run(self, step: int) -> None:
+        """Enqueue decode step ``step`` on the current stream (not synchronised)."""
+        self.step_host[0] = int(step) & 0x7FFFFFFFFFFFFFFF
+        self.graph.replay()
+
+    @property
+    def kernels_per_call(self) -> int:
+        return self.step.kernels_per_call
 
 
 def santa_decode_select(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,

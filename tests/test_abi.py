@@ -44,9 +44,10 @@ def test_status_strings_and_version():
 
 
 def test_struct_layout_matches_c():
-    # SantaDecodeParams: 4 x int32, float, int32, 2 x uint64, int32 (+pad)
-    assert ctypes.sizeof(_lib.SantaDecodeParams) == 48
+    # SantaDecodeParams: 4 x int32, float, int32, 2 x uint64, int32 (+pad), pointer
+    assert ctypes.sizeof(_lib.SantaDecodeParams) == 56
     assert _lib.SantaDecodeParams.seed.offset == 24
+    assert _lib.SantaDecodeParams.step_dev.offset == 48
     # SantaGeometry: 8 x int32, pointer, 4 x int32
     assert ctypes.sizeof(_lib.SantaGeometry) == 56
     assert _lib.SantaGeometry.block_table.offset == 32
