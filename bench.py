@@ -450,13 +450,12 @@ def load_traffic(shape):
 
 def run_e2e(args, shape, w, summ, runner):
     """Through the public decode API with host buffers, the way a serving
-    loop calls it, synchronised every step: the step's queries are copied on
-    the host into the pinned staging buffer, then one GraphedDecodeStep
-    launch (the DecodeStep bound once to the cache and summary, captured with
-    its transfers: queries and step counter host->device, selection,
-    attention, output device->pinned host), then the stream is synchronised
-    and the output is in host memory.  The per-call form (torch copies around
-    DecodeStep's santa_decode_plan + santa_decode_execute) is timed beside it."""
+    loop calls it, synchronised every step: the step's queries copied
+    host->device from pinned memory, DecodeStep (santa_decode_plan +
+    santa_decode_execute, C ABI), the output copied into pinned host memory.
+    The graph-captured form (GraphedDecodeStep: the step's queries copied on
+    the host into the pinned staging buffer, then one graph launch holding
+    the transfers, the selection and the attention) is timed beside it."""
     from santapp_b200.attention import santapp as S
     steps = args.steps
     q_all = w.queries[:steps].cpu()                     # the steps' queries on the host
@@ -493,14 +492,16 @@ def run_e2e(args, shape, w, summ, runner):
         stream.synchronize()
     dt_calls = time.perf_counter() - t1
     del graphed
-    return {"value": shape.batch * steps / dt, "unit": "tokens/s",
-            "h2d_bytes_per_step": int(q_host.numel() * 4) + 8,
+    return {"value": shape.batch * steps / dt_calls, "unit": "tokens/s",
+            "h2d_bytes_per_step": int(q_host.numel() * 4),
             "d2h_bytes_per_step": int(out_host.numel() * 4),
-            "api": "santapp_b200.attention.GraphedDecodeStep.run (DecodeStep captured with "
-                   "its transfers; C ABI santa_decode_plan / santa_decode_execute)",
-            "per_call_api": {"value": shape.batch * steps / dt_calls, "unit": "tokens/s",
-                             "api": "torch copies + DecodeStep (santa_decode_plan + "
-                                    "santa_decode_execute per step)"}}
+            "api": "santapp_b200.attention.DecodeStep (torch copies from / to pinned memory "
+                   "around santa_decode_plan + santa_decode_execute, C ABI)",
+            "graphed_api": {"value": shape.batch * steps / dt, "unit": "tokens/s",
+                            "h2d_bytes_per_step": int(q_host.numel() * 4) + 8,
+                            "api": "santapp_b200.attention.GraphedDecodeStep.run (host copy "
+                                   "into the pinned staging buffer, one graph launch with "
+                                   "the transfers, the selection and the attention)"}}
 
 
 def _port_sample(shape, seed, n_seq=1):
