@@ -112,6 +112,7 @@ static int prepare_decode(const SantaGeometry *geo, const SantaDecodeParams *p, 
     a->shard_cands = nullptr;
     a->part_out = nullptr;
     memset(&a->p2p, 0, sizeof(a->p2p));
+    a->tma = 0;  // set by the attention launcher
     decode_ws_layout(BH, summary->max_groups, geo->group, p->samples,
                      attend_partial_slots(geo, nsplit), geo->head_dim, geo->sample_end,
                      (char *)workspace, &a->ws);

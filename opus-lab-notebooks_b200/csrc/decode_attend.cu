@@ -31,6 +31,8 @@
 //   decode_attend_simt_kernel  fp32 caches, a warp per row.
 #include "decode_common.cuh"
 
+#include <cuda.h>  // CUtensorMap (the encode entry point is fetched at run time)
+
 #include <math.h>
 
 namespace santa {
@@ -174,19 +176,42 @@ constexpr int kGThreads = 32 * kGW;
 template <int D>
 struct GatherGeom {
     static constexpr int ROWB = D * 2;                // bytes of one bf16 row
-    static constexpr int PITCH = ROWB + 16;           // padded pitch: 8 rows hit 8 bank groups
-    static constexpr int TILE = kGRows * PITCH;       // one K (or V) warp tile
-    static constexpr int STAGE = 2 * TILE;            // K + V
+    static constexpr int BLOCKS = D / 64;             // 128-byte column blocks of a row
+    static constexpr int TILE = kGRows * ROWB;        // one K (or V) warp tile
+    static constexpr int STAGE = 2 * TILE;            // K + V; stages are 1024-byte aligned
     static constexpr int META = 2 * kGRows * 4;       // row masks + offsets of a stage
-    static constexpr int WARP = kGStages * (STAGE + META);
+    static constexpr int WARP = (kGStages * (STAGE + META) + 1023) / 1024 * 1024;
     static constexpr int CPR = ROWB / 16;             // 16-byte chunks per row
     static constexpr int RPI = 32 / CPR;              // rows per copy instruction
 };
 
+// Tile layout in shared memory: column block b (bytes [128 b, 128 b + 128) of
+// every row) is a [16 rows][128 bytes] block, and row r holds its 16-byte
+// chunk j of the block at slot j ^ (r % 8) -- the 128-byte swizzle a tensor
+// copy writes, which also keeps the eight rows of an ldmatrix phase on eight
+// distinct bank groups.  Byte offset of chunk c (0 .. D / 8 - 1) of row r:
+__device__ __forceinline__ int tile_off(int r, int c) {
+    return (c >> 3) * (kGRows * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+}
+
+// 2-D tensor copy (TMA engine) of one [16 rows][64 bf16] box of this GPU's
+// cluster-sorted K or V copy into shared memory, completing on an mbarrier;
+// no multicast.  x = first column (0 or 64: 128-byte aligned), y = first row.
+__device__ __forceinline__ void tma_box_g2s(void *dst, const CUtensorMap *map, int x, int y,
+                                            uint64_t *bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;\n"
+        ::"r"(smem_u32(dst)), "l"((uint64_t)(uintptr_t)map), "r"(x), "r"(y), "r"(smem_u32(bar)),
+        "l"(policy)
+        : "memory");
+}
+
 template <int D>
 inline size_t gather_smem_bytes(int BH) {
-    // rings, segment prefix [BH + 1], completed-segment bitmap [ceil(BH / 32)]
-    return 128 + (size_t)kGW * GatherGeom<D>::WARP + ((size_t)BH + 1) * 4 +
+    // 1024-byte alignment, rings, segment prefix [BH + 1], completed-segment
+    // bitmap [ceil(BH / 32)]
+    return 1024 + (size_t)kGW * GatherGeom<D>::WARP + ((size_t)BH + 1) * 4 +
            (size_t)((BH + 31) / 32) * 4;
 }
 
@@ -686,7 +711,9 @@ __device__ __forceinline__ RowEntry load_entry(const DecodeArgs &a, int bh, int 
 }
 
 template <int D>
-__global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(DecodeArgs a) {
+__global__ void __launch_bounds__(kGThreads, 1)
+    decode_attend_gather_kernel(DecodeArgs a, const __grid_constant__ CUtensorMap tmap_k,
+                                const __grid_constant__ CUtensorMap tmap_v) {
     using GG = GatherGeom<D>;
     constexpr int NT_O = D / 8;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -695,8 +722,18 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int gid = lane >> 2, tig = lane & 3;
 
-    unsigned char *base = (unsigned char *)(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
-    unsigned char *wbase = base + warp * GG::WARP;     // this warp's ring
+    unsigned char *base = (unsigned char *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    unsigned char *wbase = base + warp * GG::WARP;     // this warp's ring: stages, then metas
+    // one mbarrier per stage of every warp: completion of a stage's tensor copies
+    __shared__ __align__(8) uint64_t s_tma_bar[kGW][kGStages];
+    uint64_t *wbar = s_tma_bar[warp];
+    if (lane == 0) {
+#pragma unroll
+        for (int st = 0; st < kGStages; ++st) mbar_init(&wbar[st], 1);
+        mbar_fence_init();
+    }
+    __syncwarp();
+    uint32_t tma_pending = 0u, tma_phase = 0u;  // per stage: copies in flight, barrier parity
     int *pre = (int *)(base + kGW * GG::WARP);         // segment prefix [BH + 1]
     unsigned *done_bits = (unsigned *)(pre + BH + 1);  // segments this CTA merged (p2p)
     const bool fused = a.p2p.peers != nullptr;
@@ -813,8 +850,8 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
         auto tile_row0 = [&](int i) { return s0 + (j0 + i * kGW) * kGRows; };
         // issue the copies of my i-th tile into stage st from its prefetched entry
         auto issue = [&](int i, int st, const RowEntry &en) {
-            unsigned char *stg = wbase + st * (GG::STAGE + GG::META);
-            int *mk = (int *)(stg + GG::STAGE);
+            unsigned char *stg = wbase + st * GG::STAGE;
+            int *mk = (int *)(wbase + kGStages * GG::STAGE + st * GG::META);
             float *of = (float *)(mk + kGRows);
             // row code: >= 0 row of the cluster-sorted copy, -1 - x row x of
             // the cache (a recent-window token), INT_MIN no row
@@ -835,11 +872,35 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
                 mk[lane] = mask;
                 of[lane] = en.off;
             }
-            // row-cooperative copies: CPR lanes cover one row, so every
-            // instruction moves RPI whole rows (few cache lines per request;
-            // mapping a lane pair to each row instead measured 40% slower)
+            // sixteen consecutive rows of the cluster-sorted copy (a run of
+            // adjacent selected clusters): the tile moves as 2 * D / 64 tensor
+            // copies issued by one lane, completing on the stage's mbarrier
+            const int code0 = __shfl_sync(0xffffffffu, code, 0);
+            const bool run = a.tma && __all_sync(0xffffffffu, lane >= kGRows ||
+                                                               (en.kind == 1 && code == code0 + lane));
+            if (run) {
+                if (lane == 0) {
+                    uint64_t *bar = &wbar[st];
+                    // the stage's earlier generic-proxy reads and writes come first
+                    fence_proxy_async_smem();
+                    mbar_arrive_expect_tx(bar, (uint32_t)GG::STAGE);
+                    const int y = bh * a.geo.sample_end + code0;
+#pragma unroll
+                    for (int blk = 0; blk < GG::BLOCKS; ++blk) {
+                        tma_box_g2s(stg + blk * kGRows * 128, &tmap_k, 64 * blk, y, bar, kv_policy);
+                        tma_box_g2s(stg + GG::TILE + blk * kGRows * 128, &tmap_v, 64 * blk, y, bar,
+                                    kv_policy);
+                    }
+                }
+                tma_pending |= 1u << st;
+                (void)i;
+                return;
+            }
+            // otherwise row-cooperative 16-byte copies: CPR lanes cover one
+            // row, so every instruction moves RPI whole rows (few cache lines
+            // per request; mapping a lane pair to each row instead measured
+            // 40% slower)
             const int c = lane % GG::CPR;
-            const uint32_t kd0 = smem_u32(stg + (lane / GG::CPR) * GG::PITCH + c * 16);
 #pragma unroll
             for (int it = 0; it < kGRows / GG::RPI; ++it) {
                 const int r = it * GG::RPI + lane / GG::CPR;
@@ -850,7 +911,7 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
                 const int64_t dv = rc >= 0 ? (int64_t)((uintptr_t)sv - (uintptr_t)sk)
                                            : (int64_t)((uintptr_t)cv - (uintptr_t)ck);
                 const int ok = rc == INT_MIN ? 0 : 16;
-                const uint32_t kd = kd0 + it * GG::RPI * GG::PITCH;
+                const uint32_t kd = smem_u32(stg + tile_off(r, c));
                 asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;\n" ::"r"(kd),
                              "l"(ks + c * 16), "r"(ok), "l"(kv_policy)
                              : "memory");
@@ -897,10 +958,19 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
             __syncwarp();
 
             const int st = i % kGStages;
-            const unsigned char *stg = wbase + st * (GG::STAGE + GG::META);
+            // a stage filled by tensor copies: wait for its mbarrier (bounded;
+            // a local copy always lands -- a wait that gave up is reported in
+            // the segment's error word and the tile is used as it is)
+            if (tma_pending & (1u << st)) {
+                if (!mbar_wait(&wbar[st], (tma_phase >> st) & 1u) && lane == 0)
+                    atomicExch(&a.ws.flag[bh], 3);
+                tma_phase ^= 1u << st;
+                tma_pending &= ~(1u << st);
+            }
+            const unsigned char *stg = wbase + st * GG::STAGE;
             const char *ks_ = (const char *)stg;
             const char *vs_ = (const char *)stg + GG::TILE;
-            const int *mk = (const int *)(stg + GG::STAGE);
+            const int *mk = (const int *)(wbase + kGStages * GG::STAGE + st * GG::META);
             const float *of = (const float *)(mk + kGRows);
             const int mat = lane >> 3, mrow = lane & 7;
             float s0v[4] = {0.f, 0.f, 0.f, 0.f}, s1v[4] = {0.f, 0.f, 0.f, 0.f};
@@ -909,7 +979,7 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
                 uint32_t b0, b1, b2, b3;
                 const int r = ((mat >> 1) << 3) + mrow;
                 const int c = 2 * kk + (mat & 1);
-                ldmatrix_x4(smem_u32(ks_ + r * GG::PITCH + c * 16), b0, b1, b2, b3);
+                ldmatrix_x4(smem_u32(ks_ + tile_off(r, c)), b0, b1, b2, b3);
                 // A rows 0-7 = q hi parts, rows 8-15 = q lo parts (GQA heads
                 // fill at most 8 rows): one mma yields both halves
                 mma_bf16(s0v, qh[kk][0], ql[kk][0], qh[kk][1], ql[kk][1], b0, b1);
@@ -983,7 +1053,7 @@ __global__ void __launch_bounds__(kGThreads, 1) decode_attend_gather_kernel(Deco
                 uint32_t b0, b1, b2, b3;
                 const int r = ((mat & 1) << 3) + mrow;
                 const int c = 2 * j + (mat >> 1);
-                ldmatrix_x4_trans(smem_u32(vs_ + r * GG::PITCH + c * 16), b0, b1, b2, b3);
+                ldmatrix_x4_trans(smem_u32(vs_ + tile_off(r, c)), b0, b1, b2, b3);
                 // A rows 0-7 = p hi, rows 8-15 = p lo: accumulator rows gid
                 // and gid + 8 hold the two halves of head gid's output
                 mma_bf16(o[2 * j], ph0, pl0, ph2, pl2, b0, b1);
@@ -1199,6 +1269,45 @@ int attend_partial_slots(const SantaGeometry *geo, int nsplit) {
     return simt > gather ? simt : gather;
 }
 
+// cuTensorMapEncodeTiled from the driver, fetched once through the runtime
+// (no link against the driver library)
+typedef CUresult (*TensorMapEncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                         const cuuint64_t *, const cuuint64_t *,
+                                         const cuuint32_t *, const cuuint32_t *,
+                                         CUtensorMapInterleave, CUtensorMapSwizzle,
+                                         CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static TensorMapEncodeTiled tensor_map_encoder() {
+    static const TensorMapEncodeTiled fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            return (TensorMapEncodeTiled) nullptr;
+        }
+        return (TensorMapEncodeTiled)p;
+    }();
+    return fn;
+}
+
+// The [rows][D] bf16 cluster-sorted copy as a 2-D tensor of [16][64] boxes
+// with the 128-byte swizzle of the attention kernel's tile layout.
+template <int D>
+static bool sorted_copy_map(CUtensorMap *m, const void *base, int64_t rows) {
+    const TensorMapEncodeTiled enc = tensor_map_encoder();
+    if (!enc || !base || ((uintptr_t)base & 15) || rows <= 0 || rows >= ((int64_t)1 << 31))
+        return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)kGRows};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides,
+               box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
+
 template <int D>
 static int launch_execute_d(DecodeArgs &a, cudaStream_t stream) {
     const int BH = a.geo.batch * a.geo.num_kv_heads;
@@ -1221,7 +1330,17 @@ static int launch_execute_d(DecodeArgs &a, cudaStream_t stream) {
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        SANTA_CUDA_CHECK(cudaLaunchKernelEx(&cfg, decode_attend_gather_kernel<D>, a));
+        // tensor maps of the two cluster-sorted copies; if either cannot be
+        // made, every tile takes the 16-byte copy path
+        CUtensorMap mk, mv;
+        memset(&mk, 0, sizeof(mk));
+        memset(&mv, 0, sizeof(mv));
+        const int64_t rows = (int64_t)BH * a.geo.sample_end;
+        a.tma = sorted_copy_map<D>(&mk, a.sum.sorted_key, rows) &&
+                        sorted_copy_map<D>(&mv, a.sum.sorted_value, rows)
+                    ? 1
+                    : 0;
+        SANTA_CUDA_CHECK(cudaLaunchKernelEx(&cfg, decode_attend_gather_kernel<D>, a, mk, mv));
     } else {
         const size_t sm = simt_smem_bytes<D>(Gmax);
         if (int st = ensure_dyn_smem((const void *)decode_attend_simt_kernel<D, float>, sm))

@@ -161,6 +161,7 @@ struct DecodeArgs {
     const uint64_t *shard_cands;  // select: [num_shards][B*Hq][k] keys -> global top-k
     float *part_out;              // attend: unnormalised partial per (b, query head)
     P2PArgs p2p;                  // peers == nullptr: the caller exchanges
+    int tma;                      // attend: the sorted copies' tensor maps are valid
 };
 
 // rank r's key list region (this step's parity) in the buffer at base
