@@ -71,6 +71,10 @@ def parse_args():
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU instead of the workload's own (small profiler "
                          "captures; the reported runs use the workload's batch)")
+    ap.add_argument("--rank-share", type=int, default=1,
+                    help="one GPU runs the share of the job one of N sequence-shard ranks holds "
+                         "(1/N of the tokens, clusters, top-k clusters and samples), without the "
+                         "exchange: the per-rank cost behind the N-GPU curve")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="bound on the CPU-baseline sample")
     ap.add_argument("--transport", choices=["nccl", "p2p"], default="p2p",
@@ -376,6 +380,14 @@ def run_ours(args, rank, world):
     if args.batch is not None:
         shape = scaled_shape(shape, batch=args.batch,
                              name=shape.name.rsplit("-b", 1)[0] + f"-b{args.batch}")
+    if args.rank_share > 1:
+        n = args.rank_share
+        shape = scaled_shape(shape, name=f"{shape.name}-rank-share-1of{n}",
+                             context=shape.context // n,
+                             true_clusters=max(1, shape.true_clusters // n),
+                             n_clusters=max(1, shape.n_clusters // n),
+                             topk_clusters=max(1, shape.topk_clusters // n),
+                             samples=max(1, shape.samples // n))
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     res, (w, summ, runner) = measure_decode(args, shape, args.steps, args.warmup, dev, keep=True)
