@@ -59,6 +59,9 @@ def parse_args():
                     help="prompt length of the model workload (65536 reported; smaller for "
                          "quick checks)")
     ap.add_argument("--model-layers", type=int, default=28)
+    ap.add_argument("--kv-page-size", type=int, default=None,
+                    help="model workload: every layer's KV cache in pages of this many tokens "
+                         "(SantaB200Config.kv_page_size)")
     ap.add_argument("--mode", default="hybrid")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -738,7 +741,7 @@ def run_model(args):
     ids = torch.randint(0, 152064, (B, T), generator=g).to(dev)
     cfg = SantaB200Config(mode="hybrid", samples_per_head=256, topk_clusters=16, n_clusters=512,
                           recent_window=64, probe_queries=64, sample_seed=args.seed,
-                          kmeans=KMeansConfig())
+                          kmeans=KMeansConfig(), kv_page_size=args.kv_page_size)
     eng = SantaB200Engine(model, cfg)
     eng.log = log
     torch.cuda.synchronize()
@@ -758,6 +761,8 @@ def run_model(args):
         "data": "synthetic (random-init weights: matrices N(0, 0.02), norm gains 1, biases 0; "
                 "uniform random prompt tokens)",
         "config": {"workload": f"qwen2.5-7b-model-ctx{T}-b{B}", "layers": args.model_layers,
+                   "kv_cache": (f"paged, {args.kv_page_size}-token pages" if args.kv_page_size
+                                else "contiguous"),
                    "hidden": 3584, "query_heads": 28, "kv_heads": 4, "head_dim": 128,
                    "ffn": 18944, "vocab": 152064, "batch": B, "context": T, "clusters": 512,
                    "topk_clusters": 16, "samples": 256, "mode": "hybrid"},
