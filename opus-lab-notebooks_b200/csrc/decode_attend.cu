@@ -750,10 +750,13 @@ __global__ void __launch_bounds__(kGThreads, 1)
     // (a no-op when the launch had no such dependency).
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
 
-    if (warp == 0) {
+    {
+        // segment cost prefix, 256 segments per round over the whole CTA
+        // (one round of loads instead of a warp walking the segments)
+        __shared__ int s_wtot[kGW];
         int carry = 0;
-        for (int i0 = 0; i0 < BH; i0 += 32) {
-            const int i = i0 + lane;
+        for (int c0 = 0; c0 < BH; c0 += kGThreads) {
+            const int i = c0 + tid;
             // segment cost: kCostRow per union / recent row, kCostSample per
             // sampled row (scattered rows stream ~1.5x slower than contiguous
             // cluster rows)
@@ -767,14 +770,24 @@ __global__ void __launch_bounds__(kGThreads, 1)
                 const int y = __shfl_up_sync(0xffffffffu, x, o);
                 if (lane >= o) x += y;
             }
-            if (i < BH) pre[i + 1] = carry + x;
-            carry += __shfl_sync(0xffffffffu, x, 31);
+            if (lane == 31) s_wtot[warp] = x;
+            __syncthreads();
+            int before = 0, total = 0;
+#pragma unroll
+            for (int w = 0; w < kGW; ++w) {
+                const int v = s_wtot[w];
+                before += w < warp ? v : 0;
+                total += v;
+            }
+            if (i < BH) pre[i + 1] = carry + before + x;
+            carry += total;
+            __syncthreads();  // s_wtot is rewritten by the next round
         }
-        if (lane == 0) pre[0] = 0;
-    } else if (fused) {
-        for (int i = tid - 32; i < (BH + 31) / 32; i += kGThreads - 32) done_bits[i] = 0u;
+        if (tid == 0) pre[0] = 0;
+        if (fused)
+            for (int i = tid; i < (BH + 31) / 32; i += kGThreads) done_bits[i] = 0u;
     }
-    __syncthreads();  // the only block-wide barrier
+    __syncthreads();  // the prefix and the done bits are in place
 
     // every CTA takes an equal share [r0, r1) of the total cost; within a
     // segment (after its kCostSegment start charge), row v starts at cost
