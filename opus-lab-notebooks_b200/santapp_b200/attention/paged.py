@@ -238,7 +238,8 @@ class PagedKVCache:
         if self.dtype != torch.bfloat16:
             raise ValueError("the fused RoPE append writes bf16 pools")
         B, T, Hq, D = q.shape
-        if self._free is not None:
+        # pages are mapped only when the new tokens cross into an unmapped one
+        if self._free is not None and start + T > self._mapped * self.page_size:
             self.reserve(start + T)
         lib = _lib.load()
         _lib.check("santa_rope_append_paged", lib.santa_rope_append_paged(
