@@ -744,6 +744,12 @@ __global__ void __launch_bounds__(kGThreads, 1)
     // round trip on the tail's critical path.
     __shared__ __align__(16) DecodeArgs s_args;
     if (tid == kGThreads - 1) s_args = a;
+    // the tensor maps are kernel parameters, not outputs of the selection:
+    // their descriptors are fetched while the selection still runs
+    if (a.tma && tid == 0) {
+        asm volatile("prefetch.tensormap [%0];\n" ::"l"((uint64_t)(uintptr_t)&tmap_k) : "memory");
+        asm volatile("prefetch.tensormap [%0];\n" ::"l"((uint64_t)(uintptr_t)&tmap_v) : "memory");
+    }
     // Launched as a programmatic dependent of the selection kernel: this
     // CTA may start while the selection's last CTAs still run; everything
     // below reads what the selection wrote, so wait for it to complete
@@ -802,8 +808,24 @@ __global__ void __launch_bounds__(kGThreads, 1)
         return c <= kCostRow * ur ? ceil_div(c, kCostRow)
                                   : ur + ceil_div(c - kCostRow * ur, kCostSample);
     };
+    // first segment whose cost range ends after r0 (pre is non-decreasing; a
+    // binary search: a walk from segment 0 put the CTAs of the last segments
+    // microseconds behind the first ones)
     int bh0 = 0;
-    while (bh0 < BH && pre[bh0 + 1] <= r0) ++bh0;
+    {
+        int hi = BH;
+        while (bh0 < hi) {
+            const int mid = (bh0 + hi) >> 1;
+            if (pre[mid + 1] <= r0) bh0 = mid + 1;
+            else hi = mid;
+        }
+    }
+    // U and R of the next segment the loop meets, loaded one segment ahead
+    int nx_bh = bh0, nx_U = 0, nx_R = 0;
+    if (bh0 < BH) {
+        nx_U = a.ws.meta[(int64_t)bh0 * 8 + 1];
+        nx_R = a.ws.meta[(int64_t)bh0 * 8 + 2];
+    }
 
     const float qscale = a.p.scale * kLog2e;
     const int PSTR = partial_stride(D);
@@ -822,8 +844,19 @@ __global__ void __launch_bounds__(kGThreads, 1)
         // a CTA whose share meets the segment takes part in its merge even
         // when the share holds no row start (its warps write empty partials)
         if (c0 >= c1) continue;
-        const int32_t *meta = a.ws.meta + (int64_t)bh * 8;
-        const int U = meta[1], R = meta[2];
+        int U, R;
+        if (bh == nx_bh) {
+            U = nx_U;
+            R = nx_R;
+        } else {
+            U = a.ws.meta[(int64_t)bh * 8 + 1];
+            R = a.ws.meta[(int64_t)bh * 8 + 2];
+        }
+        if (bh + 1 < BH && pre[bh + 1] < r1) {  // the next segment's, while this one runs
+            nx_bh = bh + 1;
+            nx_U = a.ws.meta[(int64_t)(bh + 1) * 8 + 1];
+            nx_R = a.ws.meta[(int64_t)(bh + 1) * 8 + 2];
+        }
         const int s0 = row_at_cost(max(0, c0 - kCostSegment), U + R);
         const int s1 = row_at_cost(max(0, c1 - kCostSegment), U + R);
         const int nt = ceil_div(s1 - s0, kGRows);
