@@ -260,10 +260,9 @@ def measure_decode(args, shape, steps, warmup, dev, keep=False, page_size=None):
     # for serving: per step the L2 flush, then the selection and attention
     # kernels, timed on the device by event-record nodes around the two
     # kernels (the flush lies outside them).  Nothing sits between the two
-    # kernels, so the attention kernel's programmatic launch overlaps the
-    # selection's tail as in a serving loop.  A second graph of the same
-    # steps records one more event between the kernels: the phase split and
-    # the attention kernel's roofline come from it.
+    # kernels, as in a serving loop.  A second graph of the same steps
+    # records one more event between the kernels: the phase split and the
+    # attention kernel's roofline come from it.
     def capture(split):
         ev = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)]
               for _ in range(steps)]

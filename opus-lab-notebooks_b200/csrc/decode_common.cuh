@@ -557,11 +557,13 @@ __device__ __forceinline__ uint64_t decode_step_word(const SantaDecodeParams &p)
 constexpr int kCostRow = 2;     // balancing cost of a union or recent-window row
 constexpr int kCostSample = 3;  // balancing cost of a sampled (scattered) row
 // balancing cost of starting a segment (ring drain, CTA fold, the next
-// segment's q fragments, row entries and first copies: ~4 us, about 768
-// streamed rows, measured with per-CTA timers; 768 / 1536 / 2048 / 3072 swept
-// on both decode workloads, 1536 best); charged before the segment's first
-// row, so the CTA whose share covers a segment boundary takes fewer rows
-constexpr int kCostSegment = 1536;
+// segment's q fragments, row entries and first copies: ~4-5 us, measured with
+// per-CTA timers; 768 / 1024 / 1280 / 1536 / 2048 / 3072 swept on the 32K and
+// 128K decode workloads and on one rank's share of the 8-shard 128K job,
+// 1024-1536 within 1 us of each other, 1280 kept); charged before the
+// segment's first row, so the CTA whose share covers a segment boundary
+// takes fewer rows
+constexpr int kCostSegment = 1280;
 int launch_merge_shards(int rows, int head_dim, int num_shards, const float *partials,
                         float *out, float *lse, float *ess, cudaStream_t stream);
 

@@ -139,9 +139,6 @@ __global__ void __launch_bounds__(kSelThreads) decode_select_kernel(DecodeArgs a
     const int b = bh / a.geo.num_kv_heads, kv = bh - b * a.geo.num_kv_heads;
     const int g = a.geo.group;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    // the attention kernel that follows may launch now (it waits for this
-    // grid to complete before it reads anything this kernel writes)
-    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     const int Gmax = a.sum.max_groups;
     const int mode = a.p.mode;
     const int S = a.p.samples;

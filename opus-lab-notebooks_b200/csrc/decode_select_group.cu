@@ -365,9 +365,6 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
     __shared__ uint64_t meta_bar;               // the starts / lengths bulk copies
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    // the attention kernel that follows may launch now (it waits for this
-    // grid to complete before it reads anything this kernel writes)
-    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     const int g = a.geo.group;
     const int rank = (int)cl_rank();  // = blockIdx.x = the local query head
     const int h = rank;
