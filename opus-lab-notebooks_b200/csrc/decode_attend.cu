@@ -744,11 +744,16 @@ __global__ void __launch_bounds__(kGThreads, 1)
     // round trip on the tail's critical path.
     __shared__ __align__(16) DecodeArgs s_args;
     if (tid == kGThreads - 1) s_args = a;
-    // the tensor-map descriptors are fetched while the CTA computes its share
+    // the tensor maps are kernel parameters, not outputs of the selection
     if (a.tma && tid == 0) {
         asm volatile("prefetch.tensormap [%0];\n" ::"l"((uint64_t)(uintptr_t)&tmap_k) : "memory");
         asm volatile("prefetch.tensormap [%0];\n" ::"l"((uint64_t)(uintptr_t)&tmap_v) : "memory");
     }
+    // Launched as a programmatic dependent of the selection kernel, which
+    // triggers it as its CTAs finish: everything below reads what the
+    // selection wrote, so wait for that grid to complete (a no-op when the
+    // launch had no such dependency).
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
 
     {
         // segment cost prefix, 256 segments per round over the whole CTA
@@ -1358,18 +1363,23 @@ static int launch_execute_d(DecodeArgs &a, cudaStream_t stream) {
         const size_t sm = gather_smem_bytes<D>(BH);
         if (sm > 227 * 1024) return SANTA_ERR_UNSUPPORTED;
         if (int st = ensure_dyn_smem((const void *)decode_attend_gather_kernel<D>, sm)) return st;
-        // A plain stream-ordered launch after the selection kernel.  As a
-        // programmatic dependent of the selection (its CTAs resident early
-        // on the SMs the selection leaves free, waiting on
-        // griddepcontrol.wait) the step measured slower on B200: 232.5 vs
-        // 223.7 us at 128K, 81.1 vs 69.4 us at 32K.
+        // Programmatic dependent launch: the grid is scheduled as the
+        // selection kernel's CTAs finish (they trigger it at their end), so
+        // its launch latency overlaps their exit (0.4-1 us per step).  With
+        // the trigger at the selection's start instead, the attention CTAs
+        // occupied the SMs the selection left free and the step measured
+        // slower than a plain stream-ordered launch: 232.5 vs 223.7 us at
+        // 128K, 81.1 vs 69.4 us at 32K.
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((unsigned)num_sms(), 1, 1);
         cfg.blockDim = dim3(kGThreads, 1, 1);
         cfg.dynamicSmemBytes = sm;
         cfg.stream = stream;
-        cfg.attrs = nullptr;
-        cfg.numAttrs = 0;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
         // tensor maps of the two cluster-sorted copies; if either cannot be
         // made, every tile takes the 16-byte copy path
         CUtensorMap mk, mv;

@@ -736,6 +736,11 @@ __global__ void __launch_bounds__(kGrpThreads, 4) decode_select_group_kernel(Dec
             soff[i] = off;
         }
     }
+    // the attention kernel may be scheduled once every CTA of this grid got
+    // here (its griddepcontrol.wait still waits for this grid's completion
+    // and memory flush); triggered at the start instead, the attention CTAs
+    // sat on the SMs this grid left free and the step measured 4-12 us slower
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     cl_wait();  // no CTA leaves while another may still read its shared memory
 }
 
