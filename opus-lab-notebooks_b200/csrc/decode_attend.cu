@@ -459,11 +459,13 @@ __device__ void merge_segments_to_output(const DecodeArgs &a, const int *seg, co
 
 // The segments a CTA completes when each has at most kDirectMax partials:
 // one warp per (segment, head), a lane per VPL = D / 32 consecutive dims.
-// Two pairs at a time, every header and value the pair needs is loaded in
-// one batch straight from the partial slots (no staging, no barrier: the
-// whole merge is one L2 round trip), then the factors and sums are formed
-// in ascending partial order as in the staged merges (the maximum over the
-// non-empty partials, f_s = 2^(m_s - M), L = sum f_s l_s, acc = sum f_s v_s).
+// Every header and value of the pair is loaded in one batch straight from
+// the partial slots (no staging, no barrier: the whole merge is one L2 round
+// trip), then the factors and sums are formed in ascending partial order as
+// in the staged merges (the maximum over the non-empty partials,
+// f_s = 2^(m_s - M), L = sum f_s l_s, acc = sum f_s v_s).  One pair per
+// pass: the merge runs once per kernel, as the last code a CTA fetches, and
+// a second unrolled pair doubled the instructions it fetched.
 constexpr int kDirectMax = 8;
 template <int D>
 __device__ void merge_pairs_direct(const DecodeArgs &a, const int *seg, const int *first,
@@ -472,92 +474,79 @@ __device__ void merge_pairs_direct(const DecodeArgs &a, const int *seg, const in
     const int g = a.geo.group, PSTR = partial_stride(D);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int npairs = nseg * g;
-    for (int p0 = warp; p0 < npairs; p0 += 2 * kGW) {
-        float mv[2][kDirectMax], lv[2][kDirectMax], vv[2][kDirectMax][VPL];
-        float xs[2][kDirectMax][3];  // ms e1 e2 (lane 0)
-        int ns[2], bhs[2], hhs[2];
+    for (int p = warp; p < npairs; p += kGW) {
+        const int si = p / g, hh = p - si * g;
+        const int n = count[si], bh = seg[si];
+        const int ns = lane == 0 ? a.ws.head_meta[((int64_t)bh * 8 + hh) * 2 + 1] : 0;
+        const float *src = a.ws.partial + ((int64_t)first[si] + bh) * wstride + hh * PSTR;
+        float mv[kDirectMax], lv[kDirectMax], vv[kDirectMax][VPL];
+        float xs[kDirectMax][3];  // ms e1 e2 (lane 0)
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int p = p0 + u * kGW;
-            const bool on = p < npairs;
-            const int si = on ? p / g : 0, hh = on ? p - si * g : 0;
-            const int n = on ? count[si] : 0, bh = seg[si];
-            bhs[u] = bh;
-            hhs[u] = hh;
-            ns[u] = (on && lane == 0) ? a.ws.head_meta[((int64_t)bh * 8 + hh) * 2 + 1] : 0;
-            const float *src = a.ws.partial + ((int64_t)first[si] + bh) * wstride + hh * PSTR;
+        for (int s = 0; s < kDirectMax; ++s) {
+            mv[s] = -INFINITY;
+            lv[s] = 0.f;
+            xs[s][0] = -INFINITY;
+            xs[s][1] = xs[s][2] = 0.f;
 #pragma unroll
-            for (int s = 0; s < kDirectMax; ++s) {
-                mv[u][s] = -INFINITY;
-                lv[u][s] = 0.f;
-                xs[u][s][0] = -INFINITY;
-                xs[u][s][1] = xs[u][s][2] = 0.f;
-#pragma unroll
-                for (int e = 0; e < VPL; ++e) vv[u][s][e] = 0.f;
-                if (s < n) {
-                    const float *ps = src + (int64_t)s * wstride;
-                    mv[u][s] = ps[0];
-                    lv[u][s] = ps[1];
-                    if constexpr (VPL == 4) {
-                        const float4 x = *(const float4 *)(ps + 8 + 4 * lane);
-                        vv[u][s][0] = x.x;
-                        vv[u][s][1] = x.y;
-                        vv[u][s][2] = x.z;
-                        vv[u][s][3] = x.w;
-                    } else {
-                        const float2 x = *(const float2 *)(ps + 8 + 2 * lane);
-                        vv[u][s][0] = x.x;
-                        vv[u][s][1] = x.y;
-                    }
-                    if (lane == 0) {
-                        xs[u][s][0] = ps[2];
-                        xs[u][s][1] = ps[3];
-                        xs[u][s][2] = ps[4];
-                    }
+            for (int e = 0; e < VPL; ++e) vv[s][e] = 0.f;
+            if (s < n) {
+                const float *ps = src + (int64_t)s * wstride;
+                mv[s] = ps[0];
+                lv[s] = ps[1];
+                if constexpr (VPL == 4) {
+                    const float4 x = *(const float4 *)(ps + 8 + 4 * lane);
+                    vv[s][0] = x.x;
+                    vv[s][1] = x.y;
+                    vv[s][2] = x.z;
+                    vv[s][3] = x.w;
+                } else {
+                    const float2 x = *(const float2 *)(ps + 8 + 2 * lane);
+                    vv[s][0] = x.x;
+                    vv[s][1] = x.y;
+                }
+                if (lane == 0) {
+                    xs[s][0] = ps[2];
+                    xs[s][1] = ps[3];
+                    xs[s][2] = ps[4];
                 }
             }
         }
+        float M = -INFINITY, MS = -INFINITY;
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            if (p0 + u * kGW >= npairs) break;  // warp-uniform
-            float M = -INFINITY, MS = -INFINITY;
+        for (int s = 0; s < kDirectMax; ++s) {
+            if (lv[s] > 0.f) M = fmaxf(M, mv[s]);
+            if (xs[s][1] > 0.f) MS = fmaxf(MS, xs[s][0]);
+        }
+        float L = 0.f, E1 = 0.f, E2 = 0.f, acc[VPL];
 #pragma unroll
-            for (int s = 0; s < kDirectMax; ++s) {
-                if (lv[u][s] > 0.f) M = fmaxf(M, mv[u][s]);
-                if (xs[u][s][1] > 0.f) MS = fmaxf(MS, xs[u][s][0]);
+        for (int e = 0; e < VPL; ++e) acc[e] = 0.f;
+#pragma unroll
+        for (int s = 0; s < kDirectMax; ++s) {
+            const float f = lv[s] > 0.f ? exp2f(mv[s] - M) : 0.f;
+            L = fmaf(lv[s], f, L);
+#pragma unroll
+            for (int e = 0; e < VPL; ++e) acc[e] = fmaf(f, vv[s][e], acc[e]);
+            if (xs[s][1] > 0.f) {
+                const float fe = exp2f(xs[s][0] - MS);
+                E1 = fmaf(xs[s][1], fe, E1);
+                E2 = fmaf(xs[s][2], fe * fe, E2);
             }
-            float L = 0.f, E1 = 0.f, E2 = 0.f, acc[VPL];
+        }
+        const float inv_l = L > 0.f ? 1.f / L : 0.f;
+        if (!a.part_out && ((uintptr_t)a.out & 15) == 0) {
+            // one vector store per lane: the warp writes the head's row whole
+            float *o = a.out + ((int64_t)bh * g + hh) * D + VPL * lane;
+            if constexpr (VPL == 4)
+                *(float4 *)o = make_float4(acc[0] * inv_l, acc[1] * inv_l, acc[2] * inv_l,
+                                           acc[3] * inv_l);
+            else
+                *(float2 *)o = make_float2(acc[0] * inv_l, acc[1] * inv_l);
+            if (lane == 0)  // lse / ess (and the dim-0 value again, identical)
+                write_merged<D>(a, bh, hh, 0, acc[0], M, L, MS, E1, E2, ns, inv_l);
+        } else {
 #pragma unroll
-            for (int e = 0; e < VPL; ++e) acc[e] = 0.f;
-#pragma unroll
-            for (int s = 0; s < kDirectMax; ++s) {
-                const float f = lv[u][s] > 0.f ? exp2f(mv[u][s] - M) : 0.f;
-                L = fmaf(lv[u][s], f, L);
-#pragma unroll
-                for (int e = 0; e < VPL; ++e) acc[e] = fmaf(f, vv[u][s][e], acc[e]);
-                if (xs[u][s][1] > 0.f) {
-                    const float fe = exp2f(xs[u][s][0] - MS);
-                    E1 = fmaf(xs[u][s][1], fe, E1);
-                    E2 = fmaf(xs[u][s][2], fe * fe, E2);
-                }
-            }
-            const float inv_l = L > 0.f ? 1.f / L : 0.f;
-            if (!a.part_out && ((uintptr_t)a.out & 15) == 0) {
-                // one vector store per lane: the warp writes the head's row whole
-                float *o = a.out + ((int64_t)bhs[u] * g + hhs[u]) * D + VPL * lane;
-                if constexpr (VPL == 4)
-                    *(float4 *)o = make_float4(acc[0] * inv_l, acc[1] * inv_l, acc[2] * inv_l,
-                                               acc[3] * inv_l);
-                else
-                    *(float2 *)o = make_float2(acc[0] * inv_l, acc[1] * inv_l);
-                if (lane == 0)  // lse / ess (and the dim-0 value again, identical)
-                    write_merged<D>(a, bhs[u], hhs[u], 0, acc[0], M, L, MS, E1, E2, ns[u], inv_l);
-            } else {
-#pragma unroll
-                for (int e = 0; e < VPL; ++e)
-                    write_merged<D>(a, bhs[u], hhs[u], VPL * lane + e, acc[e], M, L, MS, E1, E2,
-                                    ns[u], inv_l);
-            }
+            for (int e = 0; e < VPL; ++e)
+                write_merged<D>(a, bh, hh, VPL * lane + e, acc[e], M, L, MS, E1, E2, ns, inv_l);
         }
     }
 }
