@@ -1,10 +1,10 @@
 """Host logic of the sequence-sharded decode, on CPU.
 
 The shard bounds, the sample split and the Philox seeds are checked
-directly; the two exchanges run on two gloo ranks with the kernels replaced
+directly; the two exchanges run on two and on four gloo ranks with the kernels replaced
 by their oracle restatements (``shard_candidate_keys``, ``keys_threshold``,
 ``hybrid_shard_partial``, ``merge_shard_partials``), and the merged result
-is compared with the oracle's sharded estimator over both shards' data.
+is compared with the oracle's sharded estimator over every shard's data.
 """
 import math
 import os
@@ -135,11 +135,14 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_two_gloo_ranks_exchange_and_merge_match_the_sharded_oracle():
+@pytest.mark.parametrize("world", [2, 4])
+def test_gloo_ranks_exchange_and_merge_match_the_sharded_oracle(world):
+    """Two ranks, and four (the shard count of the 4-GPU scaling run: every
+    rank's keys in the threshold, the recent window on the last rank only)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
