@@ -131,3 +131,47 @@ def test_paged_append_validates_arguments():
     # past the last page of the table
     assert lib.santa_rope_append_paged(*args, fake, 64, 4, 4, 256, None, None,
                                        None) == _lib.SANTA_ERR_INVALID_ARGUMENT
+
+
+def test_peer_exchange_layout_matches_the_library():
+    """The Python layout of a peer-memory exchange buffer (the one the
+    emulated-shard GPU test writes words into) and the library's size query
+    agree for every shard count the scaling runs use; shard counts past the
+    limit are refused."""
+    from santapp_b200.attention.sharded import exchange_layout
+    lib = _lib.load()
+    n = ctypes.c_size_t()
+    for shards in (1, 2, 4, 8, _lib.MAX_SHARDS):
+        for rows, topk, d in ((512, 32, 128), (224, 16, 128), (14, 8, 64)):
+            assert lib.santa_p2p_buffer_bytes(shards, rows, topk, d, ctypes.byref(n)) == 0
+            lay = exchange_layout(shards, rows, topk, d)
+            assert n.value == lay["bytes"], (shards, rows, topk, d)
+            # regions in order, keys after the set-up block, lines 16-byte aligned
+            assert lay["keys"] < lay["parts"] < lay["stage"] < lay["bytes"]
+            assert lay["parts"] % 16 == 0 and lay["stage"] % 16 == 0
+            assert lay["parts"] - lay["keys"] >= 2 * shards * rows * topk * 8
+    assert lib.santa_p2p_buffer_bytes(_lib.MAX_SHARDS + 1, 512, 32, 128, ctypes.byref(n)) != 0
+    assert lib.santa_p2p_buffer_bytes(2, 0, 32, 128, ctypes.byref(n)) != 0
+
+
+def test_exchange_words_carry_the_epoch():
+    """Key words carry the tag epoch % 255 + 1 in bits 24-31 (the byte a
+    global cluster id below 2^24 - 1 leaves all ones) and partial words the
+    32-bit epoch in the high half, so a consumer tells this step's words from
+    the previous step's in the same parity slot (epochs two apart)."""
+    import torch
+    from santapp_b200.attention.sharded import key_words, partial_words
+    order = torch.tensor([0x3F800000 | 0x80000000, 0x40000000 | 0x80000000], dtype=torch.int64)
+    cid = torch.tensor([5, (1 << 24) - 2], dtype=torch.int64)
+    keys = (order << 32) | (0xFFFFFFFF - cid)
+    for epoch in (1, 2, 254, 255, 256, 1000):
+        w = key_words(keys, epoch)
+        tag = (w >> 24) & 0xFF
+        assert bool((tag == epoch % 255 + 1).all())
+        assert int(((key_words(keys, epoch + 2) >> 24) & 0xFF)[0]) != int(tag[0])
+        # everything but the tag byte is the key's
+        assert bool(((w & -0xFF000001) == (keys & -0xFF000001)).all())
+        p = torch.tensor([1.5, -2.25, 0.0], dtype=torch.float32)
+        pw = partial_words(p, epoch)
+        assert bool((((pw >> 32) & 0xFFFFFFFF) == epoch).all())
+        assert torch.equal((pw & 0xFFFFFFFF).to(torch.int32).view(torch.float32), p)
